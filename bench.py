@@ -1,0 +1,442 @@
+"""Benchmark of the B200 det+rec hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload W] [--impl b200|reference]
+
+Under torchrun (N > 1) every rank owns one GPU and an independent shard of
+the work (pages are independent: no collective on the data path); the timed
+region is bracketed by a barrier + device synchronise and the reported time
+is the maximum over ranks.
+
+Workloads:
+  ctc         config 2: 512 lines x 80 steps x 18385-class fp16 logits per GPU
+  preprocess  config 3: 256 u8 HWC images (sides 600..2000) -> fp16 960x960 NCHW
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+MEASURED = ROOT / "MEASURED_PEAKS.json"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def hbm_peak():
+    if MEASURED.exists():
+        try:
+            return float(json.loads(MEASURED.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+# ---------------------------------------------------------------- clocks ----
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self._t:
+            self._t.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------- workloads ----
+class CtcWorkload:
+    """fused CTC greedy decode of fp16 logits."""
+    name = "ctc_greedy_512x80x18385_fp16"
+    metric = "lines/sec CTC greedy decode (512x80x18385 fp16 logits)"
+    unit = "lines/s"
+    dtype = "f16"
+    B, T, V = 512, 80, 18385
+
+    def __init__(self, dev, seed, units=None):
+        from turboocr_b200 import kernels as K
+        from turboocr_b200._lib import synth
+        self.K = K
+        self.dev = dev
+        if units:
+            self.B = units
+            self.units_per_step = units
+            self.algo_bytes = units * self.T * self.V * 2
+        self.x = torch.empty(self.B, self.T, self.V, dtype=torch.float16, device=dev)
+        self.plan = torch.empty(self.B * self.T, dtype=torch.int32, device=dev)
+        assert synth().tocr_synth_ctc_logits(self.x.data_ptr(), self.plan.data_ptr(), self.B,
+                                             self.T, self.V, seed, None) == 0
+        self.out = K.CtcOutputs(self.B, self.T, dev)
+        torch.cuda.synchronize()
+
+    units_per_step = B
+    launches_per_step = 2
+    algo_bytes = B * T * V * 2  # logits read once
+    l2_note = "inputs 1.51 GB > 126 MB L2 (no flush needed)"
+
+    def step(self):
+        self.K.ctc_greedy_f16(self.x, self.V, self.out)
+
+    def dominant_kernel_ms(self, iters=10):
+        s = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(iters):
+            self.step()
+        e1.record(s)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / iters
+
+    # end-to-end: pinned host logits -> H2D -> decode -> D2H of tokens/scores
+    def setup_e2e(self):
+        self.h_x = torch.empty(self.x.shape, dtype=torch.float16, pin_memory=True)
+        self.h_x.copy_(self.x)
+        self.h_tok = torch.empty(self.B * self.T, dtype=torch.int32, pin_memory=True)
+        self.h_len = torch.empty(self.B, dtype=torch.int32, pin_memory=True)
+        self.h_sc = torch.empty(self.B, dtype=torch.float32, pin_memory=True)
+        self.h2d = self.h_x.numel() * 2
+        self.d2h = self.h_tok.numel() * 4 + self.B * 8
+
+    def e2e_step(self):
+        self.x.copy_(self.h_x, non_blocking=True)
+        self.K.ctc_greedy_f16(self.x, self.V, self.out)
+        self.h_tok.copy_(self.out.tokens, non_blocking=True)
+        self.h_len.copy_(self.out.lengths, non_blocking=True)
+        self.h_sc.copy_(self.out.scores, non_blocking=True)
+
+    def cpu_baseline(self, cores, budget_s=15.0):
+        """Reference ctc_decode.cpp (decode_raw + max-softmax beside it) on
+        fp32-converted lines over `cores` std::threads, bounded sample."""
+        from oracle import ctc_oracle as co
+        n = max(cores * 2, 16)
+        sample = self.x[:n].float().cpu().numpy()
+        t0 = time.perf_counter()
+        reps = 0
+        while True:
+            co.ref_decode_batch(sample, self.V, cores, simd=True)
+            reps += 1
+            if time.perf_counter() - t0 > budget_s or reps >= 50:
+                break
+        dt = time.perf_counter() - t0
+        return {"value": n * reps / dt, "unit": self.unit, "cores": cores, "kind": "reference",
+                "sample": f"{n} lines x {reps} reps of the config-2 logits, SIMD_CTC=1, "
+                          "fp16->fp32 conversion untimed"}
+
+
+class PreprocessWorkload:
+    """batched resize/letterbox/normalise to fp16 NCHW."""
+    name = "preprocess_256img_600-2000_to_960x960_f16"
+    metric = "images/sec batched det preprocessing (256 u8 images -> fp16 960x960 NCHW)"
+    unit = "images/s"
+    dtype = "f32"
+    N, H, W = 256, 960, 960
+    launches_per_step = 1
+    l2_note = "inputs 1.3 GB + outputs 1.4 GB > 126 MB L2 (no flush needed)"
+
+    def __init__(self, dev, seed, units=None):
+        from turboocr_b200 import kernels as K
+        from turboocr_b200._lib import synth
+        self.K = K
+        if units:
+            self.N = units
+        lib = synth()
+        dims = []
+        for i in range(self.N):
+            h = 600 + int(lib.tocr_synth_hash(seed, 2000 + i, 0) >> 32) % 1401
+            w = 600 + int(lib.tocr_synth_hash(seed, 2000 + i, 1) >> 32) % 1401
+            dims.append((h, w))
+        self.dims = dims
+        sizes = [h * w * 3 for h, w in dims]
+        offs = np.concatenate([[0], np.cumsum([(s + 255) // 256 * 256 for s in sizes])])
+        self.src = torch.empty(int(offs[-1]), dtype=torch.uint8, device=dev)
+        assert lib.tocr_synth_fill_u8(self.src.data_ptr(), self.src.numel(), seed, 3, None) == 0
+        base = self.src.data_ptr()
+        content = [det_resize_max960(h, w) for h, w in dims]
+        self.content = content
+        self.meta = K.PreprocessMeta([base + int(o) for o in offs[:-1]], [w * 3 for _, w in dims],
+                                     dims, content, dev)
+        self.out = torch.empty(self.N, 3, self.H, self.W, dtype=torch.float16, device=dev)
+        self.units_per_step = self.N
+        self.algo_bytes = touched_source_bytes(dims, content) + self.N * 3 * self.H * self.W * 2
+        self.offs = offs
+        torch.cuda.synchronize()
+
+    def step(self):
+        self.K.preprocess_batch(self.meta, self.out)
+
+    def dominant_kernel_ms(self, iters=10):
+        s = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(iters):
+            self.step()
+        e1.record(s)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / iters
+
+    def setup_e2e(self):
+        self.h_src = torch.empty(self.src.numel(), dtype=torch.uint8, pin_memory=True)
+        self.h_src.copy_(self.src)
+        self.h_out = torch.empty(self.out.shape, dtype=torch.float16, pin_memory=True)
+        self.h2d = int(sum(h * w * 3 for h, w in self.dims))
+        self.d2h = self.h_out.numel() * 2
+
+    def e2e_step(self):
+        self.src.copy_(self.h_src, non_blocking=True)
+        self.K.preprocess_batch(self.meta, self.out)
+        self.h_out.copy_(self.out, non_blocking=True)
+
+    def cpu_baseline(self, cores, budget_s=15.0):
+        """cpu_paddle_det.cpp:53-94 restated with cv2 (INTER_LINEAR resize,
+        per-channel normalise, letterbox), images over `cores` threads."""
+        import cv2
+        from concurrent.futures import ThreadPoolExecutor
+        cv2.setNumThreads(1)
+        n = min(self.N, max(cores * 2, 16))
+        host = self.src.cpu().numpy()
+        imgs = [host[int(self.offs[i]):int(self.offs[i]) + self.dims[i][0] * self.dims[i][1] * 3]
+                .reshape(self.dims[i][0], self.dims[i][1], 3) for i in range(n)]
+        mean = np.array([0.485, 0.456, 0.406], np.float32)
+        istd = 1.0 / np.array([0.229, 0.224, 0.225], np.float32)
+
+        def one(i):
+            ch, cw = self.content[i]
+            r = cv2.resize(imgs[i], (cw, ch), interpolation=cv2.INTER_LINEAR)
+            f = (r.astype(np.float32) * (1 / 255.0) - mean) * istd
+            canvas = np.empty((3, self.H, self.W), np.float16)
+            canvas[:] = ((0 - mean) * istd).astype(np.float16)[:, None, None]
+            canvas[:, :ch, :cw] = f.transpose(2, 0, 1)
+            return canvas
+
+        t0 = time.perf_counter()
+        reps = 0
+        with ThreadPoolExecutor(cores) as ex:
+            while True:
+                list(ex.map(one, range(n)))
+                reps += 1
+                if time.perf_counter() - t0 > budget_s or reps >= 20:
+                    break
+        dt = time.perf_counter() - t0
+        return {"value": n * reps / dt, "unit": self.unit, "cores": cores, "kind": "port",
+                "sample": f"{n} images x {reps} reps (cv2 {cv2.__version__} resize+normalise "
+                          "restatement of cpu_paddle_det.cpp:53-94 with letterbox)"}
+
+
+def det_resize_max960(h, w):
+    """compute_det_resize with {"max", 960, 960} (det_config.h:58-81)."""
+    ratio = np.float32(1.0)
+    longest = max(h, w)
+    if longest > 960:
+        ratio = np.float32(960) / np.float32(longest)
+
+    def r32(v):
+        return max(int(round(float(v) / 32.0) * 32), 32)
+    rh, rw = r32(np.float32(h) * ratio), r32(np.float32(w) * ratio)
+    lo = max(rh, rw)
+    if lo > 960:
+        rs = 960 / lo
+        rh, rw = r32(rh * rs), r32(rw * rs)
+    return rh, rw
+
+
+def touched_source_bytes(dims, content):
+    """Exact distinct source bytes the bilinear taps touch (preprocess_kernels.cu:19-54)."""
+    total = 0
+    for (h, w), (ch, cw) in zip(dims, content):
+        def taps(n_src, n_dst):
+            s = np.float32(n_src) / np.float32(n_dst)
+            d = np.arange(n_dst, dtype=np.float32)
+            sx = (d + np.float32(0.5)) * s - np.float32(0.5)
+            x0 = np.floor(sx).astype(np.int64)
+            x1 = np.clip(x0 + 1, 0, n_src - 1)
+            x0 = np.clip(x0, 0, n_src - 1)
+            return len(np.union1d(x0, x1))
+        total += taps(h, ch) * taps(w, cw) * 3
+    return total
+
+
+WORKLOADS = {"ctc": CtcWorkload, "preprocess": PreprocessWorkload}
+
+
+# ------------------------------------------------------------------ main ----
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="ctc", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--units", type=int, default=0,
+                    help="override the per-GPU units per step (small profiling cases)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    Wl = WORKLOADS[args.workload]
+    cores = len(os.sched_getaffinity(0))
+
+    if args.impl == "reference":
+        # The reference's CPU implementation of the path, rank 0 only.
+        if rank != 0:
+            return
+        dev = torch.device("cuda", local) if torch.cuda.is_available() else None
+        wl = Wl(dev, 0x7EC00000 + (1 if args.workload == "ctc" else 2), args.units)
+        vals = []
+        for i in range(args.warmup + args.steps):
+            cb = wl.cpu_baseline(cores, budget_s=2.0)
+            if i >= args.warmup:
+                vals.append(cb["value"])
+        v = statistics.median(vals)
+        print(json.dumps({"impl": "reference", "metric": Wl.metric, "value": v, "unit": Wl.unit,
+                          "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                          "higher_is_better": True, "dtype": Wl.dtype, "data": "synthetic",
+                          "config": {"workload": Wl.name},
+                          "cpu_baseline": dict(cb, value=v),
+                          "e2e": {"value": v, "unit": Wl.unit, "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}), flush=True)
+        return
+
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=__import__("datetime").timedelta(seconds=120))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    seed = 0x7EC00000 + (1 if args.workload == "ctc" else 2) + 1000 * rank
+    wl = Wl(dev, seed, args.units)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for _ in range(args.warmup):
+        wl.step()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(args.steps):
+        wl.step()
+    e1.record(s)
+    torch.cuda.synchronize()
+    barrier()
+    ms_total = e0.elapsed_time(e1)
+    clk = clocks.stop()
+
+    # end-to-end through the public API with pinned host buffers
+    wl.setup_e2e()
+    for _ in range(2):
+        wl.e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(s)
+    n_e2e = max(3, min(args.steps, 10))
+    for _ in range(n_e2e):
+        wl.e2e_step()
+    e3.record(s)
+    torch.cuda.synchronize()
+    barrier()
+    ms_e2e = e2.elapsed_time(e3) / n_e2e
+
+    kernel_ms = wl.dominant_kernel_ms()
+    t = torch.tensor([ms_total, ms_e2e, kernel_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_total, ms_e2e, kernel_ms = t.tolist()
+
+    if rank == 0:
+        ms_step = ms_total / args.steps
+        value = wl.units_per_step * world / (ms_step / 1e3)
+        peak, peak_kind = hbm_peak()
+        achieved = wl.algo_bytes / (kernel_ms / 1e3) / 1e9
+        line = {
+            "metric": Wl.metric, "value": value, "unit": Wl.unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": Wl.dtype, "data": "synthetic (seeded generator, BASELINE config shapes)",
+            "config": {"workload": Wl.name, "units_per_gpu_per_step": wl.units_per_step,
+                       "l2": Wl.l2_note, "parallelism": f"dp{world} (independent shards)"},
+            "gpu_launches": Wl.launches_per_step * args.steps,
+            "e2e": {"value": wl.units_per_step * world / (ms_e2e / 1e3), "unit": Wl.unit,
+                    "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "peak_source": f"{peak_kind} hbm_gbs",
+                         "algorithmic_bytes_per_launch": wl.algo_bytes},
+            "clocks": clk,
+        }
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = wl.cpu_baseline(cores)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

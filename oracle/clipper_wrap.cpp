@@ -1,0 +1,44 @@
+// Test-infrastructure wrapper (oracle only): the reference's vendored
+// Clipper 6.4.2 (third_party/clipper/clipper.cpp, compiled unchanged by
+// oracle/Makefile) driven exactly like unclip() in
+// src/detection/det_postprocess.cpp:72-101 — ClipperOffset with its default
+// MiterLimit 2 / ArcTolerance 0.25, jtRound, etClosedPolygon, Execute(delta),
+// largest ring by Area. Also exposes the raw offset vertices (before the
+// union) for the GPU restatement's tests.
+#include <algorithm>
+#include <vector>
+
+#include "clipper/clipper.hpp"
+
+using namespace ClipperLib;
+
+extern "C" {
+
+// Returns the number of points of the largest ring written to out_xy (pairs),
+// 0 when the solution is empty, or -needed if cap is too small.
+int clipper_ref_unclip(const int *xy, int n, double distance, long long *out_xy, int cap,
+                       int *n_rings) {
+  ClipperOffset co;
+  Path subj;
+  for (int i = 0; i < n; ++i) subj.emplace_back(xy[2 * i], xy[2 * i + 1]);
+  co.AddPath(subj, jtRound, etClosedPolygon);
+  Paths sol;
+  co.Execute(sol, distance);
+  *n_rings = (int)sol.size();
+  if (sol.empty()) return 0;
+  const Path *best = &sol.front();
+  if (sol.size() > 1) {
+    best = &*std::max_element(sol.begin(), sol.end(), [](const Path &a, const Path &b) {
+      return Area(a) < Area(b);
+    });
+  }
+  const int m = (int)best->size();
+  if (m > cap) return -m;
+  for (int i = 0; i < m; ++i) {
+    out_xy[2 * i] = (*best)[i].X;
+    out_xy[2 * i + 1] = (*best)[i].Y;
+  }
+  return m;
+}
+
+}  // extern "C"

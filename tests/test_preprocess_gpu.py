@@ -1,0 +1,84 @@
+"""Subsystem 1 parity on the GPU: batched resize + letterbox + normalise
+(C-ABI tocr_preprocess_batch_f16/f32) against the C restatement of
+preprocess_kernels.cu. fp16 output: within 1 fp16 ulp of the round-to-nearest
+of the fp32 oracle. fp32 output: within 2 fp32 ulp."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import preprocess_oracle as po
+
+pytestmark = pytest.mark.gpu
+
+
+def ulp_dist16(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    def key(x):
+        i = x.view(np.int16).astype(np.int32)
+        return np.where(i < 0, -(i & 0x7FFF), i)
+    return np.abs(key(a) - key(b))
+
+
+def make_batch(cuda, dims, seed, pitch_pad=0):
+    rng = np.random.default_rng(seed)
+    imgs, bufs = [], []
+    for (h, w) in dims:
+        step = w * 3 + pitch_pad
+        buf = rng.integers(0, 256, size=(h, step), dtype=np.uint8)
+        imgs.append((buf, h, w, step))
+        bufs.append(torch.from_numpy(buf).to(cuda))
+    return imgs, bufs
+
+
+def run(tocr, cuda, dims, canvas, out_dtype, seed, limit=("max", 960, 960), pitch_pad=0,
+        content=None):
+    from turboocr_b200 import kernels as K
+    imgs, bufs = make_batch(cuda, dims, seed, pitch_pad)
+    if content is None:
+        content = [po.det_resize(h, w, *limit) for (h, w) in dims]
+    meta = K.PreprocessMeta([b.data_ptr() for b in bufs], [i[3] for i in imgs], dims, content,
+                            cuda)
+    out = torch.empty(len(dims), 3, canvas[0], canvas[1], dtype=out_dtype, device=cuda)
+    K.preprocess_batch(meta, out)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    refs = [po.preprocess_image(buf, content[k], canvas, hw=(h, w), step=step)
+            for k, (buf, h, w, step) in enumerate(imgs)]
+    return got, np.stack(refs), content
+
+
+@pytest.mark.parametrize("seed", [0, 1])
+def test_fp16_within_one_ulp(tocr, cuda, seed):
+    rng = np.random.default_rng(100 + seed)
+    dims = [(int(rng.integers(600, 2001)), int(rng.integers(600, 2001))) for _ in range(6)]
+    dims += [(640, 700), (960, 960), (300, 1500)]  # <=960 long side: native /32 size
+    got, ref, content = run(tocr, cuda, dims, (960, 960), torch.float16, seed)
+    d = ulp_dist16(got, ref.astype(np.float16))
+    assert d.max() <= 1, d.max()
+    # letterbox pad is normalised black
+    for k, (ch, cw) in enumerate(content):
+        if cw < 960:
+            pad = got[k, :, :, cw:]
+            exp = ((0.0 - po.DET_MEAN) * po.DET_INV_STD).astype(np.float16)
+            assert np.all(pad == exp[:, None, None])
+
+
+def test_fp32_matches_oracle(tocr, cuda):
+    dims = [(777, 1234), (2000, 600), (961, 959)]
+    got, ref, _ = run(tocr, cuda, dims, (960, 960), torch.float32, 5)
+    np.testing.assert_allclose(got, ref, rtol=0, atol=4e-6)
+
+
+def test_pitched_rows_and_upscale(tocr, cuda):
+    # "min" policy upscales small images; pitch padding exercises src step
+    dims = [(40, 90), (33, 47)]
+    got, ref, content = run(tocr, cuda, dims, (128, 256), torch.float16, 9,
+                            limit=("min", 64, 256), pitch_pad=13)
+    assert ulp_dist16(got, ref.astype(np.float16)).max() <= 1
+
+
+def test_content_larger_edge_cases(tocr, cuda):
+    # content not a multiple of 8 and a zero-content image
+    dims = [(50, 50), (60, 61)]
+    got, ref, _ = run(tocr, cuda, dims, (64, 64), torch.float16, 3,
+                      content=[(37, 45), (0, 0)])
+    assert ulp_dist16(got, ref.astype(np.float16)).max() <= 1

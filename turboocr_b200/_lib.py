@@ -1,0 +1,122 @@
+"""ctypes binding of the C-ABI (include/tocr_capi.h).
+
+The product library is loaded from this package directory only. If it is
+missing the import fails loudly: there is no CPU fallback on this path.
+Status codes are mapped to the reference's exception types
+(include/turbo_ocr/common/errors.h in TurboOCR): OcrError, CudaError,
+InferenceError, TimeoutError.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+
+TOCR_OK = 0
+TOCR_ERR_INVALID = 1
+TOCR_ERR_CUDA = 2
+TOCR_ERR_OVERFLOW = 3
+TOCR_ERR_TIMEOUT = 4
+TOCR_ERR_INJECTED = 5
+
+
+class OcrError(RuntimeError):
+    """Base of the reference's error hierarchy."""
+
+
+class CudaError(OcrError):
+    pass
+
+
+class InferenceError(OcrError):
+    pass
+
+
+class TimeoutError(OcrError):  # noqa: A001 - mirrors turbo_ocr::TimeoutError
+    pass
+
+
+class InvalidArgument(CudaError, ValueError):
+    """TOCR_ERR_INVALID / TOCR_ERR_OVERFLOW (the reference raises CudaError
+    with cudaErrorInvalidValue for these, reduce_kernels.cu:140-142)."""
+
+
+_vp = C.c_void_p
+_i = C.c_int
+_f = C.c_float
+_ll = C.c_longlong
+_u64 = C.c_uint64
+
+# name -> (restype, argtypes)
+SIGNATURES: dict[str, tuple] = {
+    "tocr_last_error_string": (C.c_char_p, []),
+    "tocr_version": (_i, []),
+    "tocr_debug_inject_error": (None, [_i, _i]),
+    "tocr_argmax_f32": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
+    "tocr_ctc_greedy_f16": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "tocr_preprocess_batch_f16": (_i, [_vp] * 7 + [_i, _i, _i, _vp, _vp, _vp]),
+    "tocr_preprocess_batch_f32": (_i, [_vp] * 7 + [_i, _i, _i, _vp, _vp, _vp]),
+    "tocr_threshold_u8": (_i, [_vp, _vp, _i, _i, _i, _f, _vp]),
+}
+
+SYNTH_SIGNATURES: dict[str, tuple] = {
+    "tocr_synth_hash": (_u64, [_u64, _u64, _u64]),
+    "tocr_synth_fill_u8": (_i, [_vp, _ll, _u64, _u64, _vp]),
+    "tocr_synth_normal_f16": (_i, [_vp, _ll, _f, _u64, _u64, _vp]),
+    "tocr_synth_ctc_logits": (_i, [_vp, _vp, _i, _i, _i, _u64, _vp]),
+}
+
+
+def _load(name: str, sigs: dict) -> C.CDLL:
+    path = PKG / name
+    if not path.exists():
+        raise ImportError(
+            f"{path} is missing: build it with `python -m turboocr_b200.build` "
+            "(the B200 path has no CPU fallback)")
+    lib = C.CDLL(str(path))
+    for fn, (res, args) in sigs.items():
+        f = getattr(lib, fn)
+        f.restype = res
+        f.argtypes = args
+    return lib
+
+
+_LIB: C.CDLL | None = None
+_SYNTH: C.CDLL | None = None
+
+
+def lib() -> C.CDLL:
+    global _LIB
+    if _LIB is None:
+        _LIB = _load("libtocr_b200.so", SIGNATURES)
+    return _LIB
+
+
+def synth() -> C.CDLL:
+    global _SYNTH
+    if _SYNTH is None:
+        _SYNTH = _load("libtocr_synth.so", SYNTH_SIGNATURES)
+    return _SYNTH
+
+
+def last_error() -> str:
+    return lib().tocr_last_error_string().decode()
+
+
+def check(status: int, where: str) -> None:
+    """Raise the reference exception matching a C-ABI status."""
+    if status == TOCR_OK:
+        return
+    msg = f"{where}: {last_error()}"
+    if status in (TOCR_ERR_INVALID, TOCR_ERR_OVERFLOW):
+        raise InvalidArgument(msg)
+    if status == TOCR_ERR_TIMEOUT:
+        raise TimeoutError(msg)
+    if status == TOCR_ERR_INJECTED:
+        raise InferenceError(msg)
+    raise CudaError(msg)
+
+
+def call(fn: str, *args) -> None:
+    check(getattr(lib(), fn)(*args), fn)

@@ -1,0 +1,220 @@
+// Subsystem 1 — batched det preprocessing (resize + letterbox + normalise).
+//
+// Reference arithmetic (TurboOCR):
+//   bilinear_sample_bgr .............. src/kernels/preprocess_kernels.cu:19-54
+//   batch kernel + letterbox pad ..... src/kernels/preprocess_kernels.cu:128-178
+//   host wrapper / det mean & std .... src/kernels/preprocess_kernels.cu:180-201
+// The per-pixel formula is kept operation for operation (same tap formula,
+// same weight products, same accumulation order, same normalisation), so the
+// fp32 value is the reference's and the fp16 output is its round-to-nearest.
+//
+// B200 design: the output is the HBM stream (2 bytes x 3 planes per pixel),
+// so each thread owns 8 consecutive canvas pixels of a row and writes them as
+// one 16-byte vector per plane; a warp therefore stores 512 contiguous bytes
+// per plane. The x-taps of a thread's 8 columns are computed once and reused
+// for every row of the CTA's band (8 rows), which takes the float->int
+// conversions off the per-pixel path. Source bytes become floats with the
+// exact 2^23 magic-number trick instead of the quarter-rate I2F conversion.
+#include "tocr_common.cuh"
+
+namespace tocr {
+namespace {
+
+constexpr int kPrepThreads = 128;  // groups of 8 columns per CTA
+constexpr int kPrepRows = 8;       // canvas rows per CTA
+
+__device__ __forceinline__ float u8f(uint32_t b) {
+  // 0x4B000000 is 2^23: (2^23 + b) - 2^23 == b exactly for 0 <= b < 2^23.
+  return __int_as_float(0x4B000000 | b) - 8388608.f;
+}
+
+template <typename OutT>
+struct Store8;
+
+template <>
+struct Store8<__half> {
+  static __device__ __forceinline__ void put(__half *p, const float v[8]) {
+    uint4 u;
+    __half2 h;
+    h = __floats2half2_rn(v[0], v[1]); u.x = *reinterpret_cast<uint32_t *>(&h);
+    h = __floats2half2_rn(v[2], v[3]); u.y = *reinterpret_cast<uint32_t *>(&h);
+    h = __floats2half2_rn(v[4], v[5]); u.z = *reinterpret_cast<uint32_t *>(&h);
+    h = __floats2half2_rn(v[6], v[7]); u.w = *reinterpret_cast<uint32_t *>(&h);
+    *reinterpret_cast<uint4 *>(p) = u;
+  }
+};
+
+template <>
+struct Store8<float> {
+  static __device__ __forceinline__ void put(float *p, const float v[8]) {
+    reinterpret_cast<float4 *>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4 *>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+  }
+};
+
+struct Norm {
+  float mean[3];
+  float inv_std[3];
+};
+
+template <typename OutT>
+__global__ void __launch_bounds__(kPrepThreads)
+preprocess_batch_kernel(const void *const *__restrict__ src_ptrs,
+                        const int *__restrict__ src_steps, const int *__restrict__ src_hs,
+                        const int *__restrict__ src_ws, const int *__restrict__ dst_hs,
+                        const int *__restrict__ dst_ws, OutT *__restrict__ dst, int W, int H,
+                        Norm nm) {
+  const int b = blockIdx.z;
+  const int gx = blockIdx.x * kPrepThreads + threadIdx.x;
+  const int x_base = gx * 8;
+  if (x_base >= W) return;
+
+  const unsigned char *src = static_cast<const unsigned char *>(src_ptrs[b]);
+  const int src_step = src_steps[b];
+  const int src_h = src_hs[b];
+  const int src_w = src_ws[b];
+  const int content_h = dst_hs[b];
+  const int content_w = dst_ws[b];
+
+  const float inv_255 = 1.0f / 255.0f;
+  const float pad0 = (0.0f - nm.mean[0]) * nm.inv_std[0];
+  const float pad1 = (0.0f - nm.mean[1]) * nm.inv_std[1];
+  const float pad2 = (0.0f - nm.mean[2]) * nm.inv_std[2];
+
+  const bool has_content = content_w > 0 && content_h > 0 && src_w > 0 && src_h > 0;
+  const float scale_x = has_content ? (float)src_w / content_w : 0.f;
+  const float scale_y = has_content ? (float)src_h / content_h : 0.f;
+
+  // x-taps of this thread's 8 columns (byte offsets of the two taps).
+  int xo0[8], xo1[8];
+  float fxs[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int dx = x_base + j;
+    float sx = (dx + 0.5f) * scale_x - 0.5f;
+    int x0 = (int)floorf(sx);
+    fxs[j] = sx - x0;
+    int x1 = x0 + 1;
+    x0 = max(0, min(x0, src_w - 1));
+    x1 = max(0, min(x1, src_w - 1));
+    xo0[j] = x0 * 3;
+    xo1[j] = x1 * 3;
+  }
+
+  const size_t plane = (size_t)H * W;
+  OutT *out0 = dst + (size_t)b * 3 * plane + x_base;
+  const int y_begin = blockIdx.y * kPrepRows;
+  const int y_end = min(H, y_begin + kPrepRows);
+
+  for (int dy = y_begin; dy < y_end; ++dy) {
+    float c0[8], c1[8], c2[8];
+    if (!has_content || dy >= content_h || x_base >= content_w) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) { c0[j] = pad0; c1[j] = pad1; c2[j] = pad2; }
+    } else {
+      float sy = (dy + 0.5f) * scale_y - 0.5f;
+      int y0 = (int)floorf(sy);
+      const float fy = sy - y0;
+      int y1 = y0 + 1;
+      y0 = max(0, min(y0, src_h - 1));
+      y1 = max(0, min(y1, src_h - 1));
+      const unsigned char *row0 = src + (size_t)y0 * src_step;
+      const unsigned char *row1 = src + (size_t)y1 * src_step;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (x_base + j >= content_w) { c0[j] = pad0; c1[j] = pad1; c2[j] = pad2; continue; }
+        const float fx = fxs[j];
+        const unsigned char *p00 = row0 + xo0[j], *p10 = row0 + xo1[j];
+        const unsigned char *p01 = row1 + xo0[j], *p11 = row1 + xo1[j];
+        const float w00 = (1.0f - fx) * (1.0f - fy);
+        const float w10 = fx * (1.0f - fy);
+        const float w01 = (1.0f - fx) * fy;
+        const float w11 = fx * fy;
+        float v[3];
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+          v[c] = w00 * u8f(__ldg(p00 + c)) + w10 * u8f(__ldg(p10 + c)) +
+                 w01 * u8f(__ldg(p01 + c)) + w11 * u8f(__ldg(p11 + c));
+        }
+        c0[j] = (v[0] * inv_255 - nm.mean[0]) * nm.inv_std[0];
+        c1[j] = (v[1] * inv_255 - nm.mean[1]) * nm.inv_std[1];
+        c2[j] = (v[2] * inv_255 - nm.mean[2]) * nm.inv_std[2];
+      }
+    }
+    OutT *o = out0 + (size_t)dy * W;
+    Store8<OutT>::put(o, c0);
+    Store8<OutT>::put(o + plane, c1);
+    Store8<OutT>::put(o + 2 * plane, c2);
+  }
+}
+
+Norm make_norm(const float *mean3, const float *inv_std3) {
+  Norm n;
+  const float dm[3] = {0.485f, 0.456f, 0.406f};
+  const float ds[3] = {1.0f / 0.229f, 1.0f / 0.224f, 1.0f / 0.225f};
+  for (int c = 0; c < 3; ++c) {
+    n.mean[c] = mean3 ? mean3[c] : dm[c];
+    n.inv_std[c] = inv_std3 ? inv_std3[c] : ds[c];
+  }
+  return n;
+}
+
+template <typename OutT>
+int launch_preprocess(const void *const *d_src_ptrs, const int *d_src_steps,
+                      const int *d_src_heights, const int *d_src_widths,
+                      const int *d_dst_heights, const int *d_dst_widths, OutT *dst,
+                      int dst_w, int dst_h, int batch_size, const float *mean3,
+                      const float *inv_std3, void *stream, const char *name) {
+  TOCR_REQUIRE(batch_size >= 0 && dst_w >= 0 && dst_h >= 0, "%s: negative size", name);
+  if (batch_size == 0 || dst_w == 0 || dst_h == 0) return TOCR_OK;
+  TOCR_REQUIRE(batch_size <= 65535, "%s: batch_size %d > 65535", name, batch_size);
+  TOCR_REQUIRE(dst_w % 8 == 0, "%s: dst_w %d must be a multiple of 8", name, dst_w);
+  TOCR_REQUIRE(d_src_ptrs && d_src_steps && d_src_heights && d_src_widths &&
+                   d_dst_heights && d_dst_widths && dst,
+               "%s: null pointer", name);
+  TOCR_REQUIRE(aligned(dst, 16), "%s: dst must be 16-byte aligned", name);
+  if ((size_t)dst_w * dst_h > (size_t)INT_MAX)
+    return set_error(TOCR_ERR_OVERFLOW, "%s: canvas %dx%d too large", name, dst_w, dst_h);
+  dim3 grid((dst_w / 8 + kPrepThreads - 1) / kPrepThreads, (dst_h + kPrepRows - 1) / kPrepRows,
+            batch_size);
+  TOCR_REQUIRE(grid.y <= 65535, "%s: dst_h %d too large", name, dst_h);
+  preprocess_batch_kernel<OutT><<<grid, kPrepThreads, 0, as_stream(stream)>>>(
+      d_src_ptrs, d_src_steps, d_src_heights, d_src_widths, d_dst_heights, d_dst_widths, dst,
+      dst_w, dst_h, make_norm(mean3, inv_std3));
+  return check_launch(name);
+}
+
+}  // namespace
+}  // namespace tocr
+
+using namespace tocr;
+
+extern "C" {
+
+TOCR_API int tocr_preprocess_batch_f16(const void *const *d_src_ptrs, const int *d_src_steps,
+                                       const int *d_src_heights, const int *d_src_widths,
+                                       const int *d_dst_heights, const int *d_dst_widths,
+                                       void *dst_f16, int dst_w, int dst_h, int batch_size,
+                                       const float *mean3, const float *inv_std3,
+                                       void *stream) {
+  TOCR_ENTRY();
+  return launch_preprocess<__half>(d_src_ptrs, d_src_steps, d_src_heights, d_src_widths,
+                                   d_dst_heights, d_dst_widths, static_cast<__half *>(dst_f16),
+                                   dst_w, dst_h, batch_size, mean3, inv_std3, stream,
+                                   "tocr_preprocess_batch_f16");
+}
+
+TOCR_API int tocr_preprocess_batch_f32(const void *const *d_src_ptrs, const int *d_src_steps,
+                                       const int *d_src_heights, const int *d_src_widths,
+                                       const int *d_dst_heights, const int *d_dst_widths,
+                                       float *dst_f32, int dst_w, int dst_h, int batch_size,
+                                       const float *mean3, const float *inv_std3,
+                                       void *stream) {
+  TOCR_ENTRY();
+  return launch_preprocess<float>(d_src_ptrs, d_src_steps, d_src_heights, d_src_widths,
+                                  d_dst_heights, d_dst_widths, dst_f32, dst_w, dst_h,
+                                  batch_size, mean3, inv_std3, stream,
+                                  "tocr_preprocess_batch_f32");
+}
+
+}  // extern "C"

@@ -1,0 +1,142 @@
+// Seeded synthetic inputs for the parity tests and bench.py (test
+// infrastructure, built as libtocr_synth.so, never linked into the product).
+//
+// One counter-based generator everywhere: value i of stream s under seed k is
+// mix64(k + golden * (mix64(s) + i + 1)) (splitmix64 finaliser), so any
+// element can be produced independently on host or device. Config seeds are
+// 0x7EC00000 + config index.
+#include "tocr_common.cuh"
+
+#include <cmath>
+
+namespace synth {
+
+__host__ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+  return z ^ (z >> 31);
+}
+__host__ __device__ __forceinline__ uint64_t hash3(uint64_t seed, uint64_t stream, uint64_t i) {
+  return mix64(seed + 0x9E3779B97F4A7C15ULL * (mix64(stream) + i + 1));
+}
+// uniform in [0,1) with 24 bits
+__host__ __device__ __forceinline__ float unif(uint64_t h) {
+  return (float)(h >> 40) * (1.0f / 16777216.0f);
+}
+// uniform integer in [lo, hi]
+__host__ __device__ __forceinline__ int unif_int(uint64_t h, int lo, int hi) {
+  return lo + (int)((h >> 32) % (uint64_t)(hi - lo + 1));
+}
+
+// ---- uniform bytes ---------------------------------------------------------
+__global__ void fill_u8_kernel(uint8_t *d, long long n, uint64_t seed, uint64_t stream) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i * 8 < n; i += stride) {
+    const uint64_t h = hash3(seed, stream, (uint64_t)i);
+    for (int k = 0; k < 8 && i * 8 + k < n; ++k) d[i * 8 + k] = (uint8_t)(h >> (8 * k));
+  }
+}
+
+// ---- CTC logits (config 2) ---------------------------------------------------
+// Plan per line: n_tok ~ U{5..40} tokens ~ U{1..V-1}, each a run of U{1..4}
+// steps, a blank run (index 0) of U{1..3} steps before every token and none
+// after; runs shrink to 1 step when the line would exceed T. plan[b*T+t] is
+// the planted index of step t or -1 (left random).
+__global__ void ctc_plan_kernel(int *plan, int B, int T, int V, uint64_t seed) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  uint64_t ctr = 0;
+  const uint64_t st = 1000 + (uint64_t)b;
+  const int n_tok = unif_int(hash3(seed, st, ctr++), 5, 40);
+  int tok[40], run[40], gap[40];
+  int total = 0;
+  for (int k = 0; k < n_tok; ++k) {
+    tok[k] = unif_int(hash3(seed, st, ctr++), 1, V - 1);
+    run[k] = unif_int(hash3(seed, st, ctr++), 1, 4);
+    gap[k] = unif_int(hash3(seed, st, ctr++), 1, 3);
+    total += run[k] + gap[k];
+  }
+  for (int k = 0; k < n_tok && total > T; ++k) { total -= gap[k] - 1; gap[k] = 1; }
+  for (int k = 0; k < n_tok && total > T; ++k) { total -= run[k] - 1; run[k] = 1; }
+  int t = 0;
+  int *p = plan + (long long)b * T;
+  for (int k = 0; k < n_tok && t < T; ++k) {
+    for (int g = 0; g < gap[k] && t < T; ++g) p[t++] = 0;
+    for (int r = 0; r < run[k] && t < T; ++r) p[t++] = tok[k];
+  }
+  for (; t < T; ++t) p[t] = -1;
+}
+
+__global__ void normal_f16_kernel(__half *d, long long n, float sigma, uint64_t seed,
+                                  uint64_t stream) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; 2 * i < n; i += stride) {
+    const uint64_t h = hash3(seed, stream, (uint64_t)i);
+    const float u1 = ((float)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
+    const float u2 = (float)((h >> 16) & 0xFFFFFF) * (1.0f / 16777216.0f);
+    const float r = sqrtf(-2.0f * logf(u1)) * sigma;
+    float s, c;
+    sincospif(2.0f * u2, &s, &c);
+    d[2 * i] = __float2half_rn(r * c);
+    if (2 * i + 1 < n) d[2 * i + 1] = __float2half_rn(r * s);
+  }
+}
+
+// One warp per row: planted index gets (row max + 2.0).
+__global__ void ctc_plant_kernel(__half *logits, const int *plan, long long rows, int V) {
+  const int lane = threadIdx.x & 31;
+  const long long r = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (r >= rows) return;
+  const int pi = plan[r];
+  if (pi < 0) return;
+  __half *row = logits + r * V;
+  float m = -INFINITY;
+  for (int j = lane; j < V; j += 32) m = fmaxf(m, __half2float(row[j]));
+  for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  __syncwarp();
+  if (lane == 0) row[pi] = __float2half_rn(m + 2.0f);
+}
+
+}  // namespace synth
+
+using namespace synth;
+
+extern "C" {
+
+TOCR_API uint64_t tocr_synth_hash(uint64_t seed, uint64_t stream, uint64_t i) {
+  return hash3(seed, stream, i);
+}
+
+TOCR_API int tocr_synth_fill_u8(void *d, long long n, uint64_t seed, uint64_t stream,
+                                void *cuda_stream) {
+  if (n <= 0) return 0;
+  const long long need = (n / 8 + 256) / 256;
+  const int grid = (int)(need < 148 * 16 ? need : 148 * 16);
+  fill_u8_kernel<<<grid, 256, 0, (cudaStream_t)cuda_stream>>>((uint8_t *)d, n, seed, stream);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+TOCR_API int tocr_synth_normal_f16(void *d, long long n, float sigma, uint64_t seed,
+                                   uint64_t stream, void *cuda_stream) {
+  if (n <= 0) return 0;
+  const long long need = (n / 2 + 256) / 256;
+  const int grid = (int)(need < 148 * 16 ? need : 148 * 16);
+  normal_f16_kernel<<<grid, 256, 0, (cudaStream_t)cuda_stream>>>((__half *)d, n, sigma, seed,
+                                                                  stream);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+// Config-2 logits: fills d_logits [B,T,V] fp16 and d_plan [B*T].
+TOCR_API int tocr_synth_ctc_logits(void *d_logits, int *d_plan, int B, int T, int V,
+                                   uint64_t seed, void *cuda_stream) {
+  cudaStream_t s = (cudaStream_t)cuda_stream;
+  const long long n = (long long)B * T * V;
+  ctc_plan_kernel<<<(B + 127) / 128, 128, 0, s>>>(d_plan, B, T, V, seed);
+  tocr_synth_normal_f16(d_logits, n, 4.0f, seed, 1, cuda_stream);
+  const long long rows = (long long)B * T;
+  ctc_plant_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, s>>>((__half *)d_logits,
+                                                                       d_plan, rows, V);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+}  // extern "C"
