@@ -58,8 +58,9 @@ void oracle_preprocess_image(const uint8_t *src, int src_h, int src_w, int step,
       for (int c = 0; c < 3; ++c) {
         const float p00 = r0[x0 * 3 + c], p10 = r0[x1 * 3 + c];
         const float p01 = r1[x0 * 3 + c], p11 = r1[x1 * 3 + c];
-        float v = w00 * p00;
-        v = fmaf(w10, p10, v);
+        /* nvcc (LLVM) contracts fadd(fmul(a,b), fmul(c,d)) into
+         * fma(a, b, c*d), then folds each further product term. */
+        float v = fmaf(w00, p00, w10 * p10);
         v = fmaf(w01, p01, v);
         v = fmaf(w11, p11, v);
         dst[c * plane + idx] = fmaf(v, inv_255, -mean[c]) * inv_std[c];

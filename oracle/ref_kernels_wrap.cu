@@ -1,0 +1,45 @@
+// Test-infrastructure wrapper (oracle only): C entry points over the
+// REFERENCE's own CUDA kernels (src/kernels/preprocess_kernels.cu and
+// src/kernels/reduce_kernels.cu, compiled unchanged from the reference tree
+// by oracle/Makefile). Used on the GPU box by tests/ to pin the fp32
+// arithmetic of the B200 kernels to the reference kernel's bits.
+#include <exception>
+
+#include "turbo_ocr/kernels/kernels.h"
+
+extern "C" {
+
+int refk_batch_preprocess(const void *const *ptrs, const int *steps, const int *sh,
+                          const int *sw, const int *dh, const int *dw, float *dst, int dst_w,
+                          int dst_h, int batch, void *stream) {
+  try {
+    turbo_ocr::kernels::cuda_batch_fused_resize_normalize_det(
+        ptrs, steps, sh, sw, dh, dw, dst, dst_w, dst_h, batch, (cudaStream_t)stream);
+  } catch (const std::exception &) {
+    return 2;
+  }
+  return 0;
+}
+
+int refk_argmax(const float *probs, int *idx, float *scores, int batch, int seq_len,
+                int classes, void *stream) {
+  try {
+    turbo_ocr::kernels::cuda_argmax(probs, idx, scores, batch, seq_len, classes,
+                                    (cudaStream_t)stream);
+  } catch (const std::exception &) {
+    return 2;
+  }
+  return 0;
+}
+
+int refk_threshold(const float *src, unsigned char *dst, int w, int h, int batch, float t,
+                   void *stream) {
+  try {
+    turbo_ocr::kernels::cuda_batch_threshold_to_u8(src, dst, w, h, batch, t,
+                                                   (cudaStream_t)stream);
+  } catch (const std::exception &) {
+    return 2;
+  }
+  return 0;
+}
+}

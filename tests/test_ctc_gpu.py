@@ -129,3 +129,20 @@ def test_argmax_f32_matches_reference_contract(tocr, cuda):
     assert np.array_equal(idx.cpu().numpy(), flat.argmax(axis=1))
     assert np.array_equal(val.cpu().numpy(), flat.max(axis=1))
     assert int(idx[0]) == 100
+
+
+def test_argmax_bit_exact_vs_reference_kernel(tocr, cuda):
+    from oracle import ref_kernels as rk
+    from turboocr_b200 import kernels as K
+    g = torch.Generator().manual_seed(12)
+    B, T, V = 8, 40, 18385
+    x = torch.rand(B, T, V, generator=g)
+    x[1, 3, 5] = x[1, 3, 4000] = 5.0  # tie
+    xd = x.to(cuda)
+    i1 = torch.empty(B * T, dtype=torch.int32, device=cuda)
+    v1 = torch.empty(B * T, dtype=torch.float32, device=cuda)
+    i2, v2 = torch.empty_like(i1), torch.empty_like(v1)
+    K.cuda_argmax(xd, i1, v1)
+    rk.argmax(xd, i2, v2)
+    torch.cuda.synchronize()
+    assert torch.equal(i1, i2) and torch.equal(v1, v2)

@@ -82,3 +82,32 @@ def test_content_larger_edge_cases(tocr, cuda):
     got, ref, _ = run(tocr, cuda, dims, (64, 64), torch.float16, 3,
                       content=[(37, 45), (0, 0)])
     assert ulp_dist16(got, ref.astype(np.float16)).max() <= 1
+
+
+def test_bit_exact_vs_reference_kernel(tocr, cuda):
+    """The reference's own kernel (compiled from its tree) is the tightest
+    oracle: the B200 fp32 output must equal it bit for bit, the fp16 output
+    must be its round-to-nearest, and the C restatement must agree too."""
+    from oracle import ref_kernels as rk
+    from turboocr_b200 import kernels as K
+    rng = np.random.default_rng(77)
+    dims = [(int(rng.integers(600, 2001)), int(rng.integers(600, 2001))) for _ in range(5)]
+    dims += [(700, 640), (960, 960)]
+    imgs, bufs = make_batch(cuda, dims, 77, pitch_pad=5)
+    content = [po.det_resize(h, w, "max", 960, 960) for (h, w) in dims]
+    meta = K.PreprocessMeta([b.data_ptr() for b in bufs], [i[3] for i in imgs], dims, content,
+                            cuda)
+    ref = torch.empty(len(dims), 3, 960, 960, dtype=torch.float32, device=cuda)
+    rk.batch_preprocess(meta, ref)
+    o32 = torch.empty_like(ref)
+    o16 = torch.empty(ref.shape, dtype=torch.float16, device=cuda)
+    K.preprocess_batch(meta, o32)
+    K.preprocess_batch(meta, o16)
+    torch.cuda.synchronize()
+    r = ref.cpu().numpy()
+    assert np.array_equal(o32.cpu().numpy().view(np.uint32), r.view(np.uint32))
+    assert np.array_equal(o16.cpu().numpy().view(np.uint16), r.astype(np.float16).view(np.uint16))
+    c = np.stack([po.preprocess_image(buf, content[k], (960, 960), hw=(h, w), step=step)
+                  for k, (buf, h, w, step) in enumerate(imgs)])
+    mism = int((c.view(np.uint32) != r.view(np.uint32)).sum())
+    assert mism == 0, f"C restatement differs from the reference kernel at {mism} values"

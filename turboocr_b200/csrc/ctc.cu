@@ -299,7 +299,7 @@ TOCR_API int tocr_ctc_greedy_f16(const void *d_logits, int batch_size, int seq_l
                "tocr_ctc_greedy_f16: bad sizes batch=%d seq_len=%d classes=%d",
                batch_size, seq_len, num_classes);
   if (batch_size == 0) return TOCR_OK;
-  TOCR_REQUIRE(d_tokens && d_lengths && d_line_scores,
+  TOCR_REQUIRE(d_lengths && d_line_scores && (d_tokens || seq_len == 0),
                "tocr_ctc_greedy_f16: null output pointer");
   if (seq_len > 0) {
     TOCR_REQUIRE(d_logits && d_step_idx && d_step_prob,
