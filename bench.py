@@ -280,6 +280,76 @@ class PreprocessWorkload:
                           "restatement of cpu_paddle_det.cpp:53-94 with letterbox)"}
 
 
+class DwPwWorkload:
+    """fused DW3x3 + PW1x1 block, INT8 PW weights on tcgen05."""
+    name = "dwpw_block_32x128x240x240_to_256_int8"
+    metric = "images/sec fused dw3x3+pw1x1 block (32x128x240x240 fp16 -> 256ch, INT8 PW)"
+    unit = "images/s"
+    dtype = "i8 (PW on tcgen05 kind::i8, DW fp16x2)"
+    N, H, W, C, CO = 32, 240, 240, 128, 256
+    launches_per_step = 1
+    l2_note = "input 472 MB + output 944 MB per step > 126 MB L2 (no flush needed)"
+    kind = 0
+
+    def __init__(self, dev, seed, units=None):
+        from turboocr_b200 import backbone as bb
+        if units:
+            self.N = units
+        self.bb = bb
+        self.params = bb.make_block_params(self.C, self.CO, 0x7EC00004)
+        self.blk = bb.DwPwBlock(self.params, self.kind, 1, dev)
+        g = torch.Generator(device=dev).manual_seed(seed)
+        self.x = torch.randn(self.N, self.H, self.W, self.C, generator=g, device=dev).to(torch.float16)
+        self.y = torch.empty(self.N, self.H, self.W, self.CO, dtype=torch.float16, device=dev)
+        self.units_per_step = self.N
+        px = self.N * self.H * self.W
+        self.algo_bytes = px * self.C * 2 + px * self.CO * 2 + self.blk.blob.numel()
+        self.algo_flops = 2 * px * self.C * (9 + self.CO)
+        torch.cuda.synchronize()
+
+    def step(self):
+        self.blk(self.x, self.y)
+
+    def dominant_kernel_ms(self, iters=10):
+        s = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(iters):
+            self.step()
+        e1.record(s)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / iters
+
+    def setup_e2e(self):
+        self.h_x = torch.empty(self.x.shape, dtype=torch.float16, pin_memory=True)
+        self.h_x.copy_(self.x)
+        self.h_y = torch.empty(self.y.shape, dtype=torch.float16, pin_memory=True)
+        self.h2d = self.h_x.numel() * 2
+        self.d2h = self.h_y.numel() * 2
+
+    def e2e_step(self):
+        self.x.copy_(self.h_x, non_blocking=True)
+        self.blk(self.x, self.y)
+        self.h_y.copy_(self.y, non_blocking=True)
+
+    def cpu_baseline(self, cores, budget_s=15.0):
+        """The same block in torch fp32 on the host (mkldnn), all threads."""
+        torch.set_num_threads(cores)
+        x = self.x[:1].float().cpu()
+        t0 = time.perf_counter()
+        reps = 0
+        with torch.no_grad():
+            while True:
+                self.bb.reference_block(x, self.params, 1)
+                reps += 1
+                if time.perf_counter() - t0 > budget_s or reps >= 30:
+                    break
+        dt = time.perf_counter() - t0
+        return {"value": reps / dt, "unit": self.unit, "cores": cores, "kind": "port",
+                "sample": f"{reps} single-image passes of the block in torch fp32 "
+                          f"({torch.__version__}, {cores} threads)"}
+
+
 def det_resize_max960(h, w):
     """compute_det_resize with {"max", 960, 960} (det_config.h:58-81)."""
     ratio = np.float32(1.0)
@@ -313,7 +383,7 @@ def touched_source_bytes(dims, content):
     return total
 
 
-WORKLOADS = {"ctc": CtcWorkload, "preprocess": PreprocessWorkload}
+WORKLOADS = {"ctc": CtcWorkload, "preprocess": PreprocessWorkload, "dwpw": DwPwWorkload}
 
 
 # ------------------------------------------------------------------ main ----
@@ -341,7 +411,7 @@ def main():
         if rank != 0:
             return
         dev = torch.device("cuda", local) if torch.cuda.is_available() else None
-        wl = Wl(dev, 0x7EC00000 + (1 if args.workload == "ctc" else 2), args.units)
+        wl = Wl(dev, 0x7EC00000 + {"ctc": 1, "preprocess": 2, "dwpw": 3}[args.workload], args.units)
         vals = []
         for i in range(args.warmup + args.steps):
             cb = wl.cpu_baseline(cores, budget_s=2.0)
@@ -363,7 +433,7 @@ def main():
                                 timeout=__import__("datetime").timedelta(seconds=120))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    seed = 0x7EC00000 + (1 if args.workload == "ctc" else 2) + 1000 * rank
+    seed = 0x7EC00000 + {"ctc": 1, "preprocess": 2, "dwpw": 3}[args.workload] + 1000 * rank
     wl = Wl(dev, seed, args.units)
 
     def barrier():

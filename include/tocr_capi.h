@@ -113,6 +113,39 @@ TOCR_API int tocr_threshold_u8(const float *d_src, uint8_t *d_dst, int w,
                                int h, int batch_size, float thresh,
                                void *stream);
 
+/* ---- subsystem 2: fused depthwise-3x3 + pointwise-1x1 block ------------- */
+
+/* Replaces one DW-separable block of the det backbone that the reference runs
+ * inside TensorRT (include/turbo_ocr/engine/trt/trt_engine.h:37; INT8/FP8 QDQ
+ * from scripts/quantize_onnx_int8.py:1-80, scripts/quantize_onnx_fp8.py:2-8;
+ * WMMA precedent tools/fused_dwpw_bench.cu:98-152).
+ *   y = hardswish(PW(hardswish(DW3x3_stride(x) + b_dw)) * s + b_pw)
+ * x: fp16 NHWC [N][H][W][C]; y: fp16 NHWC [N][Ho][Wo][C_out] with
+ * Ho = (H-1)/stride + 1 (pad 1). kind 0 = INT8, 1 = FP8-E4M3 PW weights,
+ * per output channel. d_packed is the device copy of a tocr_dwpw_pack blob.
+ * d_err (device int, caller-zeroed) receives a non-zero code if a bounded
+ * device-side wait gave up (the launch itself still returns TOCR_OK).
+ * Supported (C, C_out, stride): (128,256,1) (128,128,1) (64,128,1)
+ * (64,64,1) (32,64,1). */
+TOCR_API int tocr_dwpw_block(const void *d_x, void *d_y, int N, int H, int W,
+                             int C, int C_out, int stride, int kind,
+                             const void *d_packed, int *d_err, void *stream);
+
+/* Host-side size of a packed parameter blob for (C, C_out). */
+TOCR_API size_t tocr_dwpw_packed_bytes(int C, int C_out);
+
+/* Host-side packing of BN-folded block parameters into the kernel's blob:
+ * wdw [C][3][3], bdw [C], wpw [C_out][C], bpw [C_out] (all fp32). PW weights
+ * are quantised symmetrically per output channel (INT8: max|w|/127, FP8:
+ * max|w|/448) and laid out as the 128B-swizzled K-major tcgen05 B operand. */
+TOCR_API int tocr_dwpw_pack(int C, int C_out, int kind, const float *wdw,
+                            const float *bdw, const float *wpw,
+                            const float *bpw, void *out, size_t out_bytes);
+
+/* Dequantised PW weights [C_out][C] of a packed blob (host). */
+TOCR_API int tocr_dwpw_dequant_pw(const void *blob, int C, int C_out, int kind,
+                                  float *w_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,99 @@
+"""Subsystem 2 parity on the GPU: the fused tcgen05 DW+PW block against a
+torch fp32 reference of the same block (TF32 off). The reference uses the
+dequantised PW weights the block carries (the fp32 execution of the QDQ
+model). Tolerance: 3e-2 relative, normwise per (n, c_out) plane, for INT8 and
+FP8. Elementwise, |y - ref| is bounded against the plane's max |ref|: 3e-2 for
+FP8 (hi/lo activation split) and 5e-2 for INT8, whose per-pixel activation
+quantisation has a heavier error tail (worst element ~4e-2 over 59M values)."""
+import numpy as np
+import pytest
+import torch
+
+from turboocr_b200 import backbone as bb
+
+pytestmark = pytest.mark.gpu
+
+TOL = 3e-2
+EL_TOL = {0: 5e-2, 1: 3e-2}   # elementwise bound by kind (INT8, FP8)
+
+
+@pytest.fixture(autouse=True)
+def _no_tf32():
+    m, c = torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    yield
+    torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = m, c
+
+
+def plane_errors(y: torch.Tensor, ref: torch.Tensor):
+    """y, ref NHWC -> (max normwise rel err, max elementwise err / plane max)."""
+    d = (y.float() - ref).pow(2).sum(dim=(1, 2)).sqrt()
+    r = ref.pow(2).sum(dim=(1, 2)).sqrt().clamp_min(1e-12)
+    pm = ref.abs().amax(dim=(1, 2), keepdim=True).clamp_min(1e-12)
+    e = ((y.float() - ref).abs() / pm).amax()
+    return float((d / r).max()), float(e)
+
+
+def run_block(cuda, N, H, W, C, CO, kind, seed=0):
+    params = bb.make_block_params(C, CO, seed)
+    blk = bb.DwPwBlock(params, kind, 1, cuda)
+    g = torch.Generator(device="cpu").manual_seed(seed + 1)
+    x = torch.randn(N, H, W, C, generator=g).to(torch.float16).to(cuda)
+    y = blk(x)
+    torch.cuda.synchronize()
+    assert int(blk.err.item()) == 0
+    ref = bb.reference_block(x, params, 1, wpw=blk.dequantized_pw())
+    return y, ref, blk, x, params
+
+
+@pytest.mark.parametrize("kind", [bb.KIND_INT8, bb.KIND_FP8])
+@pytest.mark.parametrize("C,CO", [(128, 256), (128, 128), (64, 128), (64, 64), (32, 64)])
+def test_block_shapes(cuda, kind, C, CO):
+    y, ref, *_ = run_block(cuda, 2, 40, 48, C, CO, kind, seed=C + CO)
+    nw, el = plane_errors(y, ref)
+    assert nw <= TOL and el <= EL_TOL[kind], (nw, el)
+
+
+@pytest.mark.parametrize("kind", [bb.KIND_INT8, bb.KIND_FP8])
+def test_partial_tiles_and_odd_sizes(cuda, kind):
+    # 37 x 53: partial 8x16 tiles on both axes; TMA clips the stores
+    y, ref, *_ = run_block(cuda, 3, 37, 53, 128, 256, kind, seed=5)
+    nw, el = plane_errors(y, ref)
+    assert nw <= TOL and el <= EL_TOL[kind], (nw, el)
+
+
+def test_fp8_hi_lo_is_tight(cuda):
+    y, ref, *_ = run_block(cuda, 1, 32, 32, 128, 256, bb.KIND_FP8, seed=9)
+    nw, _ = plane_errors(y, ref)
+    assert nw < 5e-3, nw
+
+
+@pytest.mark.parametrize("kind", [bb.KIND_INT8, bb.KIND_FP8])
+def test_config4_full_size(cuda, kind):
+    """BASELINE config 4 at full size: x [32, 240, 240, 128] fp16 N(0,1),
+    C_out 256. Every image is compared against the fp32 reference."""
+    N, H, W, C, CO = 32, 240, 240, 128, 256
+    params = bb.make_block_params(C, CO, 0x7EC00004)
+    blk = bb.DwPwBlock(params, kind, 1, cuda)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    x = torch.randn(N, H, W, C, generator=g, device=cuda).to(torch.float16)
+    y = blk(x)
+    torch.cuda.synchronize()
+    assert int(blk.err.item()) == 0
+    wq = blk.dequantized_pw()
+    worst = (0.0, 0.0)
+    for n0 in range(0, N, 4):
+        ref = bb.reference_block(x[n0:n0 + 4], params, 1, wpw=wq)
+        nw, el = plane_errors(y[n0:n0 + 4], ref)
+        worst = (max(worst[0], nw), max(worst[1], el))
+    assert worst[0] <= TOL and worst[1] <= EL_TOL[kind], worst
+
+
+def test_int8_model_level_error_vs_unquantised_weights(cuda):
+    """Informational bound of the whole INT8 scheme (weights + activations)
+    against the unquantised fp32 block: stays within the 3e-2 budget."""
+    y, _, blk, x, params = run_block(cuda, 2, 48, 48, 128, 256, bb.KIND_INT8, seed=21)
+    ref = bb.reference_block(x, params, 1)
+    nw, _ = plane_errors(y, ref)
+    assert nw <= TOL, nw

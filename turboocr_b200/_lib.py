@@ -58,6 +58,10 @@ SIGNATURES: dict[str, tuple] = {
     "tocr_preprocess_batch_f16": (_i, [_vp] * 7 + [_i, _i, _i, _vp, _vp, _vp]),
     "tocr_preprocess_batch_f32": (_i, [_vp] * 7 + [_i, _i, _i, _vp, _vp, _vp]),
     "tocr_threshold_u8": (_i, [_vp, _vp, _i, _i, _i, _f, _vp]),
+    "tocr_dwpw_block": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp]),
+    "tocr_dwpw_packed_bytes": (C.c_size_t, [_i, _i]),
+    "tocr_dwpw_pack": (_i, [_i, _i, _i, _vp, _vp, _vp, _vp, _vp, C.c_size_t]),
+    "tocr_dwpw_dequant_pw": (_i, [_vp, _i, _i, _i, _vp]),
 }
 
 SYNTH_SIGNATURES: dict[str, tuple] = {

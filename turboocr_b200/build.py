@@ -30,7 +30,7 @@ COMMON = ["-O3", "-lineinfo", "-std=c++20", "-Xcompiler", "-fPIC", "-Xcompiler",
           "-fvisibility=hidden", f"-I{INCLUDE}", f"-I{CSRC}"]
 
 LIBS = {
-    "libtocr_b200.so": ["capi_common.cu", "ctc.cu", "preprocess.cu", "threshold.cu"],
+    "libtocr_b200.so": ["capi_common.cu", "ctc.cu", "preprocess.cu", "threshold.cu", "dwpw.cu"],
     "libtocr_synth.so": ["synth.cu"],
 }
 # C++ host sources (reference-signature shims), built into libtocr_b200.so.

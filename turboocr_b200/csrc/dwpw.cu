@@ -1,0 +1,678 @@
+// Subsystem 2 — fused depthwise-3x3 + pointwise-1x1 conv block on tcgen05.
+//
+// Reference role: one DW-separable block of the PP-OCR DBNet backbone that
+// the reference runs inside TensorRT (include/turbo_ocr/engine/trt/trt_engine.h:37,
+// precision from src/engine/onnx_to_trt.cpp:42-158, per-channel INT8 / FP8
+// weight QDQ from scripts/quantize_onnx_int8.py:1-80 and
+// scripts/quantize_onnx_fp8.py:2-8). Its benchmark precedent is
+// tools/fused_dwpw_bench.cu:98-152 (WMMA DW prologue + PW GEMM, NHWC fp16).
+//
+//   y1 = hardswish(DW3x3_s(x) * bn1 + b1)            (fp16, per channel)
+//   y  = hardswish(PW(q(y1), Wq) * dequant + b2)     (fp16 NHWC out)
+//
+// Layout: activations NHWC fp16. PW weights per-output-channel symmetric
+// INT8 or FP8-E4M3 (BN2 scale folded in before quantisation). The DW output
+// is quantised per pixel (scale = max|y1| over the channels of the pixel),
+// so the epilogue dequantises with a_scale[pixel] * w_scale[co]. FP8 uses a
+// hi/lo split of the activation (two E4M3 MMAs into one f32 accumulator).
+//
+// B200 structure (one persistent CTA per SM, 18 warps):
+//   warp 0       TMA producer: 3x3 halo tile of x (zero padding from TMA OOB
+//                fill) per 64- or 32-channel chunk, double-buffered
+//   warp 1       TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 2-9    depthwise conv in fp16x2, hardswish, per-pixel quantisation
+//                into the K-major 128B-swizzled A tile (two warps per SMSP)
+//   warps 10-17  epilogue in two column groups: tcgen05.ld the accumulator,
+//                dequant + BN bias + hardswish, 128B-swizzled staging, TMA
+//                tensor stores (two warps per SMSP, same TMEM lane quadrant)
+// Tiles are 8x16 output pixels (= MMA M 128), N = C_out, K = C_in.
+#include "tocr_common.cuh"
+#include "tc_ptx.cuh"
+
+#include <cuda.h>
+#include <cuda_fp8.h>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+
+namespace tocr {
+namespace dwpw {
+
+using namespace tocr::ptx;
+
+constexpr int TH = 8, TW = 16, TP = 128;
+constexpr int kThreads = 576;
+constexpr int kDwWarp0 = 2, kEpiWarp0 = 10;
+constexpr int kDwThreads = 256, kDwWarps = 8, kEpiWarps = 8;
+
+template <int C_, int CO_, int S_, bool FP8_, int CCH_, int XST_, int AST_>
+struct Cfg {
+  static constexpr int C = C_, CO = CO_, S = S_, CCH = CCH_, XST = XST_, AST = AST_;
+  static constexpr bool FP8 = FP8_;
+  static constexpr int NCH = C / CCH;
+  static constexpr int KATOMS = (C + 127) / 128;       // 128-byte K atoms per row
+  static constexpr int KSTEPS = C / 32;                // MMA K = 32 per instruction
+  static constexpr int HH = (TH - 1) * S + 3, HW = (TW - 1) * S + 3;
+  static constexpr int HALO = HH * HW * CCH * 2;
+  static constexpr int PARTS = CCH / 8;                // 16-byte channel vectors per chunk
+  static constexpr int SEG = PARTS / 2;                // output pixels per DW thread
+  static constexpr int NSEG = TP / SEG;
+  static constexpr int A_SUB = TP * 128;               // one K atom of A
+  static constexpr int A_TILE = A_SUB * KATOMS * (FP8 ? 2 : 1);
+  static constexpr int B_BYTES = CO * 128 * KATOMS;
+  static constexpr int STG = TP * C * 2;
+  static constexpr int OUT = TP * CO * 2;
+  static constexpr int NBOX = CO / 64;
+  static constexpr int TMEM_COLS = 2 * CO < 32 ? 32 : 2 * CO;
+  // shared memory carve-up (all 1024-aligned where the async proxy reads)
+  static constexpr int OFF_X = 0;
+  static constexpr int OFF_A = OFF_X + ((XST * HALO + 1023) / 1024) * 1024;
+  static constexpr int OFF_B = OFF_A + AST * A_TILE;
+  static constexpr int OFF_OUT = OFF_B + B_BYTES;
+  static constexpr int OFF_STG = OFF_OUT + OUT;
+  static constexpr int OFF_WDW = OFF_STG + STG;              // 9*C fp16 + C fp16
+  static constexpr int OFF_WS = OFF_WDW + 10 * C * 2;        // CO floats
+  static constexpr int OFF_BS = OFF_WS + CO * 4;             // CO floats
+  static constexpr int OFF_AMAX = OFF_BS + CO * 4;           // TP floats
+  static constexpr int OFF_SCALE = OFF_AMAX + TP * 4;        // 4 x TP floats
+  static constexpr int OFF_BAR = OFF_SCALE + 4 * TP * 4;     // mbarriers
+  static constexpr int NH = (NBOX + 1) / 2;                  // 128-column store groups
+  static constexpr int NBAR = 2 * XST + 2 * AST + 4 + 8;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;        // tmem base, abort flag
+  static constexpr int SMEM = OFF_MISC + 16;
+  static constexpr int SMEM_ALLOC = SMEM + 1024;             // runtime 1024 alignment slack
+  static_assert(C % 32 == 0 && C % CCH == 0 && (CCH == 32 || CCH == 64), "channels");
+  static_assert(CO % 64 == 0 && CO <= 256, "C_out");
+  static_assert(TW % SEG == 0 && (TP / SEG) * PARTS == kDwThreads, "thread mapping");
+  static constexpr int NGRP = CO >= 128 ? 2 : 1;        // epilogue column groups
+  static constexpr int CPG = CO / NGRP;                 // columns per group
+  static constexpr int C32_PER_GRP = CPG / 32;
+  static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
+};
+
+// Offsets of the packed parameter blob (device): B image | w_scale | bias |
+// DW weights [9][C] fp16 | DW bias [C] fp16.
+__host__ __device__ inline size_t blob_b(int) { return 0; }
+__host__ __device__ inline size_t blob_ws(int C, int CO) { return (size_t)CO * 128 * ((C + 127) / 128); }
+__host__ __device__ inline size_t blob_bs(int C, int CO) { return blob_ws(C, CO) + CO * 4; }
+__host__ __device__ inline size_t blob_wdw(int C, int CO) { return blob_bs(C, CO) + CO * 4; }
+__host__ __device__ inline size_t blob_bytes(int C, int CO) { return blob_wdw(C, CO) + 10 * C * 2; }
+
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+
+// Epilogue of 32 accumulator columns of one pixel (TMEM lane): dequantise,
+// add the folded BN bias, hardswish, pack to fp16 and write the 64 bytes into
+// the 128B-swizzled staging box that a TMA tensor store later drains.
+template <class K>
+__device__ __forceinline__ void epi_chunk(const uint32_t (&v)[32], int c32, int p, float asc,
+                                          const float *sws, const float *sbs, uint8_t *sout) {
+  uint8_t *box = sout + (c32 / 2) * (TP * 128);
+  const __half2 sixth = __float2half2_rn(1.0f / 6.0f), half_ = __float2half2_rn(0.5f);
+#pragma unroll
+  for (int q8 = 0; q8 < 4; ++q8) {
+    const float4 w0 = reinterpret_cast<const float4 *>(sws + c32 * 32 + q8 * 8)[0];
+    const float4 w1 = reinterpret_cast<const float4 *>(sws + c32 * 32 + q8 * 8)[1];
+    const float4 b0 = reinterpret_cast<const float4 *>(sbs + c32 * 32 + q8 * 8)[0];
+    const float4 b1 = reinterpret_cast<const float4 *>(sbs + c32 * 32 + q8 * 8)[1];
+    const float wsv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    const float bsv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    uint32_t packed[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float y2[2];
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk) {
+        const int cc = e * 2 + kk;
+        const uint32_t raw = v[q8 * 8 + cc];
+        const float a = K::FP8 ? __uint_as_float(raw)
+                               : __int_as_float(0x4B400000 + (int)raw) - 12582912.f;
+        y2[kk] = fmaf(a, asc * wsv[cc], bsv[cc]);
+      }
+      __half2 yh = __floats2half2_rn(y2[0], y2[1]);
+      yh = __hmul2(yh, __hfma2_sat(yh, sixth, half_));
+      packed[e] = *reinterpret_cast<uint32_t *>(&yh);
+    }
+    const int chunk = (c32 % 2) * 4 + q8;  // 16B chunk within the 128B box row
+    *reinterpret_cast<uint4 *>(box + p * 128 + ((chunk ^ (p & 7)) * 16)) =
+        make_uint4(packed[0], packed[1], packed[2], packed[3]);
+  }
+}
+
+struct Params {
+  const uint8_t *blob;
+  int N, H, W, Ho, Wo;
+  int tiles_x, tiles_y, ntiles;
+  int *err;
+};
+
+template <class K>
+__global__ void __launch_bounds__(kThreads, 1)
+dwpw_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap,
+            Params prm) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sx = smem + K::OFF_X;
+  uint8_t *sa = smem + K::OFF_A;
+  uint8_t *sb = smem + K::OFF_B;
+  uint8_t *sout = smem + K::OFF_OUT;
+  uint8_t *sstg = smem + K::OFF_STG;
+  __half *swdw = reinterpret_cast<__half *>(smem + K::OFF_WDW);
+  float *sws = reinterpret_cast<float *>(smem + K::OFF_WS);
+  float *sbs = reinterpret_cast<float *>(smem + K::OFF_BS);
+  float *samax = reinterpret_cast<float *>(smem + K::OFF_AMAX);
+  float *sscale = reinterpret_cast<float *>(smem + K::OFF_SCALE);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + K::OFF_BAR);
+  uint64_t *x_full = bars, *x_empty = bars + K::XST;
+  uint64_t *a_full = bars + 2 * K::XST, *a_empty = a_full + K::AST;
+  uint64_t *acc_full = a_empty + K::AST, *acc_empty = acc_full + 2;
+  uint64_t *scl_full = acc_empty + 2, *scl_empty = scl_full + 4;
+  uint32_t *s_tmem = reinterpret_cast<uint32_t *>(smem + K::OFF_MISC);
+  volatile int *s_abort = reinterpret_cast<volatile int *>(smem + K::OFF_MISC + 4);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+
+  // ---- one-time setup: parameters into smem, zero K padding, barriers ----
+  {
+    const uint8_t *blob = prm.blob;
+    const uint4 *gb = reinterpret_cast<const uint4 *>(blob);
+    uint4 *db = reinterpret_cast<uint4 *>(sb);
+    for (int i = tid; i < K::B_BYTES / 16; i += kThreads) db[i] = gb[i];
+    const float *gws = reinterpret_cast<const float *>(blob + blob_ws(K::C, K::CO));
+    const float *gbs = reinterpret_cast<const float *>(blob + blob_bs(K::C, K::CO));
+    for (int i = tid; i < K::CO; i += kThreads) { sws[i] = gws[i]; sbs[i] = gbs[i]; }
+    const uint16_t *gw = reinterpret_cast<const uint16_t *>(blob + blob_wdw(K::C, K::CO));
+    uint16_t *dw = reinterpret_cast<uint16_t *>(swdw);
+    for (int i = tid; i < 10 * K::C; i += kThreads) dw[i] = gw[i];
+    if (K::C % 128 != 0) {  // zero the unused K chunks of every A tile once
+      uint4 *za = reinterpret_cast<uint4 *>(sa);
+      for (int i = tid; i < K::AST * K::A_TILE / 16; i += kThreads) za[i] = make_uint4(0, 0, 0, 0);
+    }
+    if (tid == 0) {
+      for (int i = 0; i < K::XST; ++i) { mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], kDwWarps); }
+      for (int i = 0; i < K::AST; ++i) { mbar_init(&a_full[i], kDwWarps); mbar_init(&a_empty[i], 1); }
+      for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], kEpiWarps); }
+      for (int i = 0; i < 4; ++i) { mbar_init(&scl_full[i], kDwWarps); mbar_init(&scl_empty[i], kEpiWarps); }
+      *s_abort = 0;
+      fence_mbar_init();
+    }
+    if (warp == 1) {
+      tmem_alloc(s_tmem, K::TMEM_COLS);
+      tmem_relinquish();
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  }
+  const uint32_t tmem_base = *s_tmem;
+  const int tiles_per_img = prm.tiles_x * prm.tiles_y;
+
+  if (warp == 0) {
+    // =========================== TMA producer ===========================
+    if (lane == 0) {
+      tma_prefetch_desc(&xmap);
+      uint32_t g = 0;
+      for (int t = blockIdx.x; t < prm.ntiles; t += gridDim.x) {
+        const int n = t / tiles_per_img, r = t % tiles_per_img;
+        const int ty = r / prm.tiles_x, tx = r % prm.tiles_x;
+        const int ix = tx * TW * K::S - 1, iy = ty * TH * K::S - 1;
+        for (int ch = 0; ch < K::NCH; ++ch, ++g) {
+          const int st = g % K::XST;
+          if (!mbar_wait_bounded(&x_empty[st], ((g / K::XST) & 1) ^ 1, s_abort, prm.err, 11))
+            goto producer_done;
+          mbar_arrive_expect_tx(&x_full[st], K::HALO);
+          tma_load_4d(sx + st * K::HALO, &xmap, &x_full[st], ch * K::CCH, ix, iy, n);
+        }
+      }
+    producer_done:
+      // drain: every issued load must land before the CTA may exit
+      for (uint32_t k = 0; k < K::XST && k < g; ++k) {
+        const uint32_t gg = g - 1 - k;
+        volatile int no_abort = 0;
+        mbar_wait_bounded(&x_full[gg % K::XST], (gg / K::XST) & 1, &no_abort, prm.err, 12);
+      }
+    }
+  } else if (warp == 1) {
+    // ============================ MMA issuer ============================
+    if (lane == 0) {
+      const uint32_t idesc = K::FP8 ? idesc_e4m3(TP, K::CO) : idesc_i8(TP, K::CO);
+      uint32_t i = 0;
+      for (int t = blockIdx.x; t < prm.ntiles; t += gridDim.x, ++i) {
+        const int ast = i % K::AST, acs = i & 1;
+        if (!mbar_wait_bounded(&a_full[ast], (i / K::AST) & 1, s_abort, prm.err, 21)) break;
+        if (!mbar_wait_bounded(&acc_empty[acs], ((i >> 1) & 1) ^ 1, s_abort, prm.err, 22)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + acs * K::CO;
+        const uint32_t abase = smem_u32(sa + ast * K::A_TILE);
+        const uint32_t bbase = smem_u32(sb);
+        uint32_t acc = 0;
+#pragma unroll
+        for (int part = 0; part < (K::FP8 ? 2 : 1); ++part) {
+#pragma unroll
+          for (int k = 0; k < K::KSTEPS; ++k) {
+            const uint32_t aoff = part * K::A_SUB * K::KATOMS + (k / 4) * K::A_SUB + (k % 4) * 32;
+            const uint32_t boff = (k / 4) * K::CO * 128 + (k % 4) * 32;
+            const uint64_t ad = sw128_kmajor_desc(abase + aoff);
+            const uint64_t bd = sw128_kmajor_desc(bbase + boff);
+            if (K::FP8) mma_f8(d, ad, bd, idesc, acc);
+            else mma_i8(d, ad, bd, idesc, acc);
+            acc = 1;
+          }
+        }
+        mma_commit(&a_empty[ast]);
+        mma_commit(&acc_full[acs]);
+      }
+      // the accumulators must not be freed while MMAs are in flight
+      for (uint32_t k = 0; k < 2 && k < i; ++k) {
+        const uint32_t ii = i - 1 - k;
+        volatile int no_abort = 0;
+        mbar_wait_bounded(&acc_full[ii & 1], (ii >> 1) & 1, &no_abort, prm.err, 23);
+      }
+    }
+  } else if (warp < kEpiWarp0) {
+    // ===================== depthwise + quantisation =====================
+    const int dt = tid - kDwWarp0 * 32;            // 0..255
+    const int seg = dt / K::PARTS, part = dt % K::PARTS;
+    const int seg_row = seg / (TW / K::SEG), seg_col = (seg % (TW / K::SEG)) * K::SEG;
+    uint32_t g = 0, i = 0;
+    for (int t = blockIdx.x; t < prm.ntiles; t += gridDim.x, ++i) {
+      float amax[K::SEG];
+#pragma unroll
+      for (int j = 0; j < K::SEG; ++j) amax[j] = 0.f;
+      bool ok = true;
+      for (int ch = 0; ch < K::NCH; ++ch, ++g) {
+        const int st = g % K::XST;
+        if (ok) ok = mbar_wait_bounded(&x_full[st], (g / K::XST) & 1, s_abort, prm.err, 31);
+        if (!ok) continue;
+        const uint8_t *xs = sx + st * K::HALO;
+        const int c0 = ch * K::CCH + part * 8;     // first channel of this thread
+        __half2 w[9][4];
+#pragma unroll
+        for (int tp = 0; tp < 9; ++tp) {
+          const uint4 v = *reinterpret_cast<const uint4 *>(swdw + tp * K::C + c0);
+          w[tp][0] = u2h(v.x); w[tp][1] = u2h(v.y); w[tp][2] = u2h(v.z); w[tp][3] = u2h(v.w);
+        }
+        __half2 acc[K::SEG][4];
+        {
+          const uint4 bv = *reinterpret_cast<const uint4 *>(swdw + 9 * K::C + c0);
+#pragma unroll
+          for (int j = 0; j < K::SEG; ++j) {
+            acc[j][0] = u2h(bv.x); acc[j][1] = u2h(bv.y); acc[j][2] = u2h(bv.z); acc[j][3] = u2h(bv.w);
+          }
+        }
+        // every input column that the SEG outputs touch: (SEG-1)*S + 3
+#pragma unroll
+        for (int ic = 0; ic < (K::SEG - 1) * K::S + 3; ++ic) {
+          const int hx = seg_col * K::S + ic;
+#pragma unroll
+          for (int ky = 0; ky < 3; ++ky) {
+            const int hy = seg_row * K::S + ky;
+            const uint4 v = *reinterpret_cast<const uint4 *>(
+                xs + ((hy * K::HW + hx) * K::CCH + part * 8) * 2);
+            const __half2 xv[4] = {u2h(v.x), u2h(v.y), u2h(v.z), u2h(v.w)};
+#pragma unroll
+            for (int j = 0; j < K::SEG; ++j) {
+              const int kx = ic - j * K::S;
+              if (kx >= 0 && kx < 3) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) acc[j][q] = __hfma2(w[ky * 3 + kx][q], xv[q], acc[j][q]);
+              }
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&x_empty[st]);
+        // hardswish, per-pixel |max|, fp16 staging (16B vectors XOR-swizzled by pixel)
+        const __half2 sixth = __float2half2_rn(1.0f / 6.0f), half_ = __float2half2_rn(0.5f);
+#pragma unroll
+        for (int j = 0; j < K::SEG; ++j) {
+          __half2 m = __float2half2_rn(0.f);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const __half2 y = acc[j][q];
+            const __half2 h = __hmul2(y, __hfma2_sat(y, sixth, half_));
+            acc[j][q] = h;
+            m = __hmax2(m, __habs2(h));
+          }
+          amax[j] = fmaxf(amax[j], fmaxf(__low2float(m), __high2float(m)));
+          const int p = seg_row * TW + seg_col + j;
+          const int vs = (c0 / 8) ^ (p & (K::C / 8 - 1) & 7);
+          *reinterpret_cast<uint4 *>(sstg + (p * K::C + vs * 8) * 2) =
+              make_uint4(h2u(acc[j][0]), h2u(acc[j][1]), h2u(acc[j][2]), h2u(acc[j][3]));
+        }
+      }
+      // per-pixel amax across the PARTS lanes of a segment
+#pragma unroll
+      for (int j = 0; j < K::SEG; ++j) {
+#pragma unroll
+        for (int off = 1; off < K::PARTS; off <<= 1)
+          amax[j] = fmaxf(amax[j], __shfl_xor_sync(0xffffffffu, amax[j], off));
+      }
+      if (part == 0) {
+#pragma unroll
+        for (int j = 0; j < K::SEG; ++j) samax[seg_row * TW + seg_col + j] = amax[j];
+      }
+      if (!named_bar_and(1, kDwThreads, ok)) break;
+      // ---- quantise: threads 2p and 2p+1 own halves of pixel p ----
+      const int ast = i % K::AST;
+      const int ss = i & 3;
+      ok = mbar_wait_bounded(&a_empty[ast], ((i / K::AST) & 1) ^ 1, s_abort, prm.err, 32);
+      if (ok) ok = mbar_wait_bounded(&scl_empty[ss], ((i >> 2) & 1) ^ 1, s_abort, prm.err, 33);
+      if (!named_bar_and(1, kDwThreads, ok)) break;
+      {
+        const int p = dt >> 1, hh = dt & 1;
+        const float am = samax[p];
+        const float qmax = K::FP8 ? 448.f : 127.f;
+        const float inv = am > 0.f ? qmax / am : 0.f;
+        if (hh == 0) sscale[ss * TP + p] = am / qmax;
+        uint8_t *arow = sa + ast * K::A_TILE + p * 128;
+#pragma unroll
+        for (int j16 = hh * (K::C / 32); j16 < (hh + 1) * (K::C / 32); ++j16) {  // 16 ch per A chunk
+          float f[16];
+#pragma unroll
+          for (int hv = 0; hv < 2; ++hv) {
+            const int v = j16 * 2 + hv;
+            const int vs = v ^ (p & (K::C / 8 - 1) & 7);
+            const uint4 u = *reinterpret_cast<const uint4 *>(sstg + (p * K::C + vs * 8) * 2);
+            const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float2 ff = __half22float2(u2h(uu[q]));
+              f[hv * 8 + 2 * q] = ff.x;
+              f[hv * 8 + 2 * q + 1] = ff.y;
+            }
+          }
+          const int atom = j16 / 8, chunk = j16 % 8;
+          const int off = atom * K::A_SUB + ((chunk ^ (p & 7)) * 16);
+          if (!K::FP8) {
+            uint32_t wd[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint32_t b0 = __float_as_uint(fmaf(f[4 * q + 0], inv, 12582912.f));
+              const uint32_t b1 = __float_as_uint(fmaf(f[4 * q + 1], inv, 12582912.f));
+              const uint32_t b2 = __float_as_uint(fmaf(f[4 * q + 2], inv, 12582912.f));
+              const uint32_t b3 = __float_as_uint(fmaf(f[4 * q + 3], inv, 12582912.f));
+              wd[q] = __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+            }
+            *reinterpret_cast<uint4 *>(arow + off) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+          } else {
+            uint32_t hi[4], lo[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              float s4[4], r[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) s4[e] = f[4 * q + e] * inv;
+              const __nv_fp8x2_storage_t h01 = __nv_cvt_float2_to_fp8x2(make_float2(s4[0], s4[1]), __NV_SATFINITE, __NV_E4M3);
+              const __nv_fp8x2_storage_t h23 = __nv_cvt_float2_to_fp8x2(make_float2(s4[2], s4[3]), __NV_SATFINITE, __NV_E4M3);
+              const __half2_raw b01 = __nv_cvt_fp8x2_to_halfraw2(h01, __NV_E4M3);
+              const __half2_raw b23 = __nv_cvt_fp8x2_to_halfraw2(h23, __NV_E4M3);
+              const float2 g01 = __half22float2(*reinterpret_cast<const __half2 *>(&b01));
+              const float2 g23 = __half22float2(*reinterpret_cast<const __half2 *>(&b23));
+              r[0] = s4[0] - g01.x; r[1] = s4[1] - g01.y; r[2] = s4[2] - g23.x; r[3] = s4[3] - g23.y;
+              const __nv_fp8x2_storage_t l01 = __nv_cvt_float2_to_fp8x2(make_float2(r[0], r[1]), __NV_SATFINITE, __NV_E4M3);
+              const __nv_fp8x2_storage_t l23 = __nv_cvt_float2_to_fp8x2(make_float2(r[2], r[3]), __NV_SATFINITE, __NV_E4M3);
+              hi[q] = (uint32_t)h01 | ((uint32_t)h23 << 16);
+              lo[q] = (uint32_t)l01 | ((uint32_t)l23 << 16);
+            }
+            *reinterpret_cast<uint4 *>(arow + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<uint4 *>(arow + K::A_SUB * K::KATOMS + off) =
+                make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&a_full[ast]);
+          mbar_arrive(&scl_full[ss]);
+        }
+      }
+      named_bar(1, kDwThreads);  // staging and amax are free for the next tile
+    }
+
+  } else {
+    // ============================== epilogue ============================
+    const int ew = warp - kEpiWarp0;              // 0..7
+    const int grp = ew >> 2;                      // column group
+    const int quad = warp & 3;                    // TMEM lane quadrant of this warp
+    const int p = quad * 32 + lane;               // pixel = accumulator row
+    const bool active = grp < K::NGRP;
+    const bool leader = active && (ew & 3) == 0 && lane == 0;
+    if (leader) tma_prefetch_desc(&ymap);
+    uint32_t i = 0;
+    for (int t = blockIdx.x; t < prm.ntiles; t += gridDim.x, ++i) {
+      const int acs = i & 1, ss = i & 3;
+      bool ok = mbar_wait_bounded(&acc_full[acs], (i >> 1) & 1, s_abort, prm.err, 41);
+      if (ok) ok = mbar_wait_bounded(&scl_full[ss], (i >> 2) & 1, s_abort, prm.err, 42);
+      if (!named_bar_and(2 + grp, 128, ok)) break;
+      tc_fence_after();
+      const int n = t / tiles_per_img, r = t % tiles_per_img;
+      const int ty = r / prm.tiles_x, tx = r % prm.tiles_x;
+      const float asc = sscale[ss * TP + p];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&scl_empty[ss]);
+      if (active) {
+        if (leader) bulk_wait_read<0>();
+        named_bar(2 + grp, 128);
+        const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + acs * K::CO + grp * K::CPG;
+        uint32_t va[32], vb[32];
+        tmem_ld32(tbase, va);
+        tmem_ld_wait(va);
+#pragma unroll
+        for (int k = 0; k < K::C32_PER_GRP; ++k) {
+          // prefetch the next 32 columns into the other buffer, then convert this one
+          if (k + 1 < K::C32_PER_GRP) {
+            if (k & 1) tmem_ld32(tbase + (k + 1) * 32, va);
+            else tmem_ld32(tbase + (k + 1) * 32, vb);
+          }
+          if (k & 1) epi_chunk<K>(vb, grp * K::C32_PER_GRP + k, p, asc, sws, sbs, sout);
+          else epi_chunk<K>(va, grp * K::C32_PER_GRP + k, p, asc, sws, sbs, sout);
+          if (k + 1 < K::C32_PER_GRP) {
+            if (k & 1) tmem_ld_wait(va);
+            else tmem_ld_wait(vb);
+          }
+        }
+        tc_fence_before();
+        fence_proxy_async_smem();
+        named_bar(2 + grp, 128);
+        if (leader) {
+          for (int b = 0; b < K::CPG / 64; ++b) {
+            const int gb = grp * (K::CPG / 64) + b;
+            tma_store_4d(&ymap, sout + gb * (TP * 128), gb * 64, tx * TW, ty * TH, n);
+          }
+          bulk_commit();
+        }
+      } else {
+        tc_fence_before();
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acs]);
+    }
+    if (leader) bulk_wait<0>();
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, K::TMEM_COLS);
+  }
+}
+
+// --------------------------------------------------------------- host ------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int make_map_4d(CUtensorMap *m, const void *base, uint64_t d0, uint64_t d1, uint64_t d2,
+                uint64_t d3, uint32_t b0, uint32_t b1, uint32_t b2, CUtensorMapSwizzle sw) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return set_error(TOCR_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[4] = {d0, d1, d2, d3};
+  const cuuint64_t strides[3] = {d0 * 2, d0 * d1 * 2, d0 * d1 * d2 * 2};
+  const cuuint32_t box[4] = {b0, b1, b2, 1};
+  const cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void *>(base), dims, strides,
+                  box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(TOCR_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return TOCR_OK;
+}
+
+template <class K>
+int launch(const void *x, void *y, int N, int H, int W, const uint8_t *blob, int *err,
+           cudaStream_t stream) {
+  const int Ho = (H - 1) / K::S + 1, Wo = (W - 1) / K::S + 1;
+  CUtensorMap xm, ym;
+  int st = make_map_4d(&xm, x, K::C, W, H, N, K::CCH, K::HW, K::HH, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (st) return st;
+  st = make_map_4d(&ym, y, K::CO, Wo, Ho, N, 64, TW, TH, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st) return st;
+  Params p;
+  p.blob = blob;
+  p.N = N; p.H = H; p.W = W; p.Ho = Ho; p.Wo = Wo;
+  p.tiles_x = (Wo + TW - 1) / TW;
+  p.tiles_y = (Ho + TH - 1) / TH;
+  p.ntiles = N * p.tiles_x * p.tiles_y;
+  p.err = err;
+  if (p.ntiles == 0) return TOCR_OK;
+  cudaError_t e = cudaFuncSetAttribute(dwpw_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       K::SMEM_ALLOC);
+  if (e != cudaSuccess) return set_error(TOCR_ERR_CUDA, "dwpw smem attribute: %s", cudaGetErrorString(e));
+  const int grid = p.ntiles < sm_count() ? p.ntiles : sm_count();
+  dwpw_kernel<K><<<grid, kThreads, K::SMEM_ALLOC, stream>>>(xm, ym, p);
+  return check_launch("dwpw_kernel");
+}
+
+// Supported shapes: (C, C_out, stride) -> kernel configuration.
+template <bool F8>
+int dispatch(int C, int CO, int S, const void *x, void *y, int N, int H, int W,
+             const uint8_t *blob, int *err, cudaStream_t st) {
+#define TOCR_DWPW(c, co, s, cch, xst, ast)                                           \
+  if (C == c && CO == co && S == s)                                                   \
+    return launch<Cfg<c, co, s, F8, cch, xst, ast>>(x, y, N, H, W, blob, err, st);
+  TOCR_DWPW(128, 256, 1, 64, 2, (F8 ? 1 : 2))
+  TOCR_DWPW(64, 128, 1, 64, 2, 2)
+  TOCR_DWPW(64, 64, 1, 64, 2, 2)
+  TOCR_DWPW(32, 64, 1, 32, 2, 2)
+  TOCR_DWPW(128, 128, 1, 64, 2, 2)
+#undef TOCR_DWPW
+  return set_error(TOCR_ERR_INVALID, "tocr_dwpw_block: unsupported shape C=%d C_out=%d stride=%d",
+                   C, CO, S);
+}
+
+}  // namespace dwpw
+}  // namespace tocr
+
+using namespace tocr;
+
+extern "C" {
+
+TOCR_API size_t tocr_dwpw_packed_bytes(int C, int CO) {
+  if (C <= 0 || CO <= 0) return 0;
+  return dwpw::blob_bytes(C, CO);
+}
+
+TOCR_API int tocr_dwpw_pack(int C, int CO, int kind, const float *wdw, const float *bdw,
+                            const float *wpw, const float *bpw, void *out, size_t out_bytes) {
+  clear_error();
+  TOCR_REQUIRE(C > 0 && C % 32 == 0 && CO > 0 && CO % 64 == 0 && CO <= 256,
+               "tocr_dwpw_pack: unsupported shape C=%d C_out=%d", C, CO);
+  TOCR_REQUIRE(kind == 0 || kind == 1, "tocr_dwpw_pack: kind must be 0 (int8) or 1 (fp8)");
+  TOCR_REQUIRE(wdw && bdw && wpw && bpw && out, "tocr_dwpw_pack: null pointer");
+  TOCR_REQUIRE(out_bytes >= dwpw::blob_bytes(C, CO), "tocr_dwpw_pack: output too small");
+  uint8_t *o = static_cast<uint8_t *>(out);
+  memset(o, 0, dwpw::blob_bytes(C, CO));
+  const int katoms = (C + 127) / 128;
+  float *ws = reinterpret_cast<float *>(o + dwpw::blob_ws(C, CO));
+  float *bs = reinterpret_cast<float *>(o + dwpw::blob_bs(C, CO));
+  for (int co = 0; co < CO; ++co) {
+    float amax = 0.f;
+    for (int c = 0; c < C; ++c) amax = fmaxf(amax, fabsf(wpw[(size_t)co * C + c]));
+    const float qmax = kind == 0 ? 127.f : 448.f;
+    const float scale = amax > 0.f ? amax / qmax : 1.f;
+    ws[co] = scale;
+    bs[co] = bpw[co];
+    for (int c = 0; c < C; ++c) {
+      const float v = wpw[(size_t)co * C + c] / scale;
+      uint8_t q;
+      if (kind == 0) {
+        float r = rintf(v);
+        r = fminf(127.f, fmaxf(-127.f, r));
+        q = (uint8_t)(int8_t)r;
+      } else {
+        q = (uint8_t)__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
+      }
+      const int atom = c / 128, kk = c % 128, chunk = kk / 16;
+      const size_t pos = (size_t)atom * CO * 128 + (size_t)co * 128 + ((chunk ^ (co & 7)) * 16) + kk % 16;
+      o[pos] = q;
+    }
+  }
+  uint16_t *wd = reinterpret_cast<uint16_t *>(o + dwpw::blob_wdw(C, CO));
+  for (int c = 0; c < C; ++c) {
+    for (int tp = 0; tp < 9; ++tp) {
+      __half h = __float2half_rn(wdw[(size_t)c * 9 + tp]);
+      memcpy(&wd[tp * C + c], &h, 2);
+    }
+    __half hb = __float2half_rn(bdw[c]);
+    memcpy(&wd[9 * C + c], &hb, 2);
+  }
+  (void)katoms;
+  return TOCR_OK;
+}
+
+// Dequantised PW weights [CO][C] of a packed blob (what the tensor cores see).
+TOCR_API int tocr_dwpw_dequant_pw(const void *blob, int C, int CO, int kind, float *w_out) {
+  clear_error();
+  TOCR_REQUIRE(blob && w_out && C > 0 && CO > 0, "tocr_dwpw_dequant_pw: bad argument");
+  const uint8_t *o = static_cast<const uint8_t *>(blob);
+  const float *ws = reinterpret_cast<const float *>(o + dwpw::blob_ws(C, CO));
+  for (int co = 0; co < CO; ++co)
+    for (int c = 0; c < C; ++c) {
+      const int atom = c / 128, kk = c % 128, chunk = kk / 16;
+      const uint8_t q = o[(size_t)atom * CO * 128 + (size_t)co * 128 + ((chunk ^ (co & 7)) * 16) + kk % 16];
+      float v;
+      if (kind == 0) {
+        v = (float)(int8_t)q;
+      } else {
+        __half_raw hr = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)q, __NV_E4M3);
+        v = __half2float(*reinterpret_cast<__half *>(&hr));
+      }
+      w_out[(size_t)co * C + c] = v * ws[co];
+    }
+  return TOCR_OK;
+}
+
+TOCR_API int tocr_dwpw_block(const void *d_x, void *d_y, int N, int H, int W, int C, int CO,
+                             int stride, int kind, const void *d_packed, int *d_err,
+                             void *stream) {
+  TOCR_ENTRY();
+  TOCR_REQUIRE(N >= 0 && H > 0 && W > 0, "tocr_dwpw_block: bad spatial size");
+  if (N == 0) return TOCR_OK;
+  TOCR_REQUIRE(d_x && d_y && d_packed && d_err, "tocr_dwpw_block: null pointer");
+  TOCR_REQUIRE(aligned(d_x, 16) && aligned(d_y, 16) && aligned(d_packed, 16),
+               "tocr_dwpw_block: tensors must be 16-byte aligned");
+  TOCR_REQUIRE(kind == 0 || kind == 1, "tocr_dwpw_block: kind must be 0 (int8) or 1 (fp8)");
+  const uint8_t *blob = static_cast<const uint8_t *>(d_packed);
+  if (kind == 0)
+    return dwpw::dispatch<false>(C, CO, stride, d_x, d_y, N, H, W, blob, d_err, as_stream(stream));
+  return dwpw::dispatch<true>(C, CO, stride, d_x, d_y, N, H, W, blob, d_err, as_stream(stream));
+}
+
+}  // extern "C"
