@@ -8,7 +8,12 @@
 #include <algorithm>
 #include <vector>
 
+// Test access to the offsetter's intermediate (pre-union) path.
+#define private public
+#define protected public
 #include "clipper/clipper.hpp"
+#undef private
+#undef protected
 
 using namespace ClipperLib;
 
@@ -37,6 +42,27 @@ int clipper_ref_unclip(const int *xy, int n, double distance, long long *out_xy,
   for (int i = 0; i < m; ++i) {
     out_xy[2 * i] = (*best)[i].X;
     out_xy[2 * i + 1] = (*best)[i].Y;
+  }
+  return m;
+}
+
+// The raw offset path of ClipperOffset (after FixOrientations + DoOffset,
+// before the union that Execute applies). Returns its point count, 0 if the
+// offsetter produced no path, or -needed if cap is too small.
+int clipper_ref_raw_offset(const int *xy, int n, double distance, long long *out_xy, int cap) {
+  ClipperOffset co;
+  Path subj;
+  for (int i = 0; i < n; ++i) subj.emplace_back(xy[2 * i], xy[2 * i + 1]);
+  co.AddPath(subj, jtRound, etClosedPolygon);
+  co.FixOrientations();
+  co.DoOffset(distance);
+  if (co.m_destPolys.empty()) return 0;
+  const Path &p = co.m_destPolys.front();
+  const int m = (int)p.size();
+  if (m > cap) return -m;
+  for (int i = 0; i < m; ++i) {
+    out_xy[2 * i] = p[i].X;
+    out_xy[2 * i + 1] = p[i].Y;
   }
   return m;
 }

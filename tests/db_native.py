@@ -1,0 +1,100 @@
+"""Builds and loads the test-only host build of the DB geometry header
+(tests/native/db_geom_host.cpp), so CPU tests can compare each routine with
+OpenCV and with the reference's Clipper."""
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parents[1]
+SRC = ROOT / "tests" / "native" / "db_geom_host.cpp"
+HDR = ROOT / "turboocr_b200" / "csrc" / "db_geom.cuh"
+OUT = ROOT / "tests" / "native" / "_build" / "libdbgeom_host.so"
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is not None:
+        return _lib
+    OUT.parent.mkdir(exist_ok=True)
+    if not OUT.exists() or OUT.stat().st_mtime < max(SRC.stat().st_mtime, HDR.stat().st_mtime):
+        subprocess.run(["g++", "-std=c++17", "-O2", "-ffp-contract=off", "-fPIC", "-shared",
+                        f"-I{HDR.parent}", "-o", str(OUT), str(SRC)], check=True)
+    L = C.CDLL(str(OUT))
+    vp, i, d = C.c_void_p, C.c_int, C.c_double
+    L.dbh_trace.argtypes = [vp, i, i, i, i, i, vp, i]
+    L.dbh_hull.argtypes = [vp, i, vp]
+    L.dbh_min_area_rect.argtypes = [vp, i, vp]
+    L.dbh_mini_box.argtypes = [vp, i, vp, vp]
+    L.dbh_area.argtypes = [vp, i]
+    L.dbh_area.restype = d
+    L.dbh_arclen.argtypes = [vp, i]
+    L.dbh_arclen.restype = d
+    L.dbh_offset_raw.argtypes = [vp, i, d, vp, i]
+    L.dbh_poly_mask.argtypes = [vp, i, i, i, i, i, vp]
+    _lib = L
+    return L
+
+
+def _pts(p):
+    return np.ascontiguousarray(np.asarray(p, dtype=np.int32).reshape(-1, 2))
+
+
+def trace(bm, x0, y0, hole):
+    bm = np.ascontiguousarray(bm, dtype=np.uint8)
+    H, W = bm.shape
+    cap = 8 * (H + W) * 4 + 64
+    out = np.zeros((cap, 2), np.int32)
+    n = lib().dbh_trace(bm.ctypes.data, H, W, x0, y0, 1 if hole else 0, out.ctypes.data, cap)
+    assert 0 <= n <= cap
+    return out[:n]
+
+
+def hull(p):
+    p = _pts(p)
+    out = np.zeros((len(p) + 1, 2), np.int32)
+    m = lib().dbh_hull(p.ctypes.data, len(p), out.ctypes.data)
+    return out[:m]
+
+
+def min_area_rect(p):
+    p = _pts(p)
+    o = np.zeros(5, np.float32)
+    lib().dbh_min_area_rect(p.ctypes.data, len(p), o.ctypes.data)
+    return o
+
+
+def mini_box(p):
+    p = _pts(p)
+    box = np.zeros(8, np.int32)
+    ms = np.zeros(1, np.float32)
+    lib().dbh_mini_box(p.ctypes.data, len(p), box.ctypes.data, ms.ctypes.data)
+    return box.reshape(4, 2).tolist(), ms[0]
+
+
+def area(p):
+    p = _pts(p)
+    return lib().dbh_area(p.ctypes.data, len(p))
+
+
+def arclen(p):
+    p = _pts(p)
+    return lib().dbh_arclen(p.ctypes.data, len(p))
+
+
+def offset_raw(p, delta):
+    p = _pts(p)
+    cap = 1 << 16
+    out = np.zeros((cap, 2), np.int32)
+    n = lib().dbh_offset_raw(p.ctypes.data, len(p), delta, out.ctypes.data, cap)
+    return [tuple(q) for q in out[:n].tolist()]
+
+
+def poly_mask(p, x0, y0, w, h):
+    p = _pts(p)
+    m = np.zeros((h, w), np.uint8)
+    lib().dbh_poly_mask(p.ctypes.data, len(p), x0, y0, w, h, m.ctypes.data)
+    return m

@@ -1,0 +1,75 @@
+// Test-only host build of turboocr_b200/csrc/db_geom.cuh: exposes the DB
+// geometry routines over a C ABI so the CPU tests can compare them, routine
+// by routine, with OpenCV and with the reference's Clipper. Built by the
+// tests themselves (tests/db_native.py); never linked into the product.
+#include <cstring>
+#include <vector>
+
+#include "db_geom.cuh"
+
+using namespace tocr::db;
+
+extern "C" {
+
+// Border following from one start pixel; returns the point count.
+int dbh_trace(const unsigned char *bm, int H, int W, int x0, int y0, int hole, int *out, int cap) {
+  auto fg = [&](int x, int y) { return x >= 0 && y >= 0 && x < W && y < H && bm[y * W + x] != 0; };
+  return trace_border(fg, x0, y0, hole != 0, reinterpret_cast<P2 *>(out), cap, 64 * W * H + 64);
+}
+
+int dbh_hull(const int *pts, int n, int *out) {
+  std::vector<HP> work(2 * n + 2);
+  return convex_hull(reinterpret_cast<const P2 *>(pts), n, work.data(), reinterpret_cast<P2 *>(out));
+}
+
+// minAreaRect of a point sequence: writes cx, cy, w, h, angle.
+void dbh_min_area_rect(const int *pts, int n, float *out5) {
+  std::vector<HP> work(2 * n + 2);
+  std::vector<P2> hull(n + 1);
+  const int m = convex_hull(reinterpret_cast<const P2 *>(pts), n, work.data(), hull.data());
+  std::vector<float> scratch(3 * m + 3);
+  RRect r = min_area_rect(hull.data(), m, scratch.data());
+  out5[0] = r.cx; out5[1] = r.cy; out5[2] = r.w; out5[3] = r.h; out5[4] = r.angle;
+}
+
+void dbh_mini_box(const int *pts, int n, int *box8, float *min_side) {
+  std::vector<HP> work(2 * n + 2);
+  std::vector<P2> hull(n + 1);
+  const int m = convex_hull(reinterpret_cast<const P2 *>(pts), n, work.data(), hull.data());
+  std::vector<float> scratch(3 * m + 3);
+  RRect r = min_area_rect(hull.data(), m, scratch.data());
+  *min_side = r.w < r.h ? r.w : r.h;
+  mini_box(r, box8);
+}
+
+void dbh_mar_raw(const int *pts, int n, float *raw6) {
+  std::vector<HP> work(2 * n + 2);
+  std::vector<P2> hull(n + 1);
+  const int m = convex_hull(reinterpret_cast<const P2 *>(pts), n, work.data(), hull.data());
+  std::vector<float> scratch(3 * m + 3);
+  (void)min_area_rect(hull.data(), m, scratch.data(), raw6);
+}
+
+// Polygon mask of a contour over its bounding box [x0, x0+w) x [y0, y0+h).
+void dbh_poly_mask(const int *pts, int n, int x0, int y0, int w, int h, unsigned char *mask) {
+  std::vector<int> xs(n + 1);
+  memset(mask, 0, (size_t)w * h);
+  for (int y = y0; y < y0 + h; ++y)
+    poly_row_spans(reinterpret_cast<const P2 *>(pts), n, y, xs.data(), [&](int a, int b) {
+      if (a > b) { int t = a; a = b; b = t; }
+      for (int x = a; x <= b; ++x)
+        if (x >= x0 && x < x0 + w) mask[(size_t)(y - y0) * w + (x - x0)] = 1;
+    });
+}
+
+double dbh_area(const int *pts, int n) { return contour_area(reinterpret_cast<const P2 *>(pts), n); }
+double dbh_arclen(const int *pts, int n) { return arc_length(reinterpret_cast<const P2 *>(pts), n); }
+
+int dbh_offset_raw(const int *pts, int n, double delta, int *out, int cap) {
+  std::vector<P2> q(n + 1);
+  const int m = offset_prepare(reinterpret_cast<const P2 *>(pts), n, q.data());
+  if (m == 0) return 0;
+  return offset_raw(q.data(), m, delta, reinterpret_cast<P2 *>(out), cap);
+}
+
+}  // extern "C"

@@ -69,6 +69,7 @@ SYNTH_SIGNATURES: dict[str, tuple] = {
     "tocr_synth_fill_u8": (_i, [_vp, _ll, _u64, _u64, _vp]),
     "tocr_synth_normal_f16": (_i, [_vp, _ll, _f, _u64, _u64, _vp]),
     "tocr_synth_ctc_logits": (_i, [_vp, _vp, _i, _i, _i, _u64, _vp]),
+    "tocr_synth_db_map_host": (_i, [_vp, _i, _i, _i, _i, _u64, _u64]),
 }
 
 

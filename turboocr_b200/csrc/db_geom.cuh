@@ -1,0 +1,600 @@
+// DB post-processing geometry, written once for the device kernels (db.cu)
+// and for a host build used by the CPU tests. Every routine reproduces the
+// arithmetic of the reference's CPU path operation for operation:
+//
+//   border following (CHAIN_APPROX_SIMPLE) ... cv::findContours(RETR_LIST), called at
+//                                              src/detection/det_postprocess.cpp:162-163
+//   convex hull + rotating calipers ......... cv::minAreaRect, det_postprocess.cpp:129
+//   rectangle corners + corner order ........ RotatedRect::points, order_quad_tl_tr_br_bl,
+//                                              det_postprocess.cpp:104-143
+//   polygon mask mean ........................ box_score_fast, det_postprocess.cpp:15-55
+//   area / perimeter / offset distance ....... unclip, det_postprocess.cpp:57-66
+//   round-join polygon offset ............... ClipperOffset (Clipper 6.4.2, jtRound,
+//                                              etClosedPolygon), det_postprocess.cpp:72-101
+//
+// The algorithms are the published ones (Suzuki & Abe 1985 border following;
+// Andrew's monotone chain; Toussaint's rotating calipers; Vatti-style
+// positive-fill offset cleanup). The floating-point operation order was
+// fixed by testing against the libraries' outputs: OpenCV's float/double code
+// is uncontracted, while the reference builds Clipper with -O3
+// -march=x86-64-v3 (CMakeLists.txt:97-100,259-268), so its multiply-adds are
+// FMAs — written here as explicit fma() calls. Device code that includes this
+// header is compiled with -fmad=false so nothing else is contracted.
+#pragma once
+
+#include <cmath>
+#include <cstdint>
+
+#if defined(__CUDACC__)
+#define TG __host__ __device__ __forceinline__
+#else
+#define TG inline
+#endif
+
+namespace tocr {
+namespace db {
+
+struct P2 {
+  int x, y;
+};
+struct F2 {
+  float x, y;
+};
+
+// ------------------------------------------------------------------ tracing --
+// Freeman chain codes, image coordinates (y down): 0 E, 1 NE, 2 N, 3 NW,
+// 4 W, 5 SW, 6 S, 7 SE. Increasing code = counter-clockwise on screen.
+TG int code_dx(int d) { return (d == 0 || d == 1 || d == 7) ? 1 : (d >= 3 && d <= 5) ? -1 : 0; }
+TG int code_dy(int d) { return (d >= 1 && d <= 3) ? -1 : (d >= 5) ? 1 : 0; }
+
+// Follows the border that starts at pixel (x0, y0): the raster-first pixel
+// of an 8-connected foreground component (outer border, previous pixel on
+// the W side) or the foreground pixel left of the raster-first pixel of a
+// hole (hole border, previous pixel on the E side). Points are emitted where
+// the chain code changes (CHAIN_APPROX_SIMPLE); the start pixel is always
+// emitted. fg(x, y) must return false outside the image. Writes at most cap
+// points and returns the full count, or -1 if max_steps was exceeded.
+template <class FG>
+TG int trace_border(const FG &fg, int x0, int y0, bool hole, P2 *out, int cap, int max_steps) {
+  const int dstart = hole ? 0 : 4;
+  int d1 = -1;
+  for (int k = 1; k <= 8; ++k) {  // clockwise from the previous pixel
+    const int d = (dstart - k) & 7;
+    if (fg(x0 + code_dx(d), y0 + code_dy(d))) {
+      d1 = d;
+      break;
+    }
+  }
+  int n = 0;
+  if (d1 < 0) {  // isolated pixel
+    if (cap > 0) out[0] = P2{x0, y0};
+    return 1;
+  }
+  const int x1 = x0 + code_dx(d1), y1 = y0 + code_dy(d1);
+  int last_code = d1 ^ 4;
+  int x3 = x0, y3 = y0, dback = d1;
+  for (int step = 0; step < max_steps; ++step) {
+    int d4 = dback;
+    for (int k = 1; k <= 8; ++k) {  // counter-clockwise after the previous pixel
+      const int d = (dback + k) & 7;
+      if (fg(x3 + code_dx(d), y3 + code_dy(d))) {
+        d4 = d;
+        break;
+      }
+    }
+    if (d4 != last_code) {
+      if (n < cap) out[n] = P2{x3, y3};
+      ++n;
+      last_code = d4;
+    }
+    const int x4 = x3 + code_dx(d4), y4 = y3 + code_dy(d4);
+    if (x4 == x0 && y4 == y0 && x3 == x1 && y3 == y1) return n;
+    dback = (d4 + 4) & 7;
+    x3 = x4;
+    y3 = y4;
+  }
+  return -1;
+}
+
+// --------------------------------------------------------------- sorting ----
+struct HP {  // hull candidate: point + index in the input sequence
+  int x, y, idx;
+};
+TG bool hp_less(const HP &a, const HP &b) {
+  return a.x < b.x || (a.x == b.x && (a.y < b.y || (a.y == b.y && a.idx < b.idx)));
+}
+TG void hp_sift(HP *a, int start, int end) {
+  int root = start;
+  while (2 * root + 1 <= end) {
+    int child = 2 * root + 1;
+    if (child + 1 <= end && hp_less(a[child], a[child + 1])) ++child;
+    if (hp_less(a[root], a[child])) {
+      HP t = a[root];
+      a[root] = a[child];
+      a[child] = t;
+      root = child;
+    } else {
+      return;
+    }
+  }
+}
+TG void hp_sort(HP *a, int n) {  // in-place heapsort (no recursion, no allocation)
+  for (int s = (n - 2) / 2; s >= 0; --s) hp_sift(a, s, n - 1);
+  for (int e = n - 1; e > 0; --e) {
+    HP t = a[0];
+    a[0] = a[e];
+    a[e] = t;
+    hp_sift(a, 0, e - 1);
+  }
+}
+
+// ------------------------------------------------------------------ hull -----
+TG long long cross3(const HP &o, const HP &a, const HP &b) {
+  return (long long)(a.x - o.x) * (b.y - o.y) - (long long)(a.y - o.y) * (b.x - o.x);
+}
+
+// Strict convex hull (no collinear or repeated points) of pts[0..n), in the
+// orientation and with the starting vertex of cv::convexHull(clockwise=false):
+// when the input indices of the hull vertices are cyclically increasing the
+// hull starts at the smallest index, when cyclically decreasing at the
+// largest, otherwise at the vertex with the largest (x, y). `work` needs
+// 2n+1 entries and is clobbered. Returns the hull size.
+TG int convex_hull(const P2 *pts, int n, HP *work, P2 *hull) {
+  if (n <= 0) return 0;
+  HP *s = work;            // sorted points [0, n)
+  HP *h = work + n;        // hull chain, up to n+1 entries
+  for (int i = 0; i < n; ++i) s[i] = HP{pts[i].x, pts[i].y, i};
+  hp_sort(s, n);
+  int k = 0;
+  for (int i = 0; i < n; ++i) {  // lower chain
+    while (k >= 2 && cross3(h[k - 2], h[k - 1], s[i]) <= 0) --k;
+    h[k++] = s[i];
+  }
+  for (int i = n - 2, t = k + 1; i >= 0; --i) {  // upper chain
+    while (k >= t && cross3(h[k - 2], h[k - 1], s[i]) <= 0) --k;
+    h[k++] = s[i];
+  }
+  int m = k > 1 ? k - 1 : k;  // last point repeats the first
+  if (m == 2 && h[0].x == h[1].x && h[0].y == h[1].y) m = 1;
+  // starting vertex
+  int start = 0;
+  if (m >= 3) {
+    int inc = 0;
+    for (int i = 0; i < m; ++i) inc += h[(i + 1) % m].idx > h[i].idx;
+    if (inc == m - 1 || inc == 1) {
+      const bool increasing = (inc == m - 1);
+      for (int i = 1; i < m; ++i)
+        if (increasing ? h[i].idx < h[start].idx : h[i].idx > h[start].idx) start = i;
+    } else {
+      for (int i = 1; i < m; ++i)
+        if (h[i].x > h[start].x || (h[i].x == h[start].x && h[i].y > h[start].y)) start = i;
+    }
+  } else {
+    for (int i = 1; i < m; ++i)
+      if (h[i].x > h[start].x || (h[i].x == h[start].x && h[i].y > h[start].y)) start = i;
+  }
+  for (int i = 0; i < m; ++i) {
+    const HP &q = h[(start + i) % m];
+    hull[i] = P2{q.x, q.y};
+  }
+  return m;
+}
+
+// ------------------------------------------------------------ min-area rect --
+struct RRect {
+  float cx, cy, w, h, angle;  // angle in degrees, as cv::RotatedRect
+};
+
+// The angle convention of the OpenCV used by the reference's CPU path: the
+// side vector is expressed with an angle in [-90, 0) degrees (computed in
+// double, one rounding to float), swapping width and height when the
+// perpendicular side is chosen.
+TG RRect normalize_rect(RRect r, double deg) {
+  for (int it = 0; it < 4 && deg >= 0; ++it) {
+    if (deg >= 90) {
+      deg -= 180;
+    } else {
+      deg -= 90;
+      const float t = r.w; r.w = r.h; r.h = t;
+    }
+  }
+  if (deg < -90) {
+    deg += 90;
+    const float t = r.w; r.w = r.h; r.h = t;
+  }
+  r.angle = (float)deg;
+  return r;
+}
+
+// cv::minAreaRect on a hull produced by convex_hull (rotating calipers in
+// float; edge lengths and orientation tests in double).
+TG RRect min_area_rect(const P2 *hull, int n, float *scratch /* 3n floats */,
+                       float *raw6 = nullptr) {
+  RRect r{0.f, 0.f, 0.f, 0.f, 0.f};
+  if (n <= 0) return r;
+  if (n == 1) {
+    r.cx = (float)hull[0].x;
+    r.cy = (float)hull[0].y;
+    return normalize_rect(r, 0.0);
+  }
+  if (n == 2) {
+    const float x0 = (float)hull[0].x, y0 = (float)hull[0].y;
+    const float x1 = (float)hull[1].x, y1 = (float)hull[1].y;
+    r.cx = (x0 + x1) * 0.5f;
+    r.cy = (y0 + y1) * 0.5f;
+    const double dx = (double)x1 - x0, dy = (double)y1 - y0;
+    r.w = (float)sqrt(dx * dx + dy * dy);
+    r.h = 0.f;
+    return normalize_rect(r, atan2(dy, dx) * 180 / 3.141592653589793238);
+  }
+  float *ilen = scratch;       // 1 / |edge|
+  float *vx = scratch + n;     // edge vectors
+  float *vy = scratch + 2 * n;
+  int left = 0, bottom = 0, right = 0, top = 0;
+  float left_x = (float)hull[0].x, right_x = left_x;
+  float top_y = (float)hull[0].y, bottom_y = top_y;
+  for (int i = 0; i < n; ++i) {
+    const float px = (float)hull[i].x, py = (float)hull[i].y;
+    if (px < left_x) { left_x = px; left = i; }
+    if (px > right_x) { right_x = px; right = i; }
+    if (py > top_y) { top_y = py; top = i; }
+    if (py < bottom_y) { bottom_y = py; bottom = i; }
+    const int j = (i + 1 < n) ? i + 1 : 0;
+    const double dx = (double)((float)hull[j].x - px);
+    const double dy = (double)((float)hull[j].y - py);
+    vx[i] = (float)dx;
+    vy[i] = (float)dy;
+    ilen[i] = (float)(1. / sqrt(dx * dx + dy * dy));
+  }
+  float orientation = 0.f;
+  {
+    double ax = vx[n - 1], ay = vy[n - 1];
+    for (int i = 0; i < n; ++i) {
+      const double bx = vx[i], by = vy[i];
+      const double c = ax * by - ay * bx;
+      if (c != 0) {
+        orientation = (c > 0) ? 1.f : -1.f;
+        break;
+      }
+      ax = bx;
+      ay = by;
+    }
+  }
+  float ba = orientation, bb = 0.f;  // current caliper direction (a, b)
+  int seq[4] = {bottom, right, top, left};
+  float minarea = 3.402823466e+38f;
+  int best_left = 0, best_bottom = 0;
+  float best_a = 0.f, best_b = 0.f, best_w = 0.f, best_h = 0.f;
+  for (int k = 0; k < n; ++k) {
+    float dp[4];
+    dp[0] = ba * vx[seq[0]] + bb * vy[seq[0]];
+    dp[1] = -bb * vx[seq[1]] + ba * vy[seq[1]];
+    dp[2] = -ba * vx[seq[2]] - bb * vy[seq[2]];
+    dp[3] = bb * vx[seq[3]] - ba * vy[seq[3]];
+    float maxcos = dp[0] * ilen[seq[0]];
+    int main = 0;
+    for (int i = 1; i < 4; ++i) {
+      const float c = dp[i] * ilen[seq[i]];
+      if (c > maxcos) {
+        main = i;
+        maxcos = c;
+      }
+    }
+    const int pi = seq[main];
+    const float lx = vx[pi] * ilen[pi], ly = vy[pi] * ilen[pi];
+    if (main == 0) { ba = lx; bb = ly; }
+    else if (main == 1) { ba = ly; bb = -lx; }
+    else if (main == 2) { ba = -lx; bb = -ly; }
+    else { ba = -ly; bb = lx; }
+    seq[main] = (seq[main] + 1 == n) ? 0 : seq[main] + 1;
+    float dx = (float)hull[seq[1]].x - (float)hull[seq[3]].x;
+    float dy = (float)hull[seq[1]].y - (float)hull[seq[3]].y;
+    const float width = dx * ba + dy * bb;
+    dx = (float)hull[seq[2]].x - (float)hull[seq[0]].x;
+    dy = (float)hull[seq[2]].y - (float)hull[seq[0]].y;
+    const float height = -dx * bb + dy * ba;
+    const float area = width * height;
+    if (area <= minarea) {
+      minarea = area;
+      best_left = seq[3];
+      best_a = ba;
+      best_w = width;
+      best_b = bb;
+      best_h = height;
+      best_bottom = seq[0];
+    }
+  }
+  const float A1 = best_a, B1 = best_b, A2 = -best_b, B2 = best_a;
+  const float C1 = A1 * (float)hull[best_left].x + (float)hull[best_left].y * B1;
+  const float C2 = A2 * (float)hull[best_bottom].x + (float)hull[best_bottom].y * B2;
+  const float idet = 1.f / (A1 * B2 - A2 * B1);
+  const float px = (C1 * B2 - C2 * B1) * idet;
+  const float py = (A1 * C2 - A2 * C1) * idet;
+  const float o1x = A1 * best_w, o1y = B1 * best_w;
+  const float o2x = A2 * best_h, o2y = B2 * best_h;
+  if (raw6) {
+    raw6[0] = px; raw6[1] = py; raw6[2] = o1x; raw6[3] = o1y; raw6[4] = o2x; raw6[5] = o2y;
+  }
+  r.cx = px + (o1x + o2x) * 0.5f;
+  r.cy = py + (o1y + o2y) * 0.5f;
+  r.w = (float)sqrt((double)o1x * o1x + (double)o1y * o1y);
+  r.h = (float)sqrt((double)o2x * o2x + (double)o2y * o2y);
+  return normalize_rect(r, atan2((double)o1y, (double)o1x) * 180 / 3.141592653589793238);
+}
+
+// cv::RotatedRect::points corner order.
+TG void rect_points(const RRect &r, float xs[4], float ys[4]) {
+  const double ang = r.angle * 3.141592653589793238 / 180.;
+  const float b = (float)cos(ang) * 0.5f;
+  const float a = (float)sin(ang) * 0.5f;
+  xs[0] = r.cx - a * r.h - b * r.w;
+  ys[0] = r.cy + b * r.h - a * r.w;
+  xs[1] = r.cx + a * r.h - b * r.w;
+  ys[1] = r.cy - b * r.h - a * r.w;
+  xs[2] = 2 * r.cx - xs[0];
+  ys[2] = 2 * r.cy - ys[0];
+  xs[3] = 2 * r.cx - xs[1];
+  ys[3] = 2 * r.cy - ys[1];
+}
+
+// order_quad_tl_tr_br_bl (det_postprocess.cpp:104-126): stable insertion sort
+// by x, then the left pair splits into tl/bl and the right pair into tr/br by y.
+TG void order_quad(float xs[4], float ys[4]) {
+  for (int i = 1; i < 4; ++i) {
+    const float kx = xs[i], ky = ys[i];
+    int j = i - 1;
+    while (j >= 0 && xs[j] > kx) {
+      xs[j + 1] = xs[j];
+      ys[j + 1] = ys[j];
+      --j;
+    }
+    xs[j + 1] = kx;
+    ys[j + 1] = ky;
+  }
+  const int tl = (ys[0] < ys[1]) ? 0 : 1, bl = 1 - tl;
+  const int tr = (ys[2] < ys[3]) ? 2 : 3, br = 5 - tr;
+  const float ox[4] = {xs[tl], xs[tr], xs[br], xs[bl]};
+  const float oy[4] = {ys[tl], ys[tr], ys[br], ys[bl]};
+  for (int k = 0; k < 4; ++k) {
+    xs[k] = ox[k];
+    ys[k] = oy[k];
+  }
+}
+
+// std::round on float: half away from zero.
+TG int round_half_away(float v) { return (int)roundf(v); }
+
+// get_mini_boxes (det_postprocess.cpp:128-143): ordered, rounded corners.
+TG void mini_box(const RRect &r, int box[8]) {
+  float xs[4], ys[4];
+  rect_points(r, xs, ys);
+  order_quad(xs, ys);
+  for (int k = 0; k < 4; ++k) {
+    box[2 * k] = round_half_away(xs[k]);
+    box[2 * k + 1] = round_half_away(ys[k]);
+  }
+}
+
+// ------------------------------------------------------------ polygon mask --
+// The pixels cv::fillPoly(LINE_8) sets for a closed contour whose edges are
+// horizontal, vertical or diagonal (every CHAIN_APPROX_SIMPLE contour): the
+// edge pixels plus the pixels strictly inside by the even-odd rule. For row
+// y, calls span(x0, x1) (inclusive, unordered, possibly overlapping) for
+// every inside run and every edge run. `xs` is scratch for up to n crossings.
+template <class SPAN>
+TG void poly_row_spans(const P2 *p, int n, int y, int *xs, const SPAN &span) {
+  int nc = 0;
+  for (int i = 0; i < n; ++i) {
+    const P2 a = p[i], b = p[(i + 1 < n) ? i + 1 : 0];
+    // edge pixels on this row
+    if (a.y == b.y) {
+      if (a.y == y) span(a.x < b.x ? a.x : b.x, a.x < b.x ? b.x : a.x);
+      continue;
+    }
+    const int ylo = a.y < b.y ? a.y : b.y, yhi = a.y < b.y ? b.y : a.y;
+    if (y < ylo || y > yhi) continue;
+    // lattice point of the (vertical or diagonal) edge on row y
+    const int dx = b.x - a.x, dy = b.y - a.y;
+    const int x = a.x + (y - a.y) * (dx == 0 ? 0 : (dx > 0 ? 1 : -1)) * (dy > 0 ? 1 : -1);
+    span(x, x);
+    if (y < yhi) xs[nc++] = x;  // half-open crossing rule [ylo, yhi)
+  }
+  for (int i = 1; i < nc; ++i) {  // crossings in increasing x
+    const int v = xs[i];
+    int j = i - 1;
+    while (j >= 0 && xs[j] > v) {
+      xs[j + 1] = xs[j];
+      --j;
+    }
+    xs[j + 1] = v;
+  }
+  for (int i = 0; i + 1 < nc; i += 2) span(xs[i], xs[i + 1]);
+}
+
+// ------------------------------------------------- area / arc length -----------
+// cv::contourArea (unoriented) of an int polygon: exact in double.
+TG double contour_area(const P2 *p, int n) {
+  if (n < 3) return 0.;
+  double a = 0.;
+  P2 prev = p[n - 1];
+  for (int i = 0; i < n; ++i) {
+    a += (double)prev.x * p[i].y - (double)prev.y * p[i].x;
+    prev = p[i];
+  }
+  a *= 0.5;
+  return a < 0 ? -a : a;
+}
+
+// cv::arcLength(closed) of an int polygon: float segment lengths summed in double.
+TG double arc_length(const P2 *p, int n) {
+  if (n <= 1) return 0.;
+  double per = 0.;
+  float px = (float)p[n - 1].x, py = (float)p[n - 1].y;
+  for (int i = 0; i < n; ++i) {
+    const float x = (float)p[i].x, y = (float)p[i].y;
+    const float dx = x - px, dy = y - py;
+    per += sqrtf(dx * dx + dy * dy);
+    px = x;
+    py = y;
+  }
+  return per;
+}
+
+// ------------------------------------------------------------- offsetting ----
+// Clipper's Round(): half away from zero on a double, to int64.
+TG long long clip_round(double v) { return v < 0 ? (long long)(v - 0.5) : (long long)(v + 0.5); }
+
+struct DP {
+  double x, y;
+};
+
+// Unit normal of the edge p1 -> p2 (Clipper GetUnitNormal), FMA-contracted.
+TG DP unit_normal(P2 p1, P2 p2) {
+  if (p1.x == p2.x && p1.y == p2.y) return DP{0., 0.};
+  double dx = (double)(p2.x - p1.x);
+  double dy = (double)(p2.y - p1.y);
+  const double f = 1 * 1.0 / sqrt(fma(dx, dx, dy * dy));
+  dx *= f;
+  dy *= f;
+  return DP{dy, -dx};
+}
+
+// Prepares the offset path like ClipperOffset::AddPath + FixOrientations:
+// drops trailing copies of the first point and consecutive duplicates, then
+// reverses to positive orientation (Clipper's Area >= 0). Writes to q and
+// returns its length (0 when fewer than 3 distinct points remain).
+TG int offset_prepare(const P2 *p, int n, P2 *q) {
+  if (n <= 0) return 0;
+  int hi = n - 1;
+  while (hi > 0 && p[0].x == p[hi].x && p[0].y == p[hi].y) --hi;
+  int m = 0;
+  q[m++] = p[0];
+  for (int i = 1; i <= hi; ++i)
+    if (q[m - 1].x != p[i].x || q[m - 1].y != p[i].y) q[m++] = p[i];
+  if (m < 3) return 0;
+  double a = 0.;
+  for (int i = 0, j = m - 1; i < m; ++i) {
+    a = fma((double)q[j].x + q[i].x, (double)q[j].y - q[i].y, a);
+    j = i;
+  }
+  if (!(-a * 0.5 >= 0)) {
+    for (int i = 0, j = m - 1; i < j; ++i, --j) {
+      const P2 t = q[i];
+      q[i] = q[j];
+      q[j] = t;
+    }
+  }
+  return m;
+}
+
+// Raw round-join offset of the prepared closed path q[0..m) by delta > 0
+// (ClipperOffset::DoOffset + OffsetPoint + DoRound, before the union).
+// Writes at most cap points to out and returns the full count.
+TG int offset_raw(const P2 *q, int m, double delta, P2 *out, int cap) {
+  int n = 0;
+  auto emit = [&](long long x, long long y) {
+    if (n < cap) out[n] = P2{(int)x, (int)y};
+    ++n;
+  };
+  if (delta > -1.0E-20 && delta < 1.0E-20) {
+    for (int i = 0; i < m; ++i) emit(q[i].x, q[i].y);
+    return n;
+  }
+  const double ad = delta < 0 ? -delta : delta;
+  const double y = (0.25 > ad * 0.25) ? ad * 0.25 : 0.25;
+  const double pi = 3.141592653589793238, two_pi = pi * 2;
+  double steps = pi / acos(1 - y / ad);
+  if (steps > ad * pi) steps = ad * pi;
+  double m_sin = sin(two_pi / steps);
+  const double m_cos = cos(two_pi / steps);
+  const double steps_per_rad = steps / two_pi;
+  if (delta < 0.0) m_sin = -m_sin;
+  int k = m - 1;
+  for (int j = 0; j < m; ++j) {
+    const DP nk = unit_normal(q[k], q[(k + 1) % m]);
+    const DP nj = unit_normal(q[j], q[(j + 1) % m]);
+    double sinA = fma(nk.x, nj.y, -(nj.x * nk.y));
+    if (fabs(sinA * delta) < 1.0) {
+      const double cosA = fma(nk.x, nj.x, nj.y * nk.y);
+      if (cosA > 0) {
+        emit(clip_round(fma(nk.x, delta, (double)q[j].x)), clip_round(fma(nk.y, delta, (double)q[j].y)));
+        continue;
+      }
+    } else if (sinA > 1.0) {
+      sinA = 1.0;
+    } else if (sinA < -1.0) {
+      sinA = -1.0;
+    }
+    if (sinA * delta < 0) {
+      emit(clip_round(fma(nk.x, delta, (double)q[j].x)), clip_round(fma(nk.y, delta, (double)q[j].y)));
+      emit(q[j].x, q[j].y);
+      emit(clip_round(fma(nj.x, delta, (double)q[j].x)), clip_round(fma(nj.y, delta, (double)q[j].y)));
+    } else {
+      const double a = atan2(sinA, fma(nk.x, nj.x, nk.y * nj.y));
+      long long st = clip_round(steps_per_rad * fabs(a));
+      const int steps_i = st > 1 ? (int)st : 1;
+      double X = nk.x, Y = nk.y;
+      for (int i = 0; i < steps_i; ++i) {
+        emit(clip_round(fma(X, delta, (double)q[j].x)), clip_round(fma(Y, delta, (double)q[j].y)));
+        const double X2 = X;
+        X = fma(X, m_cos, -(m_sin * Y));
+        Y = fma(X2, m_sin, Y * m_cos);
+      }
+      emit(clip_round(fma(nj.x, delta, (double)q[j].x)), clip_round(fma(nj.y, delta, (double)q[j].y)));
+    }
+    k = j;
+  }
+  return n;
+}
+
+// Winding number (crossing rule) of the point (x, y) w.r.t. the closed path r[0..n).
+TG int winding_number(const P2 *r, int n, double x, double y) {
+  int wn = 0;
+  for (int i = 0; i < n; ++i) {
+    const double x1 = r[i].x, y1 = r[i].y;
+    const int j = (i + 1 < n) ? i + 1 : 0;
+    const double x2 = r[j].x, y2 = r[j].y;
+    const double c = (x2 - x1) * (y - y1) - (x - x1) * (y2 - y1);
+    if (y1 <= y) {
+      if (y2 > y && c > 0) ++wn;
+    } else {
+      if (y2 <= y && c < 0) --wn;
+    }
+  }
+  return wn;
+}
+
+// True when some point arbitrarily close to (x, y) has positive winding,
+// i.e. (x, y) lies in the closure of the union's positive-fill region.
+TG bool in_positive_closure(const P2 *r, int n, int x, int y) {
+  const double off[8][2] = {{0.3125, 0.0625}, {-0.3125, -0.0625}, {0.0625, -0.3125},
+                            {-0.0625, 0.3125}, {0.1875, 0.1875}, {-0.1875, -0.1875},
+                            {0.1875, -0.1875}, {-0.1875, 0.1875}};
+  for (int k = 0; k < 8; ++k)
+    if (winding_number(r, n, x + off[k][0], y + off[k][1]) > 0) return true;
+  return false;
+}
+
+// Exact intersection of segments ab and cd rounded half away from zero.
+TG bool seg_intersect_round(P2 a, P2 b, P2 c, P2 d, P2 &out) {
+  const long long x1 = a.x, y1 = a.y, x2 = b.x, y2 = b.y;
+  const long long x3 = c.x, y3 = c.y, x4 = d.x, y4 = d.y;
+  long long den = (x1 - x2) * (y3 - y4) - (y1 - y2) * (x3 - x4);
+  if (den == 0) return false;
+  long long tn = (x1 - x3) * (y3 - y4) - (y1 - y3) * (x3 - x4);
+  long long un = (x1 - x3) * (y1 - y2) - (y1 - y3) * (x1 - x2);
+  if (den < 0) { den = -den; tn = -tn; un = -un; }
+  if (tn < 0 || tn > den || un < 0 || un > den) return false;
+  // x = x1 + tn (x2 - x1) / den, rounded half away from zero
+  auto rdiv = [](long long num, long long dd) -> long long {  // dd > 0
+    const long long q = num >= 0 ? (2 * num + dd) / (2 * dd) : -((-2 * num + dd) / (2 * dd));
+    return q;
+  };
+  const long long nx = x1 * den + tn * (x2 - x1);
+  const long long ny = y1 * den + tn * (y2 - y1);
+  out = P2{(int)rdiv(nx, den), (int)rdiv(ny, den)};
+  return true;
+}
+
+}  // namespace db
+}  // namespace tocr

@@ -139,4 +139,38 @@ TOCR_API int tocr_synth_ctc_logits(void *d_logits, int *d_plan, int B, int T, in
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 
+// Config-1 DB probability maps (host): background U[0, 0.1]; k ~ U{kmin..kmax}
+// rotated rectangles (width U[20,400], height U[8,60], angle U[-15,15] deg,
+// centre uniform in the map) filled with U[0.6, 1.0]; a pixel belongs to a
+// rectangle when its centre (x+0.5, y+0.5) lies inside (double arithmetic);
+// later rectangles overwrite earlier ones. Returns the rectangle count.
+TOCR_API int tocr_synth_db_map_host(float *out, int H, int W, int kmin, int kmax, uint64_t seed,
+                                    uint64_t map_index) {
+  const uint64_t st = 3000 + map_index;
+  uint64_t ctr = 0;
+  for (long long i = 0; i < (long long)H * W; ++i)
+    out[i] = 0.1f * unif(hash3(seed, st + (1ull << 40), (uint64_t)i));
+  const int k = unif_int(hash3(seed, st, ctr++), kmin, kmax);
+  for (int r = 0; r < k; ++r) {
+    const double w = 20.0 + 380.0 * unif(hash3(seed, st, ctr++));
+    const double h = 8.0 + 52.0 * unif(hash3(seed, st, ctr++));
+    const double th = (-15.0 + 30.0 * unif(hash3(seed, st, ctr++))) * 3.141592653589793 / 180.0;
+    const double cx = W * (double)unif(hash3(seed, st, ctr++));
+    const double cy = H * (double)unif(hash3(seed, st, ctr++));
+    const double c = cos(th), s = sin(th);
+    const double ex = 0.5 * (fabs(w * c) + fabs(h * s)), ey = 0.5 * (fabs(w * s) + fabs(h * c));
+    const int x0 = (int)fmax(0.0, floor(cx - ex - 1)), x1 = (int)fmin(W - 1.0, ceil(cx + ex + 1));
+    const int y0 = (int)fmax(0.0, floor(cy - ey - 1)), y1 = (int)fmin(H - 1.0, ceil(cy + ey + 1));
+    const uint64_t fill_stream = st + (2ull << 40) + (uint64_t)r;
+    for (int y = y0; y <= y1; ++y)
+      for (int x = x0; x <= x1; ++x) {
+        const double dx = x + 0.5 - cx, dy = y + 0.5 - cy;
+        const double u = dx * c + dy * s, v = -dx * s + dy * c;
+        if (fabs(u) <= 0.5 * w && fabs(v) <= 0.5 * h)
+          out[(long long)y * W + x] = 0.6f + 0.4f * unif(hash3(seed, fill_stream, (uint64_t)(y * W + x)));
+      }
+  }
+  return k;
+}
+
 }  // extern "C"
