@@ -77,6 +77,19 @@ TOCR_API int tocr_ctc_greedy_f16(const void *d_logits, int batch_size,
                                  float *d_line_scores, int *d_step_idx,
                                  float *d_step_prob, void *stream);
 
+/* Allocation-free variant of tocr_ctc_greedy_f16 (no counterpart in the
+ * reference): same kernels and results, but the per-step scratch lives in a
+ * static device array of 2^20 steps (8 MiB), so batch_size * seq_len must
+ * not exceed 1048576 (TOCR_ERR_INVALID otherwise). Nothing is allocated.
+ * The first call on each device looks up the array's address
+ * (cudaGetSymbolAddress) and may load the module: make it before any stream
+ * capture. Calls that overlap on one device share the scratch and race:
+ * serialise them (one stream, or events). */
+TOCR_API int tocr_ctc_greedy_f16_noalloc(const void *d_logits, int batch_size,
+                                         int seq_len, int num_classes, int num_labels,
+                                         int *d_tokens, int *d_lengths,
+                                         float *d_line_scores, void *stream);
+
 /* ---- subsystem 1: batched det preprocessing ----------------------------- */
 
 /* Replaces turbo_ocr::kernels::cuda_batch_fused_resize_normalize_det

@@ -55,6 +55,7 @@ SIGNATURES: dict[str, tuple] = {
     "tocr_debug_inject_error": (None, [_i, _i]),
     "tocr_argmax_f32": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
     "tocr_ctc_greedy_f16": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "tocr_ctc_greedy_f16_noalloc": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "tocr_preprocess_batch_f16": (_i, [_vp] * 7 + [_i, _i, _i, _vp, _vp, _vp]),
     "tocr_preprocess_batch_f32": (_i, [_vp] * 7 + [_i, _i, _i, _vp, _vp, _vp]),
     "tocr_threshold_u8": (_i, [_vp, _vp, _i, _i, _i, _f, _vp]),

@@ -16,6 +16,7 @@
 #include "tocr_common.cuh"
 
 #include <cmath>
+#include <mutex>
 
 namespace tocr {
 namespace {
@@ -320,3 +321,86 @@ TOCR_API int tocr_ctc_greedy_f16(const void *d_logits, int batch_size, int seq_l
 }
 
 }  // extern "C"
+
+// ---- allocation-free variant -------------------------------------------------
+// tocr_ctc_greedy_f16_noalloc keeps the per-step scratch (argmax index and
+// max probability of every row) in module-scope device arrays instead of
+// caller buffers. Both arrays are fully written by ctc_rows_f16_kernel before
+// ctc_collapse_kernel reads them, so nothing has to be cleared between calls.
+namespace {
+
+constexpr long long kNoAllocMaxSteps = 1ll << 20;  // 4 MiB of indices + 4 MiB of probabilities
+constexpr int kNoAllocMaxDevices = 64;
+
+__device__ __align__(256) int g_noalloc_step_idx[kNoAllocMaxSteps];
+__device__ __align__(256) float g_noalloc_step_prob[kNoAllocMaxSteps];
+
+struct NoAllocScratch {
+  int *idx = nullptr;
+  float *prob = nullptr;
+};
+
+std::mutex g_noalloc_mu;
+NoAllocScratch g_noalloc[kNoAllocMaxDevices];
+
+// Device addresses of the scratch arrays on the current device, looked up
+// once per device (the first lookup may load the module).
+int noalloc_scratch(NoAllocScratch *out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(TOCR_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  TOCR_REQUIRE(dev >= 0 && dev < kNoAllocMaxDevices, "no-alloc CTC: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  NoAllocScratch &s = g_noalloc[dev];
+  if (!s.idx) {
+    void *pi = nullptr, *pp = nullptr;
+    e = cudaGetSymbolAddress(&pi, g_noalloc_step_idx);
+    if (e != cudaSuccess)
+      return set_error(TOCR_ERR_CUDA, "cudaGetSymbolAddress(step_idx): %s", cudaGetErrorString(e));
+    e = cudaGetSymbolAddress(&pp, g_noalloc_step_prob);
+    if (e != cudaSuccess)
+      return set_error(TOCR_ERR_CUDA, "cudaGetSymbolAddress(step_prob): %s", cudaGetErrorString(e));
+    s.idx = static_cast<int *>(pi);
+    s.prob = static_cast<float *>(pp);
+  }
+  *out = s;
+  return TOCR_OK;
+}
+
+}  // namespace
+
+extern "C" TOCR_API int tocr_ctc_greedy_f16_noalloc(const void *d_logits, int batch_size,
+                                                    int seq_len, int num_classes,
+                                                    int num_labels, int *d_tokens,
+                                                    int *d_lengths, float *d_line_scores,
+                                                    void *stream) {
+  TOCR_ENTRY();
+  TOCR_REQUIRE(batch_size >= 0 && seq_len >= 0 && num_classes > 0,
+               "tocr_ctc_greedy_f16_noalloc: bad sizes batch=%d seq_len=%d classes=%d",
+               batch_size, seq_len, num_classes);
+  const long long rows = (long long)batch_size * seq_len;
+  TOCR_REQUIRE(rows <= kNoAllocMaxSteps,
+               "tocr_ctc_greedy_f16_noalloc: batch*seq_len = %lld exceeds the static scratch of "
+               "%lld steps; use tocr_ctc_greedy_f16 with caller buffers",
+               rows, kNoAllocMaxSteps);
+  if (batch_size == 0) return TOCR_OK;
+  TOCR_REQUIRE(d_lengths && d_line_scores && (d_tokens || seq_len == 0),
+               "tocr_ctc_greedy_f16_noalloc: null output pointer");
+  NoAllocScratch scr;
+  int st = noalloc_scratch(&scr);
+  if (st != TOCR_OK) return st;
+  if (seq_len > 0) {
+    TOCR_REQUIRE(d_logits, "tocr_ctc_greedy_f16_noalloc: null logits pointer");
+    TOCR_REQUIRE(aligned(d_logits, 2),
+                 "tocr_ctc_greedy_f16_noalloc: logits must be 2-byte aligned");
+    ctc_rows_f16_kernel<<<rows_grid(ctc_rows_f16_kernel, rows), kRowsThreads, 0,
+                          as_stream(stream)>>>(reinterpret_cast<const __half *>(d_logits), rows,
+                                               num_classes, scr.idx, scr.prob);
+    st = check_launch("ctc_rows_f16_kernel");
+    if (st != TOCR_OK) return st;
+  }
+  const int blocks = (batch_size + kCollapseWarps - 1) / kCollapseWarps;
+  ctc_collapse_kernel<<<blocks, kCollapseWarps * 32, 0, as_stream(stream)>>>(
+      scr.idx, scr.prob, batch_size, seq_len, num_labels, d_tokens, d_lengths, d_line_scores);
+  return check_launch("ctc_collapse_kernel");
+}
