@@ -106,6 +106,10 @@ class ClockSampler:
 class CtcWorkload:
     """fused CTC greedy decode of fp16 logits."""
     name = "ctc_greedy_512x80x18385_fp16"
+    # DRAM read+write bytes per line of ctc_rows_f16_kernel, from the ncu capture
+    # summarised in profiles/ctc_rows_f16_512x80x18385.md (64-line case, scaled)
+    traffic_per_unit = (188_710_912 + 3_741_184) / 64
+    traffic_source = "profiles/ctc_rows_f16_512x80x18385.md"
     metric = "lines/sec CTC greedy decode (512x80x18385 fp16 logits)"
     unit = "lines/s"
     dtype = "f16"
@@ -184,6 +188,10 @@ class CtcWorkload:
 class PreprocessWorkload:
     """batched resize/letterbox/normalise to fp16 NCHW."""
     name = "preprocess_256img_600-2000_to_960x960_f16"
+    # DRAM bytes per image of preprocess_batch_kernel (32-image ncu capture, scaled;
+    # part of the output is still in L2 when that short launch ends)
+    traffic_per_unit = (160_950_016 + 131_166_976) / 32
+    traffic_source = "profiles/preprocess_256img_960_f16.md"
     metric = "images/sec batched det preprocessing (256 u8 images -> fp16 960x960 NCHW)"
     unit = "images/s"
     dtype = "f32"
@@ -283,6 +291,10 @@ class PreprocessWorkload:
 class DwPwWorkload:
     """fused DW3x3 + PW1x1 block, INT8 PW weights on tcgen05."""
     name = "dwpw_block_32x128x240x240_to_256_int8"
+    # DRAM bytes per image of dwpw_kernel (8-image ncu capture, scaled; part of
+    # the output is still in L2 when that short launch ends)
+    traffic_per_unit = (118_064_128 + 177_737_728) / 8
+    traffic_source = "profiles/dwpw_int8_32x240x240_128to256.md"
     metric = "images/sec fused dw3x3+pw1x1 block (32x128x240x240 fp16 -> 256ch, INT8 PW)"
     unit = "images/s"
     dtype = "i8 (PW on tcgen05 kind::i8, DW fp16x2)"
@@ -496,7 +508,9 @@ def main():
             "e2e": {"value": wl.units_per_step * world / (ms_e2e / 1e3), "unit": Wl.unit,
                     "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None,
+                         "frac": achieved / peak,
+                         "traffic": getattr(Wl, "traffic_per_unit", 0) * wl.units_per_step or None,
+                         "traffic_source": getattr(Wl, "traffic_source", None),
                          "peak_source": f"{peak_kind} hbm_gbs",
                          "algorithmic_bytes_per_launch": wl.algo_bytes},
             "clocks": clk,
