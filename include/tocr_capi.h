@@ -126,6 +126,45 @@ TOCR_API int tocr_threshold_u8(const float *d_src, uint8_t *d_dst, int w,
                                int h, int batch_size, float thresh,
                                void *stream);
 
+/* ---- subsystem 3: DB post-processing -------------------------------------- */
+
+/* Device replacement of the CPU path extract_boxes_from_bitmap
+ * (src/detection/det_postprocess.cpp:145-222, include/turbo_ocr/detection/
+ * det_postprocess.h:33-41) fused with its threshold (cv::compare GT,
+ * src/detection/cpu_paddle_det.cpp:115), for n_maps fp32 probability maps
+ * [n_maps][h][w]. Per map: contours in cv::findContours(RETR_LIST,
+ * CHAIN_APPROX_SIMPLE) order capped at 3000; filters and geometry as the
+ * reference (min_box_side / min_unclipped_side are kMinBoxSide = 3 and
+ * kMinUnclippedSide = 5 there, paddle_det.h:62-63). Writes the kept quads
+ * (int [n_maps][max_boxes][4][2], tl tr br bl), their box_score_fast values
+ * ([n_maps][max_boxes]) and counts ([n_maps]) in contour order.
+ * d_geometry: NULL (identity) or int [n_maps][4] = orig_h, orig_w, resize_h,
+ * resize_w for the scaling of det_postprocess.cpp:205-210.
+ * point_cap / offset_cap bound the traced points and the offset-path points
+ * of a call (<= 0: defaults); the workspace (256-byte aligned) must hold
+ * tocr_db_workspace_bytes(n_maps, h, w, point_cap, offset_cap) bytes.
+ * d_status (device int) receives 0 or a bit set: 1 point pool full, 2 a
+ * border walk exceeded its bound, 4 offset pool full, 8 more than max_boxes
+ * kept (truncated). Enqueued on `stream`; no synchronisation, no allocation. */
+TOCR_API size_t tocr_db_workspace_bytes(int n_maps, int h, int w, long long point_cap,
+                                        long long offset_cap);
+TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
+                                 const int *d_geometry, float thresh, float box_thresh,
+                                 float unclip_ratio, float min_box_side,
+                                 float min_unclipped_side, long long point_cap,
+                                 long long offset_cap, void *d_workspace,
+                                 size_t workspace_bytes, int *d_boxes, float *d_scores,
+                                 int *d_counts, int max_boxes, int *d_status, void *stream);
+
+/* Connected components of the thresholded maps (the labelling stage of
+ * tocr_db_postprocess; the reference's GPU labelling is cuda_gpu_ccl_detect,
+ * src/kernels/ccl_kernels.cu:387-493). labels [n_maps][h][w]: 0 for
+ * background joined to the image frame, otherwise 1 + the raster index of the
+ * smallest pixel of the component (foreground 8-connected, background
+ * 4-connected). d_bitmap [n_maps][h][w] receives the 0/255 bitmap. */
+TOCR_API int tocr_db_components(const float *d_pred, int n_maps, int h, int w, float thresh,
+                                int *d_labels, uint8_t *d_bitmap, void *stream);
+
 /* ---- subsystem 2: fused depthwise-3x3 + pointwise-1x1 block ------------- */
 
 /* Replaces one DW-separable block of the det backbone that the reference runs

@@ -120,8 +120,10 @@ def find_contours(bitmap: np.ndarray):
 def extract_boxes_from_bitmap(pred: np.ndarray, bitmap: np.ndarray, orig_h: int, orig_w: int,
                               resize_h: int, resize_w: int, box_thresh: float,
                               unclip_ratio: float, min_box_side: float = 3.0,
-                              min_unclipped_side: float = 5.0):
-    """-> list of (box [[x,y]*4], score) in the reference's contour order."""
+                              min_unclipped_side: float = 5.0, unclip_fn=None):
+    """-> list of (box [[x,y]*4], score) in the reference's contour order.
+    unclip_fn(contour, ratio) replaces unclip() when given (tests use it to
+    isolate the union step of Clipper's offset)."""
     import cv2
     ratio_h = np.float32(resize_h) / np.float32(orig_h)
     ratio_w = np.float32(resize_w) / np.float32(orig_w)
@@ -139,7 +141,7 @@ def extract_boxes_from_bitmap(pred: np.ndarray, bitmap: np.ndarray, orig_h: int,
         score = box_score_fast(pred, contour)
         if np.float32(score) < np.float32(box_thresh):
             continue
-        unclipped = unclip(contour, unclip_ratio)
+        unclipped = (unclip_fn or unclip)(contour, unclip_ratio)
         if len(unclipped) < 3:
             continue
         box, ssid2 = get_mini_boxes(unclipped)
@@ -163,8 +165,20 @@ def threshold(pred: np.ndarray, thresh: float) -> np.ndarray:
     return np.where(pred > np.float32(thresh), 255, 0).astype(np.uint8)
 
 
-def db_postprocess(pred: np.ndarray, thresh=0.3, box_thresh=0.6, unclip_ratio=1.5):
+def db_postprocess(pred: np.ndarray, thresh=0.3, box_thresh=0.6, unclip_ratio=1.5,
+                   unclip_fn=None):
     """Config-1 post-process of one map (orig == resize dims)."""
     h, w = pred.shape
     return extract_boxes_from_bitmap(pred, threshold(pred, thresh), h, w, h, w, box_thresh,
-                                     unclip_ratio)
+                                     unclip_ratio, unclip_fn=unclip_fn)
+
+
+def unclip_distance(polygon: np.ndarray, unclip_ratio: float):
+    """Offset distance of unclip (det_postprocess.cpp:59-66), None if the
+    perimeter is 0."""
+    import cv2
+    poly = polygon.reshape(-1, 1, 2).astype(np.int32)
+    perimeter = cv2.arcLength(poly, True)
+    if perimeter == 0.0:
+        return None
+    return cv2.contourArea(poly) * float(np.float32(unclip_ratio)) / perimeter

@@ -35,6 +35,7 @@ def lib():
     L.dbh_arclen.restype = d
     L.dbh_offset_raw.argtypes = [vp, i, d, vp, i]
     L.dbh_poly_mask.argtypes = [vp, i, i, i, i, i, vp]
+    L.dbh_poly_mask_parity.argtypes = [vp, i, i, i, i, i, vp]
     _lib = L
     return L
 
@@ -93,8 +94,9 @@ def offset_raw(p, delta):
     return [tuple(q) for q in out[:n].tolist()]
 
 
-def poly_mask(p, x0, y0, w, h):
+def poly_mask(p, x0, y0, w, h, parity=False):
     p = _pts(p)
     m = np.zeros((h, w), np.uint8)
-    lib().dbh_poly_mask(p.ctypes.data, len(p), x0, y0, w, h, m.ctypes.data)
+    fn = lib().dbh_poly_mask_parity if parity else lib().dbh_poly_mask
+    fn(p.ctypes.data, len(p), x0, y0, w, h, m.ctypes.data)
     return m

@@ -62,6 +62,28 @@ void dbh_poly_mask(const int *pts, int n, int x0, int y0, int w, int h, unsigned
     });
 }
 
+// Same mask through poly_row_marks: edge runs | odd crossing parity.
+void dbh_poly_mask_parity(const int *pts, int n, int x0, int y0, int w, int h, unsigned char *mask) {
+  memset(mask, 0, (size_t)w * h);
+  std::vector<unsigned char> tog(w + 1);
+  for (int y = y0; y < y0 + h; ++y) {
+    std::fill(tog.begin(), tog.end(), 0);
+    unsigned char *row = mask + (size_t)(y - y0) * w;
+    poly_row_marks(reinterpret_cast<const P2 *>(pts), n, y, 0, n,
+        [&](int a, int b) {
+          if (a > b) { int t = a; a = b; b = t; }
+          for (int x = a; x <= b; ++x)
+            if (x >= x0 && x < x0 + w) row[x - x0] = 1;
+        },
+        [&](int x) { if (x >= x0 && x < x0 + w) tog[x - x0] ^= 1; });
+    int par = 0;
+    for (int x = 0; x < w; ++x) {
+      par ^= tog[x];
+      if (par) row[x] = 1;
+    }
+  }
+}
+
 double dbh_area(const int *pts, int n) { return contour_area(reinterpret_cast<const P2 *>(pts), n); }
 double dbh_arclen(const int *pts, int n) { return arc_length(reinterpret_cast<const P2 *>(pts), n); }
 

@@ -5,12 +5,12 @@ src/detection/det_postprocess.cpp) and the reference's vendored Clipper.
 
 Bit-exact bars: contour starts, border following, the contour order, area,
 arc length, polygon mask and the raw Clipper offset. minAreaRect is
-bit-exact except at near ties: where two caliper positions give the same
-area, or two hull edges make the same angle with the caliper to float
-precision, OpenCV 4.13 sometimes takes the other one (20 of 30052 noise
-contours, 3 of 2912 contours overall); the test bounds that rate, checks
-the areas agree and that the rounded mini boxes of text-line contours are
-identical."""
+bit-exact as well: OpenCV 4.13 advances the caliper with the exact smallest
+angle (not the rounded float cosine), which the restatement reproduces in
+integer arithmetic. The one residue is a tie between two different
+rectangles of exactly the same area on contours that repeat points: which
+one wins depends on the hull's starting vertex, which OpenCV takes from an
+unstable sort (about 1 in 10^4 noise contours, none on text-line contours)."""
 import ctypes as C
 
 import numpy as np
@@ -98,6 +98,7 @@ def test_area_arclen_mask_exact():
             ref = np.zeros((h, w), np.uint8)
             cv2.fillPoly(ref, [(c - [x, y]).reshape(-1, 1, 2).astype(np.int32)], 1)
             assert (dn.poly_mask(c, x, y, w, h) == ref).all()
+            assert (dn.poly_mask(c, x, y, w, h, parity=True) == ref).all()
             n += 1
     assert n > 2000
 
@@ -137,21 +138,17 @@ def test_min_area_rect_and_mini_box():
             got = dn.min_area_rect(c)
             total += 1
             if not (got == ref).all():
+                # only a different rectangle of exactly the same area
                 bad += 1
-                # only equal-area ties may resolve differently
-                assert abs(float(ref[2] * ref[3]) - float(got[2] * got[3])) <= \
-                    1e-5 * float(ref[2] * ref[3]), (c.tolist(), ref, got)
-    assert total > 5000 and bad <= total // 1000, (bad, total)
-    # config-1 style maps: text-line rectangles. Box corners bit-exact; the
-    # min side (only compared against the 3 and 5 px filters) may differ by
-    # the near-tie caliper choice in a few contours
-    exact = n = 0
+                assert abs(float(ref[2]) * float(ref[3]) - float(got[2]) * float(got[3])) <= \
+                    1e-5 * float(ref[2]) * float(ref[3]), (c.tolist(), ref, got)
+    assert total > 5000 and bad * 5000 <= total, (bad, total)
+    # config-1 style maps: text-line contours and their raw offset rings
+    n = 0
     for mi in range(4):
         m = synth_map(480, 640, 20, 40, mi)
         for c in do.find_contours(do.threshold(m, 0.3)):
-            b_ref, s_ref = do.get_mini_boxes(c)
-            b, s = dn.mini_box(c)
-            assert b == b_ref and abs(s - s_ref) <= 1e-4 * s_ref, (c.tolist(), b, b_ref, s, s_ref)
-            exact += s == s_ref
-            n += 1
-    assert n > 40 and exact >= n - 3, (exact, n)
+            for pts in (c, np.array(dn.offset_raw(c, 4.5) or c.tolist(), np.int32)):
+                assert dn.mini_box(pts) == do.get_mini_boxes(pts), c.tolist()
+                n += 1
+    assert n > 80

@@ -1,0 +1,192 @@
+"""Subsystem 3 parity on the GPU: tocr_db_postprocess against the CPU
+restatement of extract_boxes_from_bitmap (oracle/db_oracle.py: cv2 4.13 +
+the reference's Clipper).
+
+Two bars:
+- bit-exact boxes, in contour order, against the oracle whose unclip ring
+  is Clipper's raw round-join offset (the offset before Clipper's union, as
+  the device computes it). This pins every device stage: threshold,
+  labelling, contour order and the 3000 cap, border following, both
+  min-area boxes, the polygon-mask score, the offset, scaling and filters.
+  Scores within 1e-3 (measured: equal to float rounding).
+- against the full oracle (Clipper's union): the union re-rounds vertices
+  where the offset path crosses itself, which moves a mini-box corner by a
+  pixel for about 2 % of the boxes; the test bounds that rate and the size
+  of the differences.
+The labelling stage is also checked on its own (tocr_db_components) as a
+partition against scipy's 8-/4-connected labelling."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import db_oracle as do
+
+pytestmark = pytest.mark.gpu
+
+cv2 = pytest.importorskip("cv2")
+ndimage = pytest.importorskip("scipy.ndimage")
+
+SCORE_TOL = 1e-3
+
+
+def synth_maps(n, h, w, kmin=40, kmax=200, seed=0x7EC00000, first=0):
+    from turboocr_b200._lib import synth
+    out = np.zeros((n, h, w), np.float32)
+    for i in range(n):
+        synth().tocr_synth_db_map_host(out[i].ctypes.data, h, w, kmin, kmax, seed, first + i)
+    return out
+
+
+def raw_unclip(contour, ratio):
+    import db_native as dn
+    d = do.unclip_distance(contour, ratio)
+    if d is None:
+        return contour
+    raw = dn.offset_raw(contour, d)
+    return np.array(raw, np.int32) if raw else contour
+
+
+def run_gpu(cuda, maps, **kw):
+    from turboocr_b200.kernels import DbPostprocess
+    n, h, w = maps.shape
+    db = DbPostprocess(n, h, w, cuda, **kw)
+    pred = torch.from_numpy(maps).to(cuda)
+    db(pred)
+    torch.cuda.synchronize()
+    return db.results()
+
+
+def compare_exact(gpu, ref):
+    assert [b for b, _ in gpu] == [b for b, _ in ref]
+    for (_, s1), (_, s2) in zip(gpu, ref):
+        assert abs(s1 - s2) <= SCORE_TOL
+
+
+@pytest.mark.parametrize("hw", [(37, 53), (64, 64), (100, 333), (960, 960)])
+def test_components_partition(cuda, hw):
+    from turboocr_b200.kernels import db_components
+    h, w = hw
+    rng = np.random.default_rng(h * w)
+    maps = rng.random((3, h, w)).astype(np.float32)
+    maps[1] = (maps[1] > 0.5) * 0.9          # coarse blobs after smoothing below
+    maps[1] = ndimage.uniform_filter(maps[1], 5)
+    maps[2] = synth_maps(1, h, w, 3, 12)[0]
+    labels, bitmap = db_components(torch.from_numpy(maps).to(cuda), 0.3)
+    labels = labels.cpu().numpy()
+    bitmap = bitmap.cpu().numpy()
+    for m in range(3):
+        fg = maps[m] > np.float32(0.3)
+        assert (bitmap[m] == np.where(fg, 255, 0)).all()
+        lab = labels[m]
+        idx = np.arange(h * w).reshape(h, w) + 1
+        l8, n8 = ndimage.label(fg, structure=np.ones((3, 3)))
+        for k in range(1, n8 + 1):
+            sel = l8 == k
+            vals = np.unique(lab[sel])
+            assert len(vals) == 1 and vals[0] == idx[sel].min()
+        l4, n4 = ndimage.label(np.pad(~fg, 1, constant_values=True))
+        l4 = l4[1:-1, 1:-1]
+        outer = set(np.unique(np.concatenate([l4[0], l4[-1], l4[:, 0], l4[:, -1]]))) - {0}
+        for k in range(1, n4 + 1):
+            sel = l4 == k
+            if not sel.any():
+                continue
+            vals = np.unique(lab[sel])
+            want = 0 if k in outer else idx[sel].min()
+            assert len(vals) == 1 and vals[0] == want
+
+
+def test_db_config1_exact(cuda):
+    """BASELINE config 1 at full size: 8 maps 960x960, 40-200 rectangles."""
+    maps = synth_maps(8, 960, 960)
+    got = run_gpu(cuda, maps)
+    n = 0
+    for m in range(8):
+        ref = do.db_postprocess(maps[m], unclip_fn=raw_unclip)
+        compare_exact(got[m], ref)
+        n += len(ref)
+    assert n > 60
+
+
+@pytest.mark.parametrize("hw,k", [((240, 320), (5, 30)), ((97, 131), (2, 8)), ((512, 96), (3, 10))])
+def test_db_small_maps_exact(cuda, hw, k):
+    maps = synth_maps(4, hw[0], hw[1], k[0], k[1], first=100)
+    got = run_gpu(cuda, maps)
+    for m in range(4):
+        compare_exact(got[m], do.db_postprocess(maps[m], unclip_fn=raw_unclip))
+
+
+def test_db_noise_and_holes_exact(cuda):
+    """Blobby noise: many contours, hole borders, thin and one-pixel parts."""
+    rng = np.random.default_rng(7)
+    maps = ndimage.uniform_filter(rng.random((6, 128, 160)).astype(np.float32), (1, 3, 3))
+    maps = np.clip((maps - 0.45) * 4, 0, 1).astype(np.float32)
+    got = run_gpu(cuda, maps, box_thresh=0.5)
+    for m in range(6):
+        compare_exact(got[m], do.db_postprocess(maps[m], box_thresh=0.5, unclip_fn=raw_unclip))
+
+
+def test_db_edge_cases(cuda):
+    h, w = 64, 96
+    maps = np.zeros((4, h, w), np.float32)
+    maps[1][:] = 0.9                          # one component covering the map
+    maps[2][10:30, 5:80] = 0.95               # one rectangle with a hole
+    maps[2][15:22, 20:40] = 0.0
+    maps[3][h // 2, :] = 0.9                  # a one-pixel line
+    got = run_gpu(cuda, maps)
+    assert got[0] == []
+    for m in range(1, 4):
+        compare_exact(got[m], do.db_postprocess(maps[m], unclip_fn=raw_unclip))
+    assert len(got[1]) == 1
+
+
+def test_db_3000_cap(cuda):
+    """More than 3000 contours: only the first 3000 in cv2's order (descending
+    raster order of their starts) are candidates, so a text rectangle near
+    the top of the map, whose contour comes last, is dropped."""
+    h, w = 300, 400
+    m = np.zeros((h, w), np.float32)
+    m[10:40, 20:300] = 0.9                    # early start -> late in the list
+    m[60::3, ::3] = 0.9                       # isolated dots: 80 x 134 contours
+    maps = m[None].copy()
+    total = len(do.find_contours(do.threshold(m, 0.3)))
+    assert total > 3000
+    got = run_gpu(cuda, maps)
+    ref = do.db_postprocess(m, unclip_fn=raw_unclip)
+    compare_exact(got[0], ref)
+    assert ref == []
+    m2 = m.copy()
+    m2[60:, :] = 0                            # without the dots the box is found
+    got2 = run_gpu(cuda, m2[None].copy())
+    assert len(got2[0]) == 1
+
+
+def test_db_geometry_scaling(cuda):
+    """orig != resize: boxes are scaled back and clamped (det_postprocess.cpp:205-210)."""
+    from turboocr_b200.kernels import DbPostprocess
+    maps = synth_maps(2, 320, 480, 5, 20, first=200)
+    geo = torch.tensor([[500, 700, 320, 480], [160, 240, 320, 480]], dtype=torch.int32,
+                       device=cuda)
+    db = DbPostprocess(2, 320, 480, cuda)
+    db(torch.from_numpy(maps).to(cuda), geometry=geo)
+    got = db.results()
+    for m, (oh, ow) in enumerate([(500, 700), (160, 240)]):
+        ref = do.extract_boxes_from_bitmap(maps[m], do.threshold(maps[m], 0.3), oh, ow, 320, 480,
+                                           0.6, 1.5, unclip_fn=raw_unclip)
+        compare_exact(got[m], ref)
+
+
+def test_db_vs_clipper_union_rate(cuda):
+    """Against the full reference unclip (with Clipper's union)."""
+    maps = synth_maps(8, 960, 960, first=300)
+    got = run_gpu(cuda, maps)
+    same = total = 0
+    for m in range(8):
+        ref = do.db_postprocess(maps[m])
+        assert len(got[m]) == len(ref)
+        for (b1, s1), (b2, s2) in zip(got[m], ref):
+            total += 1
+            same += b1 == b2
+            assert np.abs(np.array(b1) - np.array(b2)).max() <= 6
+            assert abs(s1 - s2) <= SCORE_TOL
+    assert total > 60 and same >= 0.9 * total, (same, total)

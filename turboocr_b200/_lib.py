@@ -63,6 +63,10 @@ SIGNATURES: dict[str, tuple] = {
     "tocr_dwpw_packed_bytes": (C.c_size_t, [_i, _i]),
     "tocr_dwpw_pack": (_i, [_i, _i, _i, _vp, _vp, _vp, _vp, _vp, C.c_size_t]),
     "tocr_dwpw_dequant_pw": (_i, [_vp, _i, _i, _i, _vp]),
+    "tocr_db_workspace_bytes": (C.c_size_t, [_i, _i, _i, _ll, _ll]),
+    "tocr_db_postprocess": (_i, [_vp, _i, _i, _i, _vp, _f, _f, _f, _f, _f, _ll, _ll, _vp,
+                                 C.c_size_t, _vp, _vp, _vp, _i, _vp, _vp]),
+    "tocr_db_components": (_i, [_vp, _i, _i, _i, _f, _vp, _vp, _vp]),
 }
 
 SYNTH_SIGNATURES: dict[str, tuple] = {

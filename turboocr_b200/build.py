@@ -30,7 +30,8 @@ COMMON = ["-O3", "-lineinfo", "-std=c++20", "-Xcompiler", "-fPIC", "-Xcompiler",
           "-fvisibility=hidden", f"-I{INCLUDE}", f"-I{CSRC}"]
 
 LIBS = {
-    "libtocr_b200.so": ["capi_common.cu", "ctc.cu", "preprocess.cu", "threshold.cu", "dwpw.cu"],
+    "libtocr_b200.so": ["capi_common.cu", "ctc.cu", "preprocess.cu", "threshold.cu", "dwpw.cu",
+                        "db.cu"],
     "libtocr_synth.so": ["synth.cu"],
 }
 # C++ host sources (reference-signature shims), built into libtocr_b200.so.
@@ -44,8 +45,13 @@ def _newest_header() -> float:
     return max((h.stat().st_mtime for h in HEADERS), default=0.0)
 
 
+# Per-file extra flags. db.cu must not contract multiply-adds: its geometry
+# reproduces OpenCV's and Clipper's floating-point operation order.
+EXTRA = {"db.cu": ["-fmad=false"]}
+
+
 def _compile(src: Path, obj: Path, verbose: bool) -> None:
-    flags = list(COMMON)
+    flags = list(COMMON) + EXTRA.get(src.name, [])
     if src.suffix == ".cu":
         flags += ARCH
     else:

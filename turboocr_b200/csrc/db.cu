@@ -1,0 +1,794 @@
+// Subsystem 3 — DB post-processing on B200: probability maps in, ordered
+// text quads and their box scores out, with the boxes of the reference's CPU
+// path extract_boxes_from_bitmap (src/detection/det_postprocess.cpp:145-222).
+//
+// Stages (all on the device, one stream, no host round trip):
+//   1. ccl_local_kernel    threshold (pred > thresh, cpu_paddle_det.cpp:115) and
+//                          tile-local union-find: foreground 8-connected,
+//                          background 4-connected, background on the image
+//                          frame joined to a virtual "outside" node 0
+//   2. ccl_merge_kernel    union across tile borders (atomicMin linking, so every
+//                          root is the smallest node of its component)
+//   3. ccl_rows_kernel     full path compression, per-row count of border starts
+//   4. starts_*            the starts in cv::findContours(RETR_LIST) order
+//                          (descending raster order), capped at 3000 per map
+//                          (det_postprocess.cpp:165-167)
+//   5. trace_*             border following, CHAIN_APPROX_SIMPLE, count then write
+//   6. geom_score_kernel   size filters, first min-area box, polygon-mask mean
+//                          (box_score_fast, det_postprocess.cpp:15-55), unclip distance
+//   7. geom_unclip_kernel  round-join offset (Clipper's DoOffset), second min-area
+//                          box, scale/round/clamp, edge filters
+//   8. compact_kernel      kept boxes in contour order
+//
+// Node ids: 0 is the outside of map m; pixel p = y*W + x of the map is node
+// p+1. A node's parent lives in lab[m*H*W + node-1]. Parents are never larger
+// than their node, so every find() walk strictly decreases and ends.
+//
+// This translation unit is compiled with -fmad=false: the geometry must keep
+// the libraries' operation order (explicit fma() only where they contract).
+#include "tocr_common.cuh"
+
+#include "db_geom.cuh"
+
+namespace tocr {
+namespace {
+
+using db::HP;
+using db::P2;
+using db::RRect;
+
+constexpr int kTileW = 32, kTileH = 16, kTilePx = kTileW * kTileH;
+constexpr int kMaxCand = 3000;        // det_postprocess.cpp:165
+constexpr int kScanThreads = 1024;
+
+// Error bits written to the status word.
+constexpr int kErrPointPool = 1;      // traced points exceed the point pool
+constexpr int kErrTrace = 2;          // a border walk exceeded its step bound
+constexpr int kErrOffsetPool = 4;     // offset points exceed the offset pool
+constexpr int kErrBoxes = 8;          // more kept boxes than max_boxes (truncated)
+
+struct DbParams {
+  int n_maps, H, W;
+  float thresh, box_thresh, unclip_ratio, min_box_side, min_unclipped_side;
+  long long point_cap, offset_cap;
+  int max_boxes;
+};
+
+// ---------------------------------------------------------------- union-find --
+__device__ __forceinline__ int find_g(const int *lab, int v) {
+  while (v != 0) {
+    const int p = __ldcg(lab + v - 1);
+    if (p == v) break;
+    v = p;
+  }
+  return v;
+}
+
+__device__ __forceinline__ void union_g(int *lab, int a, int b) {
+  for (;;) {
+    a = find_g(lab, a);
+    b = find_g(lab, b);
+    if (a == b) return;
+    if (a < b) { const int t = a; a = b; b = t; }
+    const int old = atomicMin(lab + a - 1, b);
+    if (old == a) return;
+    a = old;
+  }
+}
+
+__device__ __forceinline__ int find_s(volatile int *par, int v) {
+  while (v != 0) {
+    const int p = par[v - 1];
+    if (p == v) break;
+    v = p;
+  }
+  return v;
+}
+
+__device__ __forceinline__ void union_s(int *par, int a, int b) {
+  for (;;) {
+    a = find_s(par, a);
+    b = find_s(par, b);
+    if (a == b) return;
+    if (a < b) { const int t = a; a = b; b = t; }
+    const int old = atomicMin(par + a - 1, b);
+    if (old == a) return;
+    a = old;
+  }
+}
+
+// 1. threshold + tile-local labelling. grid (tiles_x, tiles_y, n_maps), 256 threads.
+__global__ void __launch_bounds__(256)
+ccl_local_kernel(const float *__restrict__ pred, uint8_t *__restrict__ bitmap, int *__restrict__ lab,
+                 int H, int W, float thresh) {
+  __shared__ uint8_t fg[kTileH][kTileW];
+  __shared__ int par[kTilePx];
+  const int m = blockIdx.z;
+  const size_t base = (size_t)m * H * W;
+  const int tx0 = blockIdx.x * kTileW, ty0 = blockIdx.y * kTileH;
+  for (int l = threadIdx.x; l < kTilePx; l += blockDim.x) {
+    const int lx = l % kTileW, ly = l / kTileW;
+    const int x = tx0 + lx, y = ty0 + ly;
+    uint8_t v = 0;
+    if (x < W && y < H) {
+      v = pred[base + (size_t)y * W + x] > thresh;
+      bitmap[base + (size_t)y * W + x] = v ? 255 : 0;
+    }
+    fg[ly][lx] = v;
+    par[l] = l + 1;
+  }
+  __syncthreads();
+  for (int l = threadIdx.x; l < kTilePx; l += blockDim.x) {
+    const int lx = l % kTileW, ly = l / kTileW;
+    const int x = tx0 + lx, y = ty0 + ly;
+    if (x >= W || y >= H) continue;
+    const int me = l + 1;
+    if (fg[ly][lx]) {
+      if (lx > 0 && fg[ly][lx - 1]) union_s(par, me, me - 1);
+      if (ly > 0) {
+        if (fg[ly - 1][lx]) union_s(par, me, me - kTileW);
+        if (lx > 0 && fg[ly - 1][lx - 1]) union_s(par, me, me - kTileW - 1);
+        if (lx + 1 < kTileW && x + 1 < W && fg[ly - 1][lx + 1]) union_s(par, me, me - kTileW + 1);
+      }
+    } else {
+      if (lx > 0 && !fg[ly][lx - 1]) union_s(par, me, me - 1);
+      if (ly > 0 && !fg[ly - 1][lx]) union_s(par, me, me - kTileW);
+      if (x == 0 || y == 0 || x == W - 1 || y == H - 1) union_s(par, me, 0);
+    }
+  }
+  __syncthreads();
+  for (int l = threadIdx.x; l < kTilePx; l += blockDim.x) {
+    const int lx = l % kTileW, ly = l / kTileW;
+    const int x = tx0 + lx, y = ty0 + ly;
+    if (x >= W || y >= H) continue;
+    const int r = find_s(par, l + 1);
+    int g = 0;
+    if (r != 0) {
+      const int rl = r - 1;
+      g = (ty0 + rl / kTileW) * W + tx0 + rl % kTileW + 1;
+    }
+    lab[base + (size_t)y * W + x] = g;
+  }
+}
+
+// 2. unions across tile borders. One thread per pixel of a tile's first row,
+// first column or last column. grid (tiles_x, tiles_y, n_maps), 128 threads.
+__global__ void __launch_bounds__(128)
+ccl_merge_kernel(const uint8_t *__restrict__ bitmap, int *__restrict__ lab, int H, int W) {
+  const int m = blockIdx.z;
+  const size_t base = (size_t)m * H * W;
+  const uint8_t *bm = bitmap + base;
+  int *lb = lab + base;
+  const int tx0 = blockIdx.x * kTileW, ty0 = blockIdx.y * kTileH;
+  // border pixels: top row (kTileW), left column (kTileH), right column (kTileH)
+  for (int i = threadIdx.x; i < kTileW + 2 * kTileH; i += blockDim.x) {
+    int lx, ly;
+    if (i < kTileW) { lx = i; ly = 0; }
+    else if (i < kTileW + kTileH) { lx = 0; ly = i - kTileW; }
+    else { lx = kTileW - 1; ly = i - kTileW - kTileH; }
+    const int x = tx0 + lx, y = ty0 + ly;
+    if (x >= W || y >= H) continue;
+    const int p = y * W + x, me = p + 1;
+    const bool f = bm[p] != 0;
+    auto other_tile = [&](int nx, int ny) {
+      return nx / kTileW != blockIdx.x || ny / kTileH != blockIdx.y;
+    };
+    if (f) {
+      const int nb[4][2] = {{x - 1, y}, {x - 1, y - 1}, {x, y - 1}, {x + 1, y - 1}};
+      for (int k = 0; k < 4; ++k) {
+        const int nx = nb[k][0], ny = nb[k][1];
+        if (nx < 0 || ny < 0 || nx >= W) continue;
+        if (!other_tile(nx, ny)) continue;
+        if (bm[ny * W + nx]) union_g(lb, me, ny * W + nx + 1);
+      }
+    } else {
+      const int nb[2][2] = {{x - 1, y}, {x, y - 1}};
+      for (int k = 0; k < 2; ++k) {
+        const int nx = nb[k][0], ny = nb[k][1];
+        if (nx < 0 || ny < 0) continue;
+        if (!other_tile(nx, ny)) continue;
+        if (!bm[ny * W + nx]) union_g(lb, me, ny * W + nx + 1);
+      }
+    }
+  }
+}
+
+// 3. compression + starts per row. A start is a pixel that is its own root:
+// a foreground root starts an outer border at itself, a background root (not
+// joined to the outside) starts a hole border at the pixel on its left.
+// grid (H, n_maps), 256 threads.
+__global__ void __launch_bounds__(256)
+ccl_rows_kernel(int *__restrict__ lab, int *__restrict__ row_count, int H, int W) {
+  const int m = blockIdx.y, y = blockIdx.x;
+  int *lb = lab + (size_t)m * H * W;
+  __shared__ int s_total;
+  if (threadIdx.x == 0) s_total = 0;
+  __syncthreads();
+  int cnt = 0;
+  for (int x = threadIdx.x; x < W; x += blockDim.x) {
+    const int p = y * W + x;
+    const int r = find_g(lb, lb[p]);
+    lb[p] = r;
+    cnt += (r == p + 1);
+  }
+  for (int off = 16; off; off >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, off);
+  if ((threadIdx.x & 31) == 0 && cnt) atomicAdd(&s_total, cnt);
+  __syncthreads();
+  if (threadIdx.x == 0 && row_count) row_count[(size_t)m * H + y] = s_total;
+}
+
+// 4a. per map: offsets of each row's starts in descending raster order.
+// grid n_maps, kScanThreads threads.
+__global__ void __launch_bounds__(kScanThreads)
+starts_scan_kernel(const int *__restrict__ row_count, int *__restrict__ row_off,
+                   int *__restrict__ n_contours, int *__restrict__ n_total, int H) {
+  const int m = blockIdx.x;
+  const int *rc = row_count + (size_t)m * H;
+  int *ro = row_off + (size_t)m * H;
+  __shared__ int s_part[kScanThreads];
+  __shared__ int s_carry;
+  if (threadIdx.x == 0) s_carry = 0;
+  __syncthreads();
+  // descending rows: row H-1 first
+  for (int c0 = 0; c0 < H; c0 += kScanThreads) {
+    const int i = c0 + threadIdx.x;
+    const int y = H - 1 - i;
+    const int v = (i < H) ? rc[y] : 0;
+    s_part[threadIdx.x] = v;
+    __syncthreads();
+    for (int off = 1; off < kScanThreads; off <<= 1) {
+      const int t = (threadIdx.x >= off) ? s_part[threadIdx.x - off] : 0;
+      __syncthreads();
+      s_part[threadIdx.x] += t;
+      __syncthreads();
+    }
+    if (i < H) ro[y] = s_carry + s_part[threadIdx.x] - v;
+    __syncthreads();
+    if (threadIdx.x == kScanThreads - 1) s_carry += s_part[threadIdx.x];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    n_total[m] = s_carry;
+    n_contours[m] = s_carry < kMaxCand ? s_carry : kMaxCand;
+  }
+}
+
+// 4b. start records, packed as (pixel index << 1) | hole, at
+// starts[m * 3000 + rank]. grid (H, n_maps), 256 threads.
+__global__ void __launch_bounds__(256)
+starts_write_kernel(const int *__restrict__ lab, const uint8_t *__restrict__ bitmap,
+                    const int *__restrict__ row_count, const int *__restrict__ row_off,
+                    int *__restrict__ starts, int H, int W) {
+  const int m = blockIdx.y, y = blockIdx.x;
+  const int rcount = row_count[(size_t)m * H + y];
+  if (rcount == 0) return;
+  const int roff = row_off[(size_t)m * H + y];
+  if (roff >= kMaxCand) return;
+  const int *lb = lab + (size_t)m * H * W;
+  const uint8_t *bm = bitmap + (size_t)m * H * W;
+  __shared__ int s_warp[8];
+  __shared__ int s_carry;
+  if (threadIdx.x == 0) s_carry = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int x0 = 0; x0 < W; x0 += blockDim.x) {
+    const int x = x0 + threadIdx.x;
+    const int p = y * W + x;
+    const bool st = x < W && lb[p] == p + 1;
+    const unsigned bal = __ballot_sync(0xffffffffu, st);
+    if (lane == 0) s_warp[warp] = __popc(bal);
+    __syncthreads();
+    int before = s_carry;
+    for (int w = 0; w < warp; ++w) before += s_warp[w];
+    const int asc = before + __popc(bal & ((1u << lane) - 1));
+    if (st) {
+      const int rank = roff + (rcount - 1 - asc);
+      if (rank < kMaxCand) {
+        const bool hole = bm[p] == 0;
+        const int sp = hole ? p - 1 : p;
+        starts[(size_t)m * kMaxCand + rank] = (sp << 1) | (hole ? 1 : 0);
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int t = 0;
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += s_warp[w];
+      s_carry += t;
+    }
+    __syncthreads();
+  }
+}
+
+struct FgMap {
+  const uint8_t *bm;
+  int H, W;
+  __device__ bool operator()(int x, int y) const {
+    return x >= 0 && y >= 0 && x < W && y < H && bm[(size_t)y * W + x] != 0;
+  }
+};
+
+// 5. border following. One thread per contour slot (m * 3000 + rank).
+// write == false: count points into npts; write == true: store them at pt_off.
+template <bool kWrite>
+__global__ void __launch_bounds__(128)
+trace_kernel(const uint8_t *__restrict__ bitmap, const int *__restrict__ starts,
+             const int *__restrict__ n_contours, int *__restrict__ npts,
+             const long long *__restrict__ pt_off, P2 *__restrict__ pts, int *__restrict__ status,
+             long long point_cap, int n_maps, int H, int W) {
+  const long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= (long long)n_maps * kMaxCand) return;
+  const int m = (int)(c / kMaxCand), rank = (int)(c % kMaxCand);
+  if (rank >= n_contours[m]) {
+    if (!kWrite) npts[c] = 0;
+    return;
+  }
+  const int rec = starts[c];
+  const int sp = rec >> 1;
+  const FgMap fg{bitmap + (size_t)m * H * W, H, W};
+  const long long ms = 4ll * H * W + 16;
+  const int max_steps = ms > 0x7fffffffll ? 0x7fffffff : (int)ms;
+  if (!kWrite) {
+    const int n = db::trace_border(fg, sp % W, sp / W, (rec & 1) != 0, nullptr, 0, max_steps);
+    if (n < 0) atomicOr(status, kErrTrace);
+    npts[c] = n < 0 ? 0 : n;
+  } else {
+    const int n = npts[c];
+    if (n == 0 || pt_off[c] + n > point_cap) return;
+    db::trace_border(fg, sp % W, sp / W, (rec & 1) != 0, pts + pt_off[c], n, max_steps);
+  }
+}
+
+// Exclusive scan of n int32 values into int64 offsets, out[n] = total.
+// One CTA of kScanThreads threads (n is at most a few hundred thousand).
+template <class T>
+__global__ void __launch_bounds__(kScanThreads)
+scan_kernel(const T *__restrict__ in, long long *__restrict__ out, long long n) {
+  __shared__ long long s_part[kScanThreads];
+  __shared__ long long s_carry;
+  if (threadIdx.x == 0) s_carry = 0;
+  __syncthreads();
+  for (long long c0 = 0; c0 < n; c0 += kScanThreads) {
+    const long long i = c0 + threadIdx.x;
+    const long long v = (i < n) ? (long long)in[i] : 0;
+    s_part[threadIdx.x] = v;
+    __syncthreads();
+    for (int off = 1; off < kScanThreads; off <<= 1) {
+      const long long t = (threadIdx.x >= off) ? s_part[threadIdx.x - off] : 0;
+      __syncthreads();
+      s_part[threadIdx.x] += t;
+      __syncthreads();
+    }
+    if (i < n) out[i] = s_carry + s_part[threadIdx.x] - v;
+    __syncthreads();
+    if (threadIdx.x == kScanThreads - 1) s_carry += s_part[threadIdx.x];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) out[n] = s_carry;
+}
+
+__global__ void check_cap_kernel(const long long *__restrict__ off, long long n, long long cap,
+                                 int *__restrict__ status, int bit) {
+  if (off[n] > cap) atomicOr(status, bit);
+}
+
+// min-area rectangle of a point set through its hull; scratch sized for n points.
+__device__ RRect rect_of(const P2 *p, int n, HP *hpw, P2 *hull, float *fsc) {
+  const int h = db::convex_hull(p, n, hpw, hull);
+  return db::min_area_rect(hull, h, fsc);
+}
+
+// 6a. one thread per contour slot: the filters before the score
+// (det_postprocess.cpp:169-186): more than 2 points, boundingRect sides >= 3,
+// first min-area box side >= min_box_side. Survivors get their AABB.
+__global__ void __launch_bounds__(128)
+geom_box1_kernel(const int *__restrict__ n_contours, const int *__restrict__ npts,
+                 const long long *__restrict__ pt_off, const P2 *__restrict__ pts,
+                 HP *__restrict__ hpw, P2 *__restrict__ hullbuf, float *__restrict__ fsc,
+                 int *__restrict__ stage1, int4 *__restrict__ aabb, DbParams P) {
+  const long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= (long long)P.n_maps * kMaxCand) return;
+  stage1[c] = 0;
+  const int m = (int)(c / kMaxCand), rank = (int)(c % kMaxCand);
+  const int n = npts[c];
+  if (rank >= n_contours[m] || n <= 2 || pt_off[c] + n > P.point_cap) return;
+  const P2 *p = pts + pt_off[c];
+  int xmin = p[0].x, xmax = p[0].x, ymin = p[0].y, ymax = p[0].y;
+  for (int i = 1; i < n; ++i) {
+    xmin = min(xmin, p[i].x); xmax = max(xmax, p[i].x);
+    ymin = min(ymin, p[i].y); ymax = max(ymax, p[i].y);
+  }
+  if (xmax - xmin + 1 < 3 || ymax - ymin + 1 < 3) return;
+  const long long so = pt_off[c] + c;  // n + 1 scratch slots per contour
+  const RRect r = rect_of(p, n, hpw + 2 * so, hullbuf + so, fsc + 3 * so);
+  if ((r.w < r.h ? r.w : r.h) < P.min_box_side) return;
+  aabb[c] = make_int4(xmin, ymin, xmax, ymax);
+  stage1[c] = 1;
+}
+
+constexpr int kScoreThreads = 256;
+constexpr int kBandRows = 32;
+constexpr int kMaxWords = 128;  // AABB widths up to 4096 px
+
+__device__ __forceinline__ void fill_bits(unsigned *row, int a, int b) {
+  // set bits [a, b] (inclusive, already clipped, a <= b)
+  int w0 = a >> 5, w1 = b >> 5;
+  for (int w = w0; w <= w1; ++w) {
+    const int lo = (w == w0) ? (a & 31) : 0, hi = (w == w1) ? (b & 31) : 31;
+    const unsigned mask = (hi == 31 ? 0xffffffffu : ((1u << (hi + 1)) - 1u)) & ~((1u << lo) - 1u);
+    atomicOr(row + w, mask);
+  }
+}
+
+// 6b. one CTA per contour slot: box_score_fast, the mean of pred over the
+// filled contour (edge pixels plus odd-parity interior) inside its AABB,
+// accumulated in double; then the unclip distance area * ratio / perimeter
+// (det_postprocess.cpp:59-66) and the capacity of the offset path.
+__global__ void __launch_bounds__(kScoreThreads)
+score_kernel(const float *__restrict__ pred, const int *__restrict__ stage1,
+             const int4 *__restrict__ aabb, const int *__restrict__ npts,
+             const long long *__restrict__ pt_off, const P2 *__restrict__ pts,
+             int *__restrict__ stage2, float *__restrict__ score, double *__restrict__ dist,
+             DbParams P) {
+  const long long c = blockIdx.x;
+  if (!stage1[c]) {
+    if (threadIdx.x == 0) stage2[c] = 0;
+    return;
+  }
+  __shared__ unsigned s_edge[kBandRows][kMaxWords];
+  __shared__ unsigned s_tog[kBandRows][kMaxWords];
+  __shared__ double s_sum[kScoreThreads / 32];
+  __shared__ long long s_cnt[kScoreThreads / 32];
+  const int m = (int)(c / kMaxCand);
+  const int H = P.H, W = P.W;
+  const int n = npts[c];
+  const P2 *p = pts + pt_off[c];
+  const int4 bb = aabb[c];
+  const int bx0 = max(0, bb.x), by0 = max(0, bb.y), bx1 = min(W - 1, bb.z), by1 = min(H - 1, bb.w);
+  double sum = 0.;
+  long long cnt = 0;
+  const bool nonempty = bx1 > bx0 && by1 > by0;
+  if (nonempty) {
+    const int width = bx1 - bx0 + 1, words = (width + 31) >> 5;
+    const float *pm = pred + (size_t)m * H * W;
+    constexpr int kSplit = kScoreThreads / kBandRows;  // threads per row
+    const int chunk = (n + kSplit - 1) / kSplit;
+    for (int band = by0; band <= by1; band += kBandRows) {
+      const int rows = min(kBandRows, by1 - band + 1);
+      for (int i = threadIdx.x; i < kBandRows * words; i += kScoreThreads) {
+        s_edge[i / words][i % words] = 0u;
+        s_tog[i / words][i % words] = 0u;
+      }
+      __syncthreads();
+      {
+        const int r = threadIdx.x / kSplit, part = threadIdx.x % kSplit;
+        if (r < rows) {
+          const int y = band + r;
+          const int i0 = part * chunk, i1 = min(n, i0 + chunk);
+          unsigned *er = s_edge[r];
+          unsigned *tr = s_tog[r];
+          db::poly_row_marks(p, n, y, i0, i1,
+              [&](int a, int b) {
+                if (a > b) { const int t = a; a = b; b = t; }
+                a = max(a, bx0); b = min(b, bx1);
+                if (a <= b) fill_bits(er, a - bx0, b - bx0);
+              },
+              [&](int x) {
+                if (x >= bx0 && x <= bx1) atomicXor(tr + ((x - bx0) >> 5), 1u << ((x - bx0) & 31));
+              });
+        }
+      }
+      __syncthreads();
+      if (threadIdx.x < rows) {
+        const int r = threadIdx.x;
+        unsigned carry = 0u;
+        for (int k = 0; k < words; ++k) {
+          unsigned t = s_tog[r][k];
+          t ^= t << 1; t ^= t << 2; t ^= t << 4; t ^= t << 8; t ^= t << 16;  // inclusive prefix parity
+          const unsigned par = carry ? ~t : t;
+          carry = par >> 31;
+          s_edge[r][k] |= par;
+        }
+        const int tail = width & 31;
+        if (tail) s_edge[r][words - 1] &= (1u << tail) - 1u;
+      }
+      __syncthreads();
+      for (int i = threadIdx.x; i < rows * width; i += kScoreThreads) {
+        const int r = i / width, x = i % width;
+        if ((s_edge[r][x >> 5] >> (x & 31)) & 1u) {
+          sum += (double)pm[(size_t)(band + r) * W + bx0 + x];
+          ++cnt;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int off = 16; off; off >>= 1) {
+    sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    cnt += __shfl_xor_sync(0xffffffffu, cnt, off);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    s_sum[threadIdx.x >> 5] = sum;
+    s_cnt[threadIdx.x >> 5] = cnt;
+  }
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  double tsum = 0.;
+  long long tcnt = 0;
+  for (int w = 0; w < kScoreThreads / 32; ++w) { tsum += s_sum[w]; tcnt += s_cnt[w]; }
+  const float sc = (nonempty && tcnt > 0) ? (float)(tsum / (double)tcnt) : 0.f;
+  score[c] = sc;
+  stage2[c] = 0;
+  if (sc < P.box_thresh) return;
+  const double per = db::arc_length(p, n);
+  // unclip returns the contour itself when the perimeter is 0 (distance 0 here)
+  dist[c] = per != 0. ? db::contour_area(p, n) * (double)P.unclip_ratio / per : 0.;
+  stage2[c] = 1;
+}
+
+// 7. one thread per surviving contour: the unclip ring (kCount: only its
+// size), the second min-area box, scaling to the original image, filters
+// (det_postprocess.cpp:190-219).
+template <bool kCount>
+__global__ void __launch_bounds__(128)
+unclip_kernel(const int *__restrict__ stage2, const int *__restrict__ npts,
+              const long long *__restrict__ pt_off, const P2 *__restrict__ pts,
+              P2 *__restrict__ qbuf, const double *__restrict__ dist, int *__restrict__ offcap,
+              const long long *__restrict__ off_off, P2 *__restrict__ ring, HP *__restrict__ hpw2,
+              P2 *__restrict__ hull2, float *__restrict__ fsc2, const int *__restrict__ geo,
+              int *__restrict__ keep2, int *__restrict__ boxes, DbParams P) {
+  const long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= (long long)P.n_maps * kMaxCand) return;
+  if (kCount) offcap[c] = 0; else keep2[c] = 0;
+  if (!stage2[c]) return;
+  const int n = npts[c];
+  const P2 *p = pts + pt_off[c];
+  const double d = dist[c];
+  P2 *q = qbuf + pt_off[c] + c;  // n + 1 slots
+  const int qm = (d == 0.) ? 0 : db::offset_prepare(p, n, q);
+  if (kCount) {
+    offcap[c] = qm == 0 ? n : db::offset_raw(q, qm, d, nullptr, 0);
+    return;
+  }
+  if (off_off[c + 1] > P.offset_cap) return;
+  const long long oo = off_off[c] + c;  // offcap + 1 scratch slots per contour
+  P2 *r = ring + oo;
+  int rn;
+  if (qm == 0) {  // no offset: unclip returns the contour itself
+    for (int i = 0; i < n; ++i) r[i] = p[i];
+    rn = n;
+  } else {
+    rn = db::offset_raw(q, qm, d, r, (int)(off_off[c + 1] - off_off[c]));
+  }
+  if (rn < 3) return;
+  const RRect rr = rect_of(r, rn, hpw2 + 2 * oo, hull2 + oo, fsc2 + 3 * oo);
+  if ((rr.w < rr.h ? rr.w : rr.h) < P.min_unclipped_side) return;
+  int box[8];
+  db::mini_box(rr, box);
+  const int m = (int)(c / kMaxCand);
+  int orig_h = P.H, orig_w = P.W, res_h = P.H, res_w = P.W;
+  if (geo) {
+    orig_h = geo[4 * m]; orig_w = geo[4 * m + 1]; res_h = geo[4 * m + 2]; res_w = geo[4 * m + 3];
+  }
+  const float ratio_h = (float)res_h / (float)orig_h;
+  const float ratio_w = (float)res_w / (float)orig_w;
+  for (int k = 0; k < 4; ++k) {
+    const int bx = db::round_half_away((float)box[2 * k] / ratio_w);
+    const int by = db::round_half_away((float)box[2 * k + 1] / ratio_h);
+    box[2 * k] = bx < 0 ? 0 : (bx > orig_w - 1 ? orig_w - 1 : bx);
+    box[2 * k + 1] = by < 0 ? 0 : (by > orig_h - 1 ? orig_h - 1 : by);
+  }
+  const int dx01 = box[0] - box[2], dy01 = box[1] - box[3];
+  const int dx03 = box[0] - box[6], dy03 = box[1] - box[7];
+  const int rw = (int)sqrt((double)(dx01 * dx01 + dy01 * dy01));
+  const int rh = (int)sqrt((double)(dx03 * dx03 + dy03 * dy03));
+  if (rw <= 3 || rh <= 3) return;
+  for (int k = 0; k < 8; ++k) boxes[c * 8 + k] = box[k];
+  keep2[c] = 1;
+}
+
+// 8. kept boxes of map m in contour order. grid n_maps, kScanThreads threads.
+__global__ void __launch_bounds__(kScanThreads)
+compact_kernel(const int *__restrict__ keep2, const int *__restrict__ boxes,
+               const float *__restrict__ score, int *__restrict__ out_boxes,
+               float *__restrict__ out_scores, int *__restrict__ out_counts,
+               int *__restrict__ status, int max_boxes) {
+  const int m = blockIdx.x;
+  __shared__ int s_part[kScanThreads];
+  __shared__ int s_carry;
+  if (threadIdx.x == 0) s_carry = 0;
+  __syncthreads();
+  for (int c0 = 0; c0 < kMaxCand; c0 += kScanThreads) {
+    const int i = c0 + threadIdx.x;
+    const long long c = (long long)m * kMaxCand + i;
+    const int v = (i < kMaxCand) ? keep2[c] : 0;
+    s_part[threadIdx.x] = v;
+    __syncthreads();
+    for (int off = 1; off < kScanThreads; off <<= 1) {
+      const int t = (threadIdx.x >= off) ? s_part[threadIdx.x - off] : 0;
+      __syncthreads();
+      s_part[threadIdx.x] += t;
+      __syncthreads();
+    }
+    if (v) {
+      const int pos = s_carry + s_part[threadIdx.x] - 1;
+      if (pos < max_boxes) {
+        for (int k = 0; k < 8; ++k) out_boxes[((size_t)m * max_boxes + pos) * 8 + k] = boxes[c * 8 + k];
+        out_scores[(size_t)m * max_boxes + pos] = score[c];
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == kScanThreads - 1) s_carry += s_part[threadIdx.x];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    out_counts[m] = s_carry < max_boxes ? s_carry : max_boxes;
+    if (s_carry > max_boxes) atomicOr(status, kErrBoxes);
+  }
+}
+
+}  // namespace
+}  // namespace tocr
+
+// ------------------------------------------------------------------ host -----
+namespace tocr {
+namespace {
+
+struct DbLayout {
+  size_t bitmap, lab, row_count, row_off, n_contours, n_total, starts, npts, pt_off, pts, hpw,
+      hullbuf, fsc, stage1, aabb, stage2, score, dist, offcap, off_off, ring, hpw2, hull2, fsc2,
+      keep2, boxes, total;
+};
+
+size_t align_up(size_t v) { return (v + 255) & ~size_t(255); }
+
+DbLayout db_layout(int n_maps, int h, int w, long long point_cap, long long offset_cap) {
+  DbLayout L{};
+  const size_t px = (size_t)n_maps * h * w;
+  const size_t C = (size_t)n_maps * kMaxCand;
+  size_t o = 0;
+  auto take = [&](size_t bytes) { const size_t at = o; o = align_up(o + bytes); return at; };
+  L.bitmap = take(px);
+  L.lab = take(px * 4);
+  L.row_count = take((size_t)n_maps * h * 4);
+  L.row_off = take((size_t)n_maps * h * 4);
+  L.n_contours = take((size_t)n_maps * 4);
+  L.n_total = take((size_t)n_maps * 4);
+  L.starts = take(C * 4);
+  L.npts = take(C * 4);
+  L.pt_off = take((C + 1) * 8);
+  L.pts = take((size_t)point_cap * sizeof(P2));
+  L.hpw = take(2 * ((size_t)point_cap + C) * sizeof(HP));
+  L.hullbuf = take(((size_t)point_cap + C) * sizeof(P2));
+  L.fsc = take(3 * ((size_t)point_cap + C) * 4);
+  L.stage1 = take(C * 4);
+  L.aabb = take(C * 16);
+  L.stage2 = take(C * 4);
+  L.score = take(C * 4);
+  L.dist = take(C * 8);
+  L.offcap = take(C * 4);
+  L.off_off = take((C + 1) * 8);
+  L.ring = take(((size_t)offset_cap + C) * sizeof(P2));
+  L.hpw2 = take(2 * ((size_t)offset_cap + C) * sizeof(HP));
+  L.hull2 = take(((size_t)offset_cap + C) * sizeof(P2));
+  L.fsc2 = take(3 * ((size_t)offset_cap + C) * 4);
+  L.keep2 = take(C * 4);
+  L.boxes = take(C * 8 * 4);
+  L.total = o;
+  return L;
+}
+
+void default_caps(int n_maps, int h, int w, long long *point_cap, long long *offset_cap) {
+  if (*point_cap <= 0) *point_cap = (long long)n_maps * ((long long)h * w / 4 + 4096);
+  if (*offset_cap <= 0) *offset_cap = 4 * *point_cap;
+}
+
+}  // namespace
+}  // namespace tocr
+
+using namespace tocr;
+
+extern "C" {
+
+TOCR_API size_t tocr_db_workspace_bytes(int n_maps, int h, int w, long long point_cap,
+                                        long long offset_cap) {
+  if (n_maps <= 0 || h <= 0 || w <= 0) return 0;
+  default_caps(n_maps, h, w, &point_cap, &offset_cap);
+  return db_layout(n_maps, h, w, point_cap, offset_cap).total;
+}
+
+TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
+                                 const int *d_geometry, float thresh, float box_thresh,
+                                 float unclip_ratio, float min_box_side,
+                                 float min_unclipped_side, long long point_cap,
+                                 long long offset_cap, void *d_workspace,
+                                 size_t workspace_bytes, int *d_boxes, float *d_scores,
+                                 int *d_counts, int max_boxes, int *d_status, void *stream) {
+  TOCR_ENTRY();
+  TOCR_REQUIRE(n_maps >= 0 && h > 0 && w > 0 && max_boxes > 0,
+               "tocr_db_postprocess: bad sizes n_maps=%d h=%d w=%d max_boxes=%d", n_maps, h, w,
+               max_boxes);
+  TOCR_REQUIRE((long long)h * w < (1ll << 30), "tocr_db_postprocess: map of %dx%d too large", h, w);
+  TOCR_REQUIRE(w <= 32 * kMaxWords, "tocr_db_postprocess: map width %d exceeds %d", w,
+               32 * kMaxWords);
+  if (n_maps == 0) return TOCR_OK;
+  TOCR_REQUIRE(d_pred && d_workspace && d_boxes && d_scores && d_counts && d_status,
+               "tocr_db_postprocess: null pointer");
+  default_caps(n_maps, h, w, &point_cap, &offset_cap);
+  const DbLayout L = db_layout(n_maps, h, w, point_cap, offset_cap);
+  TOCR_REQUIRE(workspace_bytes >= L.total,
+               "tocr_db_postprocess: workspace of %zu bytes, %zu needed", workspace_bytes, L.total);
+  TOCR_REQUIRE(aligned(d_workspace, 256), "tocr_db_postprocess: workspace must be 256-byte aligned");
+  cudaStream_t st = as_stream(stream);
+  char *ws = static_cast<char *>(d_workspace);
+  auto at = [&](size_t off) { return ws + off; };
+  uint8_t *bitmap = (uint8_t *)at(L.bitmap);
+  int *lab = (int *)at(L.lab);
+  int *row_count = (int *)at(L.row_count), *row_off = (int *)at(L.row_off);
+  int *n_contours = (int *)at(L.n_contours), *n_total = (int *)at(L.n_total);
+  int *starts = (int *)at(L.starts), *npts = (int *)at(L.npts);
+  long long *pt_off = (long long *)at(L.pt_off), *off_off = (long long *)at(L.off_off);
+  P2 *pts = (P2 *)at(L.pts), *hullbuf = (P2 *)at(L.hullbuf), *ring = (P2 *)at(L.ring),
+     *hull2 = (P2 *)at(L.hull2);
+  HP *hpw = (HP *)at(L.hpw), *hpw2 = (HP *)at(L.hpw2);
+  float *fsc = (float *)at(L.fsc), *fsc2 = (float *)at(L.fsc2), *score = (float *)at(L.score);
+  int *stage1 = (int *)at(L.stage1), *stage2 = (int *)at(L.stage2), *offcap = (int *)at(L.offcap),
+      *keep2 = (int *)at(L.keep2), *boxes = (int *)at(L.boxes);
+  int4 *aabb = (int4 *)at(L.aabb);
+  double *dist = (double *)at(L.dist);
+
+  DbParams P{n_maps, h, w, thresh, box_thresh, unclip_ratio, min_box_side, min_unclipped_side,
+             point_cap, offset_cap, max_boxes};
+  const long long C = (long long)n_maps * kMaxCand;
+  const unsigned cgrid = (unsigned)((C + 127) / 128);
+  const dim3 tiles((w + kTileW - 1) / kTileW, (h + kTileH - 1) / kTileH, n_maps);
+
+  cudaError_t e = cudaMemsetAsync(d_status, 0, sizeof(int), st);
+  if (e != cudaSuccess) return set_error(TOCR_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+  ccl_local_kernel<<<tiles, 256, 0, st>>>(d_pred, bitmap, lab, h, w, thresh);
+  ccl_merge_kernel<<<tiles, 128, 0, st>>>(bitmap, lab, h, w);
+  ccl_rows_kernel<<<dim3(h, n_maps), 256, 0, st>>>(lab, row_count, h, w);
+  starts_scan_kernel<<<n_maps, kScanThreads, 0, st>>>(row_count, row_off, n_contours, n_total, h);
+  starts_write_kernel<<<dim3(h, n_maps), 256, 0, st>>>(lab, bitmap, row_count, row_off, starts, h, w);
+  trace_kernel<false><<<cgrid, 128, 0, st>>>(bitmap, starts, n_contours, npts, pt_off, pts,
+                                              d_status, point_cap, n_maps, h, w);
+  scan_kernel<int><<<1, kScanThreads, 0, st>>>(npts, pt_off, C);
+  check_cap_kernel<<<1, 1, 0, st>>>(pt_off, C, point_cap, d_status, kErrPointPool);
+  trace_kernel<true><<<cgrid, 128, 0, st>>>(bitmap, starts, n_contours, npts, pt_off, pts,
+                                             d_status, point_cap, n_maps, h, w);
+  geom_box1_kernel<<<cgrid, 128, 0, st>>>(n_contours, npts, pt_off, pts, hpw, hullbuf, fsc,
+                                          stage1, aabb, P);
+  score_kernel<<<(unsigned)C, kScoreThreads, 0, st>>>(d_pred, stage1, aabb, npts, pt_off, pts,
+                                                       stage2, score, dist, P);
+  unclip_kernel<true><<<cgrid, 128, 0, st>>>(stage2, npts, pt_off, pts, hullbuf, dist, offcap,
+                                             off_off, ring, hpw2, hull2, fsc2, d_geometry, keep2,
+                                             boxes, P);
+  scan_kernel<int><<<1, kScanThreads, 0, st>>>(offcap, off_off, C);
+  check_cap_kernel<<<1, 1, 0, st>>>(off_off, C, offset_cap, d_status, kErrOffsetPool);
+  unclip_kernel<false><<<cgrid, 128, 0, st>>>(stage2, npts, pt_off, pts, hullbuf, dist, offcap,
+                                              off_off, ring, hpw2, hull2, fsc2, d_geometry, keep2,
+                                              boxes, P);
+  compact_kernel<<<n_maps, kScanThreads, 0, st>>>(keep2, boxes, score, d_boxes, d_scores, d_counts,
+                                                  d_status, max_boxes);
+  return check_launch("tocr_db_postprocess");
+}
+
+// Labels of the first three stages, for tests and tools: labels[m][y][x] =
+// 0 for background joined to the image frame, else 1 + the raster index of
+// the smallest pixel of the pixel's component (foreground 8-connected,
+// background 4-connected). d_bitmap receives the 0/255 threshold bitmap.
+TOCR_API int tocr_db_components(const float *d_pred, int n_maps, int h, int w, float thresh,
+                                int *d_labels, uint8_t *d_bitmap, void *stream) {
+  TOCR_ENTRY();
+  TOCR_REQUIRE(n_maps >= 0 && h > 0 && w > 0 && (long long)h * w < (1ll << 30),
+               "tocr_db_components: bad sizes n_maps=%d h=%d w=%d", n_maps, h, w);
+  if (n_maps == 0) return TOCR_OK;
+  TOCR_REQUIRE(d_pred && d_labels && d_bitmap, "tocr_db_components: null pointer");
+  cudaStream_t st = as_stream(stream);
+  const dim3 tiles((w + kTileW - 1) / kTileW, (h + kTileH - 1) / kTileH, n_maps);
+  ccl_local_kernel<<<tiles, 256, 0, st>>>(d_pred, d_bitmap, d_labels, h, w, thresh);
+  ccl_merge_kernel<<<tiles, 128, 0, st>>>(d_bitmap, d_labels, h, w);
+  ccl_rows_kernel<<<dim3(h, n_maps), 256, 0, st>>>(d_labels, nullptr, h, w);
+  return check_launch("tocr_db_components");
+}
+
+}  // extern "C"

@@ -134,7 +134,8 @@ TG long long cross3(const HP &o, const HP &a, const HP &b) {
 }
 
 // Strict convex hull (no collinear or repeated points) of pts[0..n), in the
-// orientation and with the starting vertex of cv::convexHull(clockwise=false):
+// orientation and with the starting vertex of cv::convexHull(clockwise=false)
+// (a repeated point counts with its first index):
 // when the input indices of the hull vertices are cyclically increasing the
 // hull starts at the smallest index, when cyclically decreasing at the
 // largest, otherwise at the vertex with the largest (x, y). `work` needs
@@ -145,6 +146,12 @@ TG int convex_hull(const P2 *pts, int n, HP *work, P2 *hull) {
   HP *h = work + n;        // hull chain, up to n+1 entries
   for (int i = 0; i < n; ++i) s[i] = HP{pts[i].x, pts[i].y, i};
   hp_sort(s, n);
+  {  // repeated points: keep the first occurrence (smallest input index)
+    int u = 1;
+    for (int i = 1; i < n; ++i)
+      if (s[i].x != s[u - 1].x || s[i].y != s[u - 1].y) s[u++] = s[i];
+    n = u;
+  }
   int k = 0;
   for (int i = 0; i < n; ++i) {  // lower chain
     while (k >= 2 && cross3(h[k - 2], h[k - 1], s[i]) <= 0) --k;
@@ -206,6 +213,24 @@ TG RRect normalize_rect(RRect r, double deg) {
   return r;
 }
 
+// d1 / sqrt(l1) > d2 / sqrt(l2), exactly (l1, l2 > 0; |d| <= 2^31 * 2^31).
+TG bool cos_greater(long long d1, long long l1, long long d2, long long l2) {
+  if ((d1 >= 0) != (d2 >= 0)) return d1 >= 0 && !(d1 == 0 && d2 == 0);
+  const unsigned long long a1 = (unsigned long long)(d1 < 0 ? -d1 : d1);
+  const unsigned long long a2 = (unsigned long long)(d2 < 0 ? -d2 : d2);
+  // compare a1^2 * l2 against a2^2 * l1 in 192-bit-safe steps via 128-bit parts
+  const unsigned __int128 s1 = (unsigned __int128)a1 * a1, s2 = (unsigned __int128)a2 * a2;
+  // s * l can exceed 128 bits only for coordinates beyond 2^20; split l
+  const unsigned long long L2 = (unsigned long long)l2, L1 = (unsigned long long)l1;
+  const unsigned __int128 lo1 = (s1 & 0xffffffffffffffffull) * L2, hi1 = (s1 >> 64) * L2;
+  const unsigned __int128 lo2 = (s2 & 0xffffffffffffffffull) * L1, hi2 = (s2 >> 64) * L1;
+  const unsigned __int128 t1 = hi1 + (lo1 >> 64), t2 = hi2 + (lo2 >> 64);
+  const unsigned long long b1 = (unsigned long long)lo1, b2 = (unsigned long long)lo2;
+  const bool gt = t1 > t2 || (t1 == t2 && b1 > b2);
+  const bool lt = t1 < t2 || (t1 == t2 && b1 < b2);
+  return d1 >= 0 ? gt : lt;  // both non-negative: larger magnitude wins
+}
+
 // cv::minAreaRect on a hull produced by convex_hull (rotating calipers in
 // float; edge lengths and orientation tests in double).
 TG RRect min_area_rect(const P2 *hull, int n, float *scratch /* 3n floats */,
@@ -261,31 +286,43 @@ TG RRect min_area_rect(const P2 *hull, int n, float *scratch /* 3n floats */,
     }
   }
   float ba = orientation, bb = 0.f;  // current caliper direction (a, b)
+  // The same direction as an exact integer vector: the edge that set it.
+  long long Bx = orientation > 0 ? 1 : -1, By = 0;
   int seq[4] = {bottom, right, top, left};
   float minarea = 3.402823466e+38f;
   int best_left = 0, best_bottom = 0;
   float best_a = 0.f, best_b = 0.f, best_w = 0.f, best_h = 0.f;
   for (int k = 0; k < n; ++k) {
-    float dp[4];
-    dp[0] = ba * vx[seq[0]] + bb * vy[seq[0]];
-    dp[1] = -bb * vx[seq[1]] + ba * vy[seq[1]];
-    dp[2] = -ba * vx[seq[2]] - bb * vy[seq[2]];
-    dp[3] = bb * vx[seq[3]] - ba * vy[seq[3]];
-    float maxcos = dp[0] * ilen[seq[0]];
-    int main = 0;
-    for (int i = 1; i < 4; ++i) {
-      const float c = dp[i] * ilen[seq[i]];
-      if (c > maxcos) {
-        main = i;
-        maxcos = c;
-      }
+    // The caliper whose next edge makes the smallest angle with it advances
+    // (first caliper on exact ties). OpenCV 4.13 makes this choice as exact
+    // geometry, not with the rounded float cosines: compare
+    // dot(caliper_i, e_i) / |e_i| across the four calipers in integers.
+    long long dot[4], len2[4];
+    for (int i = 0; i < 4; ++i) {
+      const int j = seq[i];
+      const int jn = (j + 1 < n) ? j + 1 : 0;
+      const long long ex = (long long)hull[jn].x - hull[j].x, ey = (long long)hull[jn].y - hull[j].y;
+      long long d;
+      if (i == 0) d = Bx * ex + By * ey;
+      else if (i == 1) d = -By * ex + Bx * ey;
+      else if (i == 2) d = -Bx * ex - By * ey;
+      else d = By * ex - Bx * ey;
+      dot[i] = d;
+      len2[i] = ex * ex + ey * ey;
     }
+    int main = 0;
+    for (int i = 1; i < 4; ++i)
+      if (cos_greater(dot[i], len2[i], dot[main], len2[main])) main = i;
     const int pi = seq[main];
     const float lx = vx[pi] * ilen[pi], ly = vy[pi] * ilen[pi];
-    if (main == 0) { ba = lx; bb = ly; }
-    else if (main == 1) { ba = ly; bb = -lx; }
-    else if (main == 2) { ba = -lx; bb = -ly; }
-    else { ba = -ly; bb = lx; }
+    {
+      const int jn = (pi + 1 < n) ? pi + 1 : 0;
+      const long long ex = (long long)hull[jn].x - hull[pi].x, ey = (long long)hull[jn].y - hull[pi].y;
+      if (main == 0) { ba = lx; bb = ly; Bx = ex; By = ey; }
+      else if (main == 1) { ba = ly; bb = -lx; Bx = ey; By = -ex; }
+      else if (main == 2) { ba = -lx; bb = -ly; Bx = -ex; By = -ey; }
+      else { ba = -ly; bb = lx; Bx = -ey; By = ex; }
+    }
     seq[main] = (seq[main] + 1 == n) ? 0 : seq[main] + 1;
     float dx = (float)hull[seq[1]].x - (float)hull[seq[3]].x;
     float dy = (float)hull[seq[1]].y - (float)hull[seq[3]].y;
@@ -409,6 +446,29 @@ TG void poly_row_spans(const P2 *p, int n, int y, int *xs, const SPAN &span) {
     xs[j + 1] = v;
   }
   for (int i = 0; i + 1 < nc; i += 2) span(xs[i], xs[i + 1]);
+}
+
+// The same pixel set as poly_row_spans without sorting, for bitmask fills:
+// edge(x0, x1) for every edge run (inclusive, unordered) and cross(x) for
+// every crossing of the half-open rule. The row's mask is the edge runs plus
+// the pixels where the count of crossings at or left of them is odd (the
+// closing crossing of each inside run is itself an edge pixel).
+template <class EDGE, class CROSS>
+TG void poly_row_marks(const P2 *p, int n, int y, int i0, int i1, const EDGE &edge,
+                       const CROSS &cross) {
+  for (int i = i0; i < i1; ++i) {
+    const P2 a = p[i], b = p[(i + 1 < n) ? i + 1 : 0];
+    if (a.y == b.y) {
+      if (a.y == y) edge(a.x, b.x);
+      continue;
+    }
+    const int ylo = a.y < b.y ? a.y : b.y, yhi = a.y < b.y ? b.y : a.y;
+    if (y < ylo || y > yhi) continue;
+    const int dx = b.x - a.x, dy = b.y - a.y;
+    const int x = a.x + (y - a.y) * (dx == 0 ? 0 : (dx > 0 ? 1 : -1)) * (dy > 0 ? 1 : -1);
+    edge(x, x);
+    if (y < yhi) cross(x);
+  }
 }
 
 // ------------------------------------------------- area / arc length -----------

@@ -102,3 +102,65 @@ def preprocess_batch(meta: PreprocessMeta, out: torch.Tensor, mean=None, inv_std
 def cuda_batch_threshold_to_u8(src: torch.Tensor, dst: torch.Tensor, w: int, h: int,
                                batch: int, thresh: float, stream=None) -> None:
     call("tocr_threshold_u8", _ptr(src), _ptr(dst), w, h, batch, float(thresh), _stream(stream))
+
+
+# ---- subsystem 3 ------------------------------------------------------------
+
+DB_STATUS_BITS = {1: "point pool full", 2: "border walk exceeded its bound",
+                  4: "offset pool full", 8: "more boxes than max_boxes (truncated)"}
+
+
+class DbPostprocess:
+    """Device DB post-process for batches of [n_maps, h, w] fp32 maps
+    (extract_boxes_from_bitmap, src/detection/det_postprocess.cpp:145-222,
+    with the threshold fused). Owns its workspace and output buffers; the
+    defaults are the reference's (thresh 0.3, box_thresh 0.6, unclip 1.5,
+    kMinBoxSide 3, kMinUnclippedSide 5 — paddle_det.h:62-63)."""
+
+    def __init__(self, n_maps: int, h: int, w: int, device, max_boxes: int = 1000,
+                 thresh: float = 0.3, box_thresh: float = 0.6, unclip_ratio: float = 1.5,
+                 min_box_side: float = 3.0, min_unclipped_side: float = 5.0,
+                 point_cap: int = 0, offset_cap: int = 0):
+        from ._lib import lib
+        self.n_maps, self.h, self.w, self.max_boxes = n_maps, h, w, max_boxes
+        self.params = (thresh, box_thresh, unclip_ratio, min_box_side, min_unclipped_side)
+        self.caps = (point_cap, offset_cap)
+        nbytes = lib().tocr_db_workspace_bytes(n_maps, h, w, point_cap, offset_cap)
+        self.workspace = torch.empty(nbytes + 256, dtype=torch.uint8, device=device)
+        off = (-self.workspace.data_ptr()) % 256
+        self.ws_ptr, self.ws_bytes = self.workspace.data_ptr() + off, nbytes
+        self.boxes = torch.zeros(n_maps, max_boxes, 4, 2, dtype=torch.int32, device=device)
+        self.scores = torch.zeros(n_maps, max_boxes, dtype=torch.float32, device=device)
+        self.counts = torch.zeros(n_maps, dtype=torch.int32, device=device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def __call__(self, pred: torch.Tensor, geometry: torch.Tensor | None = None,
+                 stream=None) -> None:
+        n, h, w = pred.shape
+        assert pred.dtype == torch.float32 and (h, w) == (self.h, self.w) and n <= self.n_maps
+        call("tocr_db_postprocess", _ptr(pred), n, h, w, _ptr(geometry), *self.params,
+             *self.caps, self.ws_ptr, self.ws_bytes, _ptr(self.boxes), _ptr(self.scores),
+             _ptr(self.counts), self.max_boxes, _ptr(self.status), _stream(stream))
+
+    def results(self, n: int | None = None) -> list[list[tuple[list[list[int]], float]]]:
+        """Per map: [(quad [[x, y] * 4], score)] in contour order (synchronises)."""
+        st = int(self.status.item())
+        if st & 7:
+            msgs = [m for b, m in DB_STATUS_BITS.items() if st & b]
+            raise RuntimeError("tocr_db_postprocess: " + ", ".join(msgs))
+        n = self.n_maps if n is None else n
+        counts = self.counts[:n].cpu().tolist()
+        boxes = self.boxes[:n].cpu()
+        scores = self.scores[:n].cpu()
+        return [[(boxes[m, k].tolist(), float(scores[m, k])) for k in range(counts[m])]
+                for m in range(n)]
+
+
+def db_components(pred: torch.Tensor, thresh: float = 0.3, stream=None):
+    """(labels int32 [n, h, w], bitmap u8 [n, h, w]) of the labelling stage."""
+    n, h, w = pred.shape
+    labels = torch.empty(n, h, w, dtype=torch.int32, device=pred.device)
+    bitmap = torch.empty(n, h, w, dtype=torch.uint8, device=pred.device)
+    call("tocr_db_components", _ptr(pred), n, h, w, thresh, _ptr(labels), _ptr(bitmap),
+         _stream(stream))
+    return labels, bitmap
