@@ -165,6 +165,63 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
 TOCR_API int tocr_db_components(const float *d_pred, int n_maps, int h, int w, float thresh,
                                 int *d_labels, uint8_t *d_bitmap, void *stream);
 
+/* ---- recognition crops (replace the host-side crop loop of PaddleRec) ----- */
+
+/* compute_crop_transform (include/turbo_ocr/common/geometry/perspective.h:25-67,
+ * perspective_math.h:16-47) for every detected quad of n_pages pages, on the
+ * device. d_boxes int [n_pages][max_boxes][4][2] and d_counts [n_pages] as
+ * written by tocr_db_postprocess. Crops are numbered page-major; d_crop_off
+ * [n_pages + 1] receives their offsets (total at [n_pages]); per crop:
+ * d_minv [9] (M_inv), d_crop_w (resize width, clamped to [1, max_width]),
+ * d_crop_page (page index), d_vertical (rotated vertical text). */
+TOCR_API int tocr_crop_transforms(const int *d_boxes, const int *d_counts, int n_pages,
+                                  int max_boxes, int target_h, int max_width, int *d_crop_off,
+                                  float *d_minv, int *d_crop_w, int *d_crop_page,
+                                  int *d_vertical, void *stream);
+
+/* batch_roi_warp_kernel / cuda_batch_roi_warp (src/kernels/preprocess_kernels.cu:211-344)
+ * over crops of several same-size pages (u8 HWC, page i at d_pages + i *
+ * page_stride, row pitch src_step), fp16 NCHW out [max_crops][3][dst_h][dst_w].
+ * The crop count is read from *d_n_crops (at most max_crops). mean3 /
+ * inv_std3 NULL = the rec defaults (0.5, 2.0); inv_scale = 1/255. */
+TOCR_API int tocr_roi_warp_f16(const uint8_t *d_pages, long long page_stride, int src_h,
+                               int src_w, int src_step, const float *d_minv, const int *d_crop_w,
+                               const int *d_crop_page, const int *d_n_crops, int max_crops,
+                               int dst_h, int dst_w, const float *mean3, const float *inv_std3,
+                               float inv_scale, void *d_dst, void *stream);
+
+/* tocr_ctc_greedy_f16 for a line count that lives on the device: lines
+ * [0, min(*d_batch, max_batch)) of d_logits [max_batch][seq_len][num_classes]
+ * are decoded (no counterpart in the reference, whose batch is a host int). */
+TOCR_API int tocr_ctc_greedy_f16_dev(const void *d_logits, const int *d_batch, int max_batch,
+                                     int seq_len, int num_classes, int num_labels,
+                                     int *d_tokens, int *d_lengths, float *d_line_scores,
+                                     int *d_step_idx, float *d_step_prob, void *stream);
+
+/* ---- end-to-end page path (config 5) --------------------------------------- */
+
+/* Det preprocessing of same-size u8 HWC pages at scale 1 (the reference's
+ * resize is then the identity; normalisation as preprocess_kernels.cu:169-177)
+ * fused with the backbone stem: 3x3 stride-2 pad-1 conv 3->32 + folded BN +
+ * hardswish, fp16 NHWC out [n][(h-1)/2+1][(w-1)/2+1][32]. d_params is a
+ * device copy of a tocr_stem_pack blob (no counterpart in the reference,
+ * whose backbone runs inside TensorRT). */
+TOCR_API size_t tocr_stem_params_bytes(void);
+TOCR_API int tocr_stem_pack(const float *w, const float *b, const float *mean3,
+                            const float *inv_std3, void *out, size_t out_bytes);
+TOCR_API int tocr_stem_f16(const uint8_t *d_pages, int n, int h, int w, long long page_stride,
+                           const void *d_params, void *d_out, void *stream);
+
+/* Synthetic DB probability map of config 5 (no trained det head exists):
+ * sigmoid(gain * (max_{|dx|<=7} ink(x+dx, y) - 0.5)), ink = 1 - mean(RGB)/255,
+ * fp32 [n][h][w]. */
+TOCR_API int tocr_ink_map(const uint8_t *d_pages, int n, int h, int w, long long page_stride,
+                          float gain, float *d_prob, void *stream);
+
+/* 1x1 conv c->1 + bias + sigmoid over fp16 NHWC pixels (the det head). */
+TOCR_API int tocr_head_sigmoid(const void *d_x, long long npix, int c, const float *d_w,
+                               float bias, float *d_out, void *stream);
+
 /* ---- subsystem 2: fused depthwise-3x3 + pointwise-1x1 block ------------- */
 
 /* Replaces one DW-separable block of the det backbone that the reference runs
@@ -178,7 +235,7 @@ TOCR_API int tocr_db_components(const float *d_pred, int n_maps, int h, int w, f
  * d_err (device int, caller-zeroed) receives a non-zero code if a bounded
  * device-side wait gave up (the launch itself still returns TOCR_OK).
  * Supported (C, C_out, stride): (128,256,1) (128,128,1) (64,128,1)
- * (64,64,1) (32,64,1). */
+ * (64,64,1) (32,64,1) and stride 2 for (64,64) (128,128) (64,128) (32,64). */
 TOCR_API int tocr_dwpw_block(const void *d_x, void *d_y, int N, int H, int W,
                              int C, int C_out, int stride, int kind,
                              const void *d_packed, int *d_err, void *stream);

@@ -5,6 +5,7 @@
 // arithmetic of the B200 kernels to the reference kernel's bits.
 #include <exception>
 
+#include "turbo_ocr/decode/gpu_image.h"
 #include "turbo_ocr/kernels/kernels.h"
 
 extern "C" {
@@ -37,6 +38,22 @@ int refk_threshold(const float *src, unsigned char *dst, int w, int h, int batch
   try {
     turbo_ocr::kernels::cuda_batch_threshold_to_u8(src, dst, w, h, batch, t,
                                                    (cudaStream_t)stream);
+  } catch (const std::exception &) {
+    return 2;
+  }
+  return 0;
+}
+
+int refk_roi_warp(const void *src, int rows, int cols, long long step, const float *minv,
+                  const int *crop_w, float *dst, int batch, int dst_h, int dst_w, void *stream) {
+  try {
+    turbo_ocr::GpuImage img;
+    img.data = const_cast<void *>(src);
+    img.step = (std::size_t)step;
+    img.rows = rows;
+    img.cols = cols;
+    turbo_ocr::kernels::cuda_batch_roi_warp(img, minv, crop_w, dst, batch, dst_h, dst_w,
+                                            (cudaStream_t)stream);
   } catch (const std::exception &) {
     return 2;
   }

@@ -13,6 +13,27 @@ HDR = ROOT / "turboocr_b200" / "csrc" / "db_geom.cuh"
 OUT = ROOT / "tests" / "native" / "_build" / "libdbgeom_host.so"
 
 _lib = None
+_crop = None
+CROP_SRC = ROOT / "tests" / "native" / "crop_host.cpp"
+CROP_HDR = ROOT / "turboocr_b200" / "csrc" / "crop_geom.cuh"
+CROP_OUT = ROOT / "tests" / "native" / "_build" / "libcrop_host.so"
+
+
+def crop_lib():
+    """Host build of crop_geom.cuh (no FMA contraction beyond its explicit fma())."""
+    global _crop
+    if _crop is not None:
+        return _crop
+    CROP_OUT.parent.mkdir(exist_ok=True)
+    if not CROP_OUT.exists() or CROP_OUT.stat().st_mtime < max(CROP_SRC.stat().st_mtime,
+                                                               CROP_HDR.stat().st_mtime):
+        subprocess.run(["g++", "-std=c++17", "-O2", "-ffp-contract=off", "-fPIC", "-shared",
+                        f"-I{CROP_HDR.parent}", "-o", str(CROP_OUT), str(CROP_SRC)], check=True)
+    L = C.CDLL(str(CROP_OUT))
+    L.crop_host_transform.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
+                                      C.c_void_p]
+    _crop = L
+    return L
 
 
 def lib():

@@ -35,15 +35,15 @@ def plane_errors(y: torch.Tensor, ref: torch.Tensor):
     return float((d / r).max()), float(e)
 
 
-def run_block(cuda, N, H, W, C, CO, kind, seed=0):
+def run_block(cuda, N, H, W, C, CO, kind, seed=0, stride=1):
     params = bb.make_block_params(C, CO, seed)
-    blk = bb.DwPwBlock(params, kind, 1, cuda)
+    blk = bb.DwPwBlock(params, kind, stride, cuda)
     g = torch.Generator(device="cpu").manual_seed(seed + 1)
     x = torch.randn(N, H, W, C, generator=g).to(torch.float16).to(cuda)
     y = blk(x)
     torch.cuda.synchronize()
     assert int(blk.err.item()) == 0
-    ref = bb.reference_block(x, params, 1, wpw=blk.dequantized_pw())
+    ref = bb.reference_block(x, params, stride, wpw=blk.dequantized_pw())
     return y, ref, blk, x, params
 
 
@@ -59,6 +59,17 @@ def test_block_shapes(cuda, kind, C, CO):
 def test_partial_tiles_and_odd_sizes(cuda, kind):
     # 37 x 53: partial 8x16 tiles on both axes; TMA clips the stores
     y, ref, *_ = run_block(cuda, 3, 37, 53, 128, 256, kind, seed=5)
+    nw, el = plane_errors(y, ref)
+    assert nw <= TOL and el <= EL_TOL[kind], (nw, el)
+
+
+@pytest.mark.parametrize("kind", [bb.KIND_INT8, bb.KIND_FP8])
+@pytest.mark.parametrize("C,CO", [(64, 64), (128, 128), (64, 128), (32, 64)])
+@pytest.mark.parametrize("hw", [(48, 64), (37, 53), (120, 120)])
+def test_stride2(cuda, kind, C, CO, hw):
+    """Stride-2 blocks of the end-to-end backbone (pad 1, Ho = (H-1)/2 + 1)."""
+    y, ref, *_ = run_block(cuda, 2, hw[0], hw[1], C, CO, kind, seed=C + 7 * CO, stride=2)
+    assert y.shape == ref.shape
     nw, el = plane_errors(y, ref)
     assert nw <= TOL and el <= EL_TOL[kind], (nw, el)
 

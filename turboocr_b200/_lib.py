@@ -67,6 +67,15 @@ SIGNATURES: dict[str, tuple] = {
     "tocr_db_postprocess": (_i, [_vp, _i, _i, _i, _vp, _f, _f, _f, _f, _f, _ll, _ll, _vp,
                                  C.c_size_t, _vp, _vp, _vp, _i, _vp, _vp]),
     "tocr_db_components": (_i, [_vp, _i, _i, _i, _f, _vp, _vp, _vp]),
+    "tocr_stem_params_bytes": (C.c_size_t, []),
+    "tocr_stem_pack": (_i, [_vp, _vp, _vp, _vp, _vp, C.c_size_t]),
+    "tocr_stem_f16": (_i, [_vp, _i, _i, _i, _ll, _vp, _vp, _vp]),
+    "tocr_ink_map": (_i, [_vp, _i, _i, _i, _ll, _f, _vp, _vp]),
+    "tocr_head_sigmoid": (_i, [_vp, _ll, _i, _vp, _f, _vp, _vp]),
+    "tocr_crop_transforms": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "tocr_roi_warp_f16": (_i, [_vp, _ll, _i, _i, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _f,
+                               _vp, _vp]),
+    "tocr_ctc_greedy_f16_dev": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp]),
 }
 
 SYNTH_SIGNATURES: dict[str, tuple] = {
@@ -75,6 +84,8 @@ SYNTH_SIGNATURES: dict[str, tuple] = {
     "tocr_synth_normal_f16": (_i, [_vp, _ll, _f, _u64, _u64, _vp]),
     "tocr_synth_ctc_logits": (_i, [_vp, _vp, _i, _i, _i, _u64, _vp]),
     "tocr_synth_db_map_host": (_i, [_vp, _i, _i, _i, _i, _u64, _u64]),
+    "tocr_synth_pages": (_i, [_vp, _i, _i, _i, _u64, _ll, _vp]),
+    "tocr_synth_rec_logits": (_i, [_vp, _vp, _i, _i, _i, _u64, _vp]),
 }
 
 

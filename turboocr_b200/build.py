@@ -31,7 +31,7 @@ COMMON = ["-O3", "-lineinfo", "-std=c++20", "-Xcompiler", "-fPIC", "-Xcompiler",
 
 LIBS = {
     "libtocr_b200.so": ["capi_common.cu", "ctc.cu", "preprocess.cu", "threshold.cu", "dwpw.cu",
-                        "db.cu"],
+                        "db.cu", "pagekernels.cu", "crop.cu"],
     "libtocr_synth.so": ["synth.cu"],
 }
 # C++ host sources (reference-signature shims), built into libtocr_b200.so.
@@ -45,9 +45,10 @@ def _newest_header() -> float:
     return max((h.stat().st_mtime for h in HEADERS), default=0.0)
 
 
-# Per-file extra flags. db.cu must not contract multiply-adds: its geometry
-# reproduces OpenCV's and Clipper's floating-point operation order.
-EXTRA = {"db.cu": ["-fmad=false"]}
+# Per-file extra flags. db.cu and crop.cu must not contract multiply-adds:
+# they reproduce the floating-point operation order of OpenCV, Clipper and
+# the reference's host geometry (explicit fma() where those contract).
+EXTRA = {"db.cu": ["-fmad=false"], "crop.cu": ["-fmad=false"]}
 
 
 def _compile(src: Path, obj: Path, verbose: bool) -> None:

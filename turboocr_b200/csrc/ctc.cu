@@ -102,8 +102,10 @@ __device__ __forceinline__ void soft_merge(SoftAcc &a, float om, int omi, float 
 
 __global__ void __launch_bounds__(kRowsThreads)
 ctc_rows_f16_kernel(const __half *__restrict__ logits, long long rows, int V,
-                    int *__restrict__ step_idx, float *__restrict__ step_prob) {
+                    int *__restrict__ step_idx, float *__restrict__ step_prob,
+                    const int *__restrict__ d_batch = nullptr, int T = 0) {
   const int lane = threadIdx.x & 31;
+  if (d_batch) rows = min(rows, (long long)(*d_batch) * T);
   const long long warps_total = (long long)gridDim.x * (kRowsThreads / 32);
   for (long long r = (long long)blockIdx.x * (kRowsThreads / 32) + (threadIdx.x >> 5);
        r < rows; r += warps_total) {
@@ -213,11 +215,13 @@ constexpr int kCollapseWarps = 4;
 __global__ void __launch_bounds__(kCollapseWarps * 32)
 ctc_collapse_kernel(const int *__restrict__ step_idx, const float *__restrict__ step_prob,
                     int batch, int T, int num_labels, int *__restrict__ tokens,
-                    int *__restrict__ lengths, float *__restrict__ scores) {
+                    int *__restrict__ lengths, float *__restrict__ scores,
+                    const int *__restrict__ d_batch = nullptr) {
   __shared__ float s_prob[kCollapseWarps][32];
   const int lane = threadIdx.x & 31;
   const int w = threadIdx.x >> 5;
   const int line = blockIdx.x * kCollapseWarps + w;
+  if (d_batch) batch = min(batch, *d_batch);
   if (line >= batch) return;
   const long long base = (long long)line * T;
   int carry = -1;  // last_index before the first step
@@ -317,6 +321,34 @@ TOCR_API int tocr_ctc_greedy_f16(const void *d_logits, int batch_size, int seq_l
   ctc_collapse_kernel<<<blocks, kCollapseWarps * 32, 0, as_stream(stream)>>>(
       d_step_idx, d_step_prob, batch_size, seq_len, num_labels, d_tokens, d_lengths,
       d_line_scores);
+  return check_launch("ctc_collapse_kernel");
+}
+
+// tocr_ctc_greedy_f16 for a batch whose size lives on the device (e.g. the
+// crop count of a detection stage, so the call can sit in a CUDA graph):
+// lines [0, min(*d_batch, max_batch)) are decoded, the rest untouched.
+TOCR_API int tocr_ctc_greedy_f16_dev(const void *d_logits, const int *d_batch, int max_batch,
+                                     int seq_len, int num_classes, int num_labels,
+                                     int *d_tokens, int *d_lengths, float *d_line_scores,
+                                     int *d_step_idx, float *d_step_prob, void *stream) {
+  TOCR_ENTRY();
+  TOCR_REQUIRE(max_batch >= 0 && seq_len > 0 && num_classes > 0,
+               "tocr_ctc_greedy_f16_dev: bad sizes max_batch=%d seq_len=%d classes=%d",
+               max_batch, seq_len, num_classes);
+  if (max_batch == 0) return TOCR_OK;
+  TOCR_REQUIRE(d_logits && d_batch && d_tokens && d_lengths && d_line_scores && d_step_idx &&
+                   d_step_prob, "tocr_ctc_greedy_f16_dev: null pointer");
+  TOCR_REQUIRE(aligned(d_logits, 2), "tocr_ctc_greedy_f16_dev: logits must be 2-byte aligned");
+  const long long rows = (long long)max_batch * seq_len;
+  ctc_rows_f16_kernel<<<rows_grid(ctc_rows_f16_kernel, rows), kRowsThreads, 0, as_stream(stream)>>>(
+      reinterpret_cast<const __half *>(d_logits), rows, num_classes, d_step_idx, d_step_prob,
+      d_batch, seq_len);
+  int st = check_launch("ctc_rows_f16_kernel");
+  if (st != TOCR_OK) return st;
+  const int blocks = (max_batch + kCollapseWarps - 1) / kCollapseWarps;
+  ctc_collapse_kernel<<<blocks, kCollapseWarps * 32, 0, as_stream(stream)>>>(
+      d_step_idx, d_step_prob, max_batch, seq_len, num_labels, d_tokens, d_lengths,
+      d_line_scores, d_batch);
   return check_launch("ctc_collapse_kernel");
 }
 

@@ -572,6 +572,10 @@ int dispatch(int C, int CO, int S, const void *x, void *y, int N, int H, int W,
   TOCR_DWPW(64, 64, 1, 64, 2, 2)
   TOCR_DWPW(32, 64, 1, 32, 2, 2)
   TOCR_DWPW(128, 128, 1, 64, 2, 2)
+  TOCR_DWPW(64, 64, 2, 64, 1, 2)
+  TOCR_DWPW(128, 128, 2, 64, 1, 2)
+  TOCR_DWPW(64, 128, 2, 64, 1, 2)
+  TOCR_DWPW(32, 64, 2, 32, 2, 2)
 #undef TOCR_DWPW
   return set_error(TOCR_ERR_INVALID, "tocr_dwpw_block: unsupported shape C=%d C_out=%d stride=%d",
                    C, CO, S);

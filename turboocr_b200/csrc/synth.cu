@@ -97,6 +97,90 @@ __global__ void ctc_plant_kernel(__half *logits, const int *plan, long long rows
   if (lane == 0) row[pi] = __float2half_rn(m + 2.0f);
 }
 
+// ---- config-5 pages ------------------------------------------------------------
+// Page m: white (255) u8 HWC. n_lines ~ U{30..80} text lines at a pitch of
+// H / n_lines; line i: glyph height ~ U{6..min(14, pitch - 3)}, left margin
+// U{16..160}, length U{120..W - 40 - left}; glyphs are black (0) rectangles of
+// width U{4..10} separated by 2 px inside a word; words of U{2..8} glyphs are
+// separated by U{6..12} px. One CTA per (line slot, page); thread 0 lays the
+// line out, all threads paint it.
+constexpr int kMaxGlyphs = 512;
+
+__global__ void __launch_bounds__(256)
+page_lines_kernel(uint8_t *pages, int H, int W, uint64_t seed, long long first_page) {
+  const long long m = blockIdx.y;
+  const int line = blockIdx.x;
+  const uint64_t st = 5000 + (uint64_t)(first_page + m);
+  const int n_lines = unif_int(hash3(seed, st, 0), 30, 80);
+  if (line >= n_lines) return;
+  __shared__ int gx0[kMaxGlyphs], gx1[kMaxGlyphs];
+  __shared__ int s_ng, s_y0, s_y1;
+  if (threadIdx.x == 0) {
+    const uint64_t ls = ((uint64_t)(first_page + m) << 8) + (uint64_t)line;
+    uint64_t ctr = 0;
+    const float pitch = (float)H / (float)n_lines;
+    const int hmax = min(14, (int)pitch - 3);
+    const int gh = unif_int(hash3(seed, ls, ctr++), 6, max(6, hmax));
+    const int yc = (int)((line + 0.5f) * pitch);
+    s_y0 = max(0, yc - gh / 2);
+    s_y1 = min(H, s_y0 + gh);
+    const int left = unif_int(hash3(seed, ls, ctr++), 16, 160);
+    const int len = unif_int(hash3(seed, ls, ctr++), 120, max(120, W - 40 - left));
+    const int end = min(W - 8, left + len);
+    int x = left, ng = 0;
+    while (x < end && ng < kMaxGlyphs) {
+      const int nw = unif_int(hash3(seed, ls, ctr++), 2, 8);
+      for (int g = 0; g < nw && x < end && ng < kMaxGlyphs; ++g) {
+        const int gw = unif_int(hash3(seed, ls, ctr++), 4, 10);
+        gx0[ng] = x;
+        gx1[ng] = min(end, x + gw);
+        ++ng;
+        x += gw + 2;
+      }
+      x += unif_int(hash3(seed, ls, ctr++), 6, 12) - 2;
+    }
+    s_ng = ng;
+  }
+  __syncthreads();
+  uint8_t *pg = pages + m * (long long)H * W * 3;
+  const int rows = s_y1 - s_y0;
+  for (int g = 0; g < s_ng; ++g) {
+    const int w = gx1[g] - gx0[g];
+    for (int i = threadIdx.x; i < w * rows * 3; i += blockDim.x) {
+      const int c = i % 3, px = (i / 3) % w, ry = (i / 3) / w;
+      pg[((long long)(s_y0 + ry) * W + gx0[g] + px) * 3 + c] = 0;
+    }
+  }
+}
+
+// ---- stand-in recognition logits for the crops of config 5 ----------------------
+// Row (crop c, step t): uniform noise in [-4, 4) with a planted value 8 at the
+// row's token, a blank (0) or a label in U{1..V-1} held for 3 steps. One
+// thread per 8 values; rows of crops >= *n_crops are not written.
+__global__ void __launch_bounds__(256)
+rec_logits_kernel(__half *logits, const int *n_crops, int max_crops, int T, int V,
+                  uint64_t seed) {
+  const long long rows_all = (long long)max_crops * T;
+  const long long rows = min(rows_all, (long long)(*n_crops) * T);
+  const long long per_row = (V + 7) / 8;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < rows * per_row;
+       i += stride) {
+    const long long r = i / per_row;
+    const int j0 = (int)(i % per_row) * 8;
+    const long long c = r / T;
+    const int t = (int)(r % T);
+    const uint64_t th = hash3(seed, 7000 + (uint64_t)c, (uint64_t)(t / 3));
+    const int tok = (th & 1) ? 0 : unif_int(th, 1, V - 1);
+    __half *row = logits + r * V;
+    const uint64_t h = hash3(seed, 9000 + (uint64_t)c, (uint64_t)t * per_row + j0 / 8);
+    for (int k = 0; k < 8 && j0 + k < V; ++k) {
+      const float u = (float)((h >> (8 * k)) & 0xFF) * (8.0f / 256.0f) - 4.0f;
+      row[j0 + k] = __float2half_rn(j0 + k == tok ? 8.0f : u);
+    }
+  }
+}
+
 }  // namespace synth
 
 using namespace synth;
@@ -171,6 +255,28 @@ TOCR_API int tocr_synth_db_map_host(float *out, int H, int W, int kmin, int kmax
       }
   }
   return k;
+}
+
+// Config-5 pages u8 [n][H][W][3] (pages first_page .. first_page + n - 1).
+TOCR_API int tocr_synth_pages(void *d_pages, int n, int H, int W, uint64_t seed,
+                              long long first_page, void *cuda_stream) {
+  if (n <= 0) return 0;
+  cudaStream_t s = (cudaStream_t)cuda_stream;
+  if (cudaMemsetAsync(d_pages, 255, (size_t)n * H * W * 3, s) != cudaSuccess) return 2;
+  page_lines_kernel<<<dim3(80, n), 256, 0, s>>>((uint8_t *)d_pages, H, W, seed, first_page);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
+}
+
+// Stand-in recognition logits fp16 [max_crops][T][V] for the first *d_n_crops crops.
+TOCR_API int tocr_synth_rec_logits(void *d_logits, const int *d_n_crops, int max_crops, int T,
+                                   int V, uint64_t seed, void *cuda_stream) {
+  if (max_crops <= 0) return 0;
+  const long long work = (long long)max_crops * T * ((V + 7) / 8);
+  const long long need = (work + 255) / 256;
+  const int grid = (int)(need < 148 * 16 ? need : 148 * 16);
+  rec_logits_kernel<<<grid, 256, 0, (cudaStream_t)cuda_stream>>>(
+      (__half *)d_logits, d_n_crops, max_crops, T, V, seed);
+  return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 
 }  // extern "C"
