@@ -47,6 +47,7 @@ def lib():
     L = C.CDLL(str(OUT))
     vp, i, d = C.c_void_p, C.c_int, C.c_double
     L.dbh_trace.argtypes = [vp, i, i, i, i, i, vp, i]
+    L.dbh_trace_bits.argtypes = [vp, i, i, i, i, i, vp, i]
     L.dbh_hull.argtypes = [vp, i, vp]
     L.dbh_min_area_rect.argtypes = [vp, i, vp]
     L.dbh_mini_box.argtypes = [vp, i, vp, vp]
@@ -65,12 +66,13 @@ def _pts(p):
     return np.ascontiguousarray(np.asarray(p, dtype=np.int32).reshape(-1, 2))
 
 
-def trace(bm, x0, y0, hole):
+def trace(bm, x0, y0, hole, bits=False):
     bm = np.ascontiguousarray(bm, dtype=np.uint8)
     H, W = bm.shape
     cap = 8 * (H + W) * 4 + 64
     out = np.zeros((cap, 2), np.int32)
-    n = lib().dbh_trace(bm.ctypes.data, H, W, x0, y0, 1 if hole else 0, out.ctypes.data, cap)
+    fn = lib().dbh_trace_bits if bits else lib().dbh_trace
+    n = fn(bm.ctypes.data, H, W, x0, y0, 1 if hole else 0, out.ctypes.data, cap)
     assert 0 <= n <= cap
     return out[:n]
 

@@ -17,6 +17,18 @@ int dbh_trace(const unsigned char *bm, int H, int W, int x0, int y0, int hole, i
   return trace_border(fg, x0, y0, hole != 0, reinterpret_cast<P2 *>(out), cap, 64 * W * H + 64);
 }
 
+// Same walk through the bit-packed neighbourhood provider used on the device.
+int dbh_trace_bits(const unsigned char *bm, int H, int W, int x0, int y0, int hole, int *out,
+                   int cap) {
+  const int words = (W + 31) / 32;
+  std::vector<uint32_t> bits((size_t)H * words, 0u);
+  for (int y = 0; y < H; ++y)
+    for (int x = 0; x < W; ++x)
+      if (bm[y * W + x]) bits[(size_t)y * words + (x >> 5)] |= 1u << (x & 31);
+  NbBits nb{bits.data(), H, W, words};
+  return trace_border_nb(nb, x0, y0, hole != 0, reinterpret_cast<P2 *>(out), cap, 64 * W * H + 64);
+}
+
 int dbh_hull(const int *pts, int n, int *out) {
   std::vector<HP> work(2 * n + 2);
   return convex_hull(reinterpret_cast<const P2 *>(pts), n, work.data(), reinterpret_cast<P2 *>(out));

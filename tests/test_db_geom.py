@@ -68,6 +68,8 @@ def test_contours_match_cv2_on_noise():
                cv2.findContours(bm.copy(), cv2.RETR_LIST, cv2.CHAIN_APPROX_SIMPLE)[0]]
         mine = [dn.trace(bm, x, y, hole).tolist() for y, x, hole in contour_starts(bm)]
         assert mine == ref
+        bits = [dn.trace(bm, x, y, hole, bits=True).tolist() for y, x, hole in contour_starts(bm)]
+        assert bits == ref
 
 
 def test_contours_match_cv2_on_db_maps():
@@ -76,6 +78,17 @@ def test_contours_match_cv2_on_db_maps():
     ref = [c.tolist() for c in do.find_contours(bm)]
     mine = [dn.trace(bm, x, y, hole).tolist() for y, x, hole in contour_starts(bm)]
     assert len(ref) > 3 and mine == ref
+    bits = [dn.trace(bm, x, y, hole, bits=True).tolist() for y, x, hole in contour_starts(bm)]
+    assert bits == ref
+
+
+def test_bit_packed_trace_wide_noise():
+    """Word boundaries of the bit-packed walk (widths above 32 columns)."""
+    for bm in noise_bitmaps(60, 9, hmax=140):
+        ref = [c.reshape(-1, 2).tolist() for c in
+               cv2.findContours(bm.copy(), cv2.RETR_LIST, cv2.CHAIN_APPROX_SIMPLE)[0]]
+        bits = [dn.trace(bm, x, y, hole, bits=True).tolist() for y, x, hole in contour_starts(bm)]
+        assert bits == ref
 
 
 def test_trace_single_pixel_and_frame():

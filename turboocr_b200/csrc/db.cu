@@ -37,7 +37,7 @@ using db::HP;
 using db::P2;
 using db::RRect;
 
-constexpr int kTileW = 32, kTileH = 16, kTilePx = kTileW * kTileH;
+constexpr int kTileW = 32, kTileH = 32, kTilePx = kTileW * kTileH;
 constexpr int kMaxCand = 3000;        // det_postprocess.cpp:165
 constexpr int kScanThreads = 1024;
 
@@ -97,51 +97,72 @@ __device__ __forceinline__ void union_s(int *par, int a, int b) {
   }
 }
 
-// 1. threshold + tile-local labelling. grid (tiles_x, tiles_y, n_maps), 256 threads.
+// 1. threshold + tile-local labelling, run based: a warp owns a tile row, the
+// row's foreground mask is one ballot, and every pixel starts out pointing at
+// the first pixel of its same-colour run. Unions are then only made where runs
+// of consecutive rows meet: at the first pixel of an overlap (one of the two
+// pixels there starts its run), plus the diagonal contacts of foreground runs
+// (NW at a run start, NE at a run end). grid (tiles_x, tiles_y, n_maps),
+// 256 threads (8 warps x 4 rows).
 __global__ void __launch_bounds__(256)
 ccl_local_kernel(const float *__restrict__ pred, uint8_t *__restrict__ bitmap, int *__restrict__ lab,
-                 int H, int W, float thresh) {
-  __shared__ uint8_t fg[kTileH][kTileW];
+                 uint32_t *__restrict__ bits, int H, int W, float thresh) {
+  __shared__ unsigned s_fg[kTileH];     // per tile row: foreground bits (bit = lx)
+  __shared__ unsigned s_start[kTileH];  // per tile row: run-start bits
   __shared__ int par[kTilePx];
   const int m = blockIdx.z;
   const size_t base = (size_t)m * H * W;
   const int tx0 = blockIdx.x * kTileW, ty0 = blockIdx.y * kTileH;
-  for (int l = threadIdx.x; l < kTilePx; l += blockDim.x) {
-    const int lx = l % kTileW, ly = l / kTileW;
-    const int x = tx0 + lx, y = ty0 + ly;
-    uint8_t v = 0;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int x = tx0 + lane;
+  const unsigned in_row = (W - tx0 >= 32) ? 0xffffffffu : ((1u << (W - tx0)) - 1u);
+  for (int ly = warp; ly < kTileH; ly += 8) {
+    const int y = ty0 + ly;
+    bool f = false;
     if (x < W && y < H) {
-      v = pred[base + (size_t)y * W + x] > thresh;
-      bitmap[base + (size_t)y * W + x] = v ? 255 : 0;
+      f = pred[base + (size_t)y * W + x] > thresh;
+      bitmap[base + (size_t)y * W + x] = f ? 255 : 0;
     }
-    fg[ly][lx] = v;
-    par[l] = l + 1;
+    const unsigned fg = __ballot_sync(0xffffffffu, f) & in_row;
+    // run starts: first pixel of the tile row, or colour differs from the left
+    const unsigned diff = (fg ^ (fg << 1)) | 1u;
+    const unsigned starts = diff & in_row;
+    if (lane == 0) {
+      s_fg[ly] = fg;
+      s_start[ly] = starts;
+      if (bits && y < H) bits[((size_t)m * H + y) * ((W + 31) >> 5) + blockIdx.x] = fg;
+    }
+    // run start at or left of this lane
+    const unsigned upto = starts & (lane == 31 ? 0xffffffffu : ((2u << lane) - 1u));
+    const int rs = 31 - __clz(upto);
+    par[ly * kTileW + lane] = ly * kTileW + rs + 1;
   }
   __syncthreads();
-  for (int l = threadIdx.x; l < kTilePx; l += blockDim.x) {
-    const int lx = l % kTileW, ly = l / kTileW;
-    const int x = tx0 + lx, y = ty0 + ly;
+  for (int ly = warp; ly < kTileH; ly += 8) {
+    const int y = ty0 + ly;
     if (x >= W || y >= H) continue;
-    const int me = l + 1;
-    if (fg[ly][lx]) {
-      if (lx > 0 && fg[ly][lx - 1]) union_s(par, me, me - 1);
-      if (ly > 0) {
-        if (fg[ly - 1][lx]) union_s(par, me, me - kTileW);
-        if (lx > 0 && fg[ly - 1][lx - 1]) union_s(par, me, me - kTileW - 1);
-        if (lx + 1 < kTileW && x + 1 < W && fg[ly - 1][lx + 1]) union_s(par, me, me - kTileW + 1);
+    const unsigned fg = s_fg[ly], st = s_start[ly];
+    const bool f = (fg >> lane) & 1u;
+    const bool is_start = (st >> lane) & 1u;
+    const bool is_end = lane == 31 || x == W - 1 || (((st >> (lane + 1)) & 1u) != 0);
+    const int me = ly * kTileW + lane + 1;
+    if (ly > 0) {
+      const unsigned fu = s_fg[ly - 1], su = s_start[ly - 1];
+      const bool fn = (fu >> lane) & 1u;
+      if (fn == f && (is_start || ((su >> lane) & 1u))) union_s(par, me, me - kTileW);
+      if (f) {
+        if (is_start && lane > 0 && ((fu >> (lane - 1)) & 1u)) union_s(par, me, me - kTileW - 1);
+        if (is_end && lane < 31 && x + 1 < W && ((fu >> (lane + 1)) & 1u))
+          union_s(par, me, me - kTileW + 1);
       }
-    } else {
-      if (lx > 0 && !fg[ly][lx - 1]) union_s(par, me, me - 1);
-      if (ly > 0 && !fg[ly - 1][lx]) union_s(par, me, me - kTileW);
-      if (x == 0 || y == 0 || x == W - 1 || y == H - 1) union_s(par, me, 0);
     }
+    if (!f && (((y == 0 || y == H - 1) && is_start) || x == 0 || x == W - 1)) union_s(par, me, 0);
   }
   __syncthreads();
-  for (int l = threadIdx.x; l < kTilePx; l += blockDim.x) {
-    const int lx = l % kTileW, ly = l / kTileW;
-    const int x = tx0 + lx, y = ty0 + ly;
+  for (int ly = warp; ly < kTileH; ly += 8) {
+    const int y = ty0 + ly;
     if (x >= W || y >= H) continue;
-    const int r = find_s(par, l + 1);
+    const int r = find_s(par, ly * kTileW + lane + 1);
     int g = 0;
     if (r != 0) {
       const int rl = r - 1;
@@ -299,19 +320,12 @@ starts_write_kernel(const int *__restrict__ lab, const uint8_t *__restrict__ bit
   }
 }
 
-struct FgMap {
-  const uint8_t *bm;
-  int H, W;
-  __device__ bool operator()(int x, int y) const {
-    return x >= 0 && y >= 0 && x < W && y < H && bm[(size_t)y * W + x] != 0;
-  }
-};
 
 // 5. border following. One thread per contour slot (m * 3000 + rank).
 // write == false: count points into npts; write == true: store them at pt_off.
 template <bool kWrite>
 __global__ void __launch_bounds__(128)
-trace_kernel(const uint8_t *__restrict__ bitmap, const int *__restrict__ starts,
+trace_kernel(const uint32_t *__restrict__ bits, const int *__restrict__ starts,
              const int *__restrict__ n_contours, int *__restrict__ npts,
              const long long *__restrict__ pt_off, P2 *__restrict__ pts, int *__restrict__ status,
              long long point_cap, int n_maps, int H, int W) {
@@ -324,17 +338,18 @@ trace_kernel(const uint8_t *__restrict__ bitmap, const int *__restrict__ starts,
   }
   const int rec = starts[c];
   const int sp = rec >> 1;
-  const FgMap fg{bitmap + (size_t)m * H * W, H, W};
+  const int words = (W + 31) >> 5;
+  db::NbBits nb{bits + (size_t)m * H * words, H, W, words};
   const long long ms = 4ll * H * W + 16;
   const int max_steps = ms > 0x7fffffffll ? 0x7fffffff : (int)ms;
   if (!kWrite) {
-    const int n = db::trace_border(fg, sp % W, sp / W, (rec & 1) != 0, nullptr, 0, max_steps);
+    const int n = db::trace_border_nb(nb, sp % W, sp / W, (rec & 1) != 0, nullptr, 0, max_steps);
     if (n < 0) atomicOr(status, kErrTrace);
     npts[c] = n < 0 ? 0 : n;
   } else {
     const int n = npts[c];
     if (n == 0 || pt_off[c] + n > point_cap) return;
-    db::trace_border(fg, sp % W, sp / W, (rec & 1) != 0, pts + pt_off[c], n, max_steps);
+    db::trace_border_nb(nb, sp % W, sp / W, (rec & 1) != 0, pts + pt_off[c], n, max_steps);
   }
 }
 
@@ -634,7 +649,7 @@ namespace tocr {
 namespace {
 
 struct DbLayout {
-  size_t bitmap, lab, row_count, row_off, n_contours, n_total, starts, npts, pt_off, pts, hpw,
+  size_t bitmap, bits, lab, row_count, row_off, n_contours, n_total, starts, npts, pt_off, pts, hpw,
       hullbuf, fsc, stage1, aabb, stage2, score, dist, offcap, off_off, ring, hpw2, hull2, fsc2,
       keep2, boxes, total;
 };
@@ -648,6 +663,7 @@ DbLayout db_layout(int n_maps, int h, int w, long long point_cap, long long offs
   size_t o = 0;
   auto take = [&](size_t bytes) { const size_t at = o; o = align_up(o + bytes); return at; };
   L.bitmap = take(px);
+  L.bits = take((size_t)n_maps * h * ((w + 31) / 32) * 4);
   L.lab = take(px * 4);
   L.row_count = take((size_t)n_maps * h * 4);
   L.row_off = take((size_t)n_maps * h * 4);
@@ -722,6 +738,7 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
   char *ws = static_cast<char *>(d_workspace);
   auto at = [&](size_t off) { return ws + off; };
   uint8_t *bitmap = (uint8_t *)at(L.bitmap);
+  uint32_t *bits = (uint32_t *)at(L.bits);
   int *lab = (int *)at(L.lab);
   int *row_count = (int *)at(L.row_count), *row_off = (int *)at(L.row_off);
   int *n_contours = (int *)at(L.n_contours), *n_total = (int *)at(L.n_total);
@@ -744,16 +761,16 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
 
   cudaError_t e = cudaMemsetAsync(d_status, 0, sizeof(int), st);
   if (e != cudaSuccess) return set_error(TOCR_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
-  ccl_local_kernel<<<tiles, 256, 0, st>>>(d_pred, bitmap, lab, h, w, thresh);
+  ccl_local_kernel<<<tiles, 256, 0, st>>>(d_pred, bitmap, lab, bits, h, w, thresh);
   ccl_merge_kernel<<<tiles, 128, 0, st>>>(bitmap, lab, h, w);
   ccl_rows_kernel<<<dim3(h, n_maps), 256, 0, st>>>(lab, row_count, h, w);
   starts_scan_kernel<<<n_maps, kScanThreads, 0, st>>>(row_count, row_off, n_contours, n_total, h);
   starts_write_kernel<<<dim3(h, n_maps), 256, 0, st>>>(lab, bitmap, row_count, row_off, starts, h, w);
-  trace_kernel<false><<<cgrid, 128, 0, st>>>(bitmap, starts, n_contours, npts, pt_off, pts,
+  trace_kernel<false><<<cgrid, 128, 0, st>>>(bits, starts, n_contours, npts, pt_off, pts,
                                               d_status, point_cap, n_maps, h, w);
   scan_kernel<int><<<1, kScanThreads, 0, st>>>(npts, pt_off, C);
   check_cap_kernel<<<1, 1, 0, st>>>(pt_off, C, point_cap, d_status, kErrPointPool);
-  trace_kernel<true><<<cgrid, 128, 0, st>>>(bitmap, starts, n_contours, npts, pt_off, pts,
+  trace_kernel<true><<<cgrid, 128, 0, st>>>(bits, starts, n_contours, npts, pt_off, pts,
                                              d_status, point_cap, n_maps, h, w);
   geom_box1_kernel<<<cgrid, 128, 0, st>>>(n_contours, npts, pt_off, pts, hpw, hullbuf, fsc,
                                           stage1, aabb, P);
@@ -785,7 +802,7 @@ TOCR_API int tocr_db_components(const float *d_pred, int n_maps, int h, int w, f
   TOCR_REQUIRE(d_pred && d_labels && d_bitmap, "tocr_db_components: null pointer");
   cudaStream_t st = as_stream(stream);
   const dim3 tiles((w + kTileW - 1) / kTileW, (h + kTileH - 1) / kTileH, n_maps);
-  ccl_local_kernel<<<tiles, 256, 0, st>>>(d_pred, d_bitmap, d_labels, h, w, thresh);
+  ccl_local_kernel<<<tiles, 256, 0, st>>>(d_pred, d_bitmap, d_labels, nullptr, h, w, thresh);
   ccl_merge_kernel<<<tiles, 128, 0, st>>>(d_bitmap, d_labels, h, w);
   ccl_rows_kernel<<<dim3(h, n_maps), 256, 0, st>>>(d_labels, nullptr, h, w);
   return check_launch("tocr_db_components");

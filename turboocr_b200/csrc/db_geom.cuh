@@ -52,17 +52,22 @@ TG int code_dy(int d) { return (d >= 1 && d <= 3) ? -1 : (d >= 5) ? 1 : 0; }
 // the W side) or the foreground pixel left of the raster-first pixel of a
 // hole (hole border, previous pixel on the E side). Points are emitted where
 // the chain code changes (CHAIN_APPROX_SIMPLE); the start pixel is always
-// emitted. fg(x, y) must return false outside the image. Writes at most cap
-// points and returns the full count, or -1 if max_steps was exceeded.
-template <class FG>
-TG int trace_border(const FG &fg, int x0, int y0, bool hole, P2 *out, int cap, int max_steps) {
+// emitted. nb(x, y) returns the 8-neighbourhood of (x, y) as a bit mask
+// (bit d set when the neighbour in chain-code direction d is foreground;
+// outside the image counts as background). Writes at most cap points and
+// returns the full count, or -1 if max_steps was exceeded.
+template <class NB>
+TG int trace_border_nb(NB &nb, int x0, int y0, bool hole, P2 *out, int cap, int max_steps) {
   const int dstart = hole ? 0 : 4;
   int d1 = -1;
-  for (int k = 1; k <= 8; ++k) {  // clockwise from the previous pixel
-    const int d = (dstart - k) & 7;
-    if (fg(x0 + code_dx(d), y0 + code_dy(d))) {
-      d1 = d;
-      break;
+  {
+    const unsigned m0 = nb(x0, y0);
+    for (int k = 1; k <= 8; ++k) {  // clockwise from the previous pixel
+      const int d = (dstart - k) & 7;
+      if ((m0 >> d) & 1u) {
+        d1 = d;
+        break;
+      }
     }
   }
   int n = 0;
@@ -74,10 +79,11 @@ TG int trace_border(const FG &fg, int x0, int y0, bool hole, P2 *out, int cap, i
   int last_code = d1 ^ 4;
   int x3 = x0, y3 = y0, dback = d1;
   for (int step = 0; step < max_steps; ++step) {
+    const unsigned m = nb(x3, y3);
     int d4 = dback;
     for (int k = 1; k <= 8; ++k) {  // counter-clockwise after the previous pixel
       const int d = (dback + k) & 7;
-      if (fg(x3 + code_dx(d), y3 + code_dy(d))) {
+      if ((m >> d) & 1u) {
         d4 = d;
         break;
       }
@@ -95,6 +101,64 @@ TG int trace_border(const FG &fg, int x0, int y0, bool hole, P2 *out, int cap, i
   }
   return -1;
 }
+
+// Neighbourhood mask from a per-pixel predicate fg(x, y).
+template <class FG>
+struct NbFromFg {
+  const FG &fg;
+  TG unsigned operator()(int x, int y) const {
+    unsigned m = 0;
+    for (int d = 0; d < 8; ++d) m |= (fg(x + code_dx(d), y + code_dy(d)) ? 1u : 0u) << d;
+    return m;
+  }
+};
+
+template <class FG>
+TG int trace_border(const FG &fg, int x0, int y0, bool hole, P2 *out, int cap, int max_steps) {
+  NbFromFg<FG> nb{fg};
+  return trace_border_nb(nb, x0, y0, hole, out, cap, max_steps);
+}
+
+// Neighbourhood masks from a bit-packed bitmap (bit x & 31 of word
+// y * words + (x >> 5)), caching the 3 x 2 words around the last centre so
+// that a walk along a row reloads once per 32 pixels.
+struct NbBits {
+  const uint32_t *bits;
+  int H, W, words;
+  int cy = -1000000, cw = -1000000;
+  uint32_t r[3][2];
+  TG unsigned operator()(int x, int y) {
+    const int w0 = (x - 1) >> 5;  // arithmetic shift: x - 1 = -1 gives -1
+    if (y != cy || w0 != cw) {
+      cy = y;
+      cw = w0;
+      for (int i = 0; i < 3; ++i) {
+        const int yy = y - 1 + i;
+        const bool row_ok = yy >= 0 && yy < H;
+        r[i][0] = (row_ok && w0 >= 0 && w0 < words) ? bits[(long long)yy * words + w0] : 0u;
+        r[i][1] = (row_ok && w0 + 1 < words) ? bits[(long long)yy * words + w0 + 1] : 0u;
+      }
+    }
+    const int sh = (x - 1) - (w0 << 5);  // bit of column x - 1 inside word w0, 0..31
+    uint32_t t[3];
+    for (int i = 0; i < 3; ++i) {
+      const unsigned long long both = ((unsigned long long)r[i][1] << 32) | r[i][0];
+      t[i] = (uint32_t)(both >> sh) & 7u;  // columns x-1, x, x+1
+    }
+    // columns beyond the image width read 0: the bitmap is zero-padded per row
+    // directions: 0 E (x+1,y) 1 NE (x+1,y-1) 2 N 3 NW 4 W 5 SW 6 S 7 SE
+    unsigned m = 0;
+    m |= ((t[1] >> 2) & 1u) << 0;
+    m |= ((t[0] >> 2) & 1u) << 1;
+    m |= ((t[0] >> 1) & 1u) << 2;
+    m |= ((t[0] >> 0) & 1u) << 3;
+    m |= ((t[1] >> 0) & 1u) << 4;
+    m |= ((t[2] >> 0) & 1u) << 5;
+    m |= ((t[2] >> 1) & 1u) << 6;
+    m |= ((t[2] >> 2) & 1u) << 7;
+    return m;
+  }
+};
 
 // --------------------------------------------------------------- sorting ----
 struct HP {  // hull candidate: point + index in the input sequence

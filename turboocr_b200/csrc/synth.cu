@@ -155,28 +155,41 @@ page_lines_kernel(uint8_t *pages, int H, int W, uint64_t seed, long long first_p
 
 // ---- stand-in recognition logits for the crops of config 5 ----------------------
 // Row (crop c, step t): uniform noise in [-4, 4) with a planted value 8 at the
-// row's token, a blank (0) or a label in U{1..V-1} held for 3 steps. One
-// thread per 8 values; rows of crops >= *n_crops are not written.
+// row's token, a blank (0) or a label in U{1..V-1} held for 3 steps. The
+// buffer is written as flat 16-byte chunks (rows are only 2-byte aligned for
+// odd V); rows of crops >= *n_crops are not written.
+__device__ __forceinline__ int rec_token(uint64_t seed, long long c, int t, int V) {
+  const uint64_t th = hash3(seed, 7000 + (uint64_t)c, (uint64_t)(t / 3));
+  return (th & 1) ? 0 : unif_int(th, 1, V - 1);
+}
+
 __global__ void __launch_bounds__(256)
 rec_logits_kernel(__half *logits, const int *n_crops, int max_crops, int T, int V,
                   uint64_t seed) {
-  const long long rows_all = (long long)max_crops * T;
-  const long long rows = min(rows_all, (long long)(*n_crops) * T);
-  const long long per_row = (V + 7) / 8;
+  const long long n_el = (long long)min(*n_crops, max_crops) * T * V;
+  const long long n_chunks = (n_el + 7) / 8;
   const long long stride = (long long)gridDim.x * blockDim.x;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < rows * per_row;
-       i += stride) {
-    const long long r = i / per_row;
-    const int j0 = (int)(i % per_row) * 8;
-    const long long c = r / T;
-    const int t = (int)(r % T);
-    const uint64_t th = hash3(seed, 7000 + (uint64_t)c, (uint64_t)(t / 3));
-    const int tok = (th & 1) ? 0 : unif_int(th, 1, V - 1);
-    __half *row = logits + r * V;
-    const uint64_t h = hash3(seed, 9000 + (uint64_t)c, (uint64_t)t * per_row + j0 / 8);
-    for (int k = 0; k < 8 && j0 + k < V; ++k) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n_chunks; i += stride) {
+    const long long e0 = i * 8;
+    long long r = e0 / V;
+    int j = (int)(e0 - r * V);
+    int tok = rec_token(seed, r / T, (int)(r % T), V);
+    const uint64_t h = hash3(seed, 9000, (uint64_t)i);
+    __align__(16) __half v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
       const float u = (float)((h >> (8 * k)) & 0xFF) * (8.0f / 256.0f) - 4.0f;
-      row[j0 + k] = __float2half_rn(j0 + k == tok ? 8.0f : u);
+      v[k] = __float2half_rn(j == tok ? 8.0f : u);
+      if (++j == V) {
+        j = 0;
+        ++r;
+        tok = rec_token(seed, r / T, (int)(r % T), V);
+      }
+    }
+    if (e0 + 8 <= n_el) {
+      *reinterpret_cast<uint4 *>(logits + e0) = *reinterpret_cast<const uint4 *>(v);
+    } else {
+      for (int k = 0; e0 + k < n_el; ++k) logits[e0 + k] = v[k];
     }
   }
 }
@@ -271,7 +284,8 @@ TOCR_API int tocr_synth_pages(void *d_pages, int n, int H, int W, uint64_t seed,
 TOCR_API int tocr_synth_rec_logits(void *d_logits, const int *d_n_crops, int max_crops, int T,
                                    int V, uint64_t seed, void *cuda_stream) {
   if (max_crops <= 0) return 0;
-  const long long work = (long long)max_crops * T * ((V + 7) / 8);
+  if ((reinterpret_cast<uintptr_t>(d_logits) & 15) != 0) return 1;
+  const long long work = ((long long)max_crops * T * V + 7) / 8;
   const long long need = (work + 255) / 256;
   const int grid = (int)(need < 148 * 16 ? need : 148 * 16);
   rec_logits_kernel<<<grid, 256, 0, (cudaStream_t)cuda_stream>>>(

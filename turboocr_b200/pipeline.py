@@ -89,7 +89,9 @@ class PagePipeline:
         self.step_idx = torch.empty(nc * REC_T, dtype=torch.int32, device=device)
         self.step_prob = torch.empty(nc * REC_T, dtype=torch.float32, device=device)
         # kernels launched per run() (for the bench's gpu_launches count)
-        self.launches_per_run = 1 + 1 + len(SCHEDULE) + 1 + 1 + 17 + 2 + 1 + 1 + 2 + 1
+        # stem + blocks + head + ink + DB (1 memset + 16 kernels) + crops (2) + warp
+        # + stand-in rec logits + CTC (2)
+        self.launches_per_run = 1 + len(SCHEDULE) + 1 + 1 + 16 + 2 + 1 + 1 + 2
 
     def run(self, pages: torch.Tensor, stream=None) -> None:
         """Enqueue the whole path for pages u8 [B, H, W, 3] (device)."""
@@ -97,8 +99,6 @@ class PagePipeline:
         assert pages.shape == (B, H, W, 3) and pages.dtype == torch.uint8
         st = _stream(stream)
         page_stride = H * W * 3
-        for blk in self.blocks:
-            blk.err.zero_()
         call("tocr_stem_f16", _ptr(pages), B, H, W, page_stride, _ptr(self.stem_blob),
              _ptr(self.acts[0]), st)
         for i, blk in enumerate(self.blocks):
