@@ -353,32 +353,61 @@ trace_kernel(const uint32_t *__restrict__ bits, const int *__restrict__ starts,
   }
 }
 
-// Exclusive scan of n int32 values into int64 offsets, out[n] = total.
-// One CTA of kScanThreads threads (n is at most a few hundred thousand).
+// Exclusive scan of the per-slot counts of n_maps x 3000 contour slots into
+// int64 offsets (out[n] = total), two passes: a per-map scan (one CTA per
+// map, warp shuffles) that leaves the map's total in tot[m], then the map
+// bases added in place.
+__device__ __forceinline__ long long warp_incl_scan(long long v, int lane) {
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const long long t = __shfl_up_sync(0xffffffffu, v, off);
+    if (lane >= off) v += t;
+  }
+  return v;
+}
+
 template <class T>
 __global__ void __launch_bounds__(kScanThreads)
-scan_kernel(const T *__restrict__ in, long long *__restrict__ out, long long n) {
-  __shared__ long long s_part[kScanThreads];
+scan_map_kernel(const T *__restrict__ in, long long *__restrict__ out, long long *__restrict__ tot) {
+  __shared__ long long s_warp[kScanThreads / 32];
   __shared__ long long s_carry;
+  const int m = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const long long base = (long long)m * kMaxCand;
   if (threadIdx.x == 0) s_carry = 0;
   __syncthreads();
-  for (long long c0 = 0; c0 < n; c0 += kScanThreads) {
-    const long long i = c0 + threadIdx.x;
-    const long long v = (i < n) ? (long long)in[i] : 0;
-    s_part[threadIdx.x] = v;
+  for (int c0 = 0; c0 < kMaxCand; c0 += kScanThreads) {
+    const int i = c0 + threadIdx.x;
+    const long long v = i < kMaxCand ? (long long)in[base + i] : 0;
+    const long long incl = warp_incl_scan(v, lane);
+    if (lane == 31) s_warp[warp] = incl;
     __syncthreads();
-    for (int off = 1; off < kScanThreads; off <<= 1) {
-      const long long t = (threadIdx.x >= off) ? s_part[threadIdx.x - off] : 0;
-      __syncthreads();
-      s_part[threadIdx.x] += t;
-      __syncthreads();
+    if (warp == 0) {
+      const long long w = lane < kScanThreads / 32 ? s_warp[lane] : 0;
+      const long long wi = warp_incl_scan(w, lane);
+      if (lane < kScanThreads / 32) s_warp[lane] = wi - w;  // exclusive warp offsets
     }
-    if (i < n) out[i] = s_carry + s_part[threadIdx.x] - v;
     __syncthreads();
-    if (threadIdx.x == kScanThreads - 1) s_carry += s_part[threadIdx.x];
+    if (i < kMaxCand) out[base + i] = s_carry + s_warp[warp] + incl - v;
+    __syncthreads();
+    if (threadIdx.x == kScanThreads - 1) s_carry += s_warp[warp] + incl;
     __syncthreads();
   }
-  if (threadIdx.x == 0) out[n] = s_carry;
+  if (threadIdx.x == 0) tot[m] = s_carry;
+}
+
+__global__ void __launch_bounds__(kScanThreads)
+scan_base_kernel(long long *__restrict__ out, const long long *__restrict__ tot, int n_maps) {
+  __shared__ long long s_base;
+  const int m = blockIdx.x;
+  if (threadIdx.x == 0) {
+    long long b = 0;
+    for (int k = 0; k < m; ++k) b += tot[k];
+    s_base = b;
+    if (m == n_maps - 1) out[(long long)n_maps * kMaxCand] = b + tot[m];
+  }
+  __syncthreads();
+  const long long base = (long long)m * kMaxCand;
+  for (int i = threadIdx.x; i < kMaxCand; i += kScanThreads) out[base + i] += s_base;
 }
 
 __global__ void check_cap_kernel(const long long *__restrict__ off, long long n, long long cap,
@@ -649,7 +678,7 @@ namespace tocr {
 namespace {
 
 struct DbLayout {
-  size_t bitmap, bits, lab, row_count, row_off, n_contours, n_total, starts, npts, pt_off, pts, hpw,
+  size_t bitmap, bits, lab, scan_tot, row_count, row_off, n_contours, n_total, starts, npts, pt_off, pts, hpw,
       hullbuf, fsc, stage1, aabb, stage2, score, dist, offcap, off_off, ring, hpw2, hull2, fsc2,
       keep2, boxes, total;
 };
@@ -665,6 +694,7 @@ DbLayout db_layout(int n_maps, int h, int w, long long point_cap, long long offs
   L.bitmap = take(px);
   L.bits = take((size_t)n_maps * h * ((w + 31) / 32) * 4);
   L.lab = take(px * 4);
+  L.scan_tot = take((size_t)n_maps * 8);
   L.row_count = take((size_t)n_maps * h * 4);
   L.row_off = take((size_t)n_maps * h * 4);
   L.n_contours = take((size_t)n_maps * 4);
@@ -740,6 +770,7 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
   uint8_t *bitmap = (uint8_t *)at(L.bitmap);
   uint32_t *bits = (uint32_t *)at(L.bits);
   int *lab = (int *)at(L.lab);
+  long long *scan_tot = (long long *)at(L.scan_tot);
   int *row_count = (int *)at(L.row_count), *row_off = (int *)at(L.row_off);
   int *n_contours = (int *)at(L.n_contours), *n_total = (int *)at(L.n_total);
   int *starts = (int *)at(L.starts), *npts = (int *)at(L.npts);
@@ -768,7 +799,8 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
   starts_write_kernel<<<dim3(h, n_maps), 256, 0, st>>>(lab, bitmap, row_count, row_off, starts, h, w);
   trace_kernel<false><<<cgrid, 128, 0, st>>>(bits, starts, n_contours, npts, pt_off, pts,
                                               d_status, point_cap, n_maps, h, w);
-  scan_kernel<int><<<1, kScanThreads, 0, st>>>(npts, pt_off, C);
+  scan_map_kernel<int><<<n_maps, kScanThreads, 0, st>>>(npts, pt_off, scan_tot);
+  scan_base_kernel<<<n_maps, kScanThreads, 0, st>>>(pt_off, scan_tot, n_maps);
   check_cap_kernel<<<1, 1, 0, st>>>(pt_off, C, point_cap, d_status, kErrPointPool);
   trace_kernel<true><<<cgrid, 128, 0, st>>>(bits, starts, n_contours, npts, pt_off, pts,
                                              d_status, point_cap, n_maps, h, w);
@@ -779,7 +811,8 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
   unclip_kernel<true><<<cgrid, 128, 0, st>>>(stage2, npts, pt_off, pts, hullbuf, dist, offcap,
                                              off_off, ring, hpw2, hull2, fsc2, d_geometry, keep2,
                                              boxes, P);
-  scan_kernel<int><<<1, kScanThreads, 0, st>>>(offcap, off_off, C);
+  scan_map_kernel<int><<<n_maps, kScanThreads, 0, st>>>(offcap, off_off, scan_tot);
+  scan_base_kernel<<<n_maps, kScanThreads, 0, st>>>(off_off, scan_tot, n_maps);
   check_cap_kernel<<<1, 1, 0, st>>>(off_off, C, offset_cap, d_status, kErrOffsetPool);
   unclip_kernel<false><<<cgrid, 128, 0, st>>>(stage2, npts, pt_off, pts, hullbuf, dist, offcap,
                                               off_off, ring, hpw2, hull2, fsc2, d_geometry, keep2,

@@ -42,6 +42,14 @@ struct F2 {
 };
 
 // ------------------------------------------------------------------ tracing --
+#if defined(__CUDA_ARCH__)
+TG int __builtin_ctz_tg(uint32_t v) { return __ffs((int)v) - 1; }
+TG int __builtin_clz_tg(uint32_t v) { return __clz((int)v); }
+#else
+TG int __builtin_ctz_tg(uint32_t v) { return __builtin_ctz(v); }
+TG int __builtin_clz_tg(uint32_t v) { return __builtin_clz(v); }
+#endif
+
 // Freeman chain codes, image coordinates (y down): 0 E, 1 NE, 2 N, 3 NW,
 // 4 W, 5 SW, 6 S, 7 SE. Increasing code = counter-clockwise on screen.
 TG int code_dx(int d) { return (d == 0 || d == 1 || d == 7) ? 1 : (d >= 3 && d <= 5) ? -1 : 0; }
@@ -98,6 +106,19 @@ TG int trace_border_nb(NB &nb, int x0, int y0, bool hole, P2 *out, int cap, int 
     dback = (d4 + 4) & 7;
     x3 = x4;
     y3 = y4;
+    // Straight horizontal stretches: from (x3, y3), after an E move the walk
+    // keeps moving E while SW, S, SE are background and E is foreground (W
+    // mirrored with NE, N, NW); such moves repeat the chain code, so no point
+    // is emitted. Jump over them (never on the start row, so the closing test
+    // above still sees the last moves).
+    if ((d4 == 0 || d4 == 4) && y3 != y0) {
+      int L = nb.run(x3, y3, d4);
+      if (L > max_steps - step - 1) L = max_steps - step - 1;
+      if (L > 0) {
+        x3 += d4 == 0 ? L : -L;
+        step += L;
+      }
+    }
   }
   return -1;
 }
@@ -110,6 +131,17 @@ struct NbFromFg {
     unsigned m = 0;
     for (int d = 0; d < 8; ++d) m |= (fg(x + code_dx(d), y + code_dy(d)) ? 1u : 0u) << d;
     return m;
+  }
+  // Number of further moves in direction dir (0 E or 4 W) that repeat it.
+  TG int run(int x, int y, int dir) const {
+    const int s = dir == 0 ? 1 : -1, side = dir == 0 ? 1 : -1;  // S row for E, N row for W
+    int L = 0;
+    for (;;) {
+      const int cx = x + s * L;
+      if (fg(cx - 1, y + side) || fg(cx, y + side) || fg(cx + 1, y + side) || !fg(cx + s, y))
+        return L;
+      ++L;
+    }
   }
 };
 
@@ -157,6 +189,52 @@ struct NbBits {
     m |= ((t[2] >> 1) & 1u) << 6;
     m |= ((t[2] >> 2) & 1u) << 7;
     return m;
+  }
+  TG uint32_t word(int y, int w) const {
+    return (y >= 0 && y < H && w >= 0 && w < words) ? bits[(long long)y * words + w] : 0u;
+  }
+  // First column >= x0 whose bit in row y equals v (W if none before the end).
+  TG int find_fwd(int y, int x0, bool v) const {
+    if (x0 < 0) {
+      if (!v) return x0;  // columns left of the image are background
+      x0 = 0;
+    }
+    for (int w = x0 >> 5; w < words; ++w) {
+      uint32_t b = word(y, w);
+      if (!v) b = ~b;
+      if (w == (x0 >> 5)) b &= ~0u << (x0 & 31);
+      if (b) {
+        const int c = (w << 5) + __builtin_ctz_tg(b);
+        return c < W ? c : W;
+      }
+    }
+    return v ? W + 64 : W;  // no set bit: never; no clear bit: columns >= W are background
+  }
+  // Last column <= x0 whose bit in row y equals v (-1 if none).
+  TG int find_bwd(int y, int x0, bool v) const {
+    if (x0 >= W) {
+      if (!v) return x0;  // columns right of the image are background
+      x0 = W - 1;
+    }
+    for (int w = x0 >> 5; w >= 0; --w) {
+      uint32_t b = word(y, w);
+      if (!v) b = ~b;
+      if (w == (x0 >> 5)) b &= (x0 & 31) == 31 ? ~0u : ((2u << (x0 & 31)) - 1u);
+      if (b) return (w << 5) + 31 - __builtin_clz_tg(b);
+    }
+    return v ? -64 : -1;
+  }
+  TG int run(int x, int y, int dir) const {
+    if (dir == 0) {
+      const int a = find_fwd(y + 1, x - 1, true);   // first foreground below, from x-1
+      const int b = find_fwd(y, x + 1, false);      // first background on the row, from x+1
+      const int L = (a < b ? a : b) - x - 1;
+      return L > 0 ? L : 0;
+    }
+    const int a = find_bwd(y - 1, x + 1, true);     // last foreground above, up to x+1
+    const int b = find_bwd(y, x - 1, false);        // last background on the row, up to x-1
+    const int L = x - 1 - (a > b ? a : b);
+    return L > 0 ? L : 0;
   }
 };
 

@@ -154,44 +154,44 @@ page_lines_kernel(uint8_t *pages, int H, int W, uint64_t seed, long long first_p
 }
 
 // ---- stand-in recognition logits for the crops of config 5 ----------------------
-// Row (crop c, step t): uniform noise in [-4, 4) with a planted value 8 at the
-// row's token, a blank (0) or a label in U{1..V-1} held for 3 steps. The
-// buffer is written as flat 16-byte chunks (rows are only 2-byte aligned for
-// odd V); rows of crops >= *n_crops are not written.
+// Row (crop c, step t): noise in [-4, 4) from a fixed 8192-entry table read
+// in flat 16-byte chunks (a pure streaming write), then a planted value 8 at
+// the row's token: a blank (0) or a label in U{1..V-1}, held for 3 steps.
+// Rows of crops >= *n_crops are not written.
 __device__ __forceinline__ int rec_token(uint64_t seed, long long c, int t, int V) {
   const uint64_t th = hash3(seed, 7000 + (uint64_t)c, (uint64_t)(t / 3));
   return (th & 1) ? 0 : unif_int(th, 1, V - 1);
 }
 
+constexpr int kNoiseChunks = 1024;  // table of 1024 x 8 halves
+
 __global__ void __launch_bounds__(256)
-rec_logits_kernel(__half *logits, const int *n_crops, int max_crops, int T, int V,
-                  uint64_t seed) {
-  const long long n_el = (long long)min(*n_crops, max_crops) * T * V;
-  const long long n_chunks = (n_el + 7) / 8;
-  const long long stride = (long long)gridDim.x * blockDim.x;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n_chunks; i += stride) {
-    const long long e0 = i * 8;
-    long long r = e0 / V;
-    int j = (int)(e0 - r * V);
-    int tok = rec_token(seed, r / T, (int)(r % T), V);
+rec_noise_kernel(__half *logits, const int *n_crops, int max_crops, int T, int V, uint64_t seed) {
+  __shared__ uint4 table[kNoiseChunks];
+  for (int i = threadIdx.x; i < kNoiseChunks; i += blockDim.x) {
     const uint64_t h = hash3(seed, 9000, (uint64_t)i);
     __align__(16) __half v[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float u = (float)((h >> (8 * k)) & 0xFF) * (8.0f / 256.0f) - 4.0f;
-      v[k] = __float2half_rn(j == tok ? 8.0f : u);
-      if (++j == V) {
-        j = 0;
-        ++r;
-        tok = rec_token(seed, r / T, (int)(r % T), V);
-      }
-    }
-    if (e0 + 8 <= n_el) {
-      *reinterpret_cast<uint4 *>(logits + e0) = *reinterpret_cast<const uint4 *>(v);
-    } else {
-      for (int k = 0; e0 + k < n_el; ++k) logits[e0 + k] = v[k];
-    }
+    for (int k = 0; k < 8; ++k)
+      v[k] = __float2half_rn((float)((h >> (8 * k)) & 0xFF) * (8.0f / 256.0f) - 4.0f);
+    table[i] = *reinterpret_cast<const uint4 *>(v);
   }
+  __syncthreads();
+  const long long n_el = (long long)min(*n_crops, max_crops) * T * V;
+  const long long n_full = n_el / 8;
+  uint4 *out = reinterpret_cast<uint4 *>(logits);
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n_full; i += stride)
+    out[i] = table[(i * 7 + (i >> 10)) & (kNoiseChunks - 1)];
+  if (blockIdx.x == 0 && threadIdx.x < (int)(n_el - n_full * 8))
+    logits[n_full * 8 + threadIdx.x] = __float2half_rn(0.0f);
+}
+
+__global__ void __launch_bounds__(256)
+rec_plant_kernel(__half *logits, const int *n_crops, int max_crops, int T, int V, uint64_t seed) {
+  const long long rows = (long long)min(*n_crops, max_crops) * T;
+  const long long r = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  logits[r * V + rec_token(seed, r / T, (int)(r % T), V)] = __float2half_rn(8.0f);
 }
 
 }  // namespace synth
@@ -285,11 +285,11 @@ TOCR_API int tocr_synth_rec_logits(void *d_logits, const int *d_n_crops, int max
                                    int V, uint64_t seed, void *cuda_stream) {
   if (max_crops <= 0) return 0;
   if ((reinterpret_cast<uintptr_t>(d_logits) & 15) != 0) return 1;
-  const long long work = ((long long)max_crops * T * V + 7) / 8;
-  const long long need = (work + 255) / 256;
-  const int grid = (int)(need < 148 * 16 ? need : 148 * 16);
-  rec_logits_kernel<<<grid, 256, 0, (cudaStream_t)cuda_stream>>>(
-      (__half *)d_logits, d_n_crops, max_crops, T, V, seed);
+  cudaStream_t s = (cudaStream_t)cuda_stream;
+  rec_noise_kernel<<<148 * 4, 256, 0, s>>>((__half *)d_logits, d_n_crops, max_crops, T, V, seed);
+  const long long rows = (long long)max_crops * T;
+  rec_plant_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>((__half *)d_logits, d_n_crops,
+                                                                  max_crops, T, V, seed);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 
