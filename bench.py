@@ -8,8 +8,11 @@ region is bracketed by a barrier + device synchronise and the reported time
 is the maximum over ranks.
 
 Workloads:
+  e2e         config 5 (default, the headline): 4096 960x960 pages split over the
+              ranks, det + rec path per page (pipeline.PagePipeline)
   ctc         config 2: 512 lines x 80 steps x 18385-class fp16 logits per GPU
   preprocess  config 3: 256 u8 HWC images (sides 600..2000) -> fp16 960x960 NCHW
+  dwpw        config 4: fused DW3x3+PW1x1 block, 32 x 240 x 240 x 128 -> 256, INT8
 """
 from __future__ import annotations
 
@@ -395,7 +398,223 @@ def touched_source_bytes(dims, content):
     return total
 
 
-WORKLOADS = {"ctc": CtcWorkload, "preprocess": PreprocessWorkload, "dwpw": DwPwWorkload}
+class E2eWorkload:
+    """BASELINE config 5 (the headline metric): 4096 synthetic 960x960 pages
+    through preprocess + stem -> 8 INT8 DW+PW blocks -> head -> DB -> crops
+    48x320 -> CTC (T=80, V=18385), split contiguously over the ranks (strong
+    scaling: the job is 4096 pages in total). One step = this rank's whole
+    shard, in micro-batches of 16 pages (turboocr_b200.pipeline.PagePipeline)."""
+    name = "e2e_4096pages_960x960_det_rec"
+    metric = "pages/sec det+rec hot path (960x960)"
+    unit = "pages/s"
+    dtype = "i8 (DW+PW blocks) / f16 activations / f32 DB map"
+    scaling = "strong"
+    TOTAL, MB = 4096, 16
+    l2_note = "pages 2.76 MB each, >= 1.4 GB of input per rank per step > 126 MB L2 (no flush needed)"
+    world = 1
+    rank = 0
+
+    def __init__(self, dev, seed, units=None):
+        from turboocr_b200 import pipeline as pl
+        self.pl = pl
+        self.dev = dev
+        per = units or self.TOTAL // self.world
+        self.n_pages = max(self.MB, (per + self.MB - 1) // self.MB * self.MB)
+        self.units_per_step = self.n_pages
+        self.n_mb = self.n_pages // self.MB
+        self.pipe = pl.PagePipeline(dev, self.MB)
+        first = self.rank * self.n_pages
+        self.pages = torch.empty(self.n_pages, 960, 960, 3, dtype=torch.uint8, device=dev)
+        from turboocr_b200._lib import synth
+        for i in range(0, self.n_pages, 256):
+            n = min(256, self.n_pages - i)
+            assert synth().tocr_synth_pages(self.pages[i].data_ptr(), n, 960, 960, 0x7EC00005,
+                                            first + i, None) == 0
+        torch.cuda.synchronize()
+        self.launches_per_step = self.n_mb * self.pipe.launches_per_run
+        self.algo_bytes = None  # set by dominant_kernel_ms (depends on the crop count)
+
+    def step(self):
+        for i in range(self.n_mb):
+            self.pipe.run(self.pages[i * self.MB:(i + 1) * self.MB])
+
+    def dominant_kernel_ms(self, iters=10):
+        """The CTC decode of one micro-batch's crops (tocr_ctc_greedy_f16_dev:
+        the logits read is the largest single stream of the path)."""
+        from turboocr_b200._lib import call
+        p = self.pipe
+        p.run(self.pages[:self.MB])
+        torch.cuda.synchronize()
+        n_crops = int(p.crop_off[self.MB].item())
+        self.algo_bytes = n_crops * self.pl.REC_T * self.pl.REC_V * 2
+        self.dominant = "ctc_rows_f16_kernel (+ collapse) over one micro-batch's crops"
+        s = torch.cuda.current_stream()
+        nc = p.crop_off[self.MB:]
+
+        def once():
+            call("tocr_ctc_greedy_f16_dev", p.logits.data_ptr(), nc.data_ptr(), p.max_crops,
+                 self.pl.REC_T, self.pl.REC_V, self.pl.REC_V, p.tokens.data_ptr(),
+                 p.lengths.data_ptr(), p.line_scores.data_ptr(), p.step_idx.data_ptr(),
+                 p.step_prob.data_ptr(), s.cuda_stream)
+        once()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(iters):
+            once()
+        e1.record(s)
+        torch.cuda.synchronize()
+        self.crops_per_page = n_crops / self.MB
+        return e0.elapsed_time(e1) / iters
+
+    def path_bytes_per_page(self):
+        """Algorithmic HBM bytes of the whole path per page: stem in/out, every
+        block's input and output, the DB map written and read, crops written,
+        stand-in logits written and read by the decode."""
+        b = 960 * 960 * 3 + 480 * 480 * 32 * 2
+        h, w = 480, 480
+        for c, co, st in self.pl.SCHEDULE:
+            ho, wo = (h - 1) // st + 1, (w - 1) // st + 1
+            b += h * w * c * 2 + ho * wo * co * 2
+            h, w = ho, wo
+        b += 960 * 960 * 3 + 2 * 960 * 960 * 4          # ink map: page read, map write + read
+        crops = getattr(self, "crops_per_page", 58.0)
+        b += crops * (3 * self.pl.REC_H * self.pl.REC_W * 2 + 2 * self.pl.REC_T * self.pl.REC_V * 2)
+        return b
+
+    # end-to-end: pinned host pages -> H2D per micro-batch (double-buffered on a
+    # copy stream) -> path -> D2H of boxes, scores, counts, tokens, line scores
+    def setup_e2e(self):
+        self.n_host = min(self.n_pages, 256)
+        self.h_pages = torch.empty(self.n_host, 960, 960, 3, dtype=torch.uint8, pin_memory=True)
+        self.h_pages.copy_(self.pages[:self.n_host])
+        self.stage = [torch.empty(self.MB, 960, 960, 3, dtype=torch.uint8, device=self.dev)
+                      for _ in range(2)]
+        self.copy_stream = torch.cuda.Stream(self.dev)
+        p = self.pipe
+        self.h_boxes = torch.empty(p.db.boxes.shape, dtype=torch.int32, pin_memory=True)
+        self.h_scores = torch.empty(p.db.scores.shape, dtype=torch.float32, pin_memory=True)
+        self.h_counts = torch.empty(p.db.counts.shape, dtype=torch.int32, pin_memory=True)
+        self.h_tokens = torch.empty(p.tokens.shape, dtype=torch.int32, pin_memory=True)
+        self.h_lengths = torch.empty(p.lengths.shape, dtype=torch.int32, pin_memory=True)
+        self.h_lscores = torch.empty(p.line_scores.shape, dtype=torch.float32, pin_memory=True)
+        self.h2d = self.n_pages * 960 * 960 * 3
+        per_mb = sum(t.numel() * 4 for t in (self.h_boxes, self.h_scores, self.h_counts,
+                                             self.h_tokens, self.h_lengths, self.h_lscores))
+        self.d2h = self.n_mb * per_mb
+
+    def _h2d(self, i, buf):
+        k = (i * self.MB) % self.n_host
+        src = self.h_pages[k:k + self.MB] if k + self.MB <= self.n_host else self.h_pages[:self.MB]
+        buf.copy_(src, non_blocking=True)
+
+    def e2e_step(self):
+        s = torch.cuda.current_stream()
+        ready = [torch.cuda.Event(), torch.cuda.Event()]
+        free = [torch.cuda.Event(), torch.cuda.Event()]
+        with torch.cuda.stream(self.copy_stream):
+            self._h2d(0, self.stage[0])
+            ready[0].record(self.copy_stream)
+        p = self.pipe
+        for i in range(self.n_mb):
+            b = i & 1
+            if i + 1 < self.n_mb:
+                nb = (i + 1) & 1
+                with torch.cuda.stream(self.copy_stream):
+                    if i >= 1:
+                        self.copy_stream.wait_event(free[nb])
+                    self._h2d(i + 1, self.stage[nb])
+                    ready[nb].record(self.copy_stream)
+            s.wait_event(ready[b])
+            p.run(self.stage[b])
+            free[b].record(s)
+            self.h_boxes.copy_(p.db.boxes, non_blocking=True)
+            self.h_scores.copy_(p.db.scores, non_blocking=True)
+            self.h_counts.copy_(p.db.counts, non_blocking=True)
+            self.h_tokens.copy_(p.tokens, non_blocking=True)
+            self.h_lengths.copy_(p.lengths, non_blocking=True)
+            self.h_lscores.copy_(p.line_scores, non_blocking=True)
+
+    def cpu_baseline(self, cores, budget_s=20.0):
+        """The path on the host, stage by stage on one page of the job, all
+        threads: det preprocessing (cv2 restatement of cpu_paddle_det.cpp:53-94),
+        the backbone in torch fp32 (stem + 8 blocks; the reference's CPU backend
+        runs its network in ORT, absent here), DB on the same probability map
+        (cv2 + the reference's Clipper, det_postprocess.cpp:145-222),
+        cv2.warpPerspective crops with the reference's crop transform
+        (cpu_paddle_rec.cpp:80-85), the reference's ctc_decode.cpp on the same
+        logits. Pages/s = 1 / the summed stage times."""
+        import cv2
+        from oracle import ctc_oracle as co
+        from oracle import db_oracle as do
+        from turboocr_b200 import backbone as bb
+        torch.set_num_threads(cores)
+        cv2.setNumThreads(cores)
+        pl = self.pl
+        p = self.pipe
+        p.run(self.pages[:self.MB])
+        torch.cuda.synchronize()
+        page = self.pages[0].cpu().numpy()
+        prob = p.prob[0].cpu().numpy()
+        k0 = int(p.db.counts[0].item())
+        logits = p.logits[:k0].float().cpu().numpy()
+        boxes = p.db.boxes[0, :k0].cpu().numpy()
+        mean = np.array([0.485, 0.456, 0.406], np.float32)
+        istd = 1.0 / np.array([0.229, 0.224, 0.225], np.float32)
+        times = {}
+        t_end = time.perf_counter() + budget_s
+        reps = 0
+        while reps < 1 or (time.perf_counter() < t_end and reps < 3):
+            t = time.perf_counter()
+            x = cv2.resize(page, (960, 960), interpolation=cv2.INTER_LINEAR)
+            x = ((x.astype(np.float32) * (1 / 255.0) - mean) * istd).transpose(2, 0, 1)[None]
+            t1 = time.perf_counter()
+            with torch.no_grad():
+                y = torch.from_numpy(np.ascontiguousarray(x))
+                y = torch.nn.functional.hardswish(torch.nn.functional.conv2d(
+                    y, torch.from_numpy(p.stem_w), torch.from_numpy(p.stem_b), stride=2, padding=1))
+                y = y.permute(0, 2, 3, 1)
+                for blk in p.blocks:
+                    y = bb.reference_block(y, blk.params, blk.stride)
+                head = torch.sigmoid(y @ p.head_w.cpu())
+            t2 = time.perf_counter()
+            dets = do.db_postprocess(prob)
+            t3 = time.perf_counter()
+            for q in boxes:
+                m, cw, _ = _crop_ref(q)
+                cv2.warpPerspective(page, m.reshape(3, 3), (pl.REC_W, pl.REC_H),
+                                    flags=cv2.INTER_LINEAR | cv2.WARP_INVERSE_MAP,
+                                    borderMode=cv2.BORDER_REPLICATE)
+            t4 = time.perf_counter()
+            co.ref_decode_batch(logits, pl.REC_V, cores, simd=True)
+            t5 = time.perf_counter()
+            for k, v in (("preprocess", t1 - t), ("backbone", t2 - t1), ("db", t3 - t2),
+                         ("crops", t4 - t3), ("ctc", t5 - t4)):
+                times[k] = times.get(k, 0.0) + v
+            reps += 1
+            del head, dets
+        per_page = sum(times.values()) / reps
+        return {"value": 1.0 / per_page, "unit": self.unit, "cores": cores, "kind": "port",
+                "sample": f"page 0 x {reps} reps, {k0} crops; stage s/page: " +
+                          ", ".join(f"{k} {v / reps:.3f}" for k, v in times.items())}
+
+
+def _crop_ref(box):
+    """The reference's compute_crop_transform (oracle/_ref/libcrop_ref.so)."""
+    import ctypes as C
+    from oracle._loader import load
+    L = load("_ref/libcrop_ref.so")
+    L.crop_ref_transform.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
+                                     C.c_void_p]
+    b = np.ascontiguousarray(np.asarray(box, np.int32).reshape(8))
+    m = np.zeros(9, np.float32)
+    cw, v = C.c_int(), C.c_int()
+    L.crop_ref_transform(b.ctypes.data, 48, 320, m.ctypes.data, C.byref(cw), C.byref(v))
+    return m, cw.value, v.value
+
+
+WORKLOADS = {"ctc": CtcWorkload, "preprocess": PreprocessWorkload, "dwpw": DwPwWorkload,
+             "e2e": E2eWorkload}
+SEEDS = {"ctc": 1, "preprocess": 2, "dwpw": 3, "e2e": 5}
 
 
 # ------------------------------------------------------------------ main ----
@@ -404,7 +623,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="ctc", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="e2e", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--units", type=int, default=0,
@@ -423,7 +642,10 @@ def main():
         if rank != 0:
             return
         dev = torch.device("cuda", local) if torch.cuda.is_available() else None
-        wl = Wl(dev, 0x7EC00000 + {"ctc": 1, "preprocess": 2, "dwpw": 3}[args.workload], args.units)
+        Wl.world, Wl.rank = 1, 0
+        if args.workload == "e2e":
+            args.units = args.units or Wl.MB
+        wl = Wl(dev, 0x7EC00000 + SEEDS[args.workload], args.units)
         vals = []
         for i in range(args.warmup + args.steps):
             cb = wl.cpu_baseline(cores, budget_s=2.0)
@@ -445,7 +667,8 @@ def main():
                                 timeout=__import__("datetime").timedelta(seconds=120))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    seed = 0x7EC00000 + {"ctc": 1, "preprocess": 2, "dwpw": 3}[args.workload] + 1000 * rank
+    seed = 0x7EC00000 + SEEDS[args.workload] + 1000 * rank
+    Wl.world, Wl.rank = world, rank
     wl = Wl(dev, seed, args.units)
 
     def barrier():
@@ -500,11 +723,12 @@ def main():
         line = {
             "metric": Wl.metric, "value": value, "unit": Wl.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": getattr(Wl, "scaling", "weak"),
+            "vs_baseline": None,
             "dtype": Wl.dtype, "data": "synthetic (seeded generator, BASELINE config shapes)",
             "config": {"workload": Wl.name, "units_per_gpu_per_step": wl.units_per_step,
                        "l2": Wl.l2_note, "parallelism": f"dp{world} (independent shards)"},
-            "gpu_launches": Wl.launches_per_step * args.steps,
+            "gpu_launches": wl.launches_per_step * args.steps,
             "e2e": {"value": wl.units_per_step * world / (ms_e2e / 1e3), "unit": Wl.unit,
                     "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -515,6 +739,21 @@ def main():
                          "algorithmic_bytes_per_launch": wl.algo_bytes},
             "clocks": clk,
         }
+        if hasattr(wl, "dominant"):
+            line["roofline"]["kernel"] = wl.dominant
+        if args.workload == "e2e":
+            from turboocr_b200.pipeline import SCHEDULE
+            line["config"].update({
+                "pages_total": wl.n_pages * world, "pages_per_gpu": wl.n_pages,
+                "micro_batch": wl.MB, "crops_per_page": round(wl.crops_per_page, 2),
+                "backbone": "stem 3->32 s2; " + ", ".join(f"{c}->{co} s{st}" for c, co, st in SCHEDULE),
+                "rec": "stand-in logits 80 x 18385 per crop (rec network out of scope)"})
+            bpp = wl.path_bytes_per_page()
+            ach = bpp * value / world / 1e9
+            line["roofline_path"] = {"bound": "hbm", "bytes_per_page": bpp,
+                                     "achieved": ach, "peak": peak, "unit": "GB/s",
+                                     "frac": ach / peak,
+                                     "note": "algorithmic bytes of every stage per page x pages/s per GPU"}
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = wl.cpu_baseline(cores)
         print(json.dumps(line), flush=True)

@@ -89,9 +89,9 @@ class PagePipeline:
         self.step_idx = torch.empty(nc * REC_T, dtype=torch.int32, device=device)
         self.step_prob = torch.empty(nc * REC_T, dtype=torch.float32, device=device)
         # kernels launched per run() (for the bench's gpu_launches count)
-        # stem + blocks + head + ink + DB (1 memset + 16 kernels) + crops (2) + warp
-        # + stand-in rec logits + CTC (2)
-        self.launches_per_run = 1 + len(SCHEDULE) + 1 + 1 + 16 + 2 + 1 + 1 + 2
+        # stem + blocks + head + ink + DB (18 kernels) + crops (2) + warp
+        # + stand-in rec logits (2) + CTC (2)
+        self.launches_per_run = 1 + len(SCHEDULE) + 1 + 1 + 18 + 2 + 1 + 2 + 2
 
     def run(self, pages: torch.Tensor, stream=None) -> None:
         """Enqueue the whole path for pages u8 [B, H, W, 3] (device)."""
