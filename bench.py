@@ -422,7 +422,12 @@ class E2eWorkload:
         self.n_pages = max(self.MB, (per + self.MB - 1) // self.MB * self.MB)
         self.units_per_step = self.n_pages
         self.n_mb = self.n_pages // self.MB
-        self.pipe = pl.PagePipeline(dev, self.MB)
+        # two pipelines on two streams: consecutive micro-batches overlap, so the
+        # latency-bound DB and crop stages of one run beside the streaming
+        # stages of the other
+        self.pipes = [pl.PagePipeline(dev, self.MB), pl.PagePipeline(dev, self.MB)]
+        self.pipe = self.pipes[0]
+        self.streams = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
         first = self.rank * self.n_pages
         self.pages = torch.empty(self.n_pages, 960, 960, 3, dtype=torch.uint8, device=dev)
         from turboocr_b200._lib import synth
@@ -431,12 +436,30 @@ class E2eWorkload:
             assert synth().tocr_synth_pages(self.pages[i].data_ptr(), n, 960, 960, 0x7EC00005,
                                             first + i, None) == 0
         torch.cuda.synchronize()
-        self.launches_per_step = self.n_mb * self.pipe.launches_per_run
+        self.launches_per_step = self.n_mb * self.pipes[0].launches_per_run
         self.algo_bytes = None  # set by dominant_kernel_ms (depends on the crop count)
 
+    def _fork(self):
+        cur = torch.cuda.current_stream()
+        ev = torch.cuda.Event()
+        ev.record(cur)
+        for st in self.streams:
+            st.wait_event(ev)
+
+    def _join(self):
+        cur = torch.cuda.current_stream()
+        for st in self.streams:
+            ev = torch.cuda.Event()
+            ev.record(st)
+            cur.wait_event(ev)
+
     def step(self):
+        self._fork()
         for i in range(self.n_mb):
-            self.pipe.run(self.pages[i * self.MB:(i + 1) * self.MB])
+            k = i & 1
+            with torch.cuda.stream(self.streams[k]):
+                self.pipes[k].run(self.pages[i * self.MB:(i + 1) * self.MB])
+        self._join()
 
     def dominant_kernel_ms(self, iters=10):
         """The CTC decode of one micro-batch's crops (tocr_ctc_greedy_f16_dev:
@@ -481,58 +504,39 @@ class E2eWorkload:
         b += crops * (3 * self.pl.REC_H * self.pl.REC_W * 2 + 2 * self.pl.REC_T * self.pl.REC_V * 2)
         return b
 
-    # end-to-end: pinned host pages -> H2D per micro-batch (double-buffered on a
-    # copy stream) -> path -> D2H of boxes, scores, counts, tokens, line scores
+    # end-to-end: pinned host pages -> H2D per micro-batch -> path -> D2H of
+    # boxes, scores, counts, tokens, line scores; each of the two streams copies
+    # its own micro-batch in and its results out, so copies overlap the other
+    # stream's compute
     def setup_e2e(self):
         self.n_host = min(self.n_pages, 256)
         self.h_pages = torch.empty(self.n_host, 960, 960, 3, dtype=torch.uint8, pin_memory=True)
         self.h_pages.copy_(self.pages[:self.n_host])
         self.stage = [torch.empty(self.MB, 960, 960, 3, dtype=torch.uint8, device=self.dev)
                       for _ in range(2)]
-        self.copy_stream = torch.cuda.Stream(self.dev)
-        p = self.pipe
-        self.h_boxes = torch.empty(p.db.boxes.shape, dtype=torch.int32, pin_memory=True)
-        self.h_scores = torch.empty(p.db.scores.shape, dtype=torch.float32, pin_memory=True)
-        self.h_counts = torch.empty(p.db.counts.shape, dtype=torch.int32, pin_memory=True)
-        self.h_tokens = torch.empty(p.tokens.shape, dtype=torch.int32, pin_memory=True)
-        self.h_lengths = torch.empty(p.lengths.shape, dtype=torch.int32, pin_memory=True)
-        self.h_lscores = torch.empty(p.line_scores.shape, dtype=torch.float32, pin_memory=True)
+        self.h_out = []
+        for p in self.pipes:
+            self.h_out.append([torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+                               for t in (p.db.boxes, p.db.scores, p.db.counts, p.tokens,
+                                         p.lengths, p.line_scores)])
         self.h2d = self.n_pages * 960 * 960 * 3
-        per_mb = sum(t.numel() * 4 for t in (self.h_boxes, self.h_scores, self.h_counts,
-                                             self.h_tokens, self.h_lengths, self.h_lscores))
+        per_mb = sum(t.numel() * t.element_size() for t in self.h_out[0])
         self.d2h = self.n_mb * per_mb
 
-    def _h2d(self, i, buf):
-        k = (i * self.MB) % self.n_host
-        src = self.h_pages[k:k + self.MB] if k + self.MB <= self.n_host else self.h_pages[:self.MB]
-        buf.copy_(src, non_blocking=True)
-
     def e2e_step(self):
-        s = torch.cuda.current_stream()
-        ready = [torch.cuda.Event(), torch.cuda.Event()]
-        free = [torch.cuda.Event(), torch.cuda.Event()]
-        with torch.cuda.stream(self.copy_stream):
-            self._h2d(0, self.stage[0])
-            ready[0].record(self.copy_stream)
-        p = self.pipe
+        self._fork()
         for i in range(self.n_mb):
-            b = i & 1
-            if i + 1 < self.n_mb:
-                nb = (i + 1) & 1
-                with torch.cuda.stream(self.copy_stream):
-                    if i >= 1:
-                        self.copy_stream.wait_event(free[nb])
-                    self._h2d(i + 1, self.stage[nb])
-                    ready[nb].record(self.copy_stream)
-            s.wait_event(ready[b])
-            p.run(self.stage[b])
-            free[b].record(s)
-            self.h_boxes.copy_(p.db.boxes, non_blocking=True)
-            self.h_scores.copy_(p.db.scores, non_blocking=True)
-            self.h_counts.copy_(p.db.counts, non_blocking=True)
-            self.h_tokens.copy_(p.tokens, non_blocking=True)
-            self.h_lengths.copy_(p.lengths, non_blocking=True)
-            self.h_lscores.copy_(p.line_scores, non_blocking=True)
+            k = i & 1
+            p = self.pipes[k]
+            with torch.cuda.stream(self.streams[k]):
+                j = (i * self.MB) % self.n_host
+                src = self.h_pages[j:j + self.MB] if j + self.MB <= self.n_host else self.h_pages[:self.MB]
+                self.stage[k].copy_(src, non_blocking=True)
+                p.run(self.stage[k])
+                for h, d in zip(self.h_out[k], (p.db.boxes, p.db.scores, p.db.counts, p.tokens,
+                                                p.lengths, p.line_scores)):
+                    h.copy_(d, non_blocking=True)
+        self._join()
 
     def cpu_baseline(self, cores, budget_s=20.0):
         """The path on the host, stage by stage on one page of the job, all

@@ -203,14 +203,14 @@ TOCR_API int tocr_ctc_greedy_f16_dev(const void *d_logits, const int *d_batch, i
 /* Det preprocessing of same-size u8 HWC pages at scale 1 (the reference's
  * resize is then the identity; normalisation as preprocess_kernels.cu:169-177)
  * fused with the backbone stem: 3x3 stride-2 pad-1 conv 3->32 + folded BN +
- * hardswish, fp16 NHWC out [n][(h-1)/2+1][(w-1)/2+1][32]. d_params is a
- * device copy of a tocr_stem_pack blob (no counterpart in the reference,
- * whose backbone runs inside TensorRT). */
+ * hardswish, fp16 NHWC out [n][(h-1)/2+1][(w-1)/2+1][32]. h_params is a
+ * HOST tocr_stem_pack blob, passed to the kernel by value (its constant
+ * bank); no counterpart in the reference, whose backbone runs in TensorRT. */
 TOCR_API size_t tocr_stem_params_bytes(void);
 TOCR_API int tocr_stem_pack(const float *w, const float *b, const float *mean3,
                             const float *inv_std3, void *out, size_t out_bytes);
 TOCR_API int tocr_stem_f16(const uint8_t *d_pages, int n, int h, int w, long long page_stride,
-                           const void *d_params, void *d_out, void *stream);
+                           const void *h_params, void *d_out, void *stream);
 
 /* Synthetic DB probability map of config 5 (no trained det head exists):
  * sigmoid(gain * (max_{|dx|<=7} ink(x+dx, y) - 0.5)), ink = 1 - mean(RGB)/255,

@@ -61,7 +61,7 @@ def test_stem_matches_torch(cuda, hw):
     call("tocr_stem_pack", sw.ctypes.data, sb.ctypes.data, None, None, blob.ctypes.data, blob.nbytes)
     Ho, Wo = (H - 1) // 2 + 1, (W - 1) // 2 + 1
     out = torch.empty(2, Ho, Wo, 32, dtype=torch.float16, device=cuda)
-    call("tocr_stem_f16", xd.data_ptr(), 2, H, W, H * W * 3, torch.from_numpy(blob).to(cuda).data_ptr(),
+    call("tocr_stem_f16", xd.data_ptr(), 2, H, W, H * W * 3, blob.ctypes.data,
          out.data_ptr(), torch.cuda.current_stream().cuda_stream)
     mean = torch.tensor([0.485, 0.456, 0.406], dtype=torch.float32, device=cuda)
     inv_std = torch.tensor([1 / 0.229, 1 / 0.224, 1 / 0.225], dtype=torch.float32, device=cuda)

@@ -106,7 +106,8 @@ __device__ __forceinline__ void union_s(int *par, int a, int b) {
 // 256 threads (8 warps x 4 rows).
 __global__ void __launch_bounds__(256)
 ccl_local_kernel(const float *__restrict__ pred, uint8_t *__restrict__ bitmap, int *__restrict__ lab,
-                 uint32_t *__restrict__ bits, int H, int W, float thresh) {
+                 uint32_t *__restrict__ bits, uint8_t *__restrict__ root_flag, int H, int W,
+                 float thresh) {
   __shared__ unsigned s_fg[kTileH];     // per tile row: foreground bits (bit = lx)
   __shared__ unsigned s_start[kTileH];  // per tile row: run-start bits
   __shared__ int par[kTilePx];
@@ -159,6 +160,19 @@ ccl_local_kernel(const float *__restrict__ pred, uint8_t *__restrict__ bitmap, i
     if (!f && (((y == 0 || y == H - 1) && is_start) || x == 0 || x == W - 1)) union_s(par, me, 0);
   }
   __syncthreads();
+  // pointer jumping until every node points at its root (vertical stacks of
+  // runs form chains up to a tile high; at most log2(1024) rounds)
+  for (int round = 0; round < 11; ++round) {
+    int changed = 0;
+    for (int i = threadIdx.x; i < kTilePx; i += blockDim.x) {
+      const int p1 = par[i];
+      if (p1 != 0) {
+        const int p2 = par[p1 - 1];
+        if (p2 != p1) { par[i] = p2; changed = 1; }
+      }
+    }
+    if (!__syncthreads_or(changed)) break;
+  }
   for (int ly = warp; ly < kTileH; ly += 8) {
     const int y = ty0 + ly;
     if (x >= W || y >= H) continue;
@@ -169,6 +183,7 @@ ccl_local_kernel(const float *__restrict__ pred, uint8_t *__restrict__ bitmap, i
       g = (ty0 + rl / kTileW) * W + tx0 + rl % kTileW + 1;
     }
     lab[base + (size_t)y * W + x] = g;
+    if (root_flag) root_flag[base + (size_t)y * W + x] = (r == ly * kTileW + lane + 1) ? 1 : 0;
   }
 }
 
@@ -211,6 +226,25 @@ ccl_merge_kernel(const uint8_t *__restrict__ bitmap, int *__restrict__ lab, int 
         if (!bm[ny * W + nx]) union_g(lb, me, ny * W + nx + 1);
       }
     }
+  }
+}
+
+// 2b. compression of the tile-local roots (flagged by stage 1), so that
+// stage 3 reaches a root in at most two hops. grid (tiles_x, tiles_y,
+// n_maps), 256 threads.
+__global__ void __launch_bounds__(256)
+ccl_roots_kernel(int *__restrict__ lab, const uint8_t *__restrict__ root_flag, int H, int W) {
+  const int m = blockIdx.z;
+  int *lb = lab + (size_t)m * H * W;
+  const uint8_t *rf = root_flag + (size_t)m * H * W;
+  const int tx0 = blockIdx.x * kTileW, ty0 = blockIdx.y * kTileH;
+  for (int l = threadIdx.x; l < kTilePx; l += blockDim.x) {
+    const int x = tx0 + (l % kTileW), y = ty0 + (l / kTileW);
+    if (x >= W || y >= H) continue;
+    const int p = y * W + x;
+    if (!rf[p]) continue;
+    const int r = find_g(lb, p + 1);
+    if (r != p + 1) atomicMin(lb + p, r);
   }
 }
 
@@ -678,7 +712,7 @@ namespace tocr {
 namespace {
 
 struct DbLayout {
-  size_t bitmap, bits, lab, scan_tot, row_count, row_off, n_contours, n_total, starts, npts, pt_off, pts, hpw,
+  size_t bitmap, root_flag, bits, lab, scan_tot, row_count, row_off, n_contours, n_total, starts, npts, pt_off, pts, hpw,
       hullbuf, fsc, stage1, aabb, stage2, score, dist, offcap, off_off, ring, hpw2, hull2, fsc2,
       keep2, boxes, total;
 };
@@ -692,6 +726,7 @@ DbLayout db_layout(int n_maps, int h, int w, long long point_cap, long long offs
   size_t o = 0;
   auto take = [&](size_t bytes) { const size_t at = o; o = align_up(o + bytes); return at; };
   L.bitmap = take(px);
+  L.root_flag = take(px);
   L.bits = take((size_t)n_maps * h * ((w + 31) / 32) * 4);
   L.lab = take(px * 4);
   L.scan_tot = take((size_t)n_maps * 8);
@@ -768,6 +803,7 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
   char *ws = static_cast<char *>(d_workspace);
   auto at = [&](size_t off) { return ws + off; };
   uint8_t *bitmap = (uint8_t *)at(L.bitmap);
+  uint8_t *root_flag = (uint8_t *)at(L.root_flag);
   uint32_t *bits = (uint32_t *)at(L.bits);
   int *lab = (int *)at(L.lab);
   long long *scan_tot = (long long *)at(L.scan_tot);
@@ -792,8 +828,9 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
 
   cudaError_t e = cudaMemsetAsync(d_status, 0, sizeof(int), st);
   if (e != cudaSuccess) return set_error(TOCR_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
-  ccl_local_kernel<<<tiles, 256, 0, st>>>(d_pred, bitmap, lab, bits, h, w, thresh);
+  ccl_local_kernel<<<tiles, 256, 0, st>>>(d_pred, bitmap, lab, bits, root_flag, h, w, thresh);
   ccl_merge_kernel<<<tiles, 128, 0, st>>>(bitmap, lab, h, w);
+  ccl_roots_kernel<<<tiles, 256, 0, st>>>(lab, root_flag, h, w);
   ccl_rows_kernel<<<dim3(h, n_maps), 256, 0, st>>>(lab, row_count, h, w);
   starts_scan_kernel<<<n_maps, kScanThreads, 0, st>>>(row_count, row_off, n_contours, n_total, h);
   starts_write_kernel<<<dim3(h, n_maps), 256, 0, st>>>(lab, bitmap, row_count, row_off, starts, h, w);
@@ -835,7 +872,8 @@ TOCR_API int tocr_db_components(const float *d_pred, int n_maps, int h, int w, f
   TOCR_REQUIRE(d_pred && d_labels && d_bitmap, "tocr_db_components: null pointer");
   cudaStream_t st = as_stream(stream);
   const dim3 tiles((w + kTileW - 1) / kTileW, (h + kTileH - 1) / kTileH, n_maps);
-  ccl_local_kernel<<<tiles, 256, 0, st>>>(d_pred, d_bitmap, d_labels, nullptr, h, w, thresh);
+  ccl_local_kernel<<<tiles, 256, 0, st>>>(d_pred, d_bitmap, d_labels, nullptr, nullptr, h, w,
+                                          thresh);
   ccl_merge_kernel<<<tiles, 128, 0, st>>>(d_bitmap, d_labels, h, w);
   ccl_rows_kernel<<<dim3(h, n_maps), 256, 0, st>>>(d_labels, nullptr, h, w);
   return check_launch("tocr_db_components");

@@ -20,6 +20,7 @@
 #include "tocr_common.cuh"
 
 #include <cmath>
+#include <cstring>
 
 namespace tocr {
 namespace {
@@ -37,51 +38,85 @@ __device__ __forceinline__ float hswish(float v) {
   return v * fminf(fmaxf(v + 3.f, 0.f), 6.f) * (1.f / 6.f);
 }
 
-// One thread per output pixel (all 32 channels). grid (ceil(Wo*Ho/256), n).
-__global__ void __launch_bounds__(256)
+// A CTA computes an 8 x 64 tile of output pixels (two per thread). The
+// 17 x 129-pixel input window is staged once in shared memory, already
+// normalised (zero outside the image: the conv pads the normalised tensor);
+// the weights arrive by value in the kernel's parameter (constant) bank, so
+// every FMA takes its weight straight from there. grid (tiles_x, tiles_y, n).
+constexpr int kStemTH = 8, kStemTW = 64;
+constexpr int kStemIH = 2 * kStemTH + 1, kStemIW = 2 * kStemTW + 1;
+
+__global__ void __launch_bounds__(256, 2)
 stem_kernel(const uint8_t *__restrict__ pages, int H, int W, long long page_stride,
-            __half *__restrict__ out, const StemParams *__restrict__ prm) {
-  __shared__ StemParams sp;
-  for (int i = threadIdx.x; i < (int)(sizeof(StemParams) / 4); i += blockDim.x)
-    reinterpret_cast<float *>(&sp)[i] = reinterpret_cast<const float *>(prm)[i];
-  __syncthreads();
+            __half *__restrict__ out, const StemParams sp) {
+  __shared__ float s_in[kStemIH][kStemIW][3];
   const int Ho = (H - 1) / 2 + 1, Wo = (W - 1) / 2 + 1;
-  const int n = blockIdx.y;
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= Ho * Wo) return;
-  const int oy = idx / Wo, ox = idx % Wo;
+  const int n = blockIdx.z;
+  const int oy0 = blockIdx.y * kStemTH, ox0 = blockIdx.x * kStemTW;
+  const int iy0 = 2 * oy0 - 1, ix0 = 2 * ox0 - 1;
   const uint8_t *pg = pages + (long long)n * page_stride;
-  float tap[27];
+  float *flat = &s_in[0][0][0];
+  for (int i = threadIdx.x; i < kStemIH * kStemIW * 3; i += blockDim.x) flat[i] = 0.f;
+  __syncthreads();
+  // 16-byte loads of each input row's byte range [bs, be) (rows are 3W bytes)
+  const long long row_bytes = 3ll * W;
+  const int bs0 = 3 * ix0, be0 = 3 * (ix0 + kStemIW);
+  const int bs = bs0 > 0 ? bs0 : 0;
+  const int be = be0 < row_bytes ? be0 : (int)row_bytes;
+  const int a0 = bs & ~15;
+  const int chunks = (be - a0 + 15) >> 4;
+  const bool vec_ok = (row_bytes & 15) == 0 && (reinterpret_cast<uintptr_t>(pg) & 15) == 0;
+  for (int i = threadIdx.x; i < kStemIH * chunks; i += blockDim.x) {
+    const int row = i / chunks, k = i % chunks;
+    const int y = iy0 + row;
+    if (y < 0 || y >= H) continue;
+    const uint8_t *rp = pg + (long long)y * row_bytes;
+    const int b0 = a0 + 16 * k;
+    uint8_t v[16];
+    if (vec_ok && b0 + 16 <= row_bytes) {
+      *reinterpret_cast<uint4 *>(v) = __ldg(reinterpret_cast<const uint4 *>(rp + b0));
+    } else {
+      for (int j = 0; j < 16; ++j) v[j] = (b0 + j < row_bytes) ? rp[b0 + j] : 0;
+    }
 #pragma unroll
-  for (int ky = 0; ky < 3; ++ky) {
+    for (int j = 0; j < 16; ++j) {
+      const int b = b0 + j;
+      if (b < bs || b >= be) continue;
+      const int lb = b - bs0;
+      const int col = lb / 3, c = lb - 3 * col;
+      flat[(row * kStemIW + col) * 3 + c] =
+          ((float)v[j] * (1.0f / 255.0f) - sp.mean[c]) * sp.inv_std[c];
+    }
+  }
+  __syncthreads();
+  for (int q = threadIdx.x; q < kStemTH * kStemTW; q += blockDim.x) {
+    const int ty = q / kStemTW, tx = q % kStemTW;
+    const int oy = oy0 + ty, ox = ox0 + tx;
+    if (oy >= Ho || ox >= Wo) continue;
+    float tap[27];
 #pragma unroll
-    for (int kx = 0; kx < 3; ++kx) {
-      const int y = 2 * oy - 1 + ky, x = 2 * ox - 1 + kx;
-      const bool in = y >= 0 && y < H && x >= 0 && x < W;
-      const uint8_t *px = pg + ((long long)y * W + x) * 3;
+    for (int ky = 0; ky < 3; ++ky)
 #pragma unroll
-      for (int c = 0; c < 3; ++c) {
-        const float v = in ? (float)px[c] : 0.f;
-        tap[(ky * 3 + kx) * 3 + c] = in ? (v * (1.0f / 255.0f) - sp.mean[c]) * sp.inv_std[c] : 0.f;
+      for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+        for (int c = 0; c < 3; ++c) tap[(ky * 3 + kx) * 3 + c] = s_in[2 * ty + ky][2 * tx + kx][c];
+    uint4 packed[kStemCo / 8];
+    uint32_t *pw = reinterpret_cast<uint32_t *>(packed);
+#pragma unroll
+    for (int co = 0; co < kStemCo; co += 2) {
+      float a0 = sp.b[co], a1 = sp.b[co + 1];
+#pragma unroll
+      for (int k = 0; k < 27; ++k) {
+        a0 = fmaf(sp.w[co][k], tap[k], a0);
+        a1 = fmaf(sp.w[co + 1][k], tap[k], a1);
       }
+      const __half2 h = __floats2half2_rn(hswish(a0), hswish(a1));
+      pw[co / 2] = *reinterpret_cast<const uint32_t *>(&h);
     }
+    uint4 *dst = reinterpret_cast<uint4 *>(out + (((long long)n * Ho + oy) * Wo + ox) * kStemCo);
+#pragma unroll
+    for (int k = 0; k < kStemCo / 8; ++k) dst[k] = packed[k];
   }
-  uint4 packed[kStemCo / 8];
-  uint32_t *pw = reinterpret_cast<uint32_t *>(packed);
-#pragma unroll
-  for (int co = 0; co < kStemCo; co += 2) {
-    float a0 = sp.b[co], a1 = sp.b[co + 1];
-#pragma unroll
-    for (int k = 0; k < 27; ++k) {
-      a0 = fmaf(sp.w[co][k], tap[k], a0);
-      a1 = fmaf(sp.w[co + 1][k], tap[k], a1);
-    }
-    const __half2 h = __floats2half2_rn(hswish(a0), hswish(a1));
-    pw[co / 2] = *reinterpret_cast<const uint32_t *>(&h);
-  }
-  uint4 *dst = reinterpret_cast<uint4 *>(out + (((long long)n * Ho + oy) * Wo + ox) * kStemCo);
-#pragma unroll
-  for (int q = 0; q < kStemCo / 8; ++q) dst[q] = packed[q];
 }
 
 // ------------------------------------------------------------- ink map -------
@@ -225,15 +260,16 @@ TOCR_API int tocr_stem_pack(const float *w /* [32][3][3][3] co,ci,ky,kx */, cons
 }
 
 TOCR_API int tocr_stem_f16(const uint8_t *d_pages, int n, int h, int w, long long page_stride,
-                           const void *d_params, void *d_out, void *stream) {
+                           const void *h_params, void *d_out, void *stream) {
   TOCR_ENTRY();
   TOCR_REQUIRE(n >= 0 && h > 0 && w > 0, "tocr_stem_f16: bad sizes n=%d h=%d w=%d", n, h, w);
   if (n == 0) return TOCR_OK;
-  TOCR_REQUIRE(d_pages && d_params && d_out && aligned(d_out, 16), "tocr_stem_f16: bad pointer");
+  TOCR_REQUIRE(d_pages && h_params && d_out && aligned(d_out, 16), "tocr_stem_f16: bad pointer");
   const int Ho = (h - 1) / 2 + 1, Wo = (w - 1) / 2 + 1;
-  const dim3 grid((unsigned)(((long long)Ho * Wo + 255) / 256), n);
-  stem_kernel<<<grid, 256, 0, as_stream(stream)>>>(d_pages, h, w, page_stride, (__half *)d_out,
-                                                   (const StemParams *)d_params);
+  StemParams sp;
+  memcpy(&sp, h_params, sizeof(sp));
+  const dim3 grid((Wo + kStemTW - 1) / kStemTW, (Ho + kStemTH - 1) / kStemTH, n);
+  stem_kernel<<<grid, 256, 0, as_stream(stream)>>>(d_pages, h, w, page_stride, (__half *)d_out, sp);
   return check_launch("stem_kernel");
 }
 

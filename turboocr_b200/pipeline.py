@@ -56,7 +56,7 @@ class PagePipeline:
         call("tocr_stem_pack", sw.ctypes.data, sb.ctypes.data, None, None, blob.ctypes.data,
              blob.nbytes)
         self.stem_w, self.stem_b = sw, sb
-        self.stem_blob = torch.from_numpy(blob).to(device)
+        self.stem_blob = blob  # host blob: the kernel takes the parameters by value
         self.blocks = []
         h, w = out_hw(H, W, 2)
         self.acts = [torch.empty(batch, h, w, 32, dtype=torch.float16, device=device)]
@@ -99,7 +99,7 @@ class PagePipeline:
         assert pages.shape == (B, H, W, 3) and pages.dtype == torch.uint8
         st = _stream(stream)
         page_stride = H * W * 3
-        call("tocr_stem_f16", _ptr(pages), B, H, W, page_stride, _ptr(self.stem_blob),
+        call("tocr_stem_f16", _ptr(pages), B, H, W, page_stride, self.stem_blob.ctypes.data,
              _ptr(self.acts[0]), st)
         for i, blk in enumerate(self.blocks):
             x, y = self.acts[i], self.acts[i + 1]
