@@ -418,7 +418,10 @@ class E2eWorkload:
         from turboocr_b200 import pipeline as pl
         self.pl = pl
         self.dev = dev
-        per = units or self.TOTAL // self.world
+        if units:
+            first, per = self.rank * units, units
+        else:
+            first, per = pl.shard(self.TOTAL, self.world, self.rank, self.MB)
         self.n_pages = max(self.MB, (per + self.MB - 1) // self.MB * self.MB)
         self.units_per_step = self.n_pages
         self.n_mb = self.n_pages // self.MB
@@ -428,7 +431,6 @@ class E2eWorkload:
         self.pipes = [pl.PagePipeline(dev, self.MB), pl.PagePipeline(dev, self.MB)]
         self.pipe = self.pipes[0]
         self.streams = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
-        first = self.rank * self.n_pages
         self.pages = torch.empty(self.n_pages, 960, 960, 3, dtype=torch.uint8, device=dev)
         from turboocr_b200._lib import synth
         for i in range(0, self.n_pages, 256):

@@ -144,6 +144,16 @@ class PagePipeline:
         return out
 
 
+def shard(total: int, world: int, rank: int, micro_batch: int = 16) -> tuple[int, int]:
+    """Contiguous page shard of one rank: (first page, page count). The job is
+    split evenly (rounded up to whole micro-batches); pages are independent,
+    so ranks never exchange data (config 5: no cross-GPU reduction)."""
+    per = (total + world - 1) // world
+    per = (per + micro_batch - 1) // micro_batch * micro_batch
+    first = min(total, rank * per)
+    return first, max(0, min(per, total - first))
+
+
 def make_pages(n: int, H: int = 960, W: int = 960, seed: int = 0x7EC00005, first: int = 0,
                device="cuda", stream=None) -> torch.Tensor:
     pages = torch.empty(n, H, W, 3, dtype=torch.uint8, device=device)
