@@ -355,36 +355,62 @@ starts_write_kernel(const int *__restrict__ lab, const uint8_t *__restrict__ bit
 }
 
 
-// 5. border following. One thread per contour slot (m * 3000 + rank).
-// write == false: count points into npts; write == true: store them at pt_off.
-template <bool kWrite>
+// 5. border following. One thread per contour slot (m * 3000 + rank): the
+// walk writes its first kSlab points into the slot's slab and counts them
+// all (npts). After the offsets are scanned, gather_kernel moves each slab
+// to the contiguous point pool; the rare contour longer than a slab is
+// walked a second time straight into the pool.
+constexpr int kSlab = 256;
+
+__device__ __forceinline__ int trace_max_steps(int H, int W) {
+  const long long ms = 4ll * H * W + 16;
+  return ms > 0x7fffffffll ? 0x7fffffff : (int)ms;
+}
+
 __global__ void __launch_bounds__(128)
 trace_kernel(const uint32_t *__restrict__ bits, const int *__restrict__ starts,
-             const int *__restrict__ n_contours, int *__restrict__ npts,
-             const long long *__restrict__ pt_off, P2 *__restrict__ pts, int *__restrict__ status,
-             long long point_cap, int n_maps, int H, int W) {
+             const int *__restrict__ n_contours, int *__restrict__ npts, P2 *__restrict__ slab,
+             int *__restrict__ status, int n_maps, int H, int W) {
   const long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= (long long)n_maps * kMaxCand) return;
   const int m = (int)(c / kMaxCand), rank = (int)(c % kMaxCand);
   if (rank >= n_contours[m]) {
-    if (!kWrite) npts[c] = 0;
+    npts[c] = 0;
     return;
   }
   const int rec = starts[c];
   const int sp = rec >> 1;
   const int words = (W + 31) >> 5;
   db::NbBits nb{bits + (size_t)m * H * words, H, W, words};
-  const long long ms = 4ll * H * W + 16;
-  const int max_steps = ms > 0x7fffffffll ? 0x7fffffff : (int)ms;
-  if (!kWrite) {
-    const int n = db::trace_border_nb(nb, sp % W, sp / W, (rec & 1) != 0, nullptr, 0, max_steps);
-    if (n < 0) atomicOr(status, kErrTrace);
-    npts[c] = n < 0 ? 0 : n;
-  } else {
-    const int n = npts[c];
-    if (n == 0 || pt_off[c] + n > point_cap) return;
-    db::trace_border_nb(nb, sp % W, sp / W, (rec & 1) != 0, pts + pt_off[c], n, max_steps);
+  const int n = db::trace_border_nb(nb, sp % W, sp / W, (rec & 1) != 0, slab + c * kSlab, kSlab,
+                                    trace_max_steps(H, W));
+  if (n < 0) atomicOr(status, kErrTrace);
+  npts[c] = n < 0 ? 0 : n;
+}
+
+// One warp per contour slot: slab -> pool (lanes copy), or a second walk.
+__global__ void __launch_bounds__(128)
+gather_kernel(const uint32_t *__restrict__ bits, const int *__restrict__ starts,
+              const int *__restrict__ npts, const long long *__restrict__ pt_off,
+              const P2 *__restrict__ slab, P2 *__restrict__ pts, long long point_cap, int n_maps,
+              int H, int W) {
+  const long long c = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (c >= (long long)n_maps * kMaxCand) return;
+  const int n = npts[c];
+  if (n == 0 || pt_off[c] + n > point_cap) return;
+  P2 *dst = pts + pt_off[c];
+  if (n <= kSlab) {
+    for (int i = lane; i < n; i += 32) dst[i] = slab[c * kSlab + i];
+    return;
   }
+  if (lane != 0) return;
+  const int m = (int)(c / kMaxCand);
+  const int rec = starts[c];
+  const int sp = rec >> 1;
+  const int words = (W + 31) >> 5;
+  db::NbBits nb{bits + (size_t)m * H * words, H, W, words};
+  db::trace_border_nb(nb, sp % W, sp / W, (rec & 1) != 0, dst, n, trace_max_steps(H, W));
 }
 
 // Exclusive scan of the per-slot counts of n_maps x 3000 contour slots into
@@ -712,7 +738,7 @@ namespace tocr {
 namespace {
 
 struct DbLayout {
-  size_t bitmap, root_flag, bits, lab, scan_tot, row_count, row_off, n_contours, n_total, starts, npts, pt_off, pts, hpw,
+  size_t bitmap, root_flag, bits, slab, lab, scan_tot, row_count, row_off, n_contours, n_total, starts, npts, pt_off, pts, hpw,
       hullbuf, fsc, stage1, aabb, stage2, score, dist, offcap, off_off, ring, hpw2, hull2, fsc2,
       keep2, boxes, total;
 };
@@ -727,6 +753,7 @@ DbLayout db_layout(int n_maps, int h, int w, long long point_cap, long long offs
   auto take = [&](size_t bytes) { const size_t at = o; o = align_up(o + bytes); return at; };
   L.bitmap = take(px);
   L.root_flag = take(px);
+  L.slab = take(C * kSlab * sizeof(P2));
   L.bits = take((size_t)n_maps * h * ((w + 31) / 32) * 4);
   L.lab = take(px * 4);
   L.scan_tot = take((size_t)n_maps * 8);
@@ -804,6 +831,7 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
   auto at = [&](size_t off) { return ws + off; };
   uint8_t *bitmap = (uint8_t *)at(L.bitmap);
   uint8_t *root_flag = (uint8_t *)at(L.root_flag);
+  P2 *slab = (P2 *)at(L.slab);
   uint32_t *bits = (uint32_t *)at(L.bits);
   int *lab = (int *)at(L.lab);
   long long *scan_tot = (long long *)at(L.scan_tot);
@@ -834,13 +862,12 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
   ccl_rows_kernel<<<dim3(h, n_maps), 256, 0, st>>>(lab, row_count, h, w);
   starts_scan_kernel<<<n_maps, kScanThreads, 0, st>>>(row_count, row_off, n_contours, n_total, h);
   starts_write_kernel<<<dim3(h, n_maps), 256, 0, st>>>(lab, bitmap, row_count, row_off, starts, h, w);
-  trace_kernel<false><<<cgrid, 128, 0, st>>>(bits, starts, n_contours, npts, pt_off, pts,
-                                              d_status, point_cap, n_maps, h, w);
+  trace_kernel<<<cgrid, 128, 0, st>>>(bits, starts, n_contours, npts, slab, d_status, n_maps, h, w);
   scan_map_kernel<int><<<n_maps, kScanThreads, 0, st>>>(npts, pt_off, scan_tot);
   scan_base_kernel<<<n_maps, kScanThreads, 0, st>>>(pt_off, scan_tot, n_maps);
   check_cap_kernel<<<1, 1, 0, st>>>(pt_off, C, point_cap, d_status, kErrPointPool);
-  trace_kernel<true><<<cgrid, 128, 0, st>>>(bits, starts, n_contours, npts, pt_off, pts,
-                                             d_status, point_cap, n_maps, h, w);
+  gather_kernel<<<(unsigned)((C * 32 + 127) / 128), 128, 0, st>>>(bits, starts, npts, pt_off, slab,
+                                                                 pts, point_cap, n_maps, h, w);
   geom_box1_kernel<<<cgrid, 128, 0, st>>>(n_contours, npts, pt_off, pts, hpw, hullbuf, fsc,
                                           stage1, aabb, P);
   score_kernel<<<(unsigned)C, kScoreThreads, 0, st>>>(d_pred, stage1, aabb, npts, pt_off, pts,

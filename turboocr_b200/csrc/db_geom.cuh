@@ -109,10 +109,14 @@ TG int trace_border_nb(NB &nb, int x0, int y0, bool hole, P2 *out, int cap, int 
     // Straight horizontal stretches: from (x3, y3), after an E move the walk
     // keeps moving E while SW, S, SE are background and E is foreground (W
     // mirrored with NE, N, NW); such moves repeat the chain code, so no point
-    // is emitted. Jump over them (never on the start row, so the closing test
-    // above still sees the last moves).
-    if ((d4 == 0 || d4 == 4) && y3 != y0) {
+    // is emitted. Jump over them; on the start row stop two pixels short of
+    // the start pixel, so the closing test above still sees the last moves.
+    if (d4 == 0 || d4 == 4) {
       int L = nb.run(x3, y3, d4);
+      if (y3 == y0) {
+        const int room = d4 == 0 ? x0 - x3 - 2 : x3 - x0 - 2;
+        if ((d4 == 0 ? x3 < x0 : x3 > x0) && L > room) L = room;
+      }
       if (L > max_steps - step - 1) L = max_steps - step - 1;
       if (L > 0) {
         x3 += d4 == 0 ? L : -L;
