@@ -65,9 +65,11 @@ def test_partial_tiles_and_odd_sizes(cuda, kind):
 
 @pytest.mark.parametrize("kind", [bb.KIND_INT8, bb.KIND_FP8])
 @pytest.mark.parametrize("C,CO", [(64, 64), (128, 128), (64, 128), (32, 64)])
-@pytest.mark.parametrize("hw", [(48, 64), (37, 53), (120, 120)])
+@pytest.mark.parametrize("hw", [(48, 64), (37, 53), (120, 120), (240, 240)])
 def test_stride2(cuda, kind, C, CO, hw):
-    """Stride-2 blocks of the end-to-end backbone (pad 1, Ho = (H-1)/2 + 1)."""
+    """Stride-2 blocks of the end-to-end backbone (pad 1, Ho = (H-1)/2 + 1).
+    (240, 240) gives more tiles than SMs, so every CTA cycles through all
+    halo/operand stages."""
     y, ref, *_ = run_block(cuda, 2, hw[0], hw[1], C, CO, kind, seed=C + 7 * CO, stride=2)
     assert y.shape == ref.shape
     nw, el = plane_errors(y, ref)

@@ -54,6 +54,8 @@ struct Cfg {
   static constexpr int KSTEPS = C / 32;                // MMA K = 32 per instruction
   static constexpr int HH = (TH - 1) * S + 3, HW = (TW - 1) * S + 3;
   static constexpr int HALO = HH * HW * CCH * 2;
+  // stage stride of the halo ring: TMA destinations must be 128-byte aligned
+  static constexpr int HALO_ST = (HALO + 127) / 128 * 128;
   static constexpr int PARTS = CCH / 8;                // 16-byte channel vectors per chunk
   static constexpr int SEG = PARTS / 2;                // output pixels per DW thread
   static constexpr int NSEG = TP / SEG;
@@ -66,7 +68,7 @@ struct Cfg {
   static constexpr int TMEM_COLS = 2 * CO < 32 ? 32 : 2 * CO;
   // shared memory carve-up (all 1024-aligned where the async proxy reads)
   static constexpr int OFF_X = 0;
-  static constexpr int OFF_A = OFF_X + ((XST * HALO + 1023) / 1024) * 1024;
+  static constexpr int OFF_A = OFF_X + ((XST * HALO_ST + 1023) / 1024) * 1024;
   static constexpr int OFF_B = OFF_A + AST * A_TILE;
   static constexpr int OFF_OUT = OFF_B + B_BYTES;
   static constexpr int OFF_STG = OFF_OUT + OUT;
@@ -88,6 +90,8 @@ struct Cfg {
   static constexpr int CPG = CO / NGRP;                 // columns per group
   static constexpr int C32_PER_GRP = CPG / 32;
   static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
+  static_assert(HALO_ST % 128 == 0 && OFF_A % 1024 == 0 && OFF_B % 1024 == 0 &&
+                OFF_OUT % 1024 == 0, "TMA / UMMA operand alignment");
 };
 
 // Offsets of the packed parameter blob (device): B image | w_scale | bias |
@@ -224,7 +228,7 @@ dwpw_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
           if (!mbar_wait_bounded(&x_empty[st], ((g / K::XST) & 1) ^ 1, s_abort, prm.err, 11))
             goto producer_done;
           mbar_arrive_expect_tx(&x_full[st], K::HALO);
-          tma_load_4d(sx + st * K::HALO, &xmap, &x_full[st], ch * K::CCH, ix, iy, n);
+          tma_load_4d(sx + st * K::HALO_ST, &xmap, &x_full[st], ch * K::CCH, ix, iy, n);
         }
       }
     producer_done:
@@ -287,7 +291,7 @@ dwpw_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
         const int st = g % K::XST;
         if (ok) ok = mbar_wait_bounded(&x_full[st], (g / K::XST) & 1, s_abort, prm.err, 31);
         if (!ok) continue;
-        const uint8_t *xs = sx + st * K::HALO;
+        const uint8_t *xs = sx + st * K::HALO_ST;
         const int c0 = ch * K::CCH + part * 8;     // first channel of this thread
         __half2 w[9][4];
 #pragma unroll
@@ -570,10 +574,10 @@ int dispatch(int C, int CO, int S, const void *x, void *y, int N, int H, int W,
   TOCR_DWPW(128, 256, 1, 64, 2, (F8 ? 1 : 2))
   TOCR_DWPW(64, 128, 1, 64, 2, 2)
   TOCR_DWPW(64, 64, 1, 64, 2, 2)
-  TOCR_DWPW(32, 64, 1, 32, 2, 2)
+  TOCR_DWPW(32, 64, 1, 32, 4, 4)
   TOCR_DWPW(128, 128, 1, 64, 2, 2)
-  TOCR_DWPW(64, 64, 2, 64, 1, 2)
-  TOCR_DWPW(128, 128, 2, 64, 1, 2)
+  TOCR_DWPW(64, 64, 2, 64, 2, (F8 ? 1 : 2))
+  TOCR_DWPW(128, 128, 2, 32, 2, 2)
   TOCR_DWPW(64, 128, 2, 64, 1, 2)
   TOCR_DWPW(32, 64, 2, 32, 2, 2)
 #undef TOCR_DWPW
