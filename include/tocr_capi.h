@@ -161,9 +161,12 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
  * src/kernels/ccl_kernels.cu:387-493). labels [n_maps][h][w]: 0 for
  * background joined to the image frame, otherwise 1 + the raster index of the
  * smallest pixel of the component (foreground 8-connected, background
- * 4-connected). d_bitmap [n_maps][h][w] receives the 0/255 bitmap. */
+ * 4-connected). d_bitmap [n_maps][h][w] receives the 0/255 bitmap.
+ * d_scratch: NULL, or tocr_db_components_scratch_bytes(n_maps, h, w) bytes
+ * that enable the background-tile shortcuts of tocr_db_postprocess. */
+TOCR_API size_t tocr_db_components_scratch_bytes(int n_maps, int h, int w);
 TOCR_API int tocr_db_components(const float *d_pred, int n_maps, int h, int w, float thresh,
-                                int *d_labels, uint8_t *d_bitmap, void *stream);
+                                int *d_labels, uint8_t *d_bitmap, void *d_scratch, void *stream);
 
 /* ---- recognition crops (replace the host-side crop loop of PaddleRec) ----- */
 

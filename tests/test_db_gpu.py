@@ -62,8 +62,9 @@ def compare_exact(gpu, ref):
         assert abs(s1 - s2) <= SCORE_TOL
 
 
+@pytest.mark.parametrize("shortcuts", [True, False])
 @pytest.mark.parametrize("hw", [(37, 53), (64, 64), (100, 333), (960, 960)])
-def test_components_partition(cuda, hw):
+def test_components_partition(cuda, hw, shortcuts):
     from turboocr_b200.kernels import db_components
     h, w = hw
     rng = np.random.default_rng(h * w)
@@ -71,7 +72,8 @@ def test_components_partition(cuda, hw):
     maps[1] = (maps[1] > 0.5) * 0.9          # coarse blobs after smoothing below
     maps[1] = ndimage.uniform_filter(maps[1], 5)
     maps[2] = synth_maps(1, h, w, 3, 12)[0]
-    labels, bitmap = db_components(torch.from_numpy(maps).to(cuda), 0.3)
+    maps[0][: h // 2] = 0.0      # a band of background-only tiles next to mixed ones
+    labels, bitmap = db_components(torch.from_numpy(maps).to(cuda), 0.3, shortcuts=shortcuts)
     labels = labels.cpu().numpy()
     bitmap = bitmap.cpu().numpy()
     for m in range(3):

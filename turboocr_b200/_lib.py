@@ -66,7 +66,8 @@ SIGNATURES: dict[str, tuple] = {
     "tocr_db_workspace_bytes": (C.c_size_t, [_i, _i, _i, _ll, _ll]),
     "tocr_db_postprocess": (_i, [_vp, _i, _i, _i, _vp, _f, _f, _f, _f, _f, _ll, _ll, _vp,
                                  C.c_size_t, _vp, _vp, _vp, _i, _vp, _vp]),
-    "tocr_db_components": (_i, [_vp, _i, _i, _i, _f, _vp, _vp, _vp]),
+    "tocr_db_components_scratch_bytes": (C.c_size_t, [_i, _i, _i]),
+    "tocr_db_components": (_i, [_vp, _i, _i, _i, _f, _vp, _vp, _vp, _vp]),
     "tocr_stem_params_bytes": (C.c_size_t, []),
     "tocr_stem_pack": (_i, [_vp, _vp, _vp, _vp, _vp, C.c_size_t]),
     "tocr_stem_f16": (_i, [_vp, _i, _i, _i, _ll, _vp, _vp, _vp]),

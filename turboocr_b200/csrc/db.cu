@@ -106,8 +106,8 @@ __device__ __forceinline__ void union_s(int *par, int a, int b) {
 // 256 threads (8 warps x 4 rows).
 __global__ void __launch_bounds__(256)
 ccl_local_kernel(const float *__restrict__ pred, uint8_t *__restrict__ bitmap, int *__restrict__ lab,
-                 uint32_t *__restrict__ bits, uint8_t *__restrict__ root_flag, int H, int W,
-                 float thresh) {
+                 uint32_t *__restrict__ bits, uint8_t *__restrict__ root_flag,
+                 uint8_t *__restrict__ tile_bg, int H, int W, float thresh) {
   __shared__ unsigned s_fg[kTileH];     // per tile row: foreground bits (bit = lx)
   __shared__ unsigned s_start[kTileH];  // per tile row: run-start bits
   __shared__ int par[kTilePx];
@@ -138,7 +138,26 @@ ccl_local_kernel(const float *__restrict__ pred, uint8_t *__restrict__ bitmap, i
     const int rs = 31 - __clz(upto);
     par[ly * kTileW + lane] = ly * kTileW + rs + 1;
   }
-  __syncthreads();
+  // Background-only tile (most of a text page): one 4-connected component,
+  // rooted at the outside when the tile touches the image frame, otherwise
+  // at the tile's first pixel. No unions needed.
+  const bool any_fg = __syncthreads_or(warp < kTileH && lane == 0 &&
+                                       (s_fg[warp] | s_fg[warp + 8] | s_fg[warp + 16] |
+                                        s_fg[warp + 24]) != 0u);
+  if (tile_bg) {
+    if (threadIdx.x == 0) tile_bg[((size_t)m * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x] = !any_fg;
+  }
+  if (!any_fg) {
+    const bool frame = tx0 == 0 || ty0 == 0 || tx0 + kTileW >= W || ty0 + kTileH >= H;
+    const int g = frame ? 0 : ty0 * W + tx0 + 1;
+    for (int ly = warp; ly < kTileH; ly += 8) {
+      const int y = ty0 + ly;
+      if (x >= W || y >= H) continue;
+      lab[base + (size_t)y * W + x] = g;
+      if (root_flag) root_flag[base + (size_t)y * W + x] = (!frame && ly == 0 && lane == 0) ? 1 : 0;
+    }
+    return;
+  }
   for (int ly = warp; ly < kTileH; ly += 8) {
     const int y = ty0 + ly;
     if (x >= W || y >= H) continue;
@@ -190,12 +209,35 @@ ccl_local_kernel(const float *__restrict__ pred, uint8_t *__restrict__ bitmap, i
 // 2. unions across tile borders. One thread per pixel of a tile's first row,
 // first column or last column. grid (tiles_x, tiles_y, n_maps), 128 threads.
 __global__ void __launch_bounds__(128)
-ccl_merge_kernel(const uint8_t *__restrict__ bitmap, int *__restrict__ lab, int H, int W) {
+ccl_merge_kernel(const uint8_t *__restrict__ bitmap, int *__restrict__ lab,
+                 const uint8_t *__restrict__ tile_bg, int H, int W) {
   const int m = blockIdx.z;
   const size_t base = (size_t)m * H * W;
   const uint8_t *bm = bitmap + base;
   int *lb = lab + base;
   const int tx0 = blockIdx.x * kTileW, ty0 = blockIdx.y * kTileH;
+  if (tile_bg) {
+    // background-only tile: its single component meets each background-only
+    // neighbour along a whole edge, so one union per such neighbour suffices
+    const size_t tb = (size_t)m * gridDim.y * gridDim.x;
+    const bool me_bg = tile_bg[tb + (size_t)blockIdx.y * gridDim.x + blockIdx.x];
+    if (me_bg) {
+      // This tile only links upward and leftward (its right neighbour links
+      // to it from its own left edge, the tile below from its top row), and a
+      // background-only tile has no foreground diagonals to follow.
+      const bool has_up = blockIdx.y > 0, has_left = blockIdx.x > 0;
+      const bool up_bg = has_up && tile_bg[tb + (size_t)(blockIdx.y - 1) * gridDim.x + blockIdx.x];
+      const bool left_bg = has_left && tile_bg[tb + (size_t)blockIdx.y * gridDim.x + blockIdx.x - 1];
+      if ((!has_up || up_bg) && (!has_left || left_bg)) {
+        if (threadIdx.x == 0) {
+          const int me = ty0 * W + tx0 + 1;
+          if (has_up) union_g(lb, me, me - W);
+          if (has_left) union_g(lb, me, me - 1);
+        }
+        return;
+      }
+    }
+  }
   // border pixels: top row (kTileW), left column (kTileH), right column (kTileH)
   for (int i = threadIdx.x; i < kTileW + 2 * kTileH; i += blockDim.x) {
     int lx, ly;
@@ -738,7 +780,7 @@ namespace tocr {
 namespace {
 
 struct DbLayout {
-  size_t bitmap, root_flag, bits, slab, lab, scan_tot, row_count, row_off, n_contours, n_total, starts, npts, pt_off, pts, hpw,
+  size_t bitmap, root_flag, tile_bg, bits, slab, lab, scan_tot, row_count, row_off, n_contours, n_total, starts, npts, pt_off, pts, hpw,
       hullbuf, fsc, stage1, aabb, stage2, score, dist, offcap, off_off, ring, hpw2, hull2, fsc2,
       keep2, boxes, total;
 };
@@ -753,6 +795,7 @@ DbLayout db_layout(int n_maps, int h, int w, long long point_cap, long long offs
   auto take = [&](size_t bytes) { const size_t at = o; o = align_up(o + bytes); return at; };
   L.bitmap = take(px);
   L.root_flag = take(px);
+  L.tile_bg = take((size_t)n_maps * ((h + kTileH - 1) / kTileH) * ((w + kTileW - 1) / kTileW));
   L.slab = take(C * kSlab * sizeof(P2));
   L.bits = take((size_t)n_maps * h * ((w + 31) / 32) * 4);
   L.lab = take(px * 4);
@@ -831,6 +874,7 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
   auto at = [&](size_t off) { return ws + off; };
   uint8_t *bitmap = (uint8_t *)at(L.bitmap);
   uint8_t *root_flag = (uint8_t *)at(L.root_flag);
+  uint8_t *tile_bg = (uint8_t *)at(L.tile_bg);
   P2 *slab = (P2 *)at(L.slab);
   uint32_t *bits = (uint32_t *)at(L.bits);
   int *lab = (int *)at(L.lab);
@@ -856,8 +900,9 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
 
   cudaError_t e = cudaMemsetAsync(d_status, 0, sizeof(int), st);
   if (e != cudaSuccess) return set_error(TOCR_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
-  ccl_local_kernel<<<tiles, 256, 0, st>>>(d_pred, bitmap, lab, bits, root_flag, h, w, thresh);
-  ccl_merge_kernel<<<tiles, 128, 0, st>>>(bitmap, lab, h, w);
+  ccl_local_kernel<<<tiles, 256, 0, st>>>(d_pred, bitmap, lab, bits, root_flag, tile_bg, h, w,
+                                          thresh);
+  ccl_merge_kernel<<<tiles, 128, 0, st>>>(bitmap, lab, tile_bg, h, w);
   ccl_roots_kernel<<<tiles, 256, 0, st>>>(lab, root_flag, h, w);
   ccl_rows_kernel<<<dim3(h, n_maps), 256, 0, st>>>(lab, row_count, h, w);
   starts_scan_kernel<<<n_maps, kScanThreads, 0, st>>>(row_count, row_off, n_contours, n_total, h);
@@ -890,8 +935,14 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
 // 0 for background joined to the image frame, else 1 + the raster index of
 // the smallest pixel of the pixel's component (foreground 8-connected,
 // background 4-connected). d_bitmap receives the 0/255 threshold bitmap.
+TOCR_API size_t tocr_db_components_scratch_bytes(int n_maps, int h, int w) {
+  if (n_maps <= 0 || h <= 0 || w <= 0) return 0;
+  const size_t tiles = (size_t)n_maps * ((h + kTileH - 1) / kTileH) * ((w + kTileW - 1) / kTileW);
+  return (size_t)n_maps * h * w + tiles;
+}
+
 TOCR_API int tocr_db_components(const float *d_pred, int n_maps, int h, int w, float thresh,
-                                int *d_labels, uint8_t *d_bitmap, void *stream) {
+                                int *d_labels, uint8_t *d_bitmap, void *d_scratch, void *stream) {
   TOCR_ENTRY();
   TOCR_REQUIRE(n_maps >= 0 && h > 0 && w > 0 && (long long)h * w < (1ll << 30),
                "tocr_db_components: bad sizes n_maps=%d h=%d w=%d", n_maps, h, w);
@@ -899,9 +950,12 @@ TOCR_API int tocr_db_components(const float *d_pred, int n_maps, int h, int w, f
   TOCR_REQUIRE(d_pred && d_labels && d_bitmap, "tocr_db_components: null pointer");
   cudaStream_t st = as_stream(stream);
   const dim3 tiles((w + kTileW - 1) / kTileW, (h + kTileH - 1) / kTileH, n_maps);
-  ccl_local_kernel<<<tiles, 256, 0, st>>>(d_pred, d_bitmap, d_labels, nullptr, nullptr, h, w,
-                                          thresh);
-  ccl_merge_kernel<<<tiles, 128, 0, st>>>(d_bitmap, d_labels, h, w);
+  uint8_t *root_flag = static_cast<uint8_t *>(d_scratch);
+  uint8_t *tile_bg = root_flag ? root_flag + (size_t)n_maps * h * w : nullptr;
+  ccl_local_kernel<<<tiles, 256, 0, st>>>(d_pred, d_bitmap, d_labels, nullptr, root_flag, tile_bg,
+                                          h, w, thresh);
+  ccl_merge_kernel<<<tiles, 128, 0, st>>>(d_bitmap, d_labels, tile_bg, h, w);
+  if (root_flag) ccl_roots_kernel<<<tiles, 256, 0, st>>>(d_labels, root_flag, h, w);
   ccl_rows_kernel<<<dim3(h, n_maps), 256, 0, st>>>(d_labels, nullptr, h, w);
   return check_launch("tocr_db_components");
 }

@@ -156,11 +156,17 @@ class DbPostprocess:
                 for m in range(n)]
 
 
-def db_components(pred: torch.Tensor, thresh: float = 0.3, stream=None):
-    """(labels int32 [n, h, w], bitmap u8 [n, h, w]) of the labelling stage."""
+def db_components(pred: torch.Tensor, thresh: float = 0.3, stream=None, shortcuts: bool = True):
+    """(labels int32 [n, h, w], bitmap u8 [n, h, w]) of the labelling stage
+    (with the background-tile shortcuts of the full DB stage by default)."""
+    from ._lib import lib
     n, h, w = pred.shape
     labels = torch.empty(n, h, w, dtype=torch.int32, device=pred.device)
     bitmap = torch.empty(n, h, w, dtype=torch.uint8, device=pred.device)
+    scratch = None
+    if shortcuts:
+        scratch = torch.empty(lib().tocr_db_components_scratch_bytes(n, h, w), dtype=torch.uint8,
+                              device=pred.device)
     call("tocr_db_components", _ptr(pred), n, h, w, thresh, _ptr(labels), _ptr(bitmap),
-         _stream(stream))
+         _ptr(scratch), _stream(stream))
     return labels, bitmap
