@@ -295,7 +295,7 @@ ccl_roots_kernel(int *__restrict__ lab, const uint8_t *__restrict__ root_flag, i
 // joined to the outside) starts a hole border at the pixel on its left.
 // grid (H, n_maps), 256 threads.
 __global__ void __launch_bounds__(256)
-ccl_rows_kernel(int *__restrict__ lab, int *__restrict__ row_count, int H, int W) {
+ccl_rows_kernel(int *__restrict__ lab, int *__restrict__ row_count, int H, int W, bool compress) {
   const int m = blockIdx.y, y = blockIdx.x;
   int *lb = lab + (size_t)m * H * W;
   __shared__ int s_total;
@@ -304,8 +304,15 @@ ccl_rows_kernel(int *__restrict__ lab, int *__restrict__ row_count, int H, int W
   int cnt = 0;
   for (int x = threadIdx.x; x < W; x += blockDim.x) {
     const int p = y * W + x;
-    const int r = find_g(lb, lb[p]);
-    lb[p] = r;
+    // A pixel starts a border iff it is the root of its component. Without
+    // compression that is still exactly "its label is itself": labels only
+    // ever point at smaller nodes, and a tile root that a merge relinked holds
+    // the smaller node it was linked to.
+    int r = lb[p];
+    if (compress) {
+      r = find_g(lb, r);
+      lb[p] = r;
+    }
     cnt += (r == p + 1);
   }
   for (int off = 16; off; off >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, off);
@@ -780,7 +787,7 @@ namespace tocr {
 namespace {
 
 struct DbLayout {
-  size_t bitmap, root_flag, tile_bg, bits, slab, lab, scan_tot, row_count, row_off, n_contours, n_total, starts, npts, pt_off, pts, hpw,
+  size_t bitmap, tile_bg, bits, slab, lab, scan_tot, row_count, row_off, n_contours, n_total, starts, npts, pt_off, pts, hpw,
       hullbuf, fsc, stage1, aabb, stage2, score, dist, offcap, off_off, ring, hpw2, hull2, fsc2,
       keep2, boxes, total;
 };
@@ -794,7 +801,6 @@ DbLayout db_layout(int n_maps, int h, int w, long long point_cap, long long offs
   size_t o = 0;
   auto take = [&](size_t bytes) { const size_t at = o; o = align_up(o + bytes); return at; };
   L.bitmap = take(px);
-  L.root_flag = take(px);
   L.tile_bg = take((size_t)n_maps * ((h + kTileH - 1) / kTileH) * ((w + kTileW - 1) / kTileW));
   L.slab = take(C * kSlab * sizeof(P2));
   L.bits = take((size_t)n_maps * h * ((w + 31) / 32) * 4);
@@ -873,7 +879,6 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
   char *ws = static_cast<char *>(d_workspace);
   auto at = [&](size_t off) { return ws + off; };
   uint8_t *bitmap = (uint8_t *)at(L.bitmap);
-  uint8_t *root_flag = (uint8_t *)at(L.root_flag);
   uint8_t *tile_bg = (uint8_t *)at(L.tile_bg);
   P2 *slab = (P2 *)at(L.slab);
   uint32_t *bits = (uint32_t *)at(L.bits);
@@ -900,11 +905,10 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
 
   cudaError_t e = cudaMemsetAsync(d_status, 0, sizeof(int), st);
   if (e != cudaSuccess) return set_error(TOCR_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
-  ccl_local_kernel<<<tiles, 256, 0, st>>>(d_pred, bitmap, lab, bits, root_flag, tile_bg, h, w,
+  ccl_local_kernel<<<tiles, 256, 0, st>>>(d_pred, bitmap, lab, bits, nullptr, tile_bg, h, w,
                                           thresh);
   ccl_merge_kernel<<<tiles, 128, 0, st>>>(bitmap, lab, tile_bg, h, w);
-  ccl_roots_kernel<<<tiles, 256, 0, st>>>(lab, root_flag, h, w);
-  ccl_rows_kernel<<<dim3(h, n_maps), 256, 0, st>>>(lab, row_count, h, w);
+  ccl_rows_kernel<<<dim3(h, n_maps), 256, 0, st>>>(lab, row_count, h, w, false);
   starts_scan_kernel<<<n_maps, kScanThreads, 0, st>>>(row_count, row_off, n_contours, n_total, h);
   starts_write_kernel<<<dim3(h, n_maps), 256, 0, st>>>(lab, bitmap, row_count, row_off, starts, h, w);
   trace_kernel<<<cgrid, 128, 0, st>>>(bits, starts, n_contours, npts, slab, d_status, n_maps, h, w);
@@ -956,7 +960,7 @@ TOCR_API int tocr_db_components(const float *d_pred, int n_maps, int h, int w, f
                                           h, w, thresh);
   ccl_merge_kernel<<<tiles, 128, 0, st>>>(d_bitmap, d_labels, tile_bg, h, w);
   if (root_flag) ccl_roots_kernel<<<tiles, 256, 0, st>>>(d_labels, root_flag, h, w);
-  ccl_rows_kernel<<<dim3(h, n_maps), 256, 0, st>>>(d_labels, nullptr, h, w);
+  ccl_rows_kernel<<<dim3(h, n_maps), 256, 0, st>>>(d_labels, nullptr, h, w, true);
   return check_launch("tocr_db_components");
 }
 
