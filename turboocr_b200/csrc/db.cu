@@ -524,8 +524,20 @@ __global__ void check_cap_kernel(const long long *__restrict__ off, long long n,
   if (off[n] > cap) atomicOr(status, bit);
 }
 
-// min-area rectangle of a point set through its hull; scratch sized for n points.
+// min-area rectangle of a point set through its hull; scratch sized for n
+// points. Point sets up to kLocalPts use thread-local arrays (cached in L1,
+// write-back) instead of the global scratch: the hull sort reads what it
+// has just written, which from global memory costs an L2 round trip each.
+constexpr int kLocalPts = 96;
+
 __device__ RRect rect_of(const P2 *p, int n, HP *hpw, P2 *hull, float *fsc) {
+  if (n <= kLocalPts) {
+    HP lw[2 * kLocalPts + 2];
+    P2 lh[kLocalPts + 1];
+    float lf[3 * kLocalPts + 3];
+    const int h = db::convex_hull(p, n, lw, lh);
+    return db::min_area_rect(lh, h, lf);
+  }
   const int h = db::convex_hull(p, n, hpw, hull);
   return db::min_area_rect(hull, h, fsc);
 }
@@ -582,15 +594,18 @@ score_kernel(const float *__restrict__ pred, const int *__restrict__ stage1,
              const long long *__restrict__ pt_off, const P2 *__restrict__ pts,
              int *__restrict__ stage2, float *__restrict__ score, double *__restrict__ dist,
              DbParams P) {
-  const long long c = blockIdx.x;
-  if (!stage1[c]) {
-    if (threadIdx.x == 0) stage2[c] = 0;
-    return;
-  }
   __shared__ unsigned s_edge[kBandRows][kMaxWords];
   __shared__ unsigned s_tog[kBandRows][kMaxWords];
   __shared__ double s_sum[kScoreThreads / 32];
   __shared__ long long s_cnt[kScoreThreads / 32];
+  // grid-stride over the contour slots: most slots are empty or filtered, so
+  // a CTA per slot would spend its time being scheduled
+  const long long n_slots = (long long)P.n_maps * kMaxCand;
+  for (long long c = blockIdx.x; c < n_slots; c += gridDim.x) {
+  if (!stage1[c]) {
+    if (threadIdx.x == 0) stage2[c] = 0;
+    continue;
+  }
   const int m = (int)(c / kMaxCand);
   const int H = P.H, W = P.W;
   const int n = npts[c];
@@ -664,18 +679,22 @@ score_kernel(const float *__restrict__ pred, const int *__restrict__ stage1,
     s_cnt[threadIdx.x >> 5] = cnt;
   }
   __syncthreads();
-  if (threadIdx.x != 0) return;
-  double tsum = 0.;
-  long long tcnt = 0;
-  for (int w = 0; w < kScoreThreads / 32; ++w) { tsum += s_sum[w]; tcnt += s_cnt[w]; }
-  const float sc = (nonempty && tcnt > 0) ? (float)(tsum / (double)tcnt) : 0.f;
-  score[c] = sc;
-  stage2[c] = 0;
-  if (sc < P.box_thresh) return;
-  const double per = db::arc_length(p, n);
-  // unclip returns the contour itself when the perimeter is 0 (distance 0 here)
-  dist[c] = per != 0. ? db::contour_area(p, n) * (double)P.unclip_ratio / per : 0.;
-  stage2[c] = 1;
+  if (threadIdx.x == 0) {
+    double tsum = 0.;
+    long long tcnt = 0;
+    for (int w = 0; w < kScoreThreads / 32; ++w) { tsum += s_sum[w]; tcnt += s_cnt[w]; }
+    const float sc = (nonempty && tcnt > 0) ? (float)(tsum / (double)tcnt) : 0.f;
+    score[c] = sc;
+    stage2[c] = 0;
+    if (sc >= P.box_thresh) {
+      const double per = db::arc_length(p, n);
+      // unclip returns the contour itself when the perimeter is 0 (distance 0 here)
+      dist[c] = per != 0. ? db::contour_area(p, n) * (double)P.unclip_ratio / per : 0.;
+      stage2[c] = 1;
+    }
+  }
+  __syncthreads();
+  }
 }
 
 // 7. one thread per surviving contour: the unclip ring (kCount: only its
@@ -704,13 +723,15 @@ unclip_kernel(const int *__restrict__ stage2, const int *__restrict__ npts,
   }
   if (off_off[c + 1] > P.offset_cap) return;
   const long long oo = off_off[c] + c;  // offcap + 1 scratch slots per contour
-  P2 *r = ring + oo;
+  const int cap = (int)(off_off[c + 1] - off_off[c]);
+  P2 local_ring[kLocalPts];
+  P2 *r = cap <= kLocalPts ? local_ring : ring + oo;
   int rn;
   if (qm == 0) {  // no offset: unclip returns the contour itself
     for (int i = 0; i < n; ++i) r[i] = p[i];
     rn = n;
   } else {
-    rn = db::offset_raw(q, qm, d, r, (int)(off_off[c + 1] - off_off[c]));
+    rn = db::offset_raw(q, qm, d, r, cap);
   }
   if (rn < 3) return;
   const RRect rr = rect_of(r, rn, hpw2 + 2 * oo, hull2 + oo, fsc2 + 3 * oo);
@@ -919,8 +940,8 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
                                                                  pts, point_cap, n_maps, h, w);
   geom_box1_kernel<<<cgrid, 128, 0, st>>>(n_contours, npts, pt_off, pts, hpw, hullbuf, fsc,
                                           stage1, aabb, P);
-  score_kernel<<<(unsigned)C, kScoreThreads, 0, st>>>(d_pred, stage1, aabb, npts, pt_off, pts,
-                                                       stage2, score, dist, P);
+  score_kernel<<<(unsigned)(C < 148 * 8 ? C : 148 * 8), kScoreThreads, 0, st>>>(
+      d_pred, stage1, aabb, npts, pt_off, pts, stage2, score, dist, P);
   unclip_kernel<true><<<cgrid, 128, 0, st>>>(stage2, npts, pt_off, pts, hullbuf, dist, offcap,
                                              off_off, ring, hpw2, hull2, fsc2, d_geometry, keep2,
                                              boxes, P);
