@@ -403,13 +403,13 @@ class E2eWorkload:
     through preprocess + stem -> 8 INT8 DW+PW blocks -> head -> DB -> crops
     48x320 -> CTC (T=80, V=18385), split contiguously over the ranks (strong
     scaling: the job is 4096 pages in total). One step = this rank's whole
-    shard, in micro-batches of 16 pages (turboocr_b200.pipeline.PagePipeline)."""
+    shard, in micro-batches of 32 pages (turboocr_b200.pipeline.PagePipeline)."""
     name = "e2e_4096pages_960x960_det_rec"
     metric = "pages/sec det+rec hot path (960x960)"
     unit = "pages/s"
     dtype = "i8 (DW+PW blocks) / f16 activations / f32 DB map"
     scaling = "strong"
-    TOTAL, MB = 4096, 16
+    TOTAL, MB = 4096, 32
     l2_note = "pages 2.76 MB each, >= 1.4 GB of input per rank per step > 126 MB L2 (no flush needed)"
     world = 1
     rank = 0
