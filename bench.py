@@ -410,6 +410,10 @@ class E2eWorkload:
     dtype = "i8 (DW+PW blocks) / f16 activations / f32 DB map"
     scaling = "strong"
     TOTAL, MB = 4096, 32
+    # DRAM bytes of the dominant launch (the CTC decode of pages 0..31's crops),
+    # from the ncu capture summarised in profiles/e2e_4096pages_960x960.md
+    traffic_per_launch = 5_026_007_296 + 3_558_912
+    traffic_source = "profiles/e2e_4096pages_960x960.md"
     l2_note = "pages 2.76 MB each, >= 1.4 GB of input per rank per step > 126 MB L2 (no flush needed)"
     world = 1
     rank = 0
@@ -739,7 +743,8 @@ def main():
                     "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
-                         "traffic": getattr(Wl, "traffic_per_unit", 0) * wl.units_per_step or None,
+                         "traffic": getattr(Wl, "traffic_per_launch", None) or
+                                    (getattr(Wl, "traffic_per_unit", 0) * wl.units_per_step or None),
                          "traffic_source": getattr(Wl, "traffic_source", None),
                          "peak_source": f"{peak_kind} hbm_gbs",
                          "algorithmic_bytes_per_launch": wl.algo_bytes},
