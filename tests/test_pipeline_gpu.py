@@ -177,6 +177,11 @@ def test_pipeline_small_batch(cuda):
         ref = do.db_postprocess(prob[m], unclip_fn=raw_unclip)
         assert [q for q, *_ in res[m]] == [b for b, _ in ref]
         assert 15 <= len(ref) <= 100, len(ref)
+        # text lines are axis-aligned here: their contours have no concave
+        # corners, so Clipper's union leaves the raw offset's hull unchanged and
+        # the boxes equal the full reference path too
+        full = do.db_postprocess(prob[m])
+        assert [q for q, *_ in res[m]] == [b for b, _ in full]
     # crops: reference kernel on page 0's crops
     from oracle import ref_kernels as rk
     k0 = len(res[0])
