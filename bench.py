@@ -13,6 +13,7 @@ Workloads:
   ctc         config 2: 512 lines x 80 steps x 18385-class fp16 logits per GPU
   preprocess  config 3: 256 u8 HWC images (sides 600..2000) -> fp16 960x960 NCHW
   dwpw        config 4: fused DW3x3+PW1x1 block, 32 x 240 x 240 x 128 -> 256, INT8
+  db          config 1: DB post-process of 8 fp32 960x960 probability maps
 """
 from __future__ import annotations
 
@@ -398,6 +399,96 @@ def touched_source_bytes(dims, content):
     return total
 
 
+class DbWorkload:
+    """DB post-process of 8 fp32 probability maps 960x960
+    (40-200 rotated text rectangles each), threshold 0.3, box_thresh 0.6,
+    unclip 1.5, fused on the device (tocr_db_postprocess). --units sets the
+    batch (the survey's sweep: 8 / 64 / 512)."""
+    name = "db_postprocess_8x960x960"
+    metric = "maps/sec DB post-process (960x960 fp32 probability maps)"
+    unit = "maps/s"
+    dtype = "f32 map / int geometry"
+    N, H, W = 8, 960, 960
+    launches_per_step = 16
+    l2_note = ("8 maps = 29.5 MB < L2: every step first writes a 256 MB buffer to flush L2 "
+               "(inside the timed step; the roofline time excludes it)")
+
+    def __init__(self, dev, seed, units=None):
+        from turboocr_b200._lib import synth
+        from turboocr_b200.kernels import DbPostprocess
+        if units:
+            self.N = units
+        self.units_per_step = self.N
+        maps = np.zeros((self.N, self.H, self.W), np.float32)
+        for i in range(self.N):
+            synth().tocr_synth_db_map_host(maps[i].ctypes.data, self.H, self.W, 40, 200, seed, i)
+        self.host_maps = maps
+        self.maps = torch.from_numpy(maps).to(dev)
+        self.db = DbPostprocess(self.N, self.H, self.W, dev, max_boxes=512)
+        self.flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        self.algo_bytes = self.N * self.H * self.W * 4  # every map read once
+        torch.cuda.synchronize()
+
+    def step(self):
+        self.flush.fill_(1)      # evict the maps from L2 (126 MB) between steps
+        self.db(self.maps)
+
+    def dominant_kernel_ms(self, iters=10):
+        """The whole DB stage of one batch (L2 flushed before each)."""
+        s = torch.cuda.current_stream()
+        t = 0.0
+        for _ in range(iters):
+            self.flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            self.db(self.maps)
+            e1.record(s)
+            torch.cuda.synchronize()
+            t += e0.elapsed_time(e1)
+        self.dominant = "tocr_db_postprocess (16 launches) per batch"
+        return t / iters
+
+    def setup_e2e(self):
+        self.h_maps = torch.empty(self.maps.shape, dtype=torch.float32, pin_memory=True)
+        self.h_maps.copy_(self.maps)
+        d = self.db
+        self.h_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+                      for t in (d.boxes, d.scores, d.counts)]
+        self.h2d = self.h_maps.numel() * 4
+        self.d2h = sum(t.numel() * t.element_size() for t in self.h_out)
+
+    def e2e_step(self):
+        self.maps.copy_(self.h_maps, non_blocking=True)
+        self.db(self.maps)
+        for h, d in zip(self.h_out, (self.db.boxes, self.db.scores, self.db.counts)):
+            h.copy_(d, non_blocking=True)
+
+    def cpu_baseline(self, cores, budget_s=15.0):
+        """The CPU restatement of extract_boxes_from_bitmap (cv2 + the
+        reference's Clipper, with cv2.compare-style threshold), one process per
+        map over all host cores."""
+        from concurrent.futures import ProcessPoolExecutor
+        import multiprocessing as mpc
+        n = self.N
+        reps = 0
+        with ProcessPoolExecutor(min(cores, n), mp_context=mpc.get_context("spawn")) as ex:
+            list(ex.map(_db_map_cpu, [self.host_maps[0]]))  # warm the workers
+            t0 = time.perf_counter()
+            while True:
+                list(ex.map(_db_map_cpu, list(self.host_maps)))
+                reps += 1
+                if time.perf_counter() - t0 > budget_s or reps >= 20:
+                    break
+        dt = time.perf_counter() - t0
+        return {"value": n * reps / dt, "unit": self.unit, "cores": min(cores, n), "kind": "port",
+                "sample": f"{n} maps x {reps} reps, one process per map (cv2 + reference Clipper)"}
+
+
+def _db_map_cpu(m):
+    from oracle import db_oracle as do
+    return len(do.db_postprocess(m))
+
+
 class E2eWorkload:
     """BASELINE config 5 (the headline metric): 4096 synthetic 960x960 pages
     through preprocess + stem -> 8 INT8 DW+PW blocks -> head -> DB -> crops
@@ -622,9 +713,10 @@ def _crop_ref(box):
     return m, cw.value, v.value
 
 
-WORKLOADS = {"ctc": CtcWorkload, "preprocess": PreprocessWorkload, "dwpw": DwPwWorkload,
+WORKLOADS = {"db": DbWorkload, "ctc": CtcWorkload, "preprocess": PreprocessWorkload,
+             "dwpw": DwPwWorkload,
              "e2e": E2eWorkload}
-SEEDS = {"ctc": 1, "preprocess": 2, "dwpw": 3, "e2e": 5}
+SEEDS = {"db": 0, "ctc": 1, "preprocess": 2, "dwpw": 3, "e2e": 5}
 
 
 # ------------------------------------------------------------------ main ----

@@ -49,6 +49,12 @@ TOCR_API int tocr_version(void);
  * count <= 0 clears the injection. Never faults a device. */
 TOCR_API void tocr_debug_inject_error(int status, int count);
 
+/* Test hook: the widest point set (x columns) tocr_db_postprocess's
+ * shared-memory geometry takes (0: every set above 96 points uses the global
+ * scratch pool; < 0: the compiled capacity, 6144). Process-wide; results do
+ * not depend on it. */
+TOCR_API void tocr_debug_db_shared_columns(int columns);
+
 /* ---- subsystem 4: CTC greedy decode ------------------------------------ */
 
 /* Replaces turbo_ocr::kernels::cuda_argmax
@@ -140,11 +146,13 @@ TOCR_API int tocr_threshold_u8(const float *d_src, uint8_t *d_dst, int w,
  * ([n_maps][max_boxes]) and counts ([n_maps]) in contour order.
  * d_geometry: NULL (identity) or int [n_maps][4] = orig_h, orig_w, resize_h,
  * resize_w for the scaling of det_postprocess.cpp:205-210.
- * point_cap / offset_cap bound the traced points and the offset-path points
- * of a call (<= 0: defaults); the workspace (256-byte aligned) must hold
+ * point_cap bounds the traced contour points of a call; offset_cap sizes a
+ * scratch pool (64 bytes per point) used only by point sets (contours,
+ * unclip rings) wider than the shared-memory geometry takes (6144 columns);
+ * <= 0: defaults. The workspace (256-byte aligned) must hold
  * tocr_db_workspace_bytes(n_maps, h, w, point_cap, offset_cap) bytes.
  * d_status (device int) receives 0 or a bit set: 1 point pool full, 2 a
- * border walk exceeded its bound, 4 offset pool full, 8 more than max_boxes
+ * border walk exceeded its bound, 4 scratch pool full, 8 more than max_boxes
  * kept (truncated). Enqueued on `stream`; no synchronisation, no allocation. */
 TOCR_API size_t tocr_db_workspace_bytes(int n_maps, int h, int w, long long point_cap,
                                         long long offset_cap);

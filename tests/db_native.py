@@ -49,6 +49,8 @@ def lib():
     L.dbh_trace.argtypes = [vp, i, i, i, i, i, vp, i]
     L.dbh_trace_bits.argtypes = [vp, i, i, i, i, i, vp, i]
     L.dbh_hull.argtypes = [vp, i, vp]
+    L.dbh_hull_table.argtypes = [vp, i, vp, i, i]
+    L.dbh_offset_parallel.argtypes = [vp, i, d, vp, i]
     L.dbh_min_area_rect.argtypes = [vp, i, vp]
     L.dbh_mini_box.argtypes = [vp, i, vp, vp]
     L.dbh_area.argtypes = [vp, i]
@@ -82,6 +84,23 @@ def hull(p):
     out = np.zeros((len(p) + 1, 2), np.int32)
     m = lib().dbh_hull(p.ctypes.data, len(p), out.ctypes.data)
     return out[:m]
+
+
+def hull_table(p, col_cap=1 << 20, hull_cap=1 << 20):
+    """The column-table hull of the device's shared-memory path."""
+    a = _pts(p)
+    out = np.zeros((len(a) + 1, 2), np.int32)
+    m = lib().dbh_hull_table(a.ctypes.data, len(a), out.ctypes.data, col_cap, hull_cap)
+    return m if m < 0 else out[:m]
+
+
+def offset_parallel(p, delta):
+    """Offset ring by independent vertices (None when a joint keeps k)."""
+    a = _pts(p)
+    cap = 64 * len(a) + 64
+    out = np.zeros((cap, 2), np.int32)
+    n = lib().dbh_offset_parallel(a.ctypes.data, len(a), float(delta), out.ctypes.data, cap)
+    return None if n < 0 else [tuple(v) for v in out[:n].tolist()]
 
 
 def min_area_rect(p):

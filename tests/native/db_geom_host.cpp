@@ -2,6 +2,7 @@
 // geometry routines over a C ABI so the CPU tests can compare them, routine
 // by routine, with OpenCV and with the reference's Clipper. Built by the
 // tests themselves (tests/db_native.py); never linked into the product.
+#include <algorithm>
 #include <cstring>
 #include <vector>
 
@@ -32,6 +33,45 @@ int dbh_trace_bits(const unsigned char *bm, int H, int W, int x0, int y0, int ho
 int dbh_hull(const int *pts, int n, int *out) {
   std::vector<HP> work(2 * n + 2);
   return convex_hull(reinterpret_cast<const P2 *>(pts), n, work.data(), reinterpret_cast<P2 *>(out));
+}
+
+// The device's shared-memory hull: the column table (lowest / highest point
+// of every x column, first index), chain over its candidates. Returns the
+// hull size (-1: more than hull_cap vertices, -2: more than col_cap columns).
+int dbh_hull_table(const int *pts, int n, int *out, int col_cap, int hull_cap) {
+  if (n <= 0) return 0;
+  int x0 = pts[0], x1 = pts[0];
+  for (int i = 1; i < n; ++i) {
+    x0 = std::min(x0, pts[2 * i]);
+    x1 = std::max(x1, pts[2 * i]);
+  }
+  const int ncols = x1 - x0 + 1;
+  if (ncols > col_cap) return -2;
+  std::vector<uint64_t> lo(ncols, kColEmpty), hi(ncols, kColEmpty);
+  for (int i = 0; i < n; ++i) col_add(lo.data(), hi.data(), pts[2 * i] - x0, pts[2 * i + 1], i);
+  std::vector<int> stk(2 * (size_t)ncols + 2);
+  return hull_from_table(lo.data(), hi.data(), ncols, x0, stk.data(), reinterpret_cast<P2 *>(out),
+                         hull_cap);
+}
+
+// Offset ring through the per-vertex form with k = j - 1 for every vertex
+// (the device's parallel emission): returns the count, or -1 when some vertex
+// before the last keeps k (the device then emits serially).
+int dbh_offset_parallel(const int *pts, int n, double delta, int *out, int cap) {
+  std::vector<P2> q(n + 1);
+  const int m = offset_prepare(reinterpret_cast<const P2 *>(pts), n, q.data());
+  if (m == 0 || offset_is_identity(delta)) return -1;
+  const OffsetConsts oc = offset_consts(delta);
+  int cnt = 0;
+  for (int j = 0; j < m; ++j) {
+    const bool keep = offset_vertex(q.data(), m, j, j == 0 ? m - 1 : j - 1, delta, oc,
+                                    [&](long long x, long long y) {
+                                      if (cnt < cap) { out[2 * cnt] = (int)x; out[2 * cnt + 1] = (int)y; }
+                                      ++cnt;
+                                    });
+    if (keep && j < m - 1) return -1;
+  }
+  return cnt;
 }
 
 // minAreaRect of a point sequence: writes cx, cy, w, h, angle.

@@ -165,3 +165,55 @@ def test_min_area_rect_and_mini_box():
                 assert dn.mini_box(pts) == do.get_mini_boxes(pts), c.tolist()
                 n += 1
     assert n > 80
+
+
+def test_column_table_hull_equals_sorted_hull():
+    """The device's shared-memory hull (lowest and highest point of every x
+    column with their first index, chain over those) returns the same
+    vertices, orientation and starting vertex as the sorted monotone chain,
+    including repeated points, vertical columns, collinear runs and
+    degenerate sets."""
+    rng = np.random.default_rng(21)
+    sets = []
+    for _ in range(3000):  # small ranges: many repeats and collinear points
+        n = int(rng.integers(1, 60))
+        r = int(rng.integers(1, 8))
+        sets.append(rng.integers(-r, r + 1, (n, 2)))
+    for _ in range(300):
+        n = int(rng.integers(3, 400))
+        sets.append(rng.integers(-2000, 2000, (n, 2)))
+    sets += [[[5, 5]] * 4, [[1, 2], [1, 9], [1, 4]], [[0, 0], [3, 3], [6, 6], [3, 3]],
+             [[0, 0], [0, 0], [1, 0], [1, 0]], [[7, -3]]]
+    for mi in range(3):  # contours and offset rings of config-1 style maps
+        m = synth_map(480, 640, 20, 60, mi)
+        for c in do.find_contours(do.threshold(m, 0.3)):
+            sets.append(c)
+            if len(c) > 2:
+                sets.append(np.array(dn.offset_raw(c, 9.5) or c.tolist(), np.int32))
+    for p in sets:
+        assert dn.hull_table(p).tolist() == dn.hull(p).tolist(), np.asarray(p).tolist()
+    wide = rng.integers(0, 5000, (500, 2))
+    assert dn.hull_table(wide, col_cap=64) == -2
+
+
+def test_parallel_offset_emission():
+    """With k = j - 1 at every vertex (the device's one-thread-per-vertex
+    emission), the ring equals Clipper's serial DoOffset whenever no joint
+    before the last keeps k; otherwise the device emits serially. Contour
+    joints turn by multiples of 45 degrees, so k is only kept for distances
+    below 1/sin(45)."""
+    same = serial = 0
+    for mi in range(3):
+        m = synth_map(480, 640, 20, 60, mi)
+        for c in do.find_contours(do.threshold(m, 0.3)):
+            if len(c) < 3:
+                continue
+            for d in (0.7, 3.0, 9.5, 40.0):
+                par = dn.offset_parallel(c, d)
+                if par is None:
+                    assert d < 1.42
+                    serial += 1
+                else:
+                    assert par == dn.offset_raw(c, d)
+                    same += 1
+    assert same > 100 and serial > 10, (same, serial)

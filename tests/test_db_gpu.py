@@ -192,3 +192,50 @@ def test_db_vs_clipper_union_rate(cuda):
             assert np.abs(np.array(b1) - np.array(b2)).max() <= 6
             assert abs(s1 - s2) <= SCORE_TOL
     assert total > 60 and same >= 0.9 * total, (same, total)
+
+
+@pytest.fixture
+def shared_columns():
+    """Sets the shared-memory geometry's column capacity for one test, then
+    restores it."""
+    from turboocr_b200._lib import lib
+    yield lambda v: lib().tocr_debug_db_shared_columns(v)
+    lib().tocr_debug_db_shared_columns(-1)
+
+
+@pytest.mark.parametrize("cap", [0, 300])
+def test_db_global_scratch_path_exact(cuda, shared_columns, cap):
+    """Point sets wider than the shared-memory column table take the
+    one-thread global scratch path (cap 0: every set above 96 points; 300
+    columns: a mix): same boxes."""
+    shared_columns(cap)
+    maps = synth_maps(3, 960, 960, first=400)
+    got = run_gpu(cuda, maps)
+    for m in range(3):
+        compare_exact(got[m], do.db_postprocess(maps[m], unclip_fn=raw_unclip))
+
+
+def test_db_scratch_pool_full_raises(cuda, shared_columns):
+    from turboocr_b200.kernels import DbPostprocess
+    shared_columns(0)
+    maps = synth_maps(2, 960, 960, first=400)
+    db = DbPostprocess(2, 960, 960, cuda, offset_cap=64)
+    db(torch.from_numpy(maps).to(cuda))
+    with pytest.raises(RuntimeError, match="scratch pool"):
+        db.results()
+
+
+@pytest.mark.parametrize("cap", [-1, 1000])
+def test_db_wide_jagged_bar_exact(cuda, shared_columns, cap):
+    """A contour of ~1300 points over 2560 columns and its ring: through the
+    shared-memory table (cap -1) and through the global path (1000 columns)."""
+    shared_columns(cap)
+    h, w = 48, 2600
+    m = np.zeros((h, w), np.float32)
+    m[12:36, 20:2580] = 0.9
+    for x in range(20, 2580, 8):
+        m[10:12, x:x + 4] = 0.9               # jagged top edge
+    got = run_gpu(cuda, m[None].copy())
+    ref = do.db_postprocess(m, unclip_fn=raw_unclip)
+    assert len(ref) == 1
+    compare_exact(got[0], ref)

@@ -53,6 +53,7 @@ SIGNATURES: dict[str, tuple] = {
     "tocr_last_error_string": (C.c_char_p, []),
     "tocr_version": (_i, []),
     "tocr_debug_inject_error": (None, [_i, _i]),
+    "tocr_debug_db_shared_columns": (None, [_i]),
     "tocr_argmax_f32": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
     "tocr_ctc_greedy_f16": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp]),
     "tocr_ctc_greedy_f16_noalloc": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),

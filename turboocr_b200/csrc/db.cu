@@ -14,10 +14,17 @@
 //                          (descending raster order), capped at 3000 per map
 //                          (det_postprocess.cpp:165-167)
 //   5. trace_*             border following, CHAIN_APPROX_SIMPLE, count then write
-//   6. geom_score_kernel   size filters, first min-area box, polygon-mask mean
-//                          (box_score_fast, det_postprocess.cpp:15-55), unclip distance
-//   7. geom_unclip_kernel  round-join offset (Clipper's DoOffset), second min-area
-//                          box, scale/round/clamp, edge filters
+//   6. geom_box1_kernel    size filters and the first min-area box, thread per
+//      geom_big_kernel     contour; contours above 96 points take a CTA each
+//                          (the lowest and highest point of every x column
+//                          gathered with shared-memory atomics, then chain
+//                          and rotating calipers over those)
+//      score_kernel        polygon-mask mean (box_score_fast,
+//                          det_postprocess.cpp:15-55), unclip distance
+//   7. unclip_kernel       round-join offset (Clipper's DoOffset), second
+//      unclip_big_kernel   min-area box, scale/round/clamp, edge filters;
+//                          rings above 96 points again take a CTA each
+//                          (vertices offset in parallel)
 //   8. compact_kernel      kept boxes in contour order
 //
 // Node ids: 0 is the outside of map m; pixel p = y*W + x of the map is node
@@ -26,6 +33,8 @@
 //
 // This translation unit is compiled with -fmad=false: the geometry must keep
 // the libraries' operation order (explicit fma() only where they contract).
+#include <atomic>
+
 #include "tocr_common.cuh"
 
 #include "db_geom.cuh"
@@ -52,7 +61,30 @@ struct DbParams {
   float thresh, box_thresh, unclip_ratio, min_box_side, min_unclipped_side;
   long long point_cap, offset_cap;
   int max_boxes;
+  int big_cols;                   // widest point set (x columns) the shared-memory path takes
+  unsigned long long pool_bytes;  // scratch pool for wider sets
 };
+
+// Point sets (contours, unclip rings) above kLocalPts points go to one CTA
+// each, reduced to a table of their x columns in shared memory (kBigCols
+// columns; the lowest and highest point of each). Wider sets, or hulls above
+// kBigHull vertices, fall back to one thread over the global scratch pool.
+constexpr int kBigThreads = 512;
+constexpr int kBigCols = 6144;
+constexpr int kBigHull = 2048;
+constexpr size_t kBigTabBytes = sizeof(uint64_t) * 2 * kBigCols;
+constexpr size_t kBigStkBytes = sizeof(int) * (2 * kBigCols + 2);
+constexpr size_t kBigHullBytes = sizeof(P2) * kBigHull;
+constexpr size_t kBigFscBytes = sizeof(float) * 3 * kBigHull;
+constexpr size_t kBigSmem = kBigTabBytes + kBigStkBytes + kBigHullBytes + kBigFscBytes;
+// the prepared offset path aliases everything after the table
+constexpr int kBigQPts = (int)((kBigSmem - kBigTabBytes) / sizeof(P2));
+constexpr unsigned long long kPoolBytesPerPoint = 64;
+static_assert(kBigSmem <= 227 * 1024, "shared memory of the CTA geometry path");
+
+// Counters of the CTA geometry path: [0] contour list length, [1] ring list
+// length, [2..3] pool bytes used (u64).
+constexpr int kCounters = 4;
 
 // ---------------------------------------------------------------- union-find --
 __device__ __forceinline__ int find_g(const int *lab, int v) {
@@ -519,37 +551,60 @@ scan_base_kernel(long long *__restrict__ out, const long long *__restrict__ tot,
   for (int i = threadIdx.x; i < kMaxCand; i += kScanThreads) out[base + i] += s_base;
 }
 
-__global__ void check_cap_kernel(const long long *__restrict__ off, long long n, long long cap,
-                                 int *__restrict__ status, int bit) {
-  if (off[n] > cap) atomicOr(status, bit);
+// Point-pool check; also zeroes the CTA geometry path's counters.
+__global__ void prep_geom_kernel(const long long *__restrict__ off, long long n, long long cap,
+                                 int *__restrict__ status, int *__restrict__ counters) {
+  if (off[n] > cap) atomicOr(status, kErrPointPool);
+  for (int i = 0; i < kCounters; ++i) counters[i] = 0;
 }
 
-// min-area rectangle of a point set through its hull; scratch sized for n
-// points. Point sets up to kLocalPts use thread-local arrays (cached in L1,
-// write-back) instead of the global scratch: the hull sort reads what it
-// has just written, which from global memory costs an L2 round trip each.
+// min-area rectangle of a small point set (n <= kLocalPts) in thread-local
+// arrays (cached in L1, write-back).
 constexpr int kLocalPts = 96;
 
-__device__ RRect rect_of(const P2 *p, int n, HP *hpw, P2 *hull, float *fsc) {
-  if (n <= kLocalPts) {
-    HP lw[2 * kLocalPts + 2];
-    P2 lh[kLocalPts + 1];
-    float lf[3 * kLocalPts + 3];
-    const int h = db::convex_hull(p, n, lw, lh);
-    return db::min_area_rect(lh, h, lf);
+__device__ RRect rect_local(const P2 *p, int n) {
+  HP lw[2 * kLocalPts + 2];
+  P2 lh[kLocalPts + 1];
+  float lf[3 * kLocalPts + 3];
+  const int h = db::convex_hull(p, n, lw, lh);
+  return db::min_area_rect(lh, h, lf);
+}
+
+__device__ char *pool_alloc(char *pool, int *counters, unsigned long long pool_bytes,
+                            unsigned long long bytes, int *status) {
+  bytes = (bytes + 15) & ~15ull;
+  auto *used = reinterpret_cast<unsigned long long *>(counters + 2);
+  const unsigned long long at = atomicAdd(used, bytes);
+  if (at + bytes > pool_bytes) {
+    atomicOr(status, kErrOffsetPool);
+    return nullptr;
   }
-  const int h = db::convex_hull(p, n, hpw, hull);
-  return db::min_area_rect(hull, h, fsc);
+  return pool + at;
+}
+
+// One thread, global scratch: the min-area rectangle of p[0..n) for sets the
+// shared-memory path cannot take. False when the pool is exhausted.
+__device__ bool rect_global(const P2 *p, int n, char *pool, int *counters,
+                            unsigned long long pool_bytes, int *status, RRect *r) {
+  const unsigned long long hp = ((2ull * n + 1) * sizeof(HP) + 15) & ~15ull;
+  const unsigned long long hl = ((n + 1ull) * sizeof(P2) + 15) & ~15ull;
+  char *w = pool_alloc(pool, counters, pool_bytes, hp + hl + 12ull * (n + 1), status);
+  if (!w) return false;
+  P2 *hull = reinterpret_cast<P2 *>(w + hp);
+  const int h = db::convex_hull(p, n, reinterpret_cast<HP *>(w), hull);
+  *r = db::min_area_rect(hull, h, reinterpret_cast<float *>(w + hp + hl));
+  return true;
 }
 
 // 6a. one thread per contour slot: the filters before the score
 // (det_postprocess.cpp:169-186): more than 2 points, boundingRect sides >= 3,
 // first min-area box side >= min_box_side. Survivors get their AABB.
+// Contours above kLocalPts points are listed for geom_big_kernel.
 __global__ void __launch_bounds__(128)
 geom_box1_kernel(const int *__restrict__ n_contours, const int *__restrict__ npts,
                  const long long *__restrict__ pt_off, const P2 *__restrict__ pts,
-                 HP *__restrict__ hpw, P2 *__restrict__ hullbuf, float *__restrict__ fsc,
-                 int *__restrict__ stage1, int4 *__restrict__ aabb, DbParams P) {
+                 int *__restrict__ stage1, int4 *__restrict__ aabb, int *__restrict__ list,
+                 int *__restrict__ counters, DbParams P) {
   const long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= (long long)P.n_maps * kMaxCand) return;
   stage1[c] = 0;
@@ -563,11 +618,119 @@ geom_box1_kernel(const int *__restrict__ n_contours, const int *__restrict__ npt
     ymin = min(ymin, p[i].y); ymax = max(ymax, p[i].y);
   }
   if (xmax - xmin + 1 < 3 || ymax - ymin + 1 < 3) return;
-  const long long so = pt_off[c] + c;  // n + 1 scratch slots per contour
-  const RRect r = rect_of(p, n, hpw + 2 * so, hullbuf + so, fsc + 3 * so);
-  if ((r.w < r.h ? r.w : r.h) < P.min_box_side) return;
   aabb[c] = make_int4(xmin, ymin, xmax, ymax);
+  if (n > kLocalPts) {
+    list[atomicAdd(counters, 1)] = (int)c;
+    return;
+  }
+  const RRect r = rect_local(p, n);
+  if ((r.w < r.h ? r.w : r.h) < P.min_box_side) return;
   stage1[c] = 1;
+}
+
+// ---- CTA geometry: one point set per CTA, all in shared memory ----------
+struct BigSmem {
+  unsigned long long *lo, *hi;  // column table
+  int *stk;
+  P2 *hull;
+  float *fsc;
+  P2 *q;  // aliases stk .. fsc (dead once the ring is in the table)
+};
+
+__device__ __forceinline__ BigSmem big_smem(uint8_t *base) {
+  BigSmem b;
+  b.lo = reinterpret_cast<unsigned long long *>(base);
+  b.hi = b.lo + kBigCols;
+  b.stk = reinterpret_cast<int *>(base + kBigTabBytes);
+  b.hull = reinterpret_cast<P2 *>(base + kBigTabBytes + kBigStkBytes);
+  b.fsc = reinterpret_cast<float *>(base + kBigTabBytes + kBigStkBytes + kBigHullBytes);
+  b.q = reinterpret_cast<P2 *>(base + kBigTabBytes);
+  return b;
+}
+
+__device__ __forceinline__ void table_clear(const BigSmem &S, int ncols) {
+  for (int c = threadIdx.x; c < ncols; c += blockDim.x) {
+    S.lo[c] = db::kColEmpty;
+    S.hi[c] = db::kColEmpty;
+  }
+}
+
+__device__ __forceinline__ void table_add(const BigSmem &S, int c, int y, int idx) {
+  atomicMin(S.lo + c, (unsigned long long)db::col_lo_key(y, idx));
+  atomicMin(S.hi + c, (unsigned long long)db::col_hi_key(y, idx));
+}
+
+// Inclusive sum of v over the CTA (kBigThreads threads); *total gets the sum.
+__device__ int cta_inclusive_sum(int v, int *total) {
+  __shared__ int s_w[kBigThreads / 32];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  int x = v;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_w[wid] = x;
+  __syncthreads();
+  int base = 0, all = 0;
+  for (int w = 0; w < kBigThreads / 32; ++w) {
+    if (w < wid) base += s_w[w];
+    all += s_w[w];
+  }
+  __syncthreads();
+  *total = all;
+  return base + x;
+}
+
+// min-area rectangle from the filled table (synchronised) of ncols columns at
+// x = base + c. False (on every thread) when the hull exceeds kBigHull
+// vertices; *r is valid in thread 0.
+__device__ bool cta_table_rect(const BigSmem &S, int ncols, int base, RRect *r) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    const int m = db::hull_from_table(reinterpret_cast<const uint64_t *>(S.lo),
+                                      reinterpret_cast<const uint64_t *>(S.hi), ncols, base, S.stk,
+                                      S.hull, kBigHull);
+    s_ok = m >= 0;
+    if (m >= 0) *r = db::min_area_rect(S.hull, m, S.fsc);
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
+// 6a'. one CTA per listed contour (grid-stride): its first min-area box.
+__global__ void __launch_bounds__(kBigThreads)
+geom_big_kernel(const int *__restrict__ list, const int *__restrict__ counters,
+                const int *__restrict__ npts, const long long *__restrict__ pt_off,
+                const P2 *__restrict__ pts, const int4 *__restrict__ aabb,
+                int *__restrict__ stage1, char *__restrict__ pool, int *__restrict__ pool_counters,
+                int *__restrict__ status, DbParams P) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const BigSmem S = big_smem(smem);
+  const int count = counters[0];
+  for (int li = blockIdx.x; li < count; li += gridDim.x) {
+    const int c = list[li];
+    const int n = npts[c];
+    const P2 *p = pts + pt_off[c];
+    const int4 bb = aabb[c];
+    const int base = bb.x, ncols = bb.z - bb.x + 1;
+    RRect r{};
+    bool ok = false;
+    if (ncols <= P.big_cols) {
+      table_clear(S, ncols);
+      __syncthreads();
+      for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const P2 v = p[i];
+        table_add(S, v.x - base, v.y, i);
+      }
+      __syncthreads();
+      ok = cta_table_rect(S, ncols, base, &r);
+    }
+    if (threadIdx.x == 0) {
+      if (!ok) ok = rect_global(p, n, pool, pool_counters, P.pool_bytes, status, &r);
+      if (ok && (r.w < r.h ? r.w : r.h) >= P.min_box_side) stage1[c] = 1;
+    }
+    __syncthreads();
+  }
 }
 
 constexpr int kScoreThreads = 256;
@@ -697,44 +860,10 @@ score_kernel(const float *__restrict__ pred, const int *__restrict__ stage1,
   }
 }
 
-// 7. one thread per surviving contour: the unclip ring (kCount: only its
-// size), the second min-area box, scaling to the original image, filters
-// (det_postprocess.cpp:190-219).
-template <bool kCount>
-__global__ void __launch_bounds__(128)
-unclip_kernel(const int *__restrict__ stage2, const int *__restrict__ npts,
-              const long long *__restrict__ pt_off, const P2 *__restrict__ pts,
-              P2 *__restrict__ qbuf, const double *__restrict__ dist, int *__restrict__ offcap,
-              const long long *__restrict__ off_off, P2 *__restrict__ ring, HP *__restrict__ hpw2,
-              P2 *__restrict__ hull2, float *__restrict__ fsc2, const int *__restrict__ geo,
-              int *__restrict__ keep2, int *__restrict__ boxes, DbParams P) {
-  const long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= (long long)P.n_maps * kMaxCand) return;
-  if (kCount) offcap[c] = 0; else keep2[c] = 0;
-  if (!stage2[c]) return;
-  const int n = npts[c];
-  const P2 *p = pts + pt_off[c];
-  const double d = dist[c];
-  P2 *q = qbuf + pt_off[c] + c;  // n + 1 slots
-  const int qm = (d == 0.) ? 0 : db::offset_prepare(p, n, q);
-  if (kCount) {
-    offcap[c] = qm == 0 ? n : db::offset_raw(q, qm, d, nullptr, 0);
-    return;
-  }
-  if (off_off[c + 1] > P.offset_cap) return;
-  const long long oo = off_off[c] + c;  // offcap + 1 scratch slots per contour
-  const int cap = (int)(off_off[c + 1] - off_off[c]);
-  P2 local_ring[kLocalPts];
-  P2 *r = cap <= kLocalPts ? local_ring : ring + oo;
-  int rn;
-  if (qm == 0) {  // no offset: unclip returns the contour itself
-    for (int i = 0; i < n; ++i) r[i] = p[i];
-    rn = n;
-  } else {
-    rn = db::offset_raw(q, qm, d, r, cap);
-  }
-  if (rn < 3) return;
-  const RRect rr = rect_of(r, rn, hpw2 + 2 * oo, hull2 + oo, fsc2 + 3 * oo);
+// Second min-area box -> quad in the original image, filters
+// (det_postprocess.cpp:200-219).
+__device__ void finish_box(const RRect &rr, long long c, const int *geo, int *keep2, int *boxes,
+                           const DbParams &P) {
   if ((rr.w < rr.h ? rr.w : rr.h) < P.min_unclipped_side) return;
   int box[8];
   db::mini_box(rr, box);
@@ -758,6 +887,180 @@ unclip_kernel(const int *__restrict__ stage2, const int *__restrict__ npts,
   if (rw <= 3 || rh <= 3) return;
   for (int k = 0; k < 8; ++k) boxes[c * 8 + k] = box[k];
   keep2[c] = 1;
+}
+
+// 7. one thread per surviving contour: the unclip ring (det_postprocess.cpp
+// :190-199, Clipper's raw round-join offset), the second min-area box and
+// finish_box. Contours or rings above kLocalPts points are listed for
+// unclip_big_kernel.
+__global__ void __launch_bounds__(128)
+unclip_kernel(const int *__restrict__ stage2, const int *__restrict__ npts,
+              const long long *__restrict__ pt_off, const P2 *__restrict__ pts,
+              const double *__restrict__ dist, const int *__restrict__ geo,
+              int *__restrict__ keep2, int *__restrict__ boxes, int *__restrict__ list,
+              int *__restrict__ counters, DbParams P) {
+  const long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= (long long)P.n_maps * kMaxCand) return;
+  keep2[c] = 0;
+  if (!stage2[c]) return;
+  const int n = npts[c];
+  if (n > kLocalPts) {
+    list[atomicAdd(counters + 1, 1)] = (int)c;
+    return;
+  }
+  const P2 *p = pts + pt_off[c];
+  const double d = dist[c];
+  P2 q[kLocalPts];
+  P2 ring[kLocalPts];
+  const int qm = (d == 0.) ? 0 : db::offset_prepare(p, n, q);
+  int rn;
+  if (qm == 0) {  // no offset: unclip returns the contour itself
+    for (int i = 0; i < n; ++i) ring[i] = p[i];
+    rn = n;
+  } else {
+    rn = db::offset_raw(q, qm, d, ring, kLocalPts);
+    if (rn > kLocalPts) {
+      list[atomicAdd(counters + 1, 1)] = (int)c;
+      return;
+    }
+  }
+  if (rn < 3) return;
+  finish_box(rect_local(ring, rn), c, geo, keep2, boxes, P);
+}
+
+// One thread, global scratch: unclip ring of rn points and its min-area box.
+__device__ bool unclip_rect_global(const P2 *p, int n, double d, int rn, char *pool,
+                                   int *counters, unsigned long long pool_bytes, int *status,
+                                   RRect *r) {
+  P2 *q = reinterpret_cast<P2 *>(
+      pool_alloc(pool, counters, pool_bytes, (n + 1ull + rn) * sizeof(P2), status));
+  if (!q) return false;
+  P2 *ring = q + n + 1;
+  const int qm = (d == 0.) ? 0 : db::offset_prepare(p, n, q);
+  if (qm == 0) {
+    for (int i = 0; i < n; ++i) ring[i] = p[i];
+  } else {
+    db::offset_raw(q, qm, d, ring, rn);
+  }
+  return rect_global(ring, rn, pool, counters, pool_bytes, status, r);
+}
+
+// 7'. one CTA per listed contour (grid-stride): the unclip ring goes
+// straight into the column table. Its vertices are emitted in parallel (a
+// thread per vertex, ring indices from a prefix sum of the per-vertex counts)
+// unless some joint keeps Clipper's previous vertex k (nearly straight
+// joints, only at distances below 1/sin 45 for contours), in which case
+// thread 0 emits serially. Then the CTA's min-area box and finish_box.
+__global__ void __launch_bounds__(kBigThreads)
+unclip_big_kernel(const int *__restrict__ list, const int *__restrict__ counters,
+                  const int *__restrict__ npts, const long long *__restrict__ pt_off,
+                  const P2 *__restrict__ pts, const int4 *__restrict__ aabb,
+                  const double *__restrict__ dist, const int *__restrict__ geo,
+                  int *__restrict__ keep2, int *__restrict__ boxes, char *__restrict__ pool,
+                  int *__restrict__ pool_counters, int *__restrict__ status, DbParams P) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ int s_qm, s_rn, s_fits;
+  __shared__ P2 *s_q;
+  const BigSmem S = big_smem(smem);
+  const int count = counters[1];
+  for (int li = blockIdx.x; li < count; li += gridDim.x) {
+    const int c = list[li];
+    const int n = npts[c];
+    const P2 *p = pts + pt_off[c];
+    const double d = dist[c];
+    const int4 bb = aabb[c];
+    // the ring stays within d + 1 of the contour's box
+    const bool near = d >= 0. && d < (double)kBigCols;
+    const int pad = near ? (int)ceil(d) + 2 : 0;
+    const int base = bb.x - pad, ncols = bb.z - bb.x + 1 + 2 * pad;
+    const bool in_smem = near && ncols <= P.big_cols;
+    if (threadIdx.x == 0) {
+      int qm = 0;
+      P2 *q = S.q;
+      if (d != 0.) {
+        if (n > kBigQPts)
+          q = reinterpret_cast<P2 *>(
+              pool_alloc(pool, pool_counters, P.pool_bytes, n * sizeof(P2), status));
+        qm = q ? db::offset_prepare(p, n, q) : -1;
+      }
+      s_qm = qm;
+      s_q = q;
+    }
+    if (in_smem) table_clear(S, ncols);
+    __syncthreads();
+    const int qm = s_qm;
+    const P2 *q = s_q;
+    if (qm < 0) {  // scratch pool exhausted (status set)
+      __syncthreads();
+      continue;
+    }
+    int rn = 0;
+    bool fits = true;
+    if (qm == 0) {  // no offset: the ring is the contour itself
+      rn = n;
+      if (in_smem)
+        for (int i = threadIdx.x; i < n; i += blockDim.x) table_add(S, p[i].x - base, p[i].y, i);
+    } else {
+      const db::OffsetConsts oc = db::offset_consts(d);
+      const int chunk = (qm + blockDim.x - 1) / blockDim.x;
+      const int j0 = min(qm, (int)threadIdx.x * chunk), j1 = min(qm, j0 + chunk);
+      int cnt = 0;
+      bool keeps = false;
+      for (int j = j0; j < j1; ++j) {
+        const bool keep = db::offset_vertex(q, qm, j, j == 0 ? qm - 1 : j - 1, d, oc,
+                                            [&](long long, long long) { ++cnt; });
+        keeps |= keep && j < qm - 1;
+      }
+      const bool serial = __syncthreads_or(keeps || db::offset_is_identity(d)) != 0;
+      if (!serial) {
+        int idx = cta_inclusive_sum(cnt, &rn) - cnt;
+        if (in_smem) {
+          bool ok = true;
+          for (int j = j0; j < j1; ++j)
+            db::offset_vertex(q, qm, j, j == 0 ? qm - 1 : j - 1, d, oc,
+                              [&](long long x, long long y) {
+                                const long long col = x - base;
+                                if (col < 0 || col >= ncols || !db::col_y_fits(y)) ok = false;
+                                else table_add(S, (int)col, (int)y, idx);
+                                ++idx;
+                              });
+          fits = __syncthreads_or(!ok) == 0;
+        }
+      } else {
+        if (threadIdx.x == 0) {
+          bool ok = true;
+          int k = 0;
+          const int total = db::offset_emit(q, qm, d, [&](long long x, long long y) {
+            const long long col = x - base;
+            if (in_smem) {
+              if (col < 0 || col >= ncols || !db::col_y_fits(y)) {
+                ok = false;
+              } else {
+                const uint64_t a = db::col_lo_key((int)y, k), b = db::col_hi_key((int)y, k);
+                if (a < S.lo[col]) S.lo[col] = a;
+                if (b < S.hi[col]) S.hi[col] = b;
+              }
+            }
+            ++k;
+          });
+          s_rn = total;
+          s_fits = ok;
+        }
+        __syncthreads();
+        rn = s_rn;
+        fits = s_fits != 0;
+      }
+    }
+    __syncthreads();
+    RRect r{};
+    bool ok = false;
+    if (rn >= 3 && in_smem && fits) ok = cta_table_rect(S, ncols, base, &r);
+    if (threadIdx.x == 0 && rn >= 3) {
+      if (!ok) ok = unclip_rect_global(p, n, d, rn, pool, pool_counters, P.pool_bytes, status, &r);
+      if (ok) finish_box(r, c, geo, keep2, boxes, P);
+    }
+    __syncthreads();
+  }
 }
 
 // 8. kept boxes of map m in contour order. grid n_maps, kScanThreads threads.
@@ -808,9 +1111,10 @@ namespace tocr {
 namespace {
 
 struct DbLayout {
-  size_t bitmap, tile_bg, bits, slab, lab, scan_tot, row_count, row_off, n_contours, n_total, starts, npts, pt_off, pts, hpw,
-      hullbuf, fsc, stage1, aabb, stage2, score, dist, offcap, off_off, ring, hpw2, hull2, fsc2,
-      keep2, boxes, total;
+  size_t bitmap, tile_bg, bits, slab, lab, scan_tot, row_count, row_off, n_contours, n_total,
+      starts, npts, pt_off, pts, stage1, aabb, stage2, score, dist, keep2, boxes, list1, list2,
+      counters, pool, total;
+  unsigned long long pool_bytes;
 };
 
 size_t align_up(size_t v) { return (v + 255) & ~size_t(255); }
@@ -835,30 +1139,29 @@ DbLayout db_layout(int n_maps, int h, int w, long long point_cap, long long offs
   L.npts = take(C * 4);
   L.pt_off = take((C + 1) * 8);
   L.pts = take((size_t)point_cap * sizeof(P2));
-  L.hpw = take(2 * ((size_t)point_cap + C) * sizeof(HP));
-  L.hullbuf = take(((size_t)point_cap + C) * sizeof(P2));
-  L.fsc = take(3 * ((size_t)point_cap + C) * 4);
   L.stage1 = take(C * 4);
   L.aabb = take(C * 16);
   L.stage2 = take(C * 4);
   L.score = take(C * 4);
   L.dist = take(C * 8);
-  L.offcap = take(C * 4);
-  L.off_off = take((C + 1) * 8);
-  L.ring = take(((size_t)offset_cap + C) * sizeof(P2));
-  L.hpw2 = take(2 * ((size_t)offset_cap + C) * sizeof(HP));
-  L.hull2 = take(((size_t)offset_cap + C) * sizeof(P2));
-  L.fsc2 = take(3 * ((size_t)offset_cap + C) * 4);
   L.keep2 = take(C * 4);
   L.boxes = take(C * 8 * 4);
+  L.list1 = take(C * 4);
+  L.list2 = take(C * 4);
+  L.counters = take(kCounters * 4);
+  L.pool_bytes = (unsigned long long)offset_cap * kPoolBytesPerPoint;
+  L.pool = take(L.pool_bytes);
   L.total = o;
   return L;
 }
 
 void default_caps(int n_maps, int h, int w, long long *point_cap, long long *offset_cap) {
   if (*point_cap <= 0) *point_cap = (long long)n_maps * ((long long)h * w / 4 + 4096);
-  if (*offset_cap <= 0) *offset_cap = 4 * *point_cap;
+  if (*offset_cap <= 0) *offset_cap = *point_cap;
 }
+
+// Test hook: the widest point set (x columns) the shared-memory geometry path takes.
+std::atomic<int> g_big_cols{kBigCols};
 
 }  // namespace
 }  // namespace tocr
@@ -885,7 +1188,8 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
   TOCR_REQUIRE(n_maps >= 0 && h > 0 && w > 0 && max_boxes > 0,
                "tocr_db_postprocess: bad sizes n_maps=%d h=%d w=%d max_boxes=%d", n_maps, h, w,
                max_boxes);
-  TOCR_REQUIRE((long long)h * w < (1ll << 30), "tocr_db_postprocess: map of %dx%d too large", h, w);
+  TOCR_REQUIRE((long long)h * w < (1ll << 30) && h < (1 << 19),
+               "tocr_db_postprocess: map of %dx%d too large", h, w);
   TOCR_REQUIRE(w <= 32 * kMaxWords, "tocr_db_postprocess: map width %d exceeds %d", w,
                32 * kMaxWords);
   if (n_maps == 0) return TOCR_OK;
@@ -908,23 +1212,29 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
   int *row_count = (int *)at(L.row_count), *row_off = (int *)at(L.row_off);
   int *n_contours = (int *)at(L.n_contours), *n_total = (int *)at(L.n_total);
   int *starts = (int *)at(L.starts), *npts = (int *)at(L.npts);
-  long long *pt_off = (long long *)at(L.pt_off), *off_off = (long long *)at(L.off_off);
-  P2 *pts = (P2 *)at(L.pts), *hullbuf = (P2 *)at(L.hullbuf), *ring = (P2 *)at(L.ring),
-     *hull2 = (P2 *)at(L.hull2);
-  HP *hpw = (HP *)at(L.hpw), *hpw2 = (HP *)at(L.hpw2);
-  float *fsc = (float *)at(L.fsc), *fsc2 = (float *)at(L.fsc2), *score = (float *)at(L.score);
-  int *stage1 = (int *)at(L.stage1), *stage2 = (int *)at(L.stage2), *offcap = (int *)at(L.offcap),
-      *keep2 = (int *)at(L.keep2), *boxes = (int *)at(L.boxes);
+  long long *pt_off = (long long *)at(L.pt_off);
+  P2 *pts = (P2 *)at(L.pts);
+  float *score = (float *)at(L.score);
+  int *stage1 = (int *)at(L.stage1), *stage2 = (int *)at(L.stage2), *keep2 = (int *)at(L.keep2),
+      *boxes = (int *)at(L.boxes), *list1 = (int *)at(L.list1), *list2 = (int *)at(L.list2),
+      *counters = (int *)at(L.counters);
+  char *pool = at(L.pool);
   int4 *aabb = (int4 *)at(L.aabb);
   double *dist = (double *)at(L.dist);
 
   DbParams P{n_maps, h, w, thresh, box_thresh, unclip_ratio, min_box_side, min_unclipped_side,
-             point_cap, offset_cap, max_boxes};
+             point_cap, offset_cap, max_boxes, g_big_cols.load(), L.pool_bytes};
   const long long C = (long long)n_maps * kMaxCand;
   const unsigned cgrid = (unsigned)((C + 127) / 128);
   const dim3 tiles((w + kTileW - 1) / kTileW, (h + kTileH - 1) / kTileH, n_maps);
 
-  cudaError_t e = cudaMemsetAsync(d_status, 0, sizeof(int), st);
+  cudaError_t e = cudaFuncSetAttribute(geom_big_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kBigSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(unclip_big_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kBigSmem);
+  if (e != cudaSuccess) return set_error(TOCR_ERR_CUDA, "db smem attribute: %s", cudaGetErrorString(e));
+  e = cudaMemsetAsync(d_status, 0, sizeof(int), st);
   if (e != cudaSuccess) return set_error(TOCR_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
   ccl_local_kernel<<<tiles, 256, 0, st>>>(d_pred, bitmap, lab, bits, nullptr, tile_bg, h, w,
                                           thresh);
@@ -935,25 +1245,32 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
   trace_kernel<<<cgrid, 128, 0, st>>>(bits, starts, n_contours, npts, slab, d_status, n_maps, h, w);
   scan_map_kernel<int><<<n_maps, kScanThreads, 0, st>>>(npts, pt_off, scan_tot);
   scan_base_kernel<<<n_maps, kScanThreads, 0, st>>>(pt_off, scan_tot, n_maps);
-  check_cap_kernel<<<1, 1, 0, st>>>(pt_off, C, point_cap, d_status, kErrPointPool);
+  prep_geom_kernel<<<1, 1, 0, st>>>(pt_off, C, point_cap, d_status, counters);
   gather_kernel<<<(unsigned)((C * 32 + 127) / 128), 128, 0, st>>>(bits, starts, npts, pt_off, slab,
                                                                  pts, point_cap, n_maps, h, w);
-  geom_box1_kernel<<<cgrid, 128, 0, st>>>(n_contours, npts, pt_off, pts, hpw, hullbuf, fsc,
-                                          stage1, aabb, P);
+  geom_box1_kernel<<<cgrid, 128, 0, st>>>(n_contours, npts, pt_off, pts, stage1, aabb, list1,
+                                          counters, P);
+  const unsigned bgrid = (unsigned)(C < sm_count() ? C : sm_count());
+  geom_big_kernel<<<bgrid, kBigThreads, kBigSmem, st>>>(list1, counters, npts, pt_off, pts, aabb,
+                                                        stage1, pool, counters, d_status, P);
   score_kernel<<<(unsigned)(C < 148 * 8 ? C : 148 * 8), kScoreThreads, 0, st>>>(
       d_pred, stage1, aabb, npts, pt_off, pts, stage2, score, dist, P);
-  unclip_kernel<true><<<cgrid, 128, 0, st>>>(stage2, npts, pt_off, pts, hullbuf, dist, offcap,
-                                             off_off, ring, hpw2, hull2, fsc2, d_geometry, keep2,
-                                             boxes, P);
-  scan_map_kernel<int><<<n_maps, kScanThreads, 0, st>>>(offcap, off_off, scan_tot);
-  scan_base_kernel<<<n_maps, kScanThreads, 0, st>>>(off_off, scan_tot, n_maps);
-  check_cap_kernel<<<1, 1, 0, st>>>(off_off, C, offset_cap, d_status, kErrOffsetPool);
-  unclip_kernel<false><<<cgrid, 128, 0, st>>>(stage2, npts, pt_off, pts, hullbuf, dist, offcap,
-                                              off_off, ring, hpw2, hull2, fsc2, d_geometry, keep2,
-                                              boxes, P);
+  unclip_kernel<<<cgrid, 128, 0, st>>>(stage2, npts, pt_off, pts, dist, d_geometry, keep2, boxes,
+                                       list2, counters, P);
+  unclip_big_kernel<<<bgrid, kBigThreads, kBigSmem, st>>>(list2, counters, npts, pt_off, pts, aabb,
+                                                          dist, d_geometry, keep2, boxes, pool,
+                                                          counters, d_status, P);
   compact_kernel<<<n_maps, kScanThreads, 0, st>>>(keep2, boxes, score, d_boxes, d_scores, d_counts,
                                                   d_status, max_boxes);
   return check_launch("tocr_db_postprocess");
+}
+
+// Test hook (tocr_capi.h): sets the widest point set (x columns) the
+// shared-memory geometry path takes (0: every set above the thread-local
+// size uses the global pool; < 0 or above the compiled capacity: the
+// compiled capacity).
+TOCR_API void tocr_debug_db_shared_columns(int columns) {
+  g_big_cols.store(columns < 0 || columns > kBigCols ? kBigCols : columns);
 }
 
 // Labels of the first three stages, for tests and tools: labels[m][y][x] =

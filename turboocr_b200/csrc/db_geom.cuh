@@ -279,13 +279,40 @@ TG long long cross3(const HP &o, const HP &a, const HP &b) {
   return (long long)(a.x - o.x) * (b.y - o.y) - (long long)(a.y - o.y) * (b.x - o.x);
 }
 
+// Writes the chain (accessor at(i) -> HP, i < m, in the order of Andrew's
+// monotone chain) to hull, rotated to cv::convexHull's starting vertex: when
+// the input indices of the hull vertices are cyclically increasing the hull
+// starts at the smallest index, when cyclically decreasing at the largest,
+// otherwise at the vertex with the largest (x, y).
+template <class AT>
+TG void hull_start_copy(int m, const AT &at, P2 *hull) {
+  int start = 0;
+  if (m >= 3) {
+    int inc = 0;
+    for (int i = 0; i < m; ++i) inc += at((i + 1) % m).idx > at(i).idx;
+    if (inc == m - 1 || inc == 1) {
+      const bool increasing = (inc == m - 1);
+      for (int i = 1; i < m; ++i)
+        if (increasing ? at(i).idx < at(start).idx : at(i).idx > at(start).idx) start = i;
+    } else {
+      for (int i = 1; i < m; ++i)
+        if (at(i).x > at(start).x || (at(i).x == at(start).x && at(i).y > at(start).y)) start = i;
+    }
+  } else {
+    for (int i = 1; i < m; ++i)
+      if (at(i).x > at(start).x || (at(i).x == at(start).x && at(i).y > at(start).y)) start = i;
+  }
+  for (int i = 0; i < m; ++i) {
+    const HP q = at((start + i) % m);
+    hull[i] = P2{q.x, q.y};
+  }
+}
+
 // Strict convex hull (no collinear or repeated points) of pts[0..n), in the
 // orientation and with the starting vertex of cv::convexHull(clockwise=false)
-// (a repeated point counts with its first index):
-// when the input indices of the hull vertices are cyclically increasing the
-// hull starts at the smallest index, when cyclically decreasing at the
-// largest, otherwise at the vertex with the largest (x, y). `work` needs
-// 2n+1 entries and is clobbered. Returns the hull size.
+// (a repeated point counts with its first index; start rule as
+// hull_start_copy). `work` needs 2n+1 entries and is clobbered. Returns the
+// hull size.
 TG int convex_hull(const P2 *pts, int n, HP *work, P2 *hull) {
   if (n <= 0) return 0;
   HP *s = work;            // sorted points [0, n)
@@ -309,27 +336,98 @@ TG int convex_hull(const P2 *pts, int n, HP *work, P2 *hull) {
   }
   int m = k > 1 ? k - 1 : k;  // last point repeats the first
   if (m == 2 && h[0].x == h[1].x && h[0].y == h[1].y) m = 1;
-  // starting vertex
-  int start = 0;
-  if (m >= 3) {
-    int inc = 0;
-    for (int i = 0; i < m; ++i) inc += h[(i + 1) % m].idx > h[i].idx;
-    if (inc == m - 1 || inc == 1) {
-      const bool increasing = (inc == m - 1);
-      for (int i = 1; i < m; ++i)
-        if (increasing ? h[i].idx < h[start].idx : h[i].idx > h[start].idx) start = i;
-    } else {
-      for (int i = 1; i < m; ++i)
-        if (h[i].x > h[start].x || (h[i].x == h[start].x && h[i].y > h[start].y)) start = i;
-    }
+  hull_start_copy(m, [&](int i) { return h[i]; }, hull);
+  return m;
+}
+
+// ----------------------------------------------------- column hull (CTA) ----
+// Only the lowest and the highest point of an x column can be strict hull
+// vertices (every other point lies between them), and a repeated point
+// counts with its first index. So a point set reduces to a table over its x
+// columns: lo[c] = min of (y, index) and hi[c] = max y with min index, each
+// packed into one u64 so that a plain (or atomic) minimum keeps it:
+// (y + 2^20) or (2^20 - 1 - y) in the top 21 bits, the index below.
+// kColEmpty marks a column without points. Requires |y| < 2^20.
+constexpr uint64_t kColEmpty = ~0ull;
+constexpr int kColYBias = 1 << 20;
+TG bool col_y_fits(long long y) { return y > -kColYBias && y < kColYBias; }
+TG uint64_t col_lo_key(int y, int idx) {
+  return ((uint64_t)(uint32_t)(y + kColYBias) << 43) | (uint64_t)(uint32_t)idx;
+}
+TG uint64_t col_hi_key(int y, int idx) {
+  return ((uint64_t)(uint32_t)(kColYBias - 1 - y) << 43) | (uint64_t)(uint32_t)idx;
+}
+TG int col_lo_y(uint64_t k) { return (int)(k >> 43) - kColYBias; }
+TG int col_hi_y(uint64_t k) { return kColYBias - 1 - (int)(k >> 43); }
+TG int col_idx(uint64_t k) { return (int)(k & 0x7FFFFFFFull); }
+TG void col_add(uint64_t *lo, uint64_t *hi, int c, int y, int idx) {  // serial form
+  const uint64_t a = col_lo_key(y, idx), b = col_hi_key(y, idx);
+  if (a < lo[c]) lo[c] = a;
+  if (b < hi[c]) hi[c] = b;
+}
+
+// Entry e of the candidate sequence (in (x, y, index) order): column e/2,
+// its lowest point (e even) or its highest (e odd; absent when the column
+// holds a single y). False when absent.
+TG bool col_entry(const uint64_t *lo, const uint64_t *hi, int base, int e, HP *out) {
+  const int c = e >> 1;
+  const uint64_t l = lo[c];
+  if (l == kColEmpty) return false;
+  if (e & 1) {
+    const uint64_t h = hi[c];
+    const int yh = col_hi_y(h);
+    if (yh == col_lo_y(l)) return false;
+    *out = HP{base + c, yh, col_idx(h)};
   } else {
-    for (int i = 1; i < m; ++i)
-      if (h[i].x > h[start].x || (h[i].x == h[start].x && h[i].y > h[start].y)) start = i;
+    *out = HP{base + c, col_lo_y(l), col_idx(l)};
   }
-  for (int i = 0; i < m; ++i) {
-    const HP &q = h[(start + i) % m];
-    hull[i] = P2{q.x, q.y};
+  return true;
+}
+
+// Andrew's monotone chain over the candidates of the table of ncols columns
+// (x = base + c): the same hull, orientation and starting vertex as
+// convex_hull on the original points. stk (entries) needs 2*ncols+1 ints.
+// Returns the hull size, or -1 when it exceeds hull_cap.
+TG int hull_from_table(const uint64_t *lo, const uint64_t *hi, int ncols, int base, int *stk,
+                       P2 *hull, int hull_cap) {
+  const int ns = 2 * ncols;
+  HP a, b, v;
+  auto at = [&](int e) {
+    HP r{0, 0, 0};
+    col_entry(lo, hi, base, e, &r);
+    return r;
+  };
+  int top = 0, last = -1;
+  for (int e = 0; e < ns; ++e) {  // lower chain
+    if (!col_entry(lo, hi, base, e, &v)) continue;
+    last = e;
+    while (top >= 2) {
+      a = at(stk[top - 2]);
+      b = at(stk[top - 1]);
+      if (cross3(a, b, v) > 0) break;
+      --top;
+    }
+    stk[top++] = e;
   }
+  if (last < 0) return 0;
+  for (int e = last - 1, t = top + 1; e >= 0; --e) {  // upper chain
+    if (!col_entry(lo, hi, base, e, &v)) continue;
+    while (top >= t) {
+      a = at(stk[top - 2]);
+      b = at(stk[top - 1]);
+      if (cross3(a, b, v) > 0) break;
+      --top;
+    }
+    stk[top++] = e;
+  }
+  int m = top > 1 ? top - 1 : top;
+  if (m == 2) {
+    a = at(stk[0]);
+    b = at(stk[1]);
+    if (a.x == b.x && a.y == b.y) m = 1;
+  }
+  if (m > hull_cap) return -1;
+  hull_start_copy(m, [&](int i) { return at(stk[i]); }, hull);
   return m;
 }
 
@@ -693,64 +791,95 @@ TG int offset_prepare(const P2 *p, int n, P2 *q) {
   return m;
 }
 
-// Raw round-join offset of the prepared closed path q[0..m) by delta > 0
-// (ClipperOffset::DoOffset + OffsetPoint + DoRound, before the union).
-// Writes at most cap points to out and returns the full count.
-TG int offset_raw(const P2 *q, int m, double delta, P2 *out, int cap) {
-  int n = 0;
-  auto emit = [&](long long x, long long y) {
-    if (n < cap) out[n] = P2{(int)x, (int)y};
-    ++n;
-  };
-  if (delta > -1.0E-20 && delta < 1.0E-20) {
-    for (int i = 0; i < m; ++i) emit(q[i].x, q[i].y);
-    return n;
-  }
+// Per-call constants of the round joins (ClipperOffset::DoOffset).
+struct OffsetConsts {
+  double m_sin, m_cos, steps_per_rad;
+};
+TG OffsetConsts offset_consts(double delta) {
   const double ad = delta < 0 ? -delta : delta;
   const double y = (0.25 > ad * 0.25) ? ad * 0.25 : 0.25;
   const double pi = 3.141592653589793238, two_pi = pi * 2;
   double steps = pi / acos(1 - y / ad);
   if (steps > ad * pi) steps = ad * pi;
-  double m_sin = sin(two_pi / steps);
-  const double m_cos = cos(two_pi / steps);
-  const double steps_per_rad = steps / two_pi;
-  if (delta < 0.0) m_sin = -m_sin;
-  int k = m - 1;
-  for (int j = 0; j < m; ++j) {
-    const DP nk = unit_normal(q[k], q[(k + 1) % m]);
-    const DP nj = unit_normal(q[j], q[(j + 1) % m]);
-    double sinA = fma(nk.x, nj.y, -(nj.x * nk.y));
-    if (fabs(sinA * delta) < 1.0) {
-      const double cosA = fma(nk.x, nj.x, nj.y * nk.y);
-      if (cosA > 0) {
-        emit(clip_round(fma(nk.x, delta, (double)q[j].x)), clip_round(fma(nk.y, delta, (double)q[j].y)));
-        continue;
-      }
-    } else if (sinA > 1.0) {
-      sinA = 1.0;
-    } else if (sinA < -1.0) {
-      sinA = -1.0;
-    }
-    if (sinA * delta < 0) {
+  OffsetConsts oc;
+  oc.m_sin = sin(two_pi / steps);
+  oc.m_cos = cos(two_pi / steps);
+  oc.steps_per_rad = steps / two_pi;
+  if (delta < 0.0) oc.m_sin = -oc.m_sin;
+  return oc;
+}
+
+// One vertex j of the offset (ClipperOffset::OffsetPoint + DoRound) with
+// previous vertex k: calls emit(x, y) for its points. Returns true when
+// Clipper keeps k for the next vertex (the early return for a nearly
+// straight joint), false when k becomes j.
+template <class EMIT>
+TG bool offset_vertex(const P2 *q, int m, int j, int k, double delta, const OffsetConsts &oc,
+                      EMIT &&emit) {
+  const DP nk = unit_normal(q[k], q[(k + 1) % m]);
+  const DP nj = unit_normal(q[j], q[(j + 1) % m]);
+  double sinA = fma(nk.x, nj.y, -(nj.x * nk.y));
+  if (fabs(sinA * delta) < 1.0) {
+    const double cosA = fma(nk.x, nj.x, nj.y * nk.y);
+    if (cosA > 0) {
       emit(clip_round(fma(nk.x, delta, (double)q[j].x)), clip_round(fma(nk.y, delta, (double)q[j].y)));
-      emit(q[j].x, q[j].y);
-      emit(clip_round(fma(nj.x, delta, (double)q[j].x)), clip_round(fma(nj.y, delta, (double)q[j].y)));
-    } else {
-      const double a = atan2(sinA, fma(nk.x, nj.x, nk.y * nj.y));
-      long long st = clip_round(steps_per_rad * fabs(a));
-      const int steps_i = st > 1 ? (int)st : 1;
-      double X = nk.x, Y = nk.y;
-      for (int i = 0; i < steps_i; ++i) {
-        emit(clip_round(fma(X, delta, (double)q[j].x)), clip_round(fma(Y, delta, (double)q[j].y)));
-        const double X2 = X;
-        X = fma(X, m_cos, -(m_sin * Y));
-        Y = fma(X2, m_sin, Y * m_cos);
-      }
-      emit(clip_round(fma(nj.x, delta, (double)q[j].x)), clip_round(fma(nj.y, delta, (double)q[j].y)));
+      return true;
     }
-    k = j;
+  } else if (sinA > 1.0) {
+    sinA = 1.0;
+  } else if (sinA < -1.0) {
+    sinA = -1.0;
   }
+  if (sinA * delta < 0) {
+    emit(clip_round(fma(nk.x, delta, (double)q[j].x)), clip_round(fma(nk.y, delta, (double)q[j].y)));
+    emit(q[j].x, q[j].y);
+    emit(clip_round(fma(nj.x, delta, (double)q[j].x)), clip_round(fma(nj.y, delta, (double)q[j].y)));
+  } else {
+    const double a = atan2(sinA, fma(nk.x, nj.x, nk.y * nj.y));
+    long long st = clip_round(oc.steps_per_rad * fabs(a));
+    const int steps_i = st > 1 ? (int)st : 1;
+    double X = nk.x, Y = nk.y;
+    for (int i = 0; i < steps_i; ++i) {
+      emit(clip_round(fma(X, delta, (double)q[j].x)), clip_round(fma(Y, delta, (double)q[j].y)));
+      const double X2 = X;
+      X = fma(X, oc.m_cos, -(oc.m_sin * Y));
+      Y = fma(X2, oc.m_sin, Y * oc.m_cos);
+    }
+    emit(clip_round(fma(nj.x, delta, (double)q[j].x)), clip_round(fma(nj.y, delta, (double)q[j].y)));
+  }
+  return false;
+}
+
+TG bool offset_is_identity(double delta) { return delta > -1.0E-20 && delta < 1.0E-20; }
+
+// Raw round-join offset of the prepared closed path q[0..m) by delta
+// (ClipperOffset::DoOffset, before the union): calls emit(x, y) for each ring
+// point in order and returns their count.
+template <class EMIT>
+TG int offset_emit(const P2 *q, int m, double delta, EMIT &&emit_out) {
+  int n = 0;
+  auto emit = [&](long long x, long long y) {
+    emit_out(x, y);
+    ++n;
+  };
+  if (offset_is_identity(delta)) {
+    for (int i = 0; i < m; ++i) emit(q[i].x, q[i].y);
+    return n;
+  }
+  const OffsetConsts oc = offset_consts(delta);
+  int k = m - 1;
+  for (int j = 0; j < m; ++j)
+    if (!offset_vertex(q, m, j, k, delta, oc, emit)) k = j;
   return n;
+}
+
+// offset_emit into out: writes at most cap points, returns the full count.
+TG int offset_raw(const P2 *q, int m, double delta, P2 *out, int cap) {
+  int n = 0;
+  return offset_emit(q, m, delta, [&](long long x, long long y) {
+    if (n < cap) out[n] = P2{(int)x, (int)y};
+    ++n;
+  });
 }
 
 // Winding number (crossing rule) of the point (x, y) w.r.t. the closed path r[0..n).

@@ -107,7 +107,7 @@ def cuda_batch_threshold_to_u8(src: torch.Tensor, dst: torch.Tensor, w: int, h: 
 # ---- subsystem 3 ------------------------------------------------------------
 
 DB_STATUS_BITS = {1: "point pool full", 2: "border walk exceeded its bound",
-                  4: "offset pool full", 8: "more boxes than max_boxes (truncated)"}
+                  4: "geometry scratch pool full", 8: "more boxes than max_boxes (truncated)"}
 
 
 class DbPostprocess:

@@ -73,7 +73,7 @@ class PagePipeline:
         if point_cap <= 0:
             point_cap = batch * 65536
         self.db = DbPostprocess(batch, H, W, device, max_boxes=max_boxes, point_cap=point_cap,
-                                offset_cap=offset_cap if offset_cap > 0 else 4 * point_cap)
+                                offset_cap=offset_cap)
         nc = batch * max_boxes
         self.max_crops = nc
         self.crop_off = torch.zeros(batch + 1, dtype=torch.int32, device=device)
@@ -89,9 +89,9 @@ class PagePipeline:
         self.step_idx = torch.empty(nc * REC_T, dtype=torch.int32, device=device)
         self.step_prob = torch.empty(nc * REC_T, dtype=torch.float32, device=device)
         # kernels launched per run() (for the bench's gpu_launches count)
-        # stem + blocks + head + ink + DB (18 kernels) + crops (2) + warp
+        # stem + blocks + head + ink + DB (16 kernels) + crops (2) + warp
         # + stand-in rec logits (2) + CTC (2)
-        self.launches_per_run = 1 + len(SCHEDULE) + 1 + 1 + 18 + 2 + 1 + 2 + 2
+        self.launches_per_run = 1 + len(SCHEDULE) + 1 + 1 + 16 + 2 + 1 + 2 + 2
 
     def run(self, pages: torch.Tensor, stream=None) -> None:
         """Enqueue the whole path for pages u8 [B, H, W, 3] (device)."""
