@@ -49,7 +49,7 @@ def lib():
     L.dbh_trace.argtypes = [vp, i, i, i, i, i, vp, i]
     L.dbh_trace_bits.argtypes = [vp, i, i, i, i, i, vp, i]
     L.dbh_hull.argtypes = [vp, i, vp]
-    L.dbh_hull_table.argtypes = [vp, i, vp, i, i]
+    L.dbh_hull_table.argtypes = [vp, i, vp, i, i, i]
     L.dbh_offset_parallel.argtypes = [vp, i, d, vp, i]
     L.dbh_min_area_rect.argtypes = [vp, i, vp]
     L.dbh_mini_box.argtypes = [vp, i, vp, vp]
@@ -86,11 +86,12 @@ def hull(p):
     return out[:m]
 
 
-def hull_table(p, col_cap=1 << 20, hull_cap=1 << 20):
+def hull_table(p, col_cap=1 << 20, hull_cap=1 << 20, interior_filter=False):
     """The column-table hull of the device's shared-memory path."""
     a = _pts(p)
     out = np.zeros((len(a) + 1, 2), np.int32)
-    m = lib().dbh_hull_table(a.ctypes.data, len(a), out.ctypes.data, col_cap, hull_cap)
+    m = lib().dbh_hull_table(a.ctypes.data, len(a), out.ctypes.data, col_cap, hull_cap,
+                             1 if interior_filter else 0)
     return m if m < 0 else out[:m]
 
 

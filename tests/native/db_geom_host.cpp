@@ -38,7 +38,9 @@ int dbh_hull(const int *pts, int n, int *out) {
 // The device's shared-memory hull: the column table (lowest / highest point
 // of every x column, first index), chain over its candidates. Returns the
 // hull size (-1: more than hull_cap vertices, -2: more than col_cap columns).
-int dbh_hull_table(const int *pts, int n, int *out, int col_cap, int hull_cap) {
+// filter != 0: candidates strictly inside the polygon of the extreme points
+// of kExtDirs directions are dropped first (the device's interior filter).
+int dbh_hull_table(const int *pts, int n, int *out, int col_cap, int hull_cap, int filter) {
   if (n <= 0) return 0;
   int x0 = pts[0], x1 = pts[0];
   for (int i = 1; i < n; ++i) {
@@ -50,8 +52,26 @@ int dbh_hull_table(const int *pts, int n, int *out, int col_cap, int hull_cap) {
   std::vector<uint64_t> lo(ncols, kColEmpty), hi(ncols, kColEmpty);
   for (int i = 0; i < n; ++i) col_add(lo.data(), hi.data(), pts[2 * i] - x0, pts[2 * i + 1], i);
   std::vector<int> stk(2 * (size_t)ncols + 2);
+  std::vector<uint32_t> keep((2 * (size_t)ncols + 31) / 32, 0u);
+  if (filter) {
+    HP ext[kExtDirs];
+    long long best[kExtDirs];
+    bool any = false;
+    HP v;
+    for (int e = 0; e < 2 * ncols; ++e) {
+      if (!col_entry(lo.data(), hi.data(), x0, e, &v)) continue;
+      for (int k = 0; k < kExtDirs; ++k) {
+        const long long d = ext_dot(k, v.x, v.y);
+        if (!any || d > best[k]) { best[k] = d; ext[k] = v; }
+      }
+      any = true;
+    }
+    for (int e = 0; e < 2 * ncols; ++e)
+      if (col_entry(lo.data(), hi.data(), x0, e, &v) && !strictly_inside_extremes(ext, kExtDirs, v))
+        keep[e >> 5] |= 1u << (e & 31);
+  }
   return hull_from_table(lo.data(), hi.data(), ncols, x0, stk.data(), reinterpret_cast<P2 *>(out),
-                         hull_cap);
+                         hull_cap, filter ? keep.data() : nullptr);
 }
 
 // Offset ring through the per-vertex form with k = j - 1 for every vertex

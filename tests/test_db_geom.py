@@ -169,7 +169,9 @@ def test_min_area_rect_and_mini_box():
 
 def test_column_table_hull_equals_sorted_hull():
     """The device's shared-memory hull (lowest and highest point of every x
-    column with their first index, chain over those) returns the same
+    column with their first index, chain over those, optionally after
+    dropping the points strictly inside the polygon of the extreme points of
+    16 directions) returns the same
     vertices, orientation and starting vertex as the sorted monotone chain,
     including repeated points, vertical columns, collinear runs and
     degenerate sets."""
@@ -191,7 +193,9 @@ def test_column_table_hull_equals_sorted_hull():
             if len(c) > 2:
                 sets.append(np.array(dn.offset_raw(c, 9.5) or c.tolist(), np.int32))
     for p in sets:
-        assert dn.hull_table(p).tolist() == dn.hull(p).tolist(), np.asarray(p).tolist()
+        ref = dn.hull(p).tolist()
+        assert dn.hull_table(p).tolist() == ref, np.asarray(p).tolist()
+        assert dn.hull_table(p, interior_filter=True).tolist() == ref, np.asarray(p).tolist()
     wide = rng.integers(0, 5000, (500, 2))
     assert dn.hull_table(wide, col_cap=64) == -2
 

@@ -33,6 +33,7 @@
 //
 // This translation unit is compiled with -fmad=false: the geometry must keep
 // the libraries' operation order (explicit fma() only where they contract).
+#include <algorithm>
 #include <atomic>
 
 #include "tocr_common.cuh"
@@ -357,8 +358,10 @@ ccl_rows_kernel(int *__restrict__ lab, int *__restrict__ row_count, int H, int W
 // grid n_maps, kScanThreads threads.
 __global__ void __launch_bounds__(kScanThreads)
 starts_scan_kernel(const int *__restrict__ row_count, int *__restrict__ row_off,
-                   int *__restrict__ n_contours, int *__restrict__ n_total, int H) {
+                   int *__restrict__ n_contours, int *__restrict__ n_total, int H,
+                   int *__restrict__ ovf_count) {
   const int m = blockIdx.x;
+  if (m == 0 && threadIdx.x == 0) *ovf_count = 0;  // overflow chunks of trace_kernel
   const int *rc = row_count + (size_t)m * H;
   int *ro = row_off + (size_t)m * H;
   __shared__ int s_part[kScanThreads];
@@ -437,11 +440,15 @@ starts_write_kernel(const int *__restrict__ lab, const uint8_t *__restrict__ bit
 
 
 // 5. border following. One thread per contour slot (m * 3000 + rank): the
-// walk writes its first kSlab points into the slot's slab and counts them
-// all (npts). After the offsets are scanned, gather_kernel moves each slab
-// to the contiguous point pool; the rare contour longer than a slab is
-// walked a second time straight into the pool.
+// walk writes its first kSlab points into the slot's slab, the rest into
+// chunks of kChunk points taken from a shared overflow pool and linked per
+// contour (ovf_first[c], ovf_next[chunk]), and counts them all (npts). After
+// the offsets are scanned, gather_kernel copies slab and chunks to the
+// contiguous point pool. When the overflow pool runs out, that contour is
+// walked a second time straight into the point pool instead.
 constexpr int kSlab = 256;
+constexpr int kChunk = 1024;
+constexpr int kOvfNone = -1, kOvfFailed = -2;
 
 __device__ __forceinline__ int trace_max_steps(int H, int W) {
   const long long ms = 4ll * H * W + 16;
@@ -451,7 +458,9 @@ __device__ __forceinline__ int trace_max_steps(int H, int W) {
 __global__ void __launch_bounds__(128)
 trace_kernel(const uint32_t *__restrict__ bits, const int *__restrict__ starts,
              const int *__restrict__ n_contours, int *__restrict__ npts, P2 *__restrict__ slab,
-             int *__restrict__ status, int n_maps, int H, int W) {
+             int *__restrict__ ovf_first, int *__restrict__ ovf_next, P2 *__restrict__ ovf_pts,
+             int *__restrict__ ovf_count, int ovf_chunks, int *__restrict__ status, int n_maps,
+             int H, int W) {
   const long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= (long long)n_maps * kMaxCand) return;
   const int m = (int)(c / kMaxCand), rank = (int)(c % kMaxCand);
@@ -463,26 +472,60 @@ trace_kernel(const uint32_t *__restrict__ bits, const int *__restrict__ starts,
   const int sp = rec >> 1;
   const int words = (W + 31) >> 5;
   db::NbBits nb{bits + (size_t)m * H * words, H, W, words};
-  const int n = db::trace_border_nb(nb, sp % W, sp / W, (rec & 1) != 0, slab + c * kSlab, kSlab,
-                                    trace_max_steps(H, W));
+  P2 *sl = slab + c * kSlab;
+  int k = 0, first = kOvfNone, chunk = -1, fill = kChunk;
+  const int n = db::trace_border_emit(
+      nb, sp % W, sp / W, (rec & 1) != 0,
+      [&](int x, int y) {
+        if (k < kSlab) {
+          sl[k] = P2{x, y};
+        } else if (first != kOvfFailed) {
+          if (fill == kChunk) {
+            const int nc = atomicAdd(ovf_count, 1);
+            if (nc >= ovf_chunks) {
+              first = kOvfFailed;
+            } else {
+              ovf_next[nc] = -1;
+              if (chunk < 0) first = nc;
+              else ovf_next[chunk] = nc;
+              chunk = nc;
+              fill = 0;
+            }
+          }
+          if (first != kOvfFailed) ovf_pts[(size_t)chunk * kChunk + fill++] = P2{x, y};
+        }
+        ++k;
+      },
+      trace_max_steps(H, W));
   if (n < 0) atomicOr(status, kErrTrace);
   npts[c] = n < 0 ? 0 : n;
+  ovf_first[c] = first;
 }
 
-// One warp per contour slot: slab -> pool (lanes copy), or a second walk.
+// One warp per contour slot: slab and overflow chunks -> pool (lanes copy),
+// or a second walk when the overflow pool ran out.
 __global__ void __launch_bounds__(128)
 gather_kernel(const uint32_t *__restrict__ bits, const int *__restrict__ starts,
               const int *__restrict__ npts, const long long *__restrict__ pt_off,
-              const P2 *__restrict__ slab, P2 *__restrict__ pts, long long point_cap, int n_maps,
-              int H, int W) {
+              const P2 *__restrict__ slab, const int *__restrict__ ovf_first,
+              const int *__restrict__ ovf_next, const P2 *__restrict__ ovf_pts,
+              P2 *__restrict__ pts, long long point_cap, int n_maps, int H, int W) {
   const long long c = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (c >= (long long)n_maps * kMaxCand) return;
   const int n = npts[c];
   if (n == 0 || pt_off[c] + n > point_cap) return;
   P2 *dst = pts + pt_off[c];
-  if (n <= kSlab) {
-    for (int i = lane; i < n; i += 32) dst[i] = slab[c * kSlab + i];
+  const int first = ovf_first[c];
+  if (n <= kSlab || first != kOvfFailed) {
+    const int ns = n < kSlab ? n : kSlab;
+    for (int i = lane; i < ns; i += 32) dst[i] = slab[c * kSlab + i];
+    int ch = first;
+    for (int done = kSlab; done < n; done += kChunk) {
+      const int cnt = n - done < kChunk ? n - done : kChunk;
+      for (int i = lane; i < cnt; i += 32) dst[done + i] = ovf_pts[(size_t)ch * kChunk + i];
+      ch = ovf_next[ch];
+    }
     return;
   }
   if (lane != 0) return;
@@ -682,14 +725,65 @@ __device__ int cta_inclusive_sum(int v, int *total) {
 }
 
 // min-area rectangle from the filled table (synchronised) of ncols columns at
-// x = base + c. False (on every thread) when the hull exceeds kBigHull
-// vertices; *r is valid in thread 0.
+// x = base + c. The CTA first finds the extreme candidates of kExtDirs
+// directions and drops the candidates strictly inside their polygon; thread
+// 0 then chains the rest. False (on every thread) when the hull exceeds
+// kBigHull vertices; *r is valid in thread 0.
 __device__ bool cta_table_rect(const BigSmem &S, int ncols, int base, RRect *r) {
   __shared__ int s_ok;
+  __shared__ unsigned long long s_ext[db::kExtDirs];
+  __shared__ HP s_poly[db::kExtDirs];
+  __shared__ uint32_t s_keep[(2 * kBigCols + 31) / 32];
+  const uint64_t *lo = reinterpret_cast<const uint64_t *>(S.lo);
+  const uint64_t *hi = reinterpret_cast<const uint64_t *>(S.hi);
+  const int ns = 2 * ncols;
+  if (threadIdx.x < db::kExtDirs) s_ext[threadIdx.x] = 0ull;
+  __syncthreads();
+  {  // extreme candidate of each direction: max of (dot + 2^31) << 32 | entry
+    unsigned long long best[db::kExtDirs];
+#pragma unroll
+    for (int k = 0; k < db::kExtDirs; ++k) best[k] = 0ull;
+    HP v;
+    for (int e = threadIdx.x; e < ns; e += blockDim.x) {
+      if (!db::col_entry(lo, hi, base, e, &v)) continue;
+#pragma unroll
+      for (int k = 0; k < db::kExtDirs; ++k) {
+        const unsigned long long key =
+            ((unsigned long long)(db::ext_dot(k, v.x, v.y) + (1ll << 31)) << 32) | (unsigned)e;
+        best[k] = key > best[k] ? key : best[k];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < db::kExtDirs; ++k) {
+      unsigned long long b = best[k];
+      for (int o = 16; o; o >>= 1) {
+        const unsigned long long t = __shfl_xor_sync(0xffffffffu, b, o);
+        b = t > b ? t : b;
+      }
+      if ((threadIdx.x & 31) == 0 && b) atomicMax(s_ext + k, b);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < db::kExtDirs) {
+    HP v{0, 0, 0};
+    db::col_entry(lo, hi, base, (int)(s_ext[threadIdx.x] & 0xffffffffu), &v);
+    s_poly[threadIdx.x] = v;
+  }
+  __syncthreads();
+  {  // keep mask, one warp per 32 entries
+    const int lane = threadIdx.x & 31;
+    for (int w = threadIdx.x >> 5; w * 32 < ns; w += blockDim.x >> 5) {
+      const int e = w * 32 + lane;
+      HP v;
+      const bool keep = e < ns && db::col_entry(lo, hi, base, e, &v) &&
+                        !db::strictly_inside_extremes(s_poly, db::kExtDirs, v);
+      const unsigned bits = __ballot_sync(0xffffffffu, keep);
+      if (lane == 0) s_keep[w] = bits;
+    }
+  }
+  __syncthreads();
   if (threadIdx.x == 0) {
-    const int m = db::hull_from_table(reinterpret_cast<const uint64_t *>(S.lo),
-                                      reinterpret_cast<const uint64_t *>(S.hi), ncols, base, S.stk,
-                                      S.hull, kBigHull);
+    const int m = db::hull_from_table(lo, hi, ncols, base, S.stk, S.hull, kBigHull, s_keep);
     s_ok = m >= 0;
     if (m >= 0) *r = db::min_area_rect(S.hull, m, S.fsc);
   }
@@ -781,8 +875,6 @@ score_kernel(const float *__restrict__ pred, const int *__restrict__ stage1,
   if (nonempty) {
     const int width = bx1 - bx0 + 1, words = (width + 31) >> 5;
     const float *pm = pred + (size_t)m * H * W;
-    constexpr int kSplit = kScoreThreads / kBandRows;  // threads per row
-    const int chunk = (n + kSplit - 1) / kSplit;
     for (int band = by0; band <= by1; band += kBandRows) {
       const int rows = min(kBandRows, by1 - band + 1);
       for (int i = threadIdx.x; i < kBandRows * words; i += kScoreThreads) {
@@ -790,24 +882,19 @@ score_kernel(const float *__restrict__ pred, const int *__restrict__ stage1,
         s_tog[i / words][i % words] = 0u;
       }
       __syncthreads();
-      {
-        const int r = threadIdx.x / kSplit, part = threadIdx.x % kSplit;
-        if (r < rows) {
-          const int y = band + r;
-          const int i0 = part * chunk, i1 = min(n, i0 + chunk);
-          unsigned *er = s_edge[r];
-          unsigned *tr = s_tog[r];
-          db::poly_row_marks(p, n, y, i0, i1,
-              [&](int a, int b) {
-                if (a > b) { const int t = a; a = b; b = t; }
-                a = max(a, bx0); b = min(b, bx1);
-                if (a <= b) fill_bits(er, a - bx0, b - bx0);
-              },
-              [&](int x) {
-                if (x >= bx0 && x <= bx1) atomicXor(tr + ((x - bx0) >> 5), 1u << ((x - bx0) & 31));
-              });
-        }
-      }
+      // edge-major: every thread takes edges and marks the rows of this band
+      // they cover (contour edges are horizontal, vertical or diagonal)
+      for (int i = threadIdx.x; i < n; i += kScoreThreads)
+        db::poly_edge_marks(p[i], p[(i + 1 < n) ? i + 1 : 0], band, band + rows - 1,
+            [&](int y, int a, int b) {
+              if (a > b) { const int t = a; a = b; b = t; }
+              a = max(a, bx0); b = min(b, bx1);
+              if (a <= b) fill_bits(s_edge[y - band], a - bx0, b - bx0);
+            },
+            [&](int y, int x) {
+              if (x >= bx0 && x <= bx1)
+                atomicXor(&s_tog[y - band][(x - bx0) >> 5], 1u << ((x - bx0) & 31));
+            });
       __syncthreads();
       if (threadIdx.x < rows) {
         const int r = threadIdx.x;
@@ -928,6 +1015,55 @@ unclip_kernel(const int *__restrict__ stage2, const int *__restrict__ npts,
   finish_box(rect_local(ring, rn), c, geo, keep2, boxes, P);
 }
 
+// offset_prepare by the whole CTA (same q, same length): the last point that
+// differs from p[0] bounds the path, consecutive repeats are dropped (a point
+// is kept when it differs from its predecessor, which is always the last
+// kept one), and the path is reversed when its shoelace sum is positive. The
+// shoelace terms are integers, so the int64 sum (any order, modular) equals
+// the sequential double sum. Returns the length, 0 when below 3.
+__device__ int cta_offset_prepare(const P2 *p, int n, P2 *q) {
+  __shared__ int s_hi;
+  __shared__ unsigned long long s_area;
+  const int t = threadIdx.x, T = blockDim.x, lane = t & 31;
+  if (t == 0) { s_hi = 0; s_area = 0ull; }
+  __syncthreads();
+  const P2 p0 = p[0];
+  int hi = 0;
+  for (int i = t; i < n; i += T)
+    if (p[i].x != p0.x || p[i].y != p0.y) hi = i;
+  for (int o = 16; o; o >>= 1) hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+  if (lane == 0) atomicMax(&s_hi, hi);
+  __syncthreads();
+  const int len = s_hi + 1;
+  const int chunk = (len + T - 1) / T;
+  const int i0 = min(len, t * chunk), i1 = min(len, i0 + chunk);
+  auto kept = [&](int i) { return i == 0 || p[i].x != p[i - 1].x || p[i].y != p[i - 1].y; };
+  int cnt = 0;
+  for (int i = i0; i < i1; ++i) cnt += kept(i);
+  int m;
+  int pos = cta_inclusive_sum(cnt, &m) - cnt;
+  for (int i = i0; i < i1; ++i)
+    if (kept(i)) q[pos++] = p[i];
+  if (m < 3) return 0;
+  __syncthreads();
+  long long a = 0;
+  for (int i = t; i < m; i += T) {
+    const P2 qj = q[i == 0 ? m - 1 : i - 1], qi = q[i];
+    a += (long long)(qj.x + qi.x) * (long long)(qj.y - qi.y);
+  }
+  for (int o = 16; o; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+  if (lane == 0) atomicAdd(&s_area, (unsigned long long)a);
+  __syncthreads();
+  if ((long long)s_area > 0)
+    for (int i = t; i < m / 2; i += T) {
+      const P2 u = q[i];
+      q[i] = q[m - 1 - i];
+      q[m - 1 - i] = u;
+    }
+  __syncthreads();
+  return m;
+}
+
 // One thread, global scratch: unclip ring of rn points and its min-area box.
 __device__ bool unclip_rect_global(const P2 *p, int n, double d, int rn, char *pool,
                                    int *counters, unsigned long long pool_bytes, int *status,
@@ -959,7 +1095,7 @@ unclip_big_kernel(const int *__restrict__ list, const int *__restrict__ counters
                   int *__restrict__ keep2, int *__restrict__ boxes, char *__restrict__ pool,
                   int *__restrict__ pool_counters, int *__restrict__ status, DbParams P) {
   extern __shared__ __align__(16) uint8_t smem[];
-  __shared__ int s_qm, s_rn, s_fits;
+  __shared__ int s_rn, s_fits;
   __shared__ P2 *s_q;
   const BigSmem S = big_smem(smem);
   const int count = counters[1];
@@ -975,25 +1111,20 @@ unclip_big_kernel(const int *__restrict__ list, const int *__restrict__ counters
     const int base = bb.x - pad, ncols = bb.z - bb.x + 1 + 2 * pad;
     const bool in_smem = near && ncols <= P.big_cols;
     if (threadIdx.x == 0) {
-      int qm = 0;
       P2 *q = S.q;
-      if (d != 0.) {
-        if (n > kBigQPts)
-          q = reinterpret_cast<P2 *>(
-              pool_alloc(pool, pool_counters, P.pool_bytes, n * sizeof(P2), status));
-        qm = q ? db::offset_prepare(p, n, q) : -1;
-      }
-      s_qm = qm;
+      if (d != 0. && n > kBigQPts)
+        q = reinterpret_cast<P2 *>(
+            pool_alloc(pool, pool_counters, P.pool_bytes, n * sizeof(P2), status));
       s_q = q;
     }
     if (in_smem) table_clear(S, ncols);
     __syncthreads();
-    const int qm = s_qm;
-    const P2 *q = s_q;
-    if (qm < 0) {  // scratch pool exhausted (status set)
+    P2 *q = s_q;
+    if (d != 0. && !q) {  // scratch pool exhausted (status set)
       __syncthreads();
       continue;
     }
+    const int qm = d == 0. ? 0 : cta_offset_prepare(p, n, q);
     int rn = 0;
     bool fits = true;
     if (qm == 0) {  // no offset: the ring is the contour itself
@@ -1113,7 +1244,8 @@ namespace {
 struct DbLayout {
   size_t bitmap, tile_bg, bits, slab, lab, scan_tot, row_count, row_off, n_contours, n_total,
       starts, npts, pt_off, pts, stage1, aabb, stage2, score, dist, keep2, boxes, list1, list2,
-      counters, pool, total;
+      counters, pool, ovf_first, ovf_next, ovf_pts, ovf_count, total;
+  int ovf_chunks;
   unsigned long long pool_bytes;
 };
 
@@ -1151,6 +1283,12 @@ DbLayout db_layout(int n_maps, int h, int w, long long point_cap, long long offs
   L.counters = take(kCounters * 4);
   L.pool_bytes = (unsigned long long)offset_cap * kPoolBytesPerPoint;
   L.pool = take(L.pool_bytes);
+  // trace overflow: the points beyond each contour's slab, in kChunk chunks
+  L.ovf_chunks = (int)std::min<long long>(point_cap / kChunk + 256, 1ll << 30);
+  L.ovf_first = take(C * 4);
+  L.ovf_next = take((size_t)L.ovf_chunks * 4);
+  L.ovf_pts = take((size_t)L.ovf_chunks * kChunk * sizeof(P2));
+  L.ovf_count = take(4);
   L.total = o;
   return L;
 }
@@ -1219,6 +1357,9 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
       *boxes = (int *)at(L.boxes), *list1 = (int *)at(L.list1), *list2 = (int *)at(L.list2),
       *counters = (int *)at(L.counters);
   char *pool = at(L.pool);
+  int *ovf_first = (int *)at(L.ovf_first), *ovf_next = (int *)at(L.ovf_next),
+      *ovf_count = (int *)at(L.ovf_count);
+  P2 *ovf_pts = (P2 *)at(L.ovf_pts);
   int4 *aabb = (int4 *)at(L.aabb);
   double *dist = (double *)at(L.dist);
 
@@ -1240,14 +1381,16 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
                                           thresh);
   ccl_merge_kernel<<<tiles, 128, 0, st>>>(bitmap, lab, tile_bg, h, w);
   ccl_rows_kernel<<<dim3(h, n_maps), 256, 0, st>>>(lab, row_count, h, w, false);
-  starts_scan_kernel<<<n_maps, kScanThreads, 0, st>>>(row_count, row_off, n_contours, n_total, h);
+  starts_scan_kernel<<<n_maps, kScanThreads, 0, st>>>(row_count, row_off, n_contours, n_total, h,
+                                                      ovf_count);
   starts_write_kernel<<<dim3(h, n_maps), 256, 0, st>>>(lab, bitmap, row_count, row_off, starts, h, w);
-  trace_kernel<<<cgrid, 128, 0, st>>>(bits, starts, n_contours, npts, slab, d_status, n_maps, h, w);
+  trace_kernel<<<cgrid, 128, 0, st>>>(bits, starts, n_contours, npts, slab, ovf_first, ovf_next,
+                                      ovf_pts, ovf_count, L.ovf_chunks, d_status, n_maps, h, w);
   scan_map_kernel<int><<<n_maps, kScanThreads, 0, st>>>(npts, pt_off, scan_tot);
   scan_base_kernel<<<n_maps, kScanThreads, 0, st>>>(pt_off, scan_tot, n_maps);
   prep_geom_kernel<<<1, 1, 0, st>>>(pt_off, C, point_cap, d_status, counters);
-  gather_kernel<<<(unsigned)((C * 32 + 127) / 128), 128, 0, st>>>(bits, starts, npts, pt_off, slab,
-                                                                 pts, point_cap, n_maps, h, w);
+  gather_kernel<<<(unsigned)((C * 32 + 127) / 128), 128, 0, st>>>(
+      bits, starts, npts, pt_off, slab, ovf_first, ovf_next, ovf_pts, pts, point_cap, n_maps, h, w);
   geom_box1_kernel<<<cgrid, 128, 0, st>>>(n_contours, npts, pt_off, pts, stage1, aabb, list1,
                                           counters, P);
   const unsigned bgrid = (unsigned)(C < sm_count() ? C : sm_count());

@@ -62,10 +62,10 @@ TG int code_dy(int d) { return (d >= 1 && d <= 3) ? -1 : (d >= 5) ? 1 : 0; }
 // the chain code changes (CHAIN_APPROX_SIMPLE); the start pixel is always
 // emitted. nb(x, y) returns the 8-neighbourhood of (x, y) as a bit mask
 // (bit d set when the neighbour in chain-code direction d is foreground;
-// outside the image counts as background). Writes at most cap points and
-// returns the full count, or -1 if max_steps was exceeded.
-template <class NB>
-TG int trace_border_nb(NB &nb, int x0, int y0, bool hole, P2 *out, int cap, int max_steps) {
+// outside the image counts as background). Calls emit(x, y) for each point
+// and returns their count, or -1 if max_steps was exceeded.
+template <class NB, class EMIT>
+TG int trace_border_emit(NB &nb, int x0, int y0, bool hole, EMIT &&emit, int max_steps) {
   const int dstart = hole ? 0 : 4;
   int d1 = -1;
   {
@@ -80,7 +80,7 @@ TG int trace_border_nb(NB &nb, int x0, int y0, bool hole, P2 *out, int cap, int 
   }
   int n = 0;
   if (d1 < 0) {  // isolated pixel
-    if (cap > 0) out[0] = P2{x0, y0};
+    emit(x0, y0);
     return 1;
   }
   const int x1 = x0 + code_dx(d1), y1 = y0 + code_dy(d1);
@@ -97,7 +97,7 @@ TG int trace_border_nb(NB &nb, int x0, int y0, bool hole, P2 *out, int cap, int 
       }
     }
     if (d4 != last_code) {
-      if (n < cap) out[n] = P2{x3, y3};
+      emit(x3, y3);
       ++n;
       last_code = d4;
     }
@@ -125,6 +125,20 @@ TG int trace_border_nb(NB &nb, int x0, int y0, bool hole, P2 *out, int cap, int 
     }
   }
   return -1;
+}
+
+// trace_border_emit into out: writes at most cap points, returns the full
+// count (or -1).
+template <class NB>
+TG int trace_border_nb(NB &nb, int x0, int y0, bool hole, P2 *out, int cap, int max_steps) {
+  int k = 0;
+  return trace_border_emit(
+      nb, x0, y0, hole,
+      [&](int x, int y) {
+        if (k < cap) out[k] = P2{x, y};
+        ++k;
+      },
+      max_steps);
 }
 
 // Neighbourhood mask from a per-pixel predicate fg(x, y).
@@ -158,6 +172,16 @@ TG int trace_border(const FG &fg, int x0, int y0, bool hole, P2 *out, int cap, i
 // Neighbourhood masks from a bit-packed bitmap (bit x & 31 of word
 // y * words + (x >> 5)), caching the 3 x 2 words around the last centre so
 // that a walk along a row reloads once per 32 pixels.
+// Read of the packed bitmap: written by an earlier kernel, read-only while
+// borders are traced, so the device reads it through the non-coherent cache.
+TG uint32_t ld_bits(const uint32_t *p) {
+#ifdef __CUDA_ARCH__
+  return __ldg(p);
+#else
+  return *p;
+#endif
+}
+
 struct NbBits {
   const uint32_t *bits;
   int H, W, words;
@@ -171,8 +195,8 @@ struct NbBits {
       for (int i = 0; i < 3; ++i) {
         const int yy = y - 1 + i;
         const bool row_ok = yy >= 0 && yy < H;
-        r[i][0] = (row_ok && w0 >= 0 && w0 < words) ? bits[(long long)yy * words + w0] : 0u;
-        r[i][1] = (row_ok && w0 + 1 < words) ? bits[(long long)yy * words + w0 + 1] : 0u;
+        r[i][0] = (row_ok && w0 >= 0 && w0 < words) ? ld_bits(bits + (long long)yy * words + w0) : 0u;
+        r[i][1] = (row_ok && w0 + 1 < words) ? ld_bits(bits + (long long)yy * words + w0 + 1) : 0u;
       }
     }
     const int sh = (x - 1) - (w0 << 5);  // bit of column x - 1 inside word w0, 0..31
@@ -195,7 +219,7 @@ struct NbBits {
     return m;
   }
   TG uint32_t word(int y, int w) const {
-    return (y >= 0 && y < H && w >= 0 && w < words) ? bits[(long long)y * words + w] : 0u;
+    return (y >= 0 && y < H && w >= 0 && w < words) ? ld_bits(bits + (long long)y * words + w) : 0u;
   }
   // First column >= x0 whose bit in row y equals v (W if none before the end).
   TG int find_fwd(int y, int x0, bool v) const {
@@ -384,12 +408,41 @@ TG bool col_entry(const uint64_t *lo, const uint64_t *hi, int base, int e, HP *o
   return true;
 }
 
+// Interior filter (Akl-Toussaint): the points extreme in kExtDirs integer
+// directions of increasing angle lie on the hull boundary and, in that
+// order, form a convex polygon inside the hull; a point strictly inside it
+// is no hull vertex and can be dropped before the chain. Directions are
+// 512 * (cos, sin) of k * 22.5 degrees, rounded.
+constexpr int kExtDirs = 16;
+TG int ext_cos(int k) {
+  const int c[16] = {512, 473, 362, 196, 0, -196, -362, -473, -512, -473, -362, -196, 0, 196, 362, 473};
+  return c[k & 15];
+}
+TG long long ext_dot(int k, int x, int y) {
+  return (long long)ext_cos(k) * x + (long long)ext_cos(k + 12) * y;
+}
+// True when v is strictly inside the polygon poly[0..k) of extreme points
+// (at least three non-degenerate edges needed; a degenerate polygon has no
+// inside).
+TG bool strictly_inside_extremes(const HP *poly, int k, const HP &v) {
+  int edges = 0;
+  for (int i = 0; i < k; ++i) {
+    const HP &a = poly[i], &b = poly[(i + 1) % k];
+    if (a.x == b.x && a.y == b.y) continue;
+    if (cross3(a, b, v) <= 0) return false;
+    ++edges;
+  }
+  return edges >= 3;
+}
+
 // Andrew's monotone chain over the candidates of the table of ncols columns
 // (x = base + c): the same hull, orientation and starting vertex as
-// convex_hull on the original points. stk (entries) needs 2*ncols+1 ints.
-// Returns the hull size, or -1 when it exceeds hull_cap.
+// convex_hull on the original points. keep (optional): bit e set for the
+// entries that may be hull vertices (every hull vertex must be kept). stk
+// (entries) needs 2*ncols+1 ints. Returns the hull size, or -1 when it
+// exceeds hull_cap.
 TG int hull_from_table(const uint64_t *lo, const uint64_t *hi, int ncols, int base, int *stk,
-                       P2 *hull, int hull_cap) {
+                       P2 *hull, int hull_cap, const uint32_t *keep = nullptr) {
   const int ns = 2 * ncols;
   HP a, b, v;
   auto at = [&](int e) {
@@ -399,6 +452,14 @@ TG int hull_from_table(const uint64_t *lo, const uint64_t *hi, int ncols, int ba
   };
   int top = 0, last = -1;
   for (int e = 0; e < ns; ++e) {  // lower chain
+    if (keep) {
+      const uint32_t w = keep[e >> 5];
+      if ((e & 31) == 0 && w == 0) {
+        e += 31;
+        continue;
+      }
+      if (!((w >> (e & 31)) & 1u)) continue;
+    }
     if (!col_entry(lo, hi, base, e, &v)) continue;
     last = e;
     while (top >= 2) {
@@ -411,6 +472,14 @@ TG int hull_from_table(const uint64_t *lo, const uint64_t *hi, int ncols, int ba
   }
   if (last < 0) return 0;
   for (int e = last - 1, t = top + 1; e >= 0; --e) {  // upper chain
+    if (keep) {
+      const uint32_t w = keep[e >> 5];
+      if ((e & 31) == 31 && w == 0) {
+        e -= 31;
+        continue;
+      }
+      if (!((w >> (e & 31)) & 1u)) continue;
+    }
     if (!col_entry(lo, hi, base, e, &v)) continue;
     while (top >= t) {
       a = at(stk[top - 2]);
@@ -692,27 +761,39 @@ TG void poly_row_spans(const P2 *p, int n, int y, int *xs, const SPAN &span) {
   for (int i = 0; i + 1 < nc; i += 2) span(xs[i], xs[i + 1]);
 }
 
+// The marks of one contour edge a -> b (horizontal, vertical or diagonal, as
+// CHAIN_APPROX_SIMPLE makes them) on the rows [ya, yb]: edge(y, x0, x1) for
+// its pixels on row y (inclusive, unordered) and cross(y, x) for its crossing
+// of row y under the half-open rule [ylo, yhi).
+template <class EDGE, class CROSS>
+TG void poly_edge_marks(P2 a, P2 b, int ya, int yb, const EDGE &edge, const CROSS &cross) {
+  if (a.y == b.y) {
+    if (a.y >= ya && a.y <= yb) edge(a.y, a.x, b.x);
+    return;
+  }
+  const int ylo = a.y < b.y ? a.y : b.y, yhi = a.y < b.y ? b.y : a.y;
+  const int y0 = ylo > ya ? ylo : ya, y1 = yhi < yb ? yhi : yb;
+  const int dx = b.x - a.x, dy = b.y - a.y;
+  const int sx = (dx == 0 ? 0 : (dx > 0 ? 1 : -1)) * (dy > 0 ? 1 : -1);
+  for (int y = y0; y <= y1; ++y) {
+    const int x = a.x + (y - a.y) * sx;  // lattice point of the edge on row y
+    edge(y, x, x);
+    if (y < yhi) cross(y, x);
+  }
+}
+
 // The same pixel set as poly_row_spans without sorting, for bitmask fills:
 // edge(x0, x1) for every edge run (inclusive, unordered) and cross(x) for
-// every crossing of the half-open rule. The row's mask is the edge runs plus
-// the pixels where the count of crossings at or left of them is odd (the
-// closing crossing of each inside run is itself an edge pixel).
+// every crossing of the half-open rule, over edges [i0, i1) on row y. The
+// row's mask is the edge runs plus the pixels where the count of crossings at
+// or left of them is odd (the closing crossing of each inside run is itself
+// an edge pixel).
 template <class EDGE, class CROSS>
 TG void poly_row_marks(const P2 *p, int n, int y, int i0, int i1, const EDGE &edge,
                        const CROSS &cross) {
-  for (int i = i0; i < i1; ++i) {
-    const P2 a = p[i], b = p[(i + 1 < n) ? i + 1 : 0];
-    if (a.y == b.y) {
-      if (a.y == y) edge(a.x, b.x);
-      continue;
-    }
-    const int ylo = a.y < b.y ? a.y : b.y, yhi = a.y < b.y ? b.y : a.y;
-    if (y < ylo || y > yhi) continue;
-    const int dx = b.x - a.x, dy = b.y - a.y;
-    const int x = a.x + (y - a.y) * (dx == 0 ? 0 : (dx > 0 ? 1 : -1)) * (dy > 0 ? 1 : -1);
-    edge(x, x);
-    if (y < yhi) cross(x);
-  }
+  for (int i = i0; i < i1; ++i)
+    poly_edge_marks(p[i], p[(i + 1 < n) ? i + 1 : 0], y, y,
+                    [&](int, int x0, int x1) { edge(x0, x1); }, [&](int, int x) { cross(x); });
 }
 
 // ------------------------------------------------- area / arc length -----------
