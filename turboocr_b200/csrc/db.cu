@@ -910,11 +910,18 @@ score_kernel(const float *__restrict__ pred, const int *__restrict__ stage1,
         if (tail) s_edge[r][words - 1] &= (1u << tail) - 1u;
       }
       __syncthreads();
-      for (int i = threadIdx.x; i < rows * width; i += kScoreThreads) {
-        const int r = i / width, x = i % width;
-        if ((s_edge[r][x >> 5] >> (x & 31)) & 1u) {
-          sum += (double)pm[(size_t)(band + r) * W + bx0 + x];
-          ++cnt;
+      // a warp per (row, 32-pixel word) of the mask: coalesced row reads,
+      // empty words skipped
+      {
+        const int lane = threadIdx.x & 31;
+        for (int k = threadIdx.x >> 5; k < rows * words; k += kScoreThreads / 32) {
+          const int r = k / words, wd = k - r * words;
+          const unsigned msk = s_edge[r][wd];
+          if (msk == 0u) continue;
+          if ((msk >> lane) & 1u) {
+            sum += (double)pm[(size_t)(band + r) * W + bx0 + (wd << 5) + lane];
+            ++cnt;
+          }
         }
       }
       __syncthreads();

@@ -78,6 +78,12 @@ TG int trace_border_emit(NB &nb, int x0, int y0, bool hole, EMIT &&emit, int max
       }
     }
   }
+  // first foreground direction counter-clockwise after `from` (the mask is
+  // rotated so that direction from+1 is bit 0); `from` itself when none
+  auto ccw_after = [](unsigned mask, int from) {
+    const unsigned r = ((mask | (mask << 8)) >> (from + 1)) & 0xFFu;
+    return r ? (from + 1 + __builtin_ctz_tg(r)) & 7 : from;
+  };
   int n = 0;
   if (d1 < 0) {  // isolated pixel
     emit(x0, y0);
@@ -87,15 +93,7 @@ TG int trace_border_emit(NB &nb, int x0, int y0, bool hole, EMIT &&emit, int max
   int last_code = d1 ^ 4;
   int x3 = x0, y3 = y0, dback = d1;
   for (int step = 0; step < max_steps; ++step) {
-    const unsigned m = nb(x3, y3);
-    int d4 = dback;
-    for (int k = 1; k <= 8; ++k) {  // counter-clockwise after the previous pixel
-      const int d = (dback + k) & 7;
-      if ((m >> d) & 1u) {
-        d4 = d;
-        break;
-      }
-    }
+    const int d4 = ccw_after(nb(x3, y3), dback);  // counter-clockwise after the previous pixel
     if (d4 != last_code) {
       emit(x3, y3);
       ++n;
@@ -172,6 +170,15 @@ TG int trace_border(const FG &fg, int x0, int y0, bool hole, P2 *out, int cap, i
 // Neighbourhood masks from a bit-packed bitmap (bit x & 31 of word
 // y * words + (x >> 5)), caching the 3 x 2 words around the last centre so
 // that a walk along a row reloads once per 32 pixels.
+// Low 32 bits of (hi:lo) >> sh, sh in [0, 31].
+TG uint32_t funnel_r(uint32_t lo, uint32_t hi, int sh) {
+#ifdef __CUDA_ARCH__
+  return __funnelshift_r(lo, hi, sh);
+#else
+  return (uint32_t)((((uint64_t)hi << 32) | lo) >> sh);
+#endif
+}
+
 // Read of the packed bitmap: written by an earlier kernel, read-only while
 // borders are traced, so the device reads it through the non-coherent cache.
 TG uint32_t ld_bits(const uint32_t *p) {
@@ -200,23 +207,15 @@ struct NbBits {
       }
     }
     const int sh = (x - 1) - (w0 << 5);  // bit of column x - 1 inside word w0, 0..31
-    uint32_t t[3];
-    for (int i = 0; i < 3; ++i) {
-      const unsigned long long both = ((unsigned long long)r[i][1] << 32) | r[i][0];
-      t[i] = (uint32_t)(both >> sh) & 7u;  // columns x-1, x, x+1
-    }
-    // columns beyond the image width read 0: the bitmap is zero-padded per row
-    // directions: 0 E (x+1,y) 1 NE (x+1,y-1) 2 N 3 NW 4 W 5 SW 6 S 7 SE
-    unsigned m = 0;
-    m |= ((t[1] >> 2) & 1u) << 0;
-    m |= ((t[0] >> 2) & 1u) << 1;
-    m |= ((t[0] >> 1) & 1u) << 2;
-    m |= ((t[0] >> 0) & 1u) << 3;
-    m |= ((t[1] >> 0) & 1u) << 4;
-    m |= ((t[2] >> 0) & 1u) << 5;
-    m |= ((t[2] >> 1) & 1u) << 6;
-    m |= ((t[2] >> 2) & 1u) << 7;
-    return m;
+    // columns x-1, x, x+1 of rows y-1, y, y+1 (columns beyond the image width
+    // read 0: the bitmap is zero-padded per row)
+    const uint32_t t0 = funnel_r(r[0][0], r[0][1], sh) & 7u;
+    const uint32_t t1 = funnel_r(r[1][0], r[1][1], sh) & 7u;
+    const uint32_t t2 = funnel_r(r[2][0], r[2][1], sh) & 7u;
+    // directions: 0 E (x+1,y) 1 NE (x+1,y-1) 2 N 3 NW 4 W 5 SW 6 S 7 SE:
+    // NE N NW are row y-1 right to left, SW S SE row y+1 left to right
+    const uint32_t rev0 = ((t0 & 1u) << 2) | (t0 & 2u) | (t0 >> 2);
+    return (t1 >> 2) | (rev0 << 1) | ((t1 & 1u) << 4) | (t2 << 5);
   }
   TG uint32_t word(int y, int w) const {
     return (y >= 0 && y < H && w >= 0 && w < words) ? ld_bits(bits + (long long)y * words + w) : 0u;
@@ -450,16 +449,28 @@ TG int hull_from_table(const uint64_t *lo, const uint64_t *hi, int ncols, int ba
     col_entry(lo, hi, base, e, &r);
     return r;
   };
-  int top = 0, last = -1;
-  for (int e = 0; e < ns; ++e) {  // lower chain
-    if (keep) {
-      const uint32_t w = keep[e >> 5];
-      if ((e & 31) == 0 && w == 0) {
-        e += 31;
-        continue;
-      }
-      if (!((w >> (e & 31)) & 1u)) continue;
+  // next kept entry at or after e (ns if none) / at or before e (-1 if none)
+  const int nw = (ns + 31) >> 5;
+  auto next_kept = [&](int e) {
+    if (!keep) return e;
+    for (int w = e >> 5; w < nw; ++w) {
+      uint32_t b = keep[w];
+      if (w == (e >> 5)) b &= ~0u << (e & 31);
+      if (b) return (w << 5) + __builtin_ctz_tg(b);
     }
+    return ns;
+  };
+  auto prev_kept = [&](int e) {
+    if (!keep) return e;
+    for (int w = e >> 5; w >= 0; --w) {
+      uint32_t b = keep[w];
+      if (w == (e >> 5)) b &= (e & 31) == 31 ? ~0u : ((2u << (e & 31)) - 1u);
+      if (b) return (w << 5) + 31 - __builtin_clz_tg(b);
+    }
+    return -1;
+  };
+  int top = 0, last = -1;
+  for (int e = next_kept(0); e < ns; e = next_kept(e + 1)) {  // lower chain
     if (!col_entry(lo, hi, base, e, &v)) continue;
     last = e;
     while (top >= 2) {
@@ -471,16 +482,9 @@ TG int hull_from_table(const uint64_t *lo, const uint64_t *hi, int ncols, int ba
     stk[top++] = e;
   }
   if (last < 0) return 0;
-  for (int e = last - 1, t = top + 1; e >= 0; --e) {  // upper chain
-    if (keep) {
-      const uint32_t w = keep[e >> 5];
-      if ((e & 31) == 31 && w == 0) {
-        e -= 31;
-        continue;
-      }
-      if (!((w >> (e & 31)) & 1u)) continue;
-    }
-    if (!col_entry(lo, hi, base, e, &v)) continue;
+  const int t = top + 1;
+  for (int e = last > 0 ? prev_kept(last - 1) : -1; e >= 0; e = e > 0 ? prev_kept(e - 1) : -1) {
+    if (!col_entry(lo, hi, base, e, &v)) continue;  // upper chain
     while (top >= t) {
       a = at(stk[top - 2]);
       b = at(stk[top - 1]);
