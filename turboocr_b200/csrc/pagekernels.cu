@@ -18,6 +18,7 @@
 // Default nvcc contraction (as the reference kernels are built): the ROI warp
 // keeps batch_roi_warp_kernel's expressions, so it rounds the same way.
 #include "tocr_common.cuh"
+#include "tc_ptx.cuh"
 
 #include <algorithm>
 #include <cmath>
@@ -39,97 +40,191 @@ __device__ __forceinline__ float hswish(float v) {
   return v * fminf(fmaxf(v + 3.f, 0.f), 6.f) * (1.f / 6.f);
 }
 
-// A CTA computes an 8 x 64 tile of output pixels. The 17 x 129-pixel input
-// window is staged once in shared memory, already normalised (zero outside
-// the image: the conv pads the normalised tensor), channel planes apart; the
-// weights go to shared memory as [tap][co]. Each thread then accumulates a
-// 4-pixel x 16-channel block in registers: per tap, four window reads (the
-// thread's pixels are 16 columns apart, so a warp reads 16 consecutive even
-// columns: no bank conflicts) and four float4 weight broadcasts feed 64 FMAs.
-// Every output keeps the tap order (ky, kx, ci) of the accumulation.
-// grid (tiles_x, tiles_y, n), 256 threads.
-constexpr int kStemTH = 8, kStemTW = 64;
-constexpr int kStemIH = 2 * kStemTH + 1, kStemIW = 2 * kStemTW + 1;
-constexpr int kStemPitch = kStemIW + 3;  // row pitch of a channel plane (floats)
+// The stem as an implicit GEMM on the tensor cores: M = 128 output pixels
+// (a 4 x 32 tile), N = 32 channels, K = the 27 taps (ky, kx, ci) padded to
+// 32. fp16 operands alone would lose too much of the fp32 conv, so every
+// operand is split into fp16 hi + lo parts (x = hi + lo, |lo| <= ulp(hi)/2)
+// and the MMAs add hi*w_hi + lo*w_hi + hi*w_lo in fp32 (the dropped lo*w_lo
+// is below 1e-6 relative): an A row is [hi(32) | lo(32)] fp16 = one 128-byte
+// K-major row, B1 rows are [w_hi | w_hi] (4 MMAs of K = 16 over the full
+// row) and B2 rows [w_lo | 0] (2 MMAs over the hi half).
+// A persistent CTA of 128 threads loops over tiles: stage the normalised
+// 9 x 65 input window (zero outside the image) in shared memory, build the
+// A tile (thread = pixel = TMEM lane), one thread issues the six MMAs into
+// 32 TMEM columns, then every thread reads its pixel's 32 accumulators
+// (tcgen05.ld), adds the bias, applies hardswish and stores 64 bytes.
+namespace stc {
+constexpr int TR = 4, TC = 32, TPX = TR * TC;   // output tile = MMA M
+constexpr int WR = 2 * TR + 1, WC = 2 * TC + 1; // input window
+constexpr int WP = WC + 3;                      // window plane row pitch (floats)
+constexpr int kThreads = 128;
+constexpr int OFF_A = 0, A_BYTES = TPX * 128;
+constexpr int B_BYTES = kStemCo * 128;
+constexpr int OFF_B1 = OFF_A + A_BYTES, OFF_B2 = OFF_B1 + B_BYTES;
+constexpr int OFF_WIN = OFF_B2 + B_BYTES;
+constexpr int OFF_BIAS = OFF_WIN + 3 * WR * WP * 4;
+constexpr int OFF_BAR = (OFF_BIAS + kStemCo * 4 + 7) / 8 * 8;
+constexpr int OFF_MISC = OFF_BAR + 8;           // TMEM address, abort flag
+constexpr int SMEM_ALLOC = OFF_MISC + 16 + 1024;  // + runtime 1024 alignment
+constexpr int TMEM_COLS = 32;
+static_assert(OFF_B1 % 1024 == 0 && OFF_B2 % 1024 == 0, "UMMA operand alignment");
+}  // namespace stc
 
-__global__ void __launch_bounds__(256, 2)
-stem_kernel(const uint8_t *__restrict__ pages, int H, int W, long long page_stride,
-            __half *__restrict__ out, const StemParams sp) {
-  __shared__ float s_in[3][kStemIH][kStemPitch];
-  __shared__ __align__(16) float s_w[27][kStemCo];
-  const int Ho = (H - 1) / 2 + 1, Wo = (W - 1) / 2 + 1;
-  const int n = blockIdx.z;
-  const int oy0 = blockIdx.y * kStemTH, ox0 = blockIdx.x * kStemTW;
-  const int iy0 = 2 * oy0 - 1, ix0 = 2 * ox0 - 1;
-  const uint8_t *pg = pages + (long long)n * page_stride;
-  for (int i = threadIdx.x; i < 27 * kStemCo; i += blockDim.x) {
-    const int k = i / kStemCo, co = i - k * kStemCo;
-    s_w[k][co] = sp.w[co][k];
-  }
-  // one window pixel per item: its three bytes, normalised (0 outside)
-  const long long row_bytes = 3ll * W;
-  for (int i = threadIdx.x; i < kStemIH * kStemIW; i += blockDim.x) {
-    const int row = i / kStemIW, col = i - row * kStemIW;
-    const int y = iy0 + row, x = ix0 + col;
-    float v0 = 0.f, v1 = 0.f, v2 = 0.f;
-    if (y >= 0 && y < H && x >= 0 && x < W) {
-      const uint8_t *px = pg + (long long)y * row_bytes + 3ll * x;
-      v0 = ((float)__ldg(px) * (1.0f / 255.0f) - sp.mean[0]) * sp.inv_std[0];
-      v1 = ((float)__ldg(px + 1) * (1.0f / 255.0f) - sp.mean[1]) * sp.inv_std[1];
-      v2 = ((float)__ldg(px + 2) * (1.0f / 255.0f) - sp.mean[2]) * sp.inv_std[2];
+__device__ int g_stem_err;  // first bounded-wait timeout code, 0 if none
+
+// Byte offset of 16-byte chunk `chunk` of row `row` in a K-major tile with
+// 128-byte rows in the 128B-swizzle layout (8-row groups 1024 bytes apart).
+__device__ __forceinline__ uint32_t sw128_off(int row, int chunk) {
+  return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ uint32_t pack_h2(__half a, __half b) {
+  const __half2 h = __halves2half2(a, b);
+  return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+__global__ void __launch_bounds__(stc::kThreads)
+stem_tc_kernel(const uint8_t *__restrict__ pages, int H, int W, long long page_stride,
+               __half *__restrict__ out, const StemParams sp, int tiles_x, int tiles_y,
+               int ntiles) {
+  using namespace ptx;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sa = smem + stc::OFF_A, *sb1 = smem + stc::OFF_B1, *sb2 = smem + stc::OFF_B2;
+  float *win = reinterpret_cast<float *>(smem + stc::OFF_WIN);
+  float *sbias = reinterpret_cast<float *>(smem + stc::OFF_BIAS);
+  uint64_t *bar = reinterpret_cast<uint64_t *>(smem + stc::OFF_BAR);
+  uint32_t *s_tmem = reinterpret_cast<uint32_t *>(smem + stc::OFF_MISC);
+  volatile int *s_abort = reinterpret_cast<volatile int *>(smem + stc::OFF_MISC + 4);
+  const int tid = threadIdx.x, warp = tid >> 5;
+
+  // ---- setup: split weights into the two B tiles, bias, barrier, TMEM ----
+  for (int i = tid; i < kStemCo * 8; i += stc::kThreads) {
+    const int co = i >> 3, j = i & 7;
+    uint32_t h1[4], h2[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      __half hi[2], lo[2];
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int k = 8 * (j & 3) + 2 * e + q;
+        const float w = k < 27 ? sp.w[co][k] : 0.f;
+        hi[q] = __float2half_rn(w);
+        lo[q] = __float2half_rn(w - __half2float(hi[q]));
+      }
+      h1[e] = pack_h2(hi[0], hi[1]);
+      h2[e] = j < 4 ? pack_h2(lo[0], lo[1]) : 0u;
     }
-    s_in[0][row][col] = v0;
-    s_in[1][row][col] = v1;
-    s_in[2][row][col] = v2;
+    *reinterpret_cast<uint4 *>(sb1 + sw128_off(co, j)) = make_uint4(h1[0], h1[1], h1[2], h1[3]);
+    *reinterpret_cast<uint4 *>(sb2 + sw128_off(co, j)) = make_uint4(h2[0], h2[1], h2[2], h2[3]);
+  }
+  if (tid < kStemCo) sbias[tid] = sp.b[tid];
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    *s_abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(s_tmem, stc::TMEM_COLS);
+    tmem_relinquish();
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  const int Ho = (H - 1) / 2 + 1, Wo = (W - 1) / 2 + 1;
+  const int tiles_per_img = tiles_x * tiles_y;
+  const long long row_bytes = 3ll * W;
+  const int py = tid / stc::TC, px = tid % stc::TC;  // this thread's pixel in the tile
+  constexpr uint32_t kIdesc = idesc_f16(stc::TPX, kStemCo);
+  uint32_t it = 0;
+  for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+    const int n = t / tiles_per_img, r = t % tiles_per_img;
+    const int oy0 = (r / tiles_x) * stc::TR, ox0 = (r % tiles_x) * stc::TC;
+    const int iy0 = 2 * oy0 - 1, ix0 = 2 * ox0 - 1;
+    const uint8_t *pg = pages + (long long)n * page_stride;
+    for (int i = tid; i < stc::WR * stc::WC; i += stc::kThreads) {
+      const int row = i / stc::WC, col = i - row * stc::WC;
+      const int y = iy0 + row, x = ix0 + col;
+      float v0 = 0.f, v1 = 0.f, v2 = 0.f;
+      if (y >= 0 && y < H && x >= 0 && x < W) {
+        const uint8_t *q = pg + (long long)y * row_bytes + 3ll * x;
+        v0 = ((float)__ldg(q) * (1.0f / 255.0f) - sp.mean[0]) * sp.inv_std[0];
+        v1 = ((float)__ldg(q + 1) * (1.0f / 255.0f) - sp.mean[1]) * sp.inv_std[1];
+        v2 = ((float)__ldg(q + 2) * (1.0f / 255.0f) - sp.mean[2]) * sp.inv_std[2];
+      }
+      win[(0 * stc::WR + row) * stc::WP + col] = v0;
+      win[(1 * stc::WR + row) * stc::WP + col] = v1;
+      win[(2 * stc::WR + row) * stc::WP + col] = v2;
+    }
+    __syncthreads();
+    {  // A row of this pixel: taps in (ky, kx, ci) order, hi then lo
+      __half hi[32], lo[32];
+#pragma unroll
+      for (int ky = 0; ky < 3; ++ky)
+#pragma unroll
+        for (int kx = 0; kx < 3; ++kx)
+#pragma unroll
+          for (int ci = 0; ci < 3; ++ci) {
+            const int k = (ky * 3 + kx) * 3 + ci;
+            const float v = win[(ci * stc::WR + 2 * py + ky) * stc::WP + 2 * px + kx];
+            hi[k] = __float2half_rn(v);
+            lo[k] = __float2half_rn(v - __half2float(hi[k]));
+          }
+#pragma unroll
+      for (int k = 27; k < 32; ++k) hi[k] = lo[k] = __float2half_rn(0.f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const __half *src = j < 4 ? hi + 8 * j : lo + 8 * (j - 4);
+        *reinterpret_cast<uint4 *>(sa + sw128_off(tid, j)) =
+            make_uint4(pack_h2(src[0], src[1]), pack_h2(src[2], src[3]), pack_h2(src[4], src[5]),
+                       pack_h2(src[6], src[7]));
+      }
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t a = smem_u32(sa), b1 = smem_u32(sb1), b2 = smem_u32(sb2);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        mma_f16(tmem, sw128_kmajor_desc(a + 32 * k), sw128_kmajor_desc(b1 + 32 * k), kIdesc,
+                k > 0 ? 1u : 0u);
+#pragma unroll
+      for (int k = 0; k < 2; ++k)
+        mma_f16(tmem, sw128_kmajor_desc(a + 32 * k), sw128_kmajor_desc(b2 + 32 * k), kIdesc, 1u);
+      mma_commit(bar);
+    }
+    const bool ok = __syncthreads_and(mbar_wait_bounded(bar, it & 1, s_abort, &g_stem_err, 41));
+    if (!ok) break;
+    tc_fence_after();
+    uint32_t v[32];
+    tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16), v);
+    tmem_ld_wait(v);
+    const int oy = oy0 + py, ox = ox0 + px;
+    if (oy < Ho && ox < Wo) {
+      uint4 packed[kStemCo / 8];
+      uint32_t *pw = reinterpret_cast<uint32_t *>(packed);
+#pragma unroll
+      for (int c = 0; c < kStemCo; c += 2) {
+        const __half2 h = __floats2half2_rn(hswish(__uint_as_float(v[c]) + sbias[c]),
+                                            hswish(__uint_as_float(v[c + 1]) + sbias[c + 1]));
+        pw[c / 2] = *reinterpret_cast<const uint32_t *>(&h);
+      }
+      uint4 *dst = reinterpret_cast<uint4 *>(out + (((long long)n * Ho + oy) * Wo + ox) * kStemCo);
+#pragma unroll
+      for (int k = 0; k < kStemCo / 8; ++k) dst[k] = packed[k];
+    }
+    tc_fence_before();
+    __syncthreads();
   }
   __syncthreads();
-  const int half = threadIdx.x & 1;          // output channels 16 * half .. + 15
-  const int g = threadIdx.x >> 1;            // 128 pixel groups
-  const int ty = g >> 4, gx = g & 15;        // pixels (ty, gx + 16 j), j = 0..3
-  float acc[4][16];
-#pragma unroll
-  for (int j = 0; j < 4; ++j)
-#pragma unroll
-    for (int c = 0; c < 16; ++c) acc[j][c] = sp.b[16 * half + c];
-#pragma unroll
-  for (int ky = 0; ky < 3; ++ky)
-#pragma unroll
-    for (int kx = 0; kx < 3; ++kx)
-#pragma unroll
-      for (int ci = 0; ci < 3; ++ci) {
-        const int k = (ky * 3 + kx) * 3 + ci;
-        float t[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) t[j] = s_in[ci][2 * ty + ky][2 * (gx + 16 * j) + kx];
-        const float4 *wv = reinterpret_cast<const float4 *>(&s_w[k][16 * half]);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float4 w4 = wv[q];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            acc[j][4 * q + 0] = fmaf(w4.x, t[j], acc[j][4 * q + 0]);
-            acc[j][4 * q + 1] = fmaf(w4.y, t[j], acc[j][4 * q + 1]);
-            acc[j][4 * q + 2] = fmaf(w4.z, t[j], acc[j][4 * q + 2]);
-            acc[j][4 * q + 3] = fmaf(w4.w, t[j], acc[j][4 * q + 3]);
-          }
-        }
-      }
-  const int oy = oy0 + ty;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int ox = ox0 + gx + 16 * j;
-    if (oy >= Ho || ox >= Wo) continue;
-    uint4 packed[2];
-    uint32_t *pw = reinterpret_cast<uint32_t *>(packed);
-#pragma unroll
-    for (int c = 0; c < 16; c += 2) {
-      const __half2 h = __floats2half2_rn(hswish(acc[j][c]), hswish(acc[j][c + 1]));
-      pw[c / 2] = *reinterpret_cast<const uint32_t *>(&h);
-    }
-    uint4 *dst = reinterpret_cast<uint4 *>(out + (((long long)n * Ho + oy) * Wo + ox) * kStemCo +
-                                           16 * half);
-    dst[0] = packed[0];
-    dst[1] = packed[1];
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, stc::TMEM_COLS);
   }
 }
 
@@ -356,9 +451,17 @@ TOCR_API int tocr_stem_f16(const uint8_t *d_pages, int n, int h, int w, long lon
   const int Ho = (h - 1) / 2 + 1, Wo = (w - 1) / 2 + 1;
   StemParams sp;
   memcpy(&sp, h_params, sizeof(sp));
-  const dim3 grid((Wo + kStemTW - 1) / kStemTW, (Ho + kStemTH - 1) / kStemTH, n);
-  stem_kernel<<<grid, 256, 0, as_stream(stream)>>>(d_pages, h, w, page_stride, (__half *)d_out, sp);
-  return check_launch("stem_kernel");
+  const int tiles_x = (Wo + stc::TC - 1) / stc::TC, tiles_y = (Ho + stc::TR - 1) / stc::TR;
+  const long long ntiles = (long long)n * tiles_x * tiles_y;
+  TOCR_REQUIRE(ntiles < (1ll << 31), "tocr_stem_f16: too many tiles");
+  cudaError_t e = cudaFuncSetAttribute(stem_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       stc::SMEM_ALLOC);
+  if (e != cudaSuccess) return set_error(TOCR_ERR_CUDA, "stem smem attribute: %s", cudaGetErrorString(e));
+  // persistent CTAs: as many as fit per SM (6 by shared memory; 6 x 32 TMEM columns)
+  const long long grid = std::min<long long>(ntiles, (long long)sm_count() * 6);
+  stem_tc_kernel<<<(unsigned)grid, stc::kThreads, stc::SMEM_ALLOC, as_stream(stream)>>>(
+      d_pages, h, w, page_stride, (__half *)d_out, sp, tiles_x, tiles_y, (int)ntiles);
+  return check_launch("stem_tc_kernel");
 }
 
 TOCR_API int tocr_ink_map(const uint8_t *d_pages, int n, int h, int w, long long page_stride,

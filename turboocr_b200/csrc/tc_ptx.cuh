@@ -159,6 +159,15 @@ __device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t adesc, uint64_t
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D[tmem] (+)= A x B^T with fp16 inputs, f32 accumulate (K = 16 per instruction).
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // Arrive (once) on an mbarrier when all previously issued MMAs of this
 // thread have completed.
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
@@ -218,6 +227,11 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t smem_addr) {
 // kind::f8f6f4 with E4M3 -> c_format F32 (1), a/b format 0.
 __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
   return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
+// kind::f16 with fp16 A and B -> c_format F32 (1), a/b format F16 (0).
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(N >> 3) << 17) |
          ((uint32_t)(M >> 4) << 24);
 }
 __host__ __device__ constexpr uint32_t idesc_e4m3(int M, int N) {
