@@ -30,10 +30,14 @@ namespace {
 // ---------------------------------------------------------------- stem -------
 constexpr int kStemCo = 32;
 
+// The det normalisation (b / 255 - mean) * inv_std is folded into the conv:
+// conv = (sum_k w_k inv_std_c b_k) / 255 + bias - sum_k w_k inv_std_c mean_c
+// over the taps inside the image. Taps outside the image are zero in the
+// normalised tensor, so their share of the constant comes back through corr.
 struct StemParams {
-  float w[kStemCo][27];  // [co][ky][kx][ci], BN folded
-  float b[kStemCo];
-  float mean[3], inv_std[3];
+  float w[kStemCo][27];      // w * inv_std[ci], taps [ky][kx][ci], BN folded
+  float b0[kStemCo];         // bias - sum over all 27 taps of w * inv_std * mean
+  float corr[9][kStemCo];    // per tap position (ky, kx): sum_ci w * inv_std * mean
 };
 
 __device__ __forceinline__ float hswish(float v) {
@@ -42,32 +46,38 @@ __device__ __forceinline__ float hswish(float v) {
 
 // The stem as an implicit GEMM on the tensor cores: M = 128 output pixels
 // (a 4 x 32 tile), N = 32 channels, K = the 27 taps (ky, kx, ci) padded to
-// 32. fp16 operands alone would lose too much of the fp32 conv, so every
-// operand is split into fp16 hi + lo parts (x = hi + lo, |lo| <= ulp(hi)/2)
-// and the MMAs add hi*w_hi + lo*w_hi + hi*w_lo in fp32 (the dropped lo*w_lo
-// is below 1e-6 relative): an A row is [hi(32) | lo(32)] fp16 = one 128-byte
-// K-major row, B1 rows are [w_hi | w_hi] (4 MMAs of K = 16 over the full
-// row) and B2 rows [w_lo | 0] (2 MMAs over the hi half).
-// A persistent CTA of 128 threads loops over tiles: stage the normalised
-// 9 x 65 input window (zero outside the image) in shared memory, build the
-// A tile (thread = pixel = TMEM lane), one thread issues the six MMAs into
-// 32 TMEM columns, then every thread reads its pixel's 32 accumulators
-// (tcgen05.ld), adds the bias, applies hardswish and stores 64 bytes.
+// 32, on the raw bytes (exact in fp16) against the normalisation-folded
+// weights. fp16 weights alone would lose too much of the fp32 conv, so each
+// is split into fp16 hi + lo (w = hi + lo to about 2^-22): an A row is the
+// tap bytes twice, [b(32) | b(32)], one 128-byte K-major row, and a B row is
+// [w_hi(32) | w_lo(32)], so four MMAs of K = 16 over the row accumulate
+// sum b (w_hi + w_lo) in fp32. The epilogue scales by 1/255 and adds the
+// folded bias (and, on the image border, the correction of the taps that
+// fall outside).
+// A persistent CTA of 128 threads loops over tiles. The bytes of the 9 x 65
+// input window arrive as one 16-byte chunk per thread, loaded a tile ahead
+// (in flight while the current tile runs) and parked in shared memory; each
+// thread (= pixel = TMEM lane) normalises its 27 taps from there (zero
+// outside the image: the conv pads the normalised tensor) into its A row,
+// one thread issues the six MMAs into 32 TMEM columns, then every thread
+// reads its pixel's 32 accumulators (tcgen05.ld), adds the bias, applies
+// hardswish and stores 64 bytes.
 namespace stc {
 constexpr int TR = 4, TC = 32, TPX = TR * TC;   // output tile = MMA M
 constexpr int WR = 2 * TR + 1, WC = 2 * TC + 1; // input window
-constexpr int WP = WC + 3;                      // window plane row pitch (floats)
+constexpr int WB = 224;                         // window row bytes: 14 chunks of 16
 constexpr int kThreads = 128;
+static_assert(WR * (WB / 16) <= kThreads, "one window chunk per thread");
 constexpr int OFF_A = 0, A_BYTES = TPX * 128;
 constexpr int B_BYTES = kStemCo * 128;
-constexpr int OFF_B1 = OFF_A + A_BYTES, OFF_B2 = OFF_B1 + B_BYTES;
-constexpr int OFF_WIN = OFF_B2 + B_BYTES;
-constexpr int OFF_BIAS = OFF_WIN + 3 * WR * WP * 4;
-constexpr int OFF_BAR = (OFF_BIAS + kStemCo * 4 + 7) / 8 * 8;
+constexpr int OFF_B = OFF_A + A_BYTES;
+constexpr int OFF_WIN = OFF_B + B_BYTES;
+constexpr int OFF_BIAS = OFF_WIN + WR * WB;      // b0 [32] then corr [9][32]
+constexpr int OFF_BAR = (OFF_BIAS + 10 * kStemCo * 4 + 7) / 8 * 8;
 constexpr int OFF_MISC = OFF_BAR + 8;           // TMEM address, abort flag
 constexpr int SMEM_ALLOC = OFF_MISC + 16 + 1024;  // + runtime 1024 alignment
 constexpr int TMEM_COLS = 32;
-static_assert(OFF_B1 % 1024 == 0 && OFF_B2 % 1024 == 0, "UMMA operand alignment");
+static_assert(OFF_B % 1024 == 0, "UMMA operand alignment");
 }  // namespace stc
 
 __device__ int g_stem_err;  // first bounded-wait timeout code, 0 if none
@@ -83,7 +93,7 @@ __device__ __forceinline__ uint32_t pack_h2(__half a, __half b) {
   return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-__global__ void __launch_bounds__(stc::kThreads)
+__global__ void __launch_bounds__(stc::kThreads, 6)
 stem_tc_kernel(const uint8_t *__restrict__ pages, int H, int W, long long page_stride,
                __half *__restrict__ out, const StemParams sp, int tiles_x, int tiles_y,
                int ntiles) {
@@ -91,35 +101,34 @@ stem_tc_kernel(const uint8_t *__restrict__ pages, int H, int W, long long page_s
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *sa = smem + stc::OFF_A, *sb1 = smem + stc::OFF_B1, *sb2 = smem + stc::OFF_B2;
-  float *win = reinterpret_cast<float *>(smem + stc::OFF_WIN);
+  uint8_t *sa = smem + stc::OFF_A, *sb = smem + stc::OFF_B;
+  uint8_t *win = smem + stc::OFF_WIN;
   float *sbias = reinterpret_cast<float *>(smem + stc::OFF_BIAS);
   uint64_t *bar = reinterpret_cast<uint64_t *>(smem + stc::OFF_BAR);
   uint32_t *s_tmem = reinterpret_cast<uint32_t *>(smem + stc::OFF_MISC);
   volatile int *s_abort = reinterpret_cast<volatile int *>(smem + stc::OFF_MISC + 4);
   const int tid = threadIdx.x, warp = tid >> 5;
 
-  // ---- setup: split weights into the two B tiles, bias, barrier, TMEM ----
+  // ---- setup: split weights into the B tile [hi | lo], bias, barrier, TMEM ----
   for (int i = tid; i < kStemCo * 8; i += stc::kThreads) {
     const int co = i >> 3, j = i & 7;
-    uint32_t h1[4], h2[4];
+    uint32_t h[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      __half hi[2], lo[2];
+      __half v[2];
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
         const int k = 8 * (j & 3) + 2 * e + q;
         const float w = k < 27 ? sp.w[co][k] : 0.f;
-        hi[q] = __float2half_rn(w);
-        lo[q] = __float2half_rn(w - __half2float(hi[q]));
+        const __half hi = __float2half_rn(w);
+        v[q] = j < 4 ? hi : __float2half_rn(w - __half2float(hi));
       }
-      h1[e] = pack_h2(hi[0], hi[1]);
-      h2[e] = j < 4 ? pack_h2(lo[0], lo[1]) : 0u;
+      h[e] = pack_h2(v[0], v[1]);
     }
-    *reinterpret_cast<uint4 *>(sb1 + sw128_off(co, j)) = make_uint4(h1[0], h1[1], h1[2], h1[3]);
-    *reinterpret_cast<uint4 *>(sb2 + sw128_off(co, j)) = make_uint4(h2[0], h2[1], h2[2], h2[3]);
+    *reinterpret_cast<uint4 *>(sb + sw128_off(co, j)) = make_uint4(h[0], h[1], h[2], h[3]);
   }
-  if (tid < kStemCo) sbias[tid] = sp.b[tid];
+  for (int i = tid; i < 10 * kStemCo; i += stc::kThreads)
+    sbias[i] = i < kStemCo ? sp.b0[i] : sp.corr[(i - kStemCo) / kStemCo][i % kStemCo];
   if (tid == 0) {
     mbar_init(bar, 1);
     *s_abort = 0;
@@ -140,65 +149,81 @@ stem_tc_kernel(const uint8_t *__restrict__ pages, int H, int W, long long page_s
   const long long row_bytes = 3ll * W;
   const int py = tid / stc::TC, px = tid % stc::TC;  // this thread's pixel in the tile
   constexpr uint32_t kIdesc = idesc_f16(stc::TPX, kStemCo);
+  const bool vec_ok = (row_bytes & 15) == 0 && (reinterpret_cast<uintptr_t>(pages) & 15) == 0 &&
+                      (page_stride & 15) == 0;
+  // this thread's window chunk of tile t: row tid / 14, bytes [a0 + 16 k, +16)
+  const int crow = tid / (stc::WB / 16), ck = tid % (stc::WB / 16);
+  auto load_chunk = [&](int t) {
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (t >= ntiles || crow >= stc::WR) return v;
+    const int n = t / tiles_per_img, r = t % tiles_per_img;
+    const int y = 2 * (r / tiles_x) * stc::TR - 1 + crow;
+    const long long b0 = 3ll * (2 * (r % tiles_x) * stc::TC - 1);
+    const long long a0 = b0 >= 0 ? (b0 & ~15ll) : -16;
+    const long long b = a0 + 16 * ck;
+    if (y < 0 || y >= H || b < 0 || b >= row_bytes) return v;
+    const uint8_t *q = pages + (long long)n * page_stride + (long long)y * row_bytes + b;
+    if (vec_ok) return __ldg(reinterpret_cast<const uint4 *>(q));
+    uint8_t tmp[16];
+    for (int j = 0; j < 16; ++j) tmp[j] = b + j < row_bytes ? __ldg(q + j) : 0;
+    memcpy(&v, tmp, 16);
+    return v;
+  };
+  uint4 chunk = load_chunk(blockIdx.x);
   uint32_t it = 0;
   for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
     const int n = t / tiles_per_img, r = t % tiles_per_img;
     const int oy0 = (r / tiles_x) * stc::TR, ox0 = (r % tiles_x) * stc::TC;
     const int iy0 = 2 * oy0 - 1, ix0 = 2 * ox0 - 1;
-    const uint8_t *pg = pages + (long long)n * page_stride;
-    for (int i = tid; i < stc::WR * stc::WC; i += stc::kThreads) {
-      const int row = i / stc::WC, col = i - row * stc::WC;
-      const int y = iy0 + row, x = ix0 + col;
-      float v0 = 0.f, v1 = 0.f, v2 = 0.f;
-      if (y >= 0 && y < H && x >= 0 && x < W) {
-        const uint8_t *q = pg + (long long)y * row_bytes + 3ll * x;
-        v0 = ((float)__ldg(q) * (1.0f / 255.0f) - sp.mean[0]) * sp.inv_std[0];
-        v1 = ((float)__ldg(q + 1) * (1.0f / 255.0f) - sp.mean[1]) * sp.inv_std[1];
-        v2 = ((float)__ldg(q + 2) * (1.0f / 255.0f) - sp.mean[2]) * sp.inv_std[2];
-      }
-      win[(0 * stc::WR + row) * stc::WP + col] = v0;
-      win[(1 * stc::WR + row) * stc::WP + col] = v1;
-      win[(2 * stc::WR + row) * stc::WP + col] = v2;
-    }
+    const long long b0 = 3ll * ix0;
+    const long long a0 = b0 >= 0 ? (b0 & ~15ll) : -16;
+    if (crow < stc::WR) *reinterpret_cast<uint4 *>(win + crow * stc::WB + 16 * ck) = chunk;
     __syncthreads();
-    {  // A row of this pixel: taps in (ky, kx, ci) order, hi then lo
-      __half hi[32], lo[32];
+    chunk = load_chunk(t + gridDim.x);  // next tile's window, in flight meanwhile
+    {  // A row of this pixel: tap bytes in (ky, kx, ci) order, twice
+      uint32_t pk[16];
+      __half prev = __ushort2half_rn(0);
 #pragma unroll
-      for (int ky = 0; ky < 3; ++ky)
+      for (int ky = 0; ky < 3; ++ky) {
+        const int y = iy0 + 2 * py + ky;
+        const uint8_t *wr = win + (2 * py + ky) * stc::WB;
 #pragma unroll
-        for (int kx = 0; kx < 3; ++kx)
+        for (int kx = 0; kx < 3; ++kx) {
+          const int x = ix0 + 2 * px + kx;
+          const bool in = y >= 0 && y < H && x >= 0 && x < W;
+          const int off = (int)(3ll * x - a0);
 #pragma unroll
           for (int ci = 0; ci < 3; ++ci) {
             const int k = (ky * 3 + kx) * 3 + ci;
-            const float v = win[(ci * stc::WR + 2 * py + ky) * stc::WP + 2 * px + kx];
-            hi[k] = __float2half_rn(v);
-            lo[k] = __float2half_rn(v - __half2float(hi[k]));
+            const __half v = __ushort2half_rn(in ? wr[off + ci] : 0);
+            if (k & 1) pk[k >> 1] = pack_h2(prev, v);
+            else prev = v;
           }
+        }
+      }
+      pk[13] = pack_h2(prev, __ushort2half_rn(0));  // tap 26, then zero padding
+      pk[14] = pk[15] = 0u;
 #pragma unroll
-      for (int k = 27; k < 32; ++k) hi[k] = lo[k] = __float2half_rn(0.f);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const __half *src = j < 4 ? hi + 8 * j : lo + 8 * (j - 4);
-        *reinterpret_cast<uint4 *>(sa + sw128_off(tid, j)) =
-            make_uint4(pack_h2(src[0], src[1]), pack_h2(src[2], src[3]), pack_h2(src[4], src[5]),
-                       pack_h2(src[6], src[7]));
+      for (int j = 0; j < 4; ++j) {
+        const uint4 c = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+        *reinterpret_cast<uint4 *>(sa + sw128_off(tid, j)) = c;
+        *reinterpret_cast<uint4 *>(sa + sw128_off(tid, j + 4)) = c;
       }
     }
     fence_proxy_async_smem();
     __syncthreads();
-    if (tid == 0) {
+    bool waited = true;
+    if (tid == 0) {  // the other threads wait at the barrier below, not spinning
       tc_fence_after();
-      const uint32_t a = smem_u32(sa), b1 = smem_u32(sb1), b2 = smem_u32(sb2);
+      const uint32_t a = smem_u32(sa), b = smem_u32(sb);
 #pragma unroll
       for (int k = 0; k < 4; ++k)
-        mma_f16(tmem, sw128_kmajor_desc(a + 32 * k), sw128_kmajor_desc(b1 + 32 * k), kIdesc,
+        mma_f16(tmem, sw128_kmajor_desc(a + 32 * k), sw128_kmajor_desc(b + 32 * k), kIdesc,
                 k > 0 ? 1u : 0u);
-#pragma unroll
-      for (int k = 0; k < 2; ++k)
-        mma_f16(tmem, sw128_kmajor_desc(a + 32 * k), sw128_kmajor_desc(b2 + 32 * k), kIdesc, 1u);
       mma_commit(bar);
+      waited = mbar_wait_bounded(bar, it & 1, s_abort, &g_stem_err, 41);
     }
-    const bool ok = __syncthreads_and(mbar_wait_bounded(bar, it & 1, s_abort, &g_stem_err, 41));
+    const bool ok = __syncthreads_and(waited);
     if (!ok) break;
     tc_fence_after();
     uint32_t v[32];
@@ -206,12 +231,23 @@ stem_tc_kernel(const uint8_t *__restrict__ pages, int H, int W, long long page_s
     tmem_ld_wait(v);
     const int oy = oy0 + py, ox = ox0 + px;
     if (oy < Ho && ox < Wo) {
+      float f[kStemCo];
+#pragma unroll
+      for (int c = 0; c < kStemCo; ++c) f[c] = fmaf(__uint_as_float(v[c]), 1.0f / 255.0f, sbias[c]);
+      const int y0 = 2 * oy - 1, x0 = 2 * ox - 1;
+      if (y0 < 0 || x0 < 0 || y0 + 2 >= H || x0 + 2 >= W) {  // taps outside the image
+        for (int pos = 0; pos < 9; ++pos) {
+          const int yy = y0 + pos / 3, xx = x0 + pos % 3;
+          if (yy >= 0 && yy < H && xx >= 0 && xx < W) continue;
+#pragma unroll
+          for (int c = 0; c < kStemCo; ++c) f[c] += sbias[kStemCo * (1 + pos) + c];
+        }
+      }
       uint4 packed[kStemCo / 8];
       uint32_t *pw = reinterpret_cast<uint32_t *>(packed);
 #pragma unroll
       for (int c = 0; c < kStemCo; c += 2) {
-        const __half2 h = __floats2half2_rn(hswish(__uint_as_float(v[c]) + sbias[c]),
-                                            hswish(__uint_as_float(v[c + 1]) + sbias[c + 1]));
+        const __half2 h = __floats2half2_rn(hswish(f[c]), hswish(f[c + 1]));
         pw[c / 2] = *reinterpret_cast<const uint32_t *>(&h);
       }
       uint4 *dst = reinterpret_cast<uint4 *>(out + (((long long)n * Ho + oy) * Wo + ox) * kStemCo);
@@ -425,18 +461,27 @@ TOCR_API int tocr_stem_pack(const float *w /* [32][3][3][3] co,ci,ky,kx */, cons
                             size_t out_bytes) {
   TOCR_REQUIRE(w && b && out && out_bytes >= sizeof(StemParams), "tocr_stem_pack: bad arguments");
   StemParams p{};
-  const float dm[3] = {0.485f, 0.456f, 0.406f};
-  const float ds[3] = {1.0f / 0.229f, 1.0f / 0.224f, 1.0f / 0.225f};
-  for (int co = 0; co < kStemCo; ++co) {
-    for (int ci = 0; ci < 3; ++ci)
-      for (int ky = 0; ky < 3; ++ky)
-        for (int kx = 0; kx < 3; ++kx)
-          p.w[co][(ky * 3 + kx) * 3 + ci] = w[((co * 3 + ci) * 3 + ky) * 3 + kx];
-    p.b[co] = b[co];
-  }
+  const double dm[3] = {0.485, 0.456, 0.406};
+  const double ds[3] = {1.0 / 0.229, 1.0 / 0.224, 1.0 / 0.225};
+  double mean[3], inv[3];
   for (int c = 0; c < 3; ++c) {
-    p.mean[c] = mean3 ? mean3[c] : dm[c];
-    p.inv_std[c] = inv_std3 ? inv_std3[c] : ds[c];
+    mean[c] = mean3 ? (double)mean3[c] : (double)(float)dm[c];
+    inv[c] = inv_std3 ? (double)inv_std3[c] : (double)(float)ds[c];
+  }
+  for (int co = 0; co < kStemCo; ++co) {
+    double total = 0.;
+    for (int ky = 0; ky < 3; ++ky)
+      for (int kx = 0; kx < 3; ++kx) {
+        double cpos = 0.;
+        for (int ci = 0; ci < 3; ++ci) {
+          const double wv = w[((co * 3 + ci) * 3 + ky) * 3 + kx];
+          p.w[co][(ky * 3 + kx) * 3 + ci] = (float)(wv * inv[ci]);
+          cpos += wv * inv[ci] * mean[ci];
+        }
+        p.corr[ky * 3 + kx][co] = (float)cpos;
+        total += cpos;
+      }
+    p.b0[co] = (float)((double)b[co] - total);
   }
   memcpy(out, &p, sizeof(p));
   return TOCR_OK;
