@@ -52,7 +52,15 @@ struct Cfg {
   static constexpr int NCH = C / CCH;
   static constexpr int KATOMS = (C + 127) / 128;       // 128-byte K atoms per row
   static constexpr int KSTEPS = C / 32;                // MMA K = 32 per instruction
-  static constexpr int HH = (TH - 1) * S + 3, HW = (TW - 1) * S + 3;
+  // Stride-1 blocks with 32-channel chunks (64-byte halo pixels): a DW warp
+  // takes 8 segments down 8 tile rows (ROWMAP) and the halo box is one
+  // column wider than needed, so its rows are 19 x 64 bytes apart and
+  // consecutive rows fall in opposite 64-byte bank halves: a warp's 16-byte
+  // halo loads (8 rows x 4 channel parts) then take the minimum 4 shared-
+  // memory wavefronts instead of 8 (8 segments along one row all start
+  // 128 bytes apart, on the same banks).
+  static constexpr bool ROWMAP = S_ == 1 && CCH_ == 32;
+  static constexpr int HH = (TH - 1) * S + 3, HW = (TW - 1) * S + 3 + (ROWMAP ? 1 : 0);
   static constexpr int HALO = HH * HW * CCH * 2;
   // stage stride of the halo ring: TMA destinations must be 128-byte aligned
   static constexpr int HALO_ST = (HALO + 127) / 128 * 128;
@@ -280,7 +288,8 @@ dwpw_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
     // ===================== depthwise + quantisation =====================
     const int dt = tid - kDwWarp0 * 32;            // 0..255
     const int seg = dt / K::PARTS, part = dt % K::PARTS;
-    const int seg_row = seg / (TW / K::SEG), seg_col = (seg % (TW / K::SEG)) * K::SEG;
+    const int seg_row = K::ROWMAP ? seg % TH : seg / (TW / K::SEG);
+    const int seg_col = (K::ROWMAP ? seg / TH : seg % (TW / K::SEG)) * K::SEG;
     uint32_t g = 0, i = 0;
     for (int t = blockIdx.x; t < prm.ntiles; t += gridDim.x, ++i) {
       float amax[K::SEG];
