@@ -83,9 +83,9 @@ constexpr int kBigQPts = (int)((kBigSmem - kBigTabBytes) / sizeof(P2));
 constexpr unsigned long long kPoolBytesPerPoint = 64;
 static_assert(kBigSmem <= 227 * 1024, "shared memory of the CTA geometry path");
 
-// Counters of the CTA geometry path: [0] contour list length, [1] ring list
-// length, [2..3] pool bytes used (u64).
-constexpr int kCounters = 4;
+// Counters of the geometry stages: [0] contour list length, [1] ring list
+// length, [2..3] pool bytes used (u64), [4] scored-slot list length.
+constexpr int kCounters = 6;
 
 // ---------------------------------------------------------------- union-find --
 __device__ __forceinline__ int find_g(const int *lab, int v) {
@@ -647,10 +647,13 @@ __global__ void __launch_bounds__(128)
 geom_box1_kernel(const int *__restrict__ n_contours, const int *__restrict__ npts,
                  const long long *__restrict__ pt_off, const P2 *__restrict__ pts,
                  int *__restrict__ stage1, int4 *__restrict__ aabb, int *__restrict__ list,
-                 int *__restrict__ counters, DbParams P) {
+                 int *__restrict__ counters, int *__restrict__ score_done,
+                 int *__restrict__ score_list, int *__restrict__ stage2, DbParams P) {
   const long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= (long long)P.n_maps * kMaxCand) return;
   stage1[c] = 0;
+  stage2[c] = 0;
+  score_done[c] = 0;
   const int m = (int)(c / kMaxCand), rank = (int)(c % kMaxCand);
   const int n = npts[c];
   if (rank >= n_contours[m] || n <= 2 || pt_off[c] + n > P.point_cap) return;
@@ -669,6 +672,7 @@ geom_box1_kernel(const int *__restrict__ n_contours, const int *__restrict__ npt
   const RRect r = rect_local(p, n);
   if ((r.w < r.h ? r.w : r.h) < P.min_box_side) return;
   stage1[c] = 1;
+  score_list[atomicAdd(counters + 4, 1)] = (int)c;
 }
 
 // ---- CTA geometry: one point set per CTA, all in shared memory ----------
@@ -796,8 +800,8 @@ __global__ void __launch_bounds__(kBigThreads)
 geom_big_kernel(const int *__restrict__ list, const int *__restrict__ counters,
                 const int *__restrict__ npts, const long long *__restrict__ pt_off,
                 const P2 *__restrict__ pts, const int4 *__restrict__ aabb,
-                int *__restrict__ stage1, char *__restrict__ pool, int *__restrict__ pool_counters,
-                int *__restrict__ status, DbParams P) {
+                int *__restrict__ stage1, int *__restrict__ score_list, char *__restrict__ pool,
+                int *__restrict__ pool_counters, int *__restrict__ status, DbParams P) {
   extern __shared__ __align__(16) uint8_t smem[];
   const BigSmem S = big_smem(smem);
   const int count = counters[0];
@@ -821,7 +825,10 @@ geom_big_kernel(const int *__restrict__ list, const int *__restrict__ counters,
     }
     if (threadIdx.x == 0) {
       if (!ok) ok = rect_global(p, n, pool, pool_counters, P.pool_bytes, status, &r);
-      if (ok && (r.w < r.h ? r.w : r.h) >= P.min_box_side) stage1[c] = 1;
+      if (ok && (r.w < r.h ? r.w : r.h) >= P.min_box_side) {
+        stage1[c] = 1;
+        score_list[atomicAdd(pool_counters + 4, 1)] = c;
+      }
     }
     __syncthreads();
   }
@@ -841,28 +848,34 @@ __device__ __forceinline__ void fill_bits(unsigned *row, int a, int b) {
   }
 }
 
-// 6b. one CTA per contour slot: box_score_fast, the mean of pred over the
-// filled contour (edge pixels plus odd-parity interior) inside its AABB,
-// accumulated in double; then the unclip distance area * ratio / perimeter
-// (det_postprocess.cpp:59-66) and the capacity of the offset path.
+// 6b. box_score_fast: the mean of pred over the filled contour (edge pixels
+// plus odd-parity interior) inside its AABB, accumulated in double; then the
+// unclip distance area * ratio / perimeter (det_postprocess.cpp:59-66).
+// grid (x, kScoreGroups): the x CTAs stride over the list of slots that
+// passed the first filters (score_list) and CTA group g takes the slot's
+// 32-row bands g, g + G, ... so
+// that a large contour is summed by G CTAs at once. Each group leaves its
+// partial sum (only groups that own a band take part); the last group to
+// finish a slot (counter done[c]) adds the partials in group order
+// (deterministic) and writes the score.
+constexpr int kScoreGroups = 8;
+
 __global__ void __launch_bounds__(kScoreThreads)
-score_kernel(const float *__restrict__ pred, const int *__restrict__ stage1,
-             const int4 *__restrict__ aabb, const int *__restrict__ npts,
+score_kernel(const float *__restrict__ pred, const int *__restrict__ score_list,
+             const int *__restrict__ counters, const int4 *__restrict__ aabb, const int *__restrict__ npts,
              const long long *__restrict__ pt_off, const P2 *__restrict__ pts,
              int *__restrict__ stage2, float *__restrict__ score, double *__restrict__ dist,
-             DbParams P) {
+             double *__restrict__ part_sum, long long *__restrict__ part_cnt,
+             int *__restrict__ done, DbParams P) {
   __shared__ unsigned s_edge[kBandRows][kMaxWords];
   __shared__ unsigned s_tog[kBandRows][kMaxWords];
   __shared__ double s_sum[kScoreThreads / 32];
   __shared__ long long s_cnt[kScoreThreads / 32];
-  // grid-stride over the contour slots: most slots are empty or filtered, so
-  // a CTA per slot would spend its time being scheduled
-  const long long n_slots = (long long)P.n_maps * kMaxCand;
-  for (long long c = blockIdx.x; c < n_slots; c += gridDim.x) {
-  if (!stage1[c]) {
-    if (threadIdx.x == 0) stage2[c] = 0;
-    continue;
-  }
+  __shared__ int s_last;
+  const int g = blockIdx.y;
+  const int count = counters[4];
+  for (int li = blockIdx.x; li < count; li += gridDim.x) {
+  const long long c = score_list[li];
   const int m = (int)(c / kMaxCand);
   const int H = P.H, W = P.W;
   const int n = npts[c];
@@ -872,10 +885,14 @@ score_kernel(const float *__restrict__ pred, const int *__restrict__ stage1,
   double sum = 0.;
   long long cnt = 0;
   const bool nonempty = bx1 > bx0 && by1 > by0;
+  // groups that own a band take part (at least group 0)
+  const int bands = nonempty ? (by1 - by0) / kBandRows + 1 : 1;
+  const int groups = bands < kScoreGroups ? bands : kScoreGroups;
+  if (g >= groups) continue;
   if (nonempty) {
     const int width = bx1 - bx0 + 1, words = (width + 31) >> 5;
     const float *pm = pred + (size_t)m * H * W;
-    for (int band = by0; band <= by1; band += kBandRows) {
+    for (int band = by0 + g * kBandRows; band <= by1; band += kScoreGroups * kBandRows) {
       const int rows = min(kBandRows, by1 - band + 1);
       for (int i = threadIdx.x; i < kBandRows * words; i += kScoreThreads) {
         s_edge[i / words][i % words] = 0u;
@@ -910,18 +927,29 @@ score_kernel(const float *__restrict__ pred, const int *__restrict__ stage1,
         if (tail) s_edge[r][words - 1] &= (1u << tail) - 1u;
       }
       __syncthreads();
-      // a warp per (row, 32-pixel word) of the mask: coalesced row reads,
-      // empty words skipped
+      // a warp per (row, 32-pixel word) of the mask, four words in flight
+      // per warp: coalesced row reads, empty words skipped
       {
         const int lane = threadIdx.x & 31;
-        for (int k = threadIdx.x >> 5; k < rows * words; k += kScoreThreads / 32) {
-          const int r = k / words, wd = k - r * words;
-          const unsigned msk = s_edge[r][wd];
-          if (msk == 0u) continue;
-          if ((msk >> lane) & 1u) {
-            sum += (double)pm[(size_t)(band + r) * W + bx0 + (wd << 5) + lane];
-            ++cnt;
+        constexpr int kWarps = kScoreThreads / 32, kUnroll = 4;
+        const int total = rows * words;
+        for (int k0 = threadIdx.x >> 5; k0 < total; k0 += kWarps * kUnroll) {
+          float v[kUnroll];
+          bool on[kUnroll];
+#pragma unroll
+          for (int u = 0; u < kUnroll; ++u) {
+            const int k = k0 + u * kWarps;
+            on[u] = false;
+            v[u] = 0.f;
+            if (k < total) {
+              const int r = k / words, wd = k - r * words;
+              on[u] = (s_edge[r][wd] >> lane) & 1u;
+              if (on[u]) v[u] = pm[(size_t)(band + r) * W + bx0 + (wd << 5) + lane];
+            }
           }
+#pragma unroll
+          for (int u = 0; u < kUnroll; ++u)
+            if (on[u]) { sum += (double)v[u]; ++cnt; }
         }
       }
       __syncthreads();
@@ -940,6 +968,20 @@ score_kernel(const float *__restrict__ pred, const int *__restrict__ stage1,
     double tsum = 0.;
     long long tcnt = 0;
     for (int w = 0; w < kScoreThreads / 32; ++w) { tsum += s_sum[w]; tcnt += s_cnt[w]; }
+    part_sum[c * kScoreGroups + g] = tsum;
+    part_cnt[c * kScoreGroups + g] = tcnt;
+    __threadfence();
+    s_last = atomicAdd(done + c, 1) == groups - 1;
+  }
+  __syncthreads();
+  if (s_last && threadIdx.x == 0) {
+    __threadfence();
+    double tsum = 0.;
+    long long tcnt = 0;
+    for (int k = 0; k < groups; ++k) {
+      tsum += __ldcg(part_sum + c * kScoreGroups + k);
+      tcnt += __ldcg(part_cnt + c * kScoreGroups + k);
+    }
     const float sc = (nonempty && tcnt > 0) ? (float)(tsum / (double)tcnt) : 0.f;
     score[c] = sc;
     stage2[c] = 0;
@@ -1250,8 +1292,9 @@ namespace {
 
 struct DbLayout {
   size_t bitmap, tile_bg, bits, slab, lab, scan_tot, row_count, row_off, n_contours, n_total,
-      starts, npts, pt_off, pts, stage1, aabb, stage2, score, dist, keep2, boxes, list1, list2,
-      counters, pool, ovf_first, ovf_next, ovf_pts, ovf_count, total;
+      starts, npts, pt_off, pts, stage1, aabb, stage2, score, dist, keep2, boxes, list1, list2, list3,
+      counters, pool, ovf_first, ovf_next, ovf_pts, ovf_count, part_sum, part_cnt, score_done,
+      total;
   int ovf_chunks;
   unsigned long long pool_bytes;
 };
@@ -1287,6 +1330,7 @@ DbLayout db_layout(int n_maps, int h, int w, long long point_cap, long long offs
   L.boxes = take(C * 8 * 4);
   L.list1 = take(C * 4);
   L.list2 = take(C * 4);
+  L.list3 = take(C * 4);
   L.counters = take(kCounters * 4);
   L.pool_bytes = (unsigned long long)offset_cap * kPoolBytesPerPoint;
   L.pool = take(L.pool_bytes);
@@ -1296,6 +1340,9 @@ DbLayout db_layout(int n_maps, int h, int w, long long point_cap, long long offs
   L.ovf_next = take((size_t)L.ovf_chunks * 4);
   L.ovf_pts = take((size_t)L.ovf_chunks * kChunk * sizeof(P2));
   L.ovf_count = take(4);
+  L.part_sum = take(C * kScoreGroups * 8);
+  L.part_cnt = take(C * kScoreGroups * 8);
+  L.score_done = take(C * 4);
   L.total = o;
   return L;
 }
@@ -1362,11 +1409,15 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
   float *score = (float *)at(L.score);
   int *stage1 = (int *)at(L.stage1), *stage2 = (int *)at(L.stage2), *keep2 = (int *)at(L.keep2),
       *boxes = (int *)at(L.boxes), *list1 = (int *)at(L.list1), *list2 = (int *)at(L.list2),
+      *list3 = (int *)at(L.list3),
       *counters = (int *)at(L.counters);
   char *pool = at(L.pool);
   int *ovf_first = (int *)at(L.ovf_first), *ovf_next = (int *)at(L.ovf_next),
       *ovf_count = (int *)at(L.ovf_count);
   P2 *ovf_pts = (P2 *)at(L.ovf_pts);
+  double *part_sum = (double *)at(L.part_sum);
+  long long *part_cnt = (long long *)at(L.part_cnt);
+  int *score_done = (int *)at(L.score_done);
   int4 *aabb = (int4 *)at(L.aabb);
   double *dist = (double *)at(L.dist);
 
@@ -1399,12 +1450,13 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
   gather_kernel<<<(unsigned)((C * 32 + 127) / 128), 128, 0, st>>>(
       bits, starts, npts, pt_off, slab, ovf_first, ovf_next, ovf_pts, pts, point_cap, n_maps, h, w);
   geom_box1_kernel<<<cgrid, 128, 0, st>>>(n_contours, npts, pt_off, pts, stage1, aabb, list1,
-                                          counters, P);
+                                          counters, score_done, list3, stage2, P);
   const unsigned bgrid = (unsigned)(C < sm_count() ? C : sm_count());
   geom_big_kernel<<<bgrid, kBigThreads, kBigSmem, st>>>(list1, counters, npts, pt_off, pts, aabb,
-                                                        stage1, pool, counters, d_status, P);
-  score_kernel<<<(unsigned)(C < 148 * 8 ? C : 148 * 8), kScoreThreads, 0, st>>>(
-      d_pred, stage1, aabb, npts, pt_off, pts, stage2, score, dist, P);
+                                                        stage1, list3, pool, counters, d_status, P);
+  score_kernel<<<dim3((unsigned)(C < 148 * 8 ? C : 148 * 8), kScoreGroups), kScoreThreads, 0, st>>>(
+      d_pred, list3, counters, aabb, npts, pt_off, pts, stage2, score, dist, part_sum, part_cnt,
+      score_done, P);
   unclip_kernel<<<cgrid, 128, 0, st>>>(stage2, npts, pt_off, pts, dist, d_geometry, keep2, boxes,
                                        list2, counters, P);
   unclip_big_kernel<<<bgrid, kBigThreads, kBigSmem, st>>>(list2, counters, npts, pt_off, pts, aabb,
