@@ -501,6 +501,10 @@ class E2eWorkload:
     dtype = "i8 (DW+PW blocks) / f16 activations / f32 DB map"
     scaling = "strong"
     TOTAL, MB = 4096, 32
+    # pipelines (one stream each) that overlap consecutive micro-batches:
+    # measured 7507 / 7646 / 7728 / 7752 / 7762 pages/s for 2 / 3 / 4 / 6 / 8;
+    # each holds about 13 GB (mostly the stand-in logits of 4096 crop slots)
+    NP = 6
     # DRAM bytes of the dominant launch (the CTC decode of pages 0..31's crops),
     # from the ncu capture summarised in profiles/e2e_4096pages_960x960.md
     traffic_per_launch = 5_026_007_296 + 3_558_912
@@ -520,12 +524,12 @@ class E2eWorkload:
         self.n_pages = max(self.MB, (per + self.MB - 1) // self.MB * self.MB)
         self.units_per_step = self.n_pages
         self.n_mb = self.n_pages // self.MB
-        # two pipelines on two streams: consecutive micro-batches overlap, so the
+        # NP pipelines on NP streams: consecutive micro-batches overlap, so the
         # latency-bound DB and crop stages of one run beside the streaming
         # stages of the other
-        self.pipes = [pl.PagePipeline(dev, self.MB), pl.PagePipeline(dev, self.MB)]
+        self.pipes = [pl.PagePipeline(dev, self.MB) for _ in range(self.NP)]
         self.pipe = self.pipes[0]
-        self.streams = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
+        self.streams = [torch.cuda.Stream(dev) for _ in range(self.NP)]
         self.pages = torch.empty(self.n_pages, 960, 960, 3, dtype=torch.uint8, device=dev)
         from turboocr_b200._lib import synth
         for i in range(0, self.n_pages, 256):
@@ -553,7 +557,7 @@ class E2eWorkload:
     def step(self):
         self._fork()
         for i in range(self.n_mb):
-            k = i & 1
+            k = i % self.NP
             with torch.cuda.stream(self.streams[k]):
                 self.pipes[k].run(self.pages[i * self.MB:(i + 1) * self.MB])
         self._join()
@@ -602,7 +606,7 @@ class E2eWorkload:
         return b
 
     # end-to-end: pinned host pages -> H2D per micro-batch -> path -> D2H of
-    # boxes, scores, counts, tokens, line scores; each of the two streams copies
+    # boxes, scores, counts, tokens, line scores; each stream copies
     # its own micro-batch in and its results out, so copies overlap the other
     # stream's compute
     def setup_e2e(self):
@@ -610,7 +614,7 @@ class E2eWorkload:
         self.h_pages = torch.empty(self.n_host, 960, 960, 3, dtype=torch.uint8, pin_memory=True)
         self.h_pages.copy_(self.pages[:self.n_host])
         self.stage = [torch.empty(self.MB, 960, 960, 3, dtype=torch.uint8, device=self.dev)
-                      for _ in range(2)]
+                      for _ in range(self.NP)]
         self.h_out = []
         for p in self.pipes:
             self.h_out.append([torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
@@ -623,7 +627,7 @@ class E2eWorkload:
     def e2e_step(self):
         self._fork()
         for i in range(self.n_mb):
-            k = i & 1
+            k = i % self.NP
             p = self.pipes[k]
             with torch.cuda.stream(self.streams[k]):
                 j = (i * self.MB) % self.n_host
