@@ -8,19 +8,22 @@
 // same weight products, same accumulation order, same normalisation), so the
 // fp32 value is the reference's and the fp16 output is its round-to-nearest.
 //
-// B200 design: the output is the HBM stream (2 bytes x 3 planes per pixel),
-// so each thread owns 8 consecutive canvas pixels of a row and writes them as
-// one 16-byte vector per plane; a warp therefore stores 512 contiguous bytes
-// per plane. The x-taps of a thread's 8 columns are computed once and reused
-// for every row of the CTA's band (8 rows), which takes the float->int
-// conversions off the per-pixel path. Source bytes become floats with the
-// exact 2^23 magic-number trick instead of the quarter-rate I2F conversion.
+// B200 design: each thread owns 2 neighbouring canvas columns, so the lanes
+// of a warp cover 64 consecutive columns: their bilinear taps fall in one
+// short, contiguous span of each source row (a few L1 wavefronts per byte
+// load, not one cache line per lane), and each plane is written as one
+// 4-byte pair per lane (128 contiguous bytes per warp for fp16). The x-taps
+// of a thread's 2 columns are computed once and reused for every row of the
+// CTA's band (8 rows), which takes the float->int conversions off the
+// per-pixel path. Source bytes become floats with the exact 2^23
+// magic-number trick instead of the quarter-rate I2F conversion.
 #include "tocr_common.cuh"
 
 namespace tocr {
 namespace {
 
-constexpr int kPrepThreads = 128;  // groups of 8 columns per CTA
+constexpr int kPrepThreads = 160;  // pairs of columns per CTA (320 columns)
+constexpr int kPrepCols = 2;       // columns per thread
 constexpr int kPrepRows = 8;       // canvas rows per CTA
 
 __device__ __forceinline__ float u8f(uint32_t b) {
@@ -29,29 +32,19 @@ __device__ __forceinline__ float u8f(uint32_t b) {
 }
 
 template <typename OutT>
-struct Store8;
-
+struct Store2;
 template <>
-struct Store8<__half> {
-  static __device__ __forceinline__ void put(__half *p, const float v[8]) {
-    uint4 u;
-    __half2 h;
-    h = __floats2half2_rn(v[0], v[1]); u.x = *reinterpret_cast<uint32_t *>(&h);
-    h = __floats2half2_rn(v[2], v[3]); u.y = *reinterpret_cast<uint32_t *>(&h);
-    h = __floats2half2_rn(v[4], v[5]); u.z = *reinterpret_cast<uint32_t *>(&h);
-    h = __floats2half2_rn(v[6], v[7]); u.w = *reinterpret_cast<uint32_t *>(&h);
-    *reinterpret_cast<uint4 *>(p) = u;
+struct Store2<__half> {
+  static __device__ __forceinline__ void put(__half *p, const float v[2]) {
+    *reinterpret_cast<__half2 *>(p) = __floats2half2_rn(v[0], v[1]);
   }
 };
-
 template <>
-struct Store8<float> {
-  static __device__ __forceinline__ void put(float *p, const float v[8]) {
-    reinterpret_cast<float4 *>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
-    reinterpret_cast<float4 *>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+struct Store2<float> {
+  static __device__ __forceinline__ void put(float *p, const float v[2]) {
+    *reinterpret_cast<float2 *>(p) = make_float2(v[0], v[1]);
   }
 };
-
 struct Norm {
   float mean[3];
   float inv_std[3];
@@ -66,7 +59,7 @@ preprocess_batch_kernel(const void *const *__restrict__ src_ptrs,
                         Norm nm) {
   const int b = blockIdx.z;
   const int gx = blockIdx.x * kPrepThreads + threadIdx.x;
-  const int x_base = gx * 8;
+  const int x_base = gx * kPrepCols;
   if (x_base >= W) return;
 
   const unsigned char *src = static_cast<const unsigned char *>(src_ptrs[b]);
@@ -85,11 +78,11 @@ preprocess_batch_kernel(const void *const *__restrict__ src_ptrs,
   const float scale_x = has_content ? (float)src_w / content_w : 0.f;
   const float scale_y = has_content ? (float)src_h / content_h : 0.f;
 
-  // x-taps of this thread's 8 columns (byte offsets of the two taps).
-  int xo0[8], xo1[8];
-  float fxs[8];
+  // x-taps of this thread's columns (byte offsets of the two taps).
+  int xo0[kPrepCols], xo1[kPrepCols];
+  float fxs[kPrepCols];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
+  for (int j = 0; j < kPrepCols; ++j) {
     const int dx = x_base + j;
     float sx = (dx + 0.5f) * scale_x - 0.5f;
     int x0 = (int)floorf(sx);
@@ -107,10 +100,10 @@ preprocess_batch_kernel(const void *const *__restrict__ src_ptrs,
   const int y_end = min(H, y_begin + kPrepRows);
 
   for (int dy = y_begin; dy < y_end; ++dy) {
-    float c0[8], c1[8], c2[8];
+    float c0[kPrepCols], c1[kPrepCols], c2[kPrepCols];
     if (!has_content || dy >= content_h || x_base >= content_w) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) { c0[j] = pad0; c1[j] = pad1; c2[j] = pad2; }
+      for (int j = 0; j < kPrepCols; ++j) { c0[j] = pad0; c1[j] = pad1; c2[j] = pad2; }
     } else {
       float sy = (dy + 0.5f) * scale_y - 0.5f;
       int y0 = (int)floorf(sy);
@@ -121,7 +114,7 @@ preprocess_batch_kernel(const void *const *__restrict__ src_ptrs,
       const unsigned char *row0 = src + (size_t)y0 * src_step;
       const unsigned char *row1 = src + (size_t)y1 * src_step;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < kPrepCols; ++j) {
         if (x_base + j >= content_w) { c0[j] = pad0; c1[j] = pad1; c2[j] = pad2; continue; }
         const float fx = fxs[j];
         const unsigned char *p00 = row0 + xo0[j], *p10 = row0 + xo1[j];
@@ -142,9 +135,9 @@ preprocess_batch_kernel(const void *const *__restrict__ src_ptrs,
       }
     }
     OutT *o = out0 + (size_t)dy * W;
-    Store8<OutT>::put(o, c0);
-    Store8<OutT>::put(o + plane, c1);
-    Store8<OutT>::put(o + 2 * plane, c2);
+    Store2<OutT>::put(o, c0);
+    Store2<OutT>::put(o + plane, c1);
+    Store2<OutT>::put(o + 2 * plane, c2);
   }
 }
 
@@ -175,7 +168,7 @@ int launch_preprocess(const void *const *d_src_ptrs, const int *d_src_steps,
   TOCR_REQUIRE(aligned(dst, 16), "%s: dst must be 16-byte aligned", name);
   if ((size_t)dst_w * dst_h > (size_t)INT_MAX)
     return set_error(TOCR_ERR_OVERFLOW, "%s: canvas %dx%d too large", name, dst_w, dst_h);
-  dim3 grid((dst_w / 8 + kPrepThreads - 1) / kPrepThreads, (dst_h + kPrepRows - 1) / kPrepRows,
+  dim3 grid((dst_w / kPrepCols + kPrepThreads - 1) / kPrepThreads, (dst_h + kPrepRows - 1) / kPrepRows,
             batch_size);
   TOCR_REQUIRE(grid.y <= 65535, "%s: dst_h %d too large", name, dst_h);
   preprocess_batch_kernel<OutT><<<grid, kPrepThreads, 0, as_stream(stream)>>>(
