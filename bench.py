@@ -861,7 +861,7 @@ def main():
                                      "achieved": ach, "peak": peak, "unit": "GB/s",
                                      "frac": ach / peak,
                                      "note": "algorithmic bytes of every stage per page x pages/s per GPU"}
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and world == 1:  # rank 0 at N=1 only
             line["cpu_baseline"] = wl.cpu_baseline(cores)
         print(json.dumps(line), flush=True)
     if world > 1:
