@@ -214,14 +214,21 @@ TOCR_API int tocr_ctc_greedy_f16_dev(const void *d_logits, const int *d_batch, i
 /* Det preprocessing of same-size u8 HWC pages at scale 1 (the reference's
  * resize is then the identity; normalisation as preprocess_kernels.cu:169-177)
  * fused with the backbone stem: 3x3 stride-2 pad-1 conv 3->32 + folded BN +
- * hardswish, fp16 NHWC out [n][(h-1)/2+1][(w-1)/2+1][32]. h_params is a
- * HOST tocr_stem_pack blob, passed to the kernel by value (its constant
- * bank); no counterpart in the reference, whose backbone runs in TensorRT. */
+ * hardswish, fp16 NHWC out [n][(h-1)/2+1][(w-1)/2+1][32], as an implicit
+ * GEMM on tcgen05 (fp32-accurate: split fp16 weights). h_params is a HOST
+ * tocr_stem_pack blob (normalisation folded into the weights), passed to the
+ * kernel by value; no counterpart in the reference, whose backbone runs in
+ * TensorRT. */
 TOCR_API size_t tocr_stem_params_bytes(void);
 TOCR_API int tocr_stem_pack(const float *w, const float *b, const float *mean3,
                             const float *inv_std3, void *out, size_t out_bytes);
 TOCR_API int tocr_stem_f16(const uint8_t *d_pages, int n, int h, int w, long long page_stride,
                            const void *h_params, void *d_out, void *stream);
+/* The stem runs on the tensor cores with bounded waits; a wait that gives up
+ * (no completion within about a second) ends the kernel and records a
+ * non-zero code. This writes that code to *out_code (0: none) and clears it;
+ * it synchronises the current device. */
+TOCR_API int tocr_stem_take_error(int *out_code);
 
 /* Synthetic DB probability map of config 5 (no trained det head exists):
  * sigmoid(gain * (max_{|dx|<=7} ink(x+dx, y) - 0.5)), ink = 1 - mean(RGB)/255,

@@ -71,6 +71,7 @@ SIGNATURES: dict[str, tuple] = {
     "tocr_db_components": (_i, [_vp, _i, _i, _i, _f, _vp, _vp, _vp, _vp]),
     "tocr_stem_params_bytes": (C.c_size_t, []),
     "tocr_stem_pack": (_i, [_vp, _vp, _vp, _vp, _vp, C.c_size_t]),
+    "tocr_stem_take_error": (_i, [_vp]),
     "tocr_stem_f16": (_i, [_vp, _i, _i, _i, _ll, _vp, _vp, _vp]),
     "tocr_ink_map": (_i, [_vp, _i, _i, _i, _ll, _f, _vp, _vp]),
     "tocr_head_sigmoid": (_i, [_vp, _ll, _i, _vp, _f, _vp, _vp]),

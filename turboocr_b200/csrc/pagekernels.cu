@@ -509,6 +509,23 @@ TOCR_API int tocr_stem_f16(const uint8_t *d_pages, int n, int h, int w, long lon
   return check_launch("stem_tc_kernel");
 }
 
+// The stem's bounded waits record the first timeout in a device word: this
+// writes it to *out_code (0: none), clears it, and synchronises the current
+// device.
+TOCR_API int tocr_stem_take_error(int *out_code) {
+  TOCR_ENTRY();
+  TOCR_REQUIRE(out_code, "tocr_stem_take_error: null pointer");
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_stem_err, sizeof(int));
+  if (e == cudaSuccess) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_stem_err, &zero, sizeof(int));
+  }
+  if (e != cudaSuccess) return set_error(TOCR_ERR_CUDA, "tocr_stem_take_error: %s", cudaGetErrorString(e));
+  *out_code = v;
+  return TOCR_OK;
+}
+
 TOCR_API int tocr_ink_map(const uint8_t *d_pages, int n, int h, int w, long long page_stride,
                           float gain, float *d_prob, void *stream) {
   TOCR_ENTRY();

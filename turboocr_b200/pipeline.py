@@ -125,7 +125,12 @@ class PagePipeline:
              _ptr(self.step_idx), _ptr(self.step_prob), st)
 
     def errors(self) -> int:
-        return int(sum(int(b.err.item()) for b in self.blocks))
+        """Non-zero when a tensor-core kernel of the path gave up a bounded
+        wait (DW+PW blocks, stem); synchronises."""
+        import ctypes as C
+        code = C.c_int(0)
+        call("tocr_stem_take_error", C.addressof(code))
+        return int(sum(int(b.err.item()) for b in self.blocks)) + int(code.value)
 
     def results(self):
         """Per page: list of (quad, box score, token ids, line score) (synchronises)."""
