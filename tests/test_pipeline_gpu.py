@@ -72,6 +72,9 @@ def test_stem_matches_torch(cuda, hw):
     torch.cuda.synchronize()
     err = (out.float() - ref).abs() - (2e-3 + 1e-3 * ref.abs())
     assert float(err.max()) <= 0, float((out.float() - ref).abs().max())
+    code = C.c_int(-1)  # no bounded wait of the tensor-core stem gave up
+    call("tocr_stem_take_error", C.addressof(code))
+    assert code.value == 0
 
 
 def test_ink_map(cuda):
