@@ -88,11 +88,20 @@ static_assert(kBigSmem <= 227 * 1024, "shared memory of the CTA geometry path");
 constexpr int kCounters = 6;
 
 // ---------------------------------------------------------------- union-find --
-__device__ __forceinline__ int find_g(const int *lab, int v) {
+// Root of v with path halving: each visited node is re-pointed at its
+// grandparent. The write only lowers a parent to one of its ancestors (an
+// atomicMin, so a smaller link made meanwhile is kept), which leaves every
+// node in its set, keeps parents smaller than their nodes and never touches
+// a root: "root iff its label is itself" still holds, and union_g re-finds
+// roots in its loop.
+__device__ __forceinline__ int find_g(int *lab, int v) {
   while (v != 0) {
     const int p = __ldcg(lab + v - 1);
     if (p == v) break;
-    v = p;
+    if (p == 0) return 0;
+    const int g = __ldcg(lab + p - 1);
+    if (g != p) atomicMin(lab + v - 1, g);
+    v = g;
   }
   return v;
 }
