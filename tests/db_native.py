@@ -51,6 +51,7 @@ def lib():
     L.dbh_hull.argtypes = [vp, i, vp]
     L.dbh_hull_table.argtypes = [vp, i, vp, i, i, i]
     L.dbh_offset_parallel.argtypes = [vp, i, d, vp, i]
+    L.dbh_offset_prepare.argtypes = [vp, i, vp, i]
     L.dbh_min_area_rect.argtypes = [vp, i, vp]
     L.dbh_mini_box.argtypes = [vp, i, vp, vp]
     L.dbh_area.argtypes = [vp, i]
@@ -93,6 +94,14 @@ def hull_table(p, col_cap=1 << 20, hull_cap=1 << 20, interior_filter=False):
     m = lib().dbh_hull_table(a.ctypes.data, len(a), out.ctypes.data, col_cap, hull_cap,
                              1 if interior_filter else 0)
     return m if m < 0 else out[:m]
+
+
+def offset_prepare(p, rule=False):
+    """The prepared offset path (sequential form, or the CTA's rule)."""
+    a = _pts(p)
+    out = np.zeros((len(a) + 1, 2), np.int32)
+    m = lib().dbh_offset_prepare(a.ctypes.data, len(a), out.ctypes.data, 1 if rule else 0)
+    return out[:m].tolist()
 
 
 def offset_parallel(p, delta):

@@ -74,6 +74,14 @@ int dbh_hull_table(const int *pts, int n, int *out, int col_cap, int hull_cap, i
                          hull_cap, filter ? keep.data() : nullptr);
 }
 
+// offset_prepare (rule != 0: in the CTA form, offset_prepare_rule); returns
+// the prepared length, out holds it.
+int dbh_offset_prepare(const int *pts, int n, int *out, int rule) {
+  const P2 *p = reinterpret_cast<const P2 *>(pts);
+  P2 *q = reinterpret_cast<P2 *>(out);
+  return rule ? offset_prepare_rule(p, n, q) : offset_prepare(p, n, q);
+}
+
 // Offset ring through the per-vertex form with k = j - 1 for every vertex
 // (the device's parallel emission): returns the count, or -1 when some vertex
 // before the last keeps k (the device then emits serially).

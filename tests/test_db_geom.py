@@ -221,3 +221,25 @@ def test_parallel_offset_emission():
                     assert par == dn.offset_raw(c, d)
                     same += 1
     assert same > 100 and serial > 10, (same, serial)
+
+
+def test_cta_offset_prepare_rule():
+    """The CTA's path preparation (keep a point iff it differs from its
+    predecessor, orientation from the int64 shoelace sum) equals Clipper's
+    sequential AddPath + FixOrientations restatement, including repeated
+    points, closing repeats and both orientations."""
+    rng = np.random.default_rng(5)
+    sets = []
+    for bm in noise_bitmaps(300, 9):
+        sets += [c for c in do.find_contours(bm)]
+    for _ in range(2000):
+        n = int(rng.integers(1, 40))
+        pts = rng.integers(-3, 4, (n, 2))
+        if rng.random() < 0.3 and n > 1:
+            pts[-1] = pts[0]            # closing repeat
+        sets.append(pts)
+    same = 0
+    for p in sets:
+        assert dn.offset_prepare(p, rule=True) == dn.offset_prepare(p), np.asarray(p).tolist()
+        same += 1
+    assert same > 3000

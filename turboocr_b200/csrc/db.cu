@@ -1095,7 +1095,7 @@ __device__ int cta_offset_prepare(const P2 *p, int n, P2 *q) {
   const int len = s_hi + 1;
   const int chunk = (len + T - 1) / T;
   const int i0 = min(len, t * chunk), i1 = min(len, i0 + chunk);
-  auto kept = [&](int i) { return i == 0 || p[i].x != p[i - 1].x || p[i].y != p[i - 1].y; };
+  auto kept = [&](int i) { return db::prep_kept(p, i); };
   int cnt = 0;
   for (int i = i0; i < i1; ++i) cnt += kept(i);
   int m;
@@ -1105,10 +1105,7 @@ __device__ int cta_offset_prepare(const P2 *p, int n, P2 *q) {
   if (m < 3) return 0;
   __syncthreads();
   long long a = 0;
-  for (int i = t; i < m; i += T) {
-    const P2 qj = q[i == 0 ? m - 1 : i - 1], qi = q[i];
-    a += (long long)(qj.x + qi.x) * (long long)(qj.y - qi.y);
-  }
+  for (int i = t; i < m; i += T) a += db::shoelace_term(q, m, i);
   for (int o = 16; o; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
   if (lane == 0) atomicAdd(&s_area, (unsigned long long)a);
   __syncthreads();

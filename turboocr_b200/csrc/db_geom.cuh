@@ -876,6 +876,39 @@ TG int offset_prepare(const P2 *p, int n, P2 *q) {
   return m;
 }
 
+// offset_prepare in the form one CTA computes it: the path runs to the
+// last point that differs from p[0]; a point is kept when it differs from
+// its predecessor (the predecessor is always the last point kept); the
+// orientation test sums the integer shoelace terms in int64, which equals
+// the sequential double sum (every term is an integer, partial sums stay
+// far below 2^53). Host tests compare it with offset_prepare.
+TG bool prep_kept(const P2 *p, int i) {
+  return i == 0 || p[i].x != p[i - 1].x || p[i].y != p[i - 1].y;
+}
+TG long long shoelace_term(const P2 *q, int m, int i) {
+  const P2 a = q[i == 0 ? m - 1 : i - 1], b = q[i];
+  return (long long)(a.x + b.x) * (long long)(a.y - b.y);
+}
+TG int offset_prepare_rule(const P2 *p, int n, P2 *q) {
+  if (n <= 0) return 0;
+  int hi = 0;
+  for (int i = 0; i < n; ++i)
+    if (p[i].x != p[0].x || p[i].y != p[0].y) hi = i;
+  int m = 0;
+  for (int i = 0; i <= hi; ++i)
+    if (prep_kept(p, i)) q[m++] = p[i];
+  if (m < 3) return 0;
+  long long a = 0;
+  for (int i = 0; i < m; ++i) a += shoelace_term(q, m, i);
+  if (a > 0)
+    for (int i = 0, j = m - 1; i < j; ++i, --j) {
+      const P2 t = q[i];
+      q[i] = q[j];
+      q[j] = t;
+    }
+  return m;
+}
+
 // Per-call constants of the round joins (ClipperOffset::DoOffset).
 struct OffsetConsts {
   double m_sin, m_cos, steps_per_rad;
