@@ -43,6 +43,11 @@ struct StemParams {
 __device__ __forceinline__ float hswish(float v) {
   return v * fminf(fmaxf(v + 3.f, 0.f), 6.f) * (1.f / 6.f);
 }
+// The same function as v * clamp(v / 6 + 1/2, 0, 1): one saturating FMA and
+// one multiply.
+__device__ __forceinline__ float hswish_sat(float v) {
+  return v * __saturatef(fmaf(v, 1.f / 6.f, 0.5f));
+}
 
 // The stem as an implicit GEMM on the tensor cores: M = 128 output pixels
 // (a 4 x 32 tile), N = 32 channels, K = the 27 taps (ky, kx, ci) padded to
@@ -231,9 +236,10 @@ stem_tc_kernel(const uint8_t *__restrict__ pages, int H, int W, long long page_s
     tmem_ld_wait(v);
     const int oy = oy0 + py, ox = ox0 + px;
     if (oy < Ho && ox < Wo) {
+      // the folded bias straight from the parameter bank (FMA operand)
       float f[kStemCo];
 #pragma unroll
-      for (int c = 0; c < kStemCo; ++c) f[c] = fmaf(__uint_as_float(v[c]), 1.0f / 255.0f, sbias[c]);
+      for (int c = 0; c < kStemCo; ++c) f[c] = fmaf(__uint_as_float(v[c]), 1.0f / 255.0f, sp.b0[c]);
       const int y0 = 2 * oy - 1, x0 = 2 * ox - 1;
       if (y0 < 0 || x0 < 0 || y0 + 2 >= H || x0 + 2 >= W) {  // taps outside the image
         for (int pos = 0; pos < 9; ++pos) {
@@ -247,7 +253,7 @@ stem_tc_kernel(const uint8_t *__restrict__ pages, int H, int W, long long page_s
       uint32_t *pw = reinterpret_cast<uint32_t *>(packed);
 #pragma unroll
       for (int c = 0; c < kStemCo; c += 2) {
-        const __half2 h = __floats2half2_rn(hswish(f[c]), hswish(f[c + 1]));
+        const __half2 h = __floats2half2_rn(hswish_sat(f[c]), hswish_sat(f[c + 1]));
         pw[c / 2] = *reinterpret_cast<const uint32_t *>(&h);
       }
       uint4 *dst = reinterpret_cast<uint4 *>(out + (((long long)n * Ho + oy) * Wo + ox) * kStemCo);
