@@ -70,3 +70,42 @@ def test_fault_injection_surfaces_as_inference_error(tocr):
         assert lib.tocr_threshold_u8(None, None, 4, 4, 1, 0.3, None) == 1
     finally:
         lib.tocr_debug_inject_error(0, 0)
+
+
+def test_geometry_and_page_entries_reject_bad_arguments_without_gpu(tocr):
+    """Argument checks of the DB, stem, crop and warp entries run before any
+    CUDA call."""
+    import ctypes as C
+    lib = tocr.lib()
+    # DB: a map taller than the geometry's coordinate range, too wide for
+    # the box-score masks, a workspace that is too small
+    st = lib.tocr_db_postprocess(C.c_void_p(1), 1, 1 << 19, 8, None, 0.3, 0.6, 1.5, 3.0, 5.0,
+                                 0, 0, C.c_void_p(256), 1 << 30, C.c_void_p(1), C.c_void_p(1),
+                                 C.c_void_p(1), 10, C.c_void_p(1), None)
+    assert st == 1 and "too large" in tocr._lib.last_error()
+    st = lib.tocr_db_postprocess(C.c_void_p(1), 1, 64, 5000, None, 0.3, 0.6, 1.5, 3.0, 5.0,
+                                 0, 0, C.c_void_p(256), 1 << 30, C.c_void_p(1), C.c_void_p(1),
+                                 C.c_void_p(1), 10, C.c_void_p(1), None)
+    assert st == 1 and "width" in tocr._lib.last_error()
+    need = lib.tocr_db_workspace_bytes(2, 96, 128, 0, 0)
+    assert need > 0
+    st = lib.tocr_db_postprocess(C.c_void_p(1), 2, 96, 128, None, 0.3, 0.6, 1.5, 3.0, 5.0,
+                                 0, 0, C.c_void_p(256), need - 1, C.c_void_p(1), C.c_void_p(1),
+                                 C.c_void_p(1), 10, C.c_void_p(1), None)
+    assert st == 1 and "workspace" in tocr._lib.last_error()
+    # a bigger scratch pool needs a bigger workspace; zero maps is a no-op
+    assert lib.tocr_db_workspace_bytes(2, 96, 128, 0, 1 << 20) > need
+    assert lib.tocr_db_postprocess(None, 0, 96, 128, None, 0.3, 0.6, 1.5, 3.0, 5.0, 0, 0, None,
+                                   0, None, None, None, 10, None, None) == 0
+    # stem, ink map, ROI warp, crop transforms
+    assert lib.tocr_stem_f16(None, -1, 960, 960, 0, None, None, None) == 1
+    assert lib.tocr_stem_f16(None, 0, 960, 960, 0, None, None, None) == 0
+    assert lib.tocr_stem_take_error(None) == 1
+    assert lib.tocr_ink_map(None, 1, 0, 960, 0, 12.0, None, None) == 1
+    assert lib.tocr_roi_warp_f16(None, 0, 960, 960, 2880, None, None, None, None, -1, 48, 320,
+                                 None, None, 1.0, None, None) == 1
+    assert lib.tocr_roi_warp_f16(None, 0, 960, 960, 2880, None, None, None, None, 0, 48, 320,
+                                 None, None, 1.0, None, None) == 0
+    small = bytearray(8)
+    buf = (C.c_char * len(small)).from_buffer(small)
+    assert lib.tocr_stem_pack(None, None, None, None, buf, 8) == 1
