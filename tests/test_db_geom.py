@@ -243,3 +243,42 @@ def test_cta_offset_prepare_rule():
         assert dn.offset_prepare(p, rule=True) == dn.offset_prepare(p), np.asarray(p).tolist()
         same += 1
     assert same > 3000
+
+
+# ---- property tests of the CTA geometry path (hypothesis) -------------------
+from hypothesis import given, settings, strategies as st  # noqa: E402
+
+_coord = st.integers(min_value=-300000, max_value=300000)
+_small = st.integers(min_value=-6, max_value=6)
+
+
+@settings(max_examples=300, deadline=None)
+@given(st.lists(st.tuples(_coord, _coord), min_size=1, max_size=80)
+       | st.lists(st.tuples(_small, _small), min_size=1, max_size=60))
+def test_property_column_hull(pts):
+    """Column-table hull, with and without the interior filter, equals the
+    sorted monotone chain on arbitrary point sets (wide coordinates or
+    heavy repetition)."""
+    p = np.array(pts, np.int32)
+    ref = dn.hull(p).tolist()
+    assert dn.hull_table(p).tolist() == ref
+    assert dn.hull_table(p, interior_filter=True).tolist() == ref
+
+
+@settings(max_examples=300, deadline=None)
+@given(st.lists(st.tuples(_small, _small), min_size=1, max_size=50))
+def test_property_offset_prepare_rule(pts):
+    p = np.array(pts, np.int32)
+    assert dn.offset_prepare(p, rule=True) == dn.offset_prepare(p)
+
+
+@settings(max_examples=200, deadline=None)
+@given(st.lists(st.tuples(st.integers(0, 60), st.integers(0, 60)), min_size=3, max_size=40),
+       st.floats(min_value=0.5, max_value=60.0))
+def test_property_parallel_offset(pts, d):
+    """Per-vertex emission equals the serial offset whenever no joint before
+    the last keeps Clipper's previous vertex (the device then uses it)."""
+    p = np.array(pts, np.int32)
+    par = dn.offset_parallel(p, d)
+    if par is not None:
+        assert par == dn.offset_raw(p, d)
