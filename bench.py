@@ -110,14 +110,15 @@ class ClockSampler:
 class CtcWorkload:
     """fused CTC greedy decode of fp16 logits."""
     name = "ctc_greedy_512x80x18385_fp16"
-    # DRAM read+write bytes per line of ctc_rows_f16_kernel, from the ncu capture
-    # summarised in profiles/ctc_rows_f16_512x80x18385.md (64-line case, scaled)
+    # DRAM read+write bytes per line of ctc_rows_f16_kernel: one ncu capture
+    # (dram__bytes_read.sum + dram__bytes_write.sum) of a 64-line case, scaled
     traffic_per_unit = (188_710_912 + 3_741_184) / 64
-    traffic_source = "profiles/ctc_rows_f16_512x80x18385.md"
+    traffic_source = "ncu dram__bytes_read/write.sum, 64-line capture scaled per line"
     metric = "lines/sec CTC greedy decode (512x80x18385 fp16 logits)"
     unit = "lines/s"
     dtype = "f16"
     B, T, V = 512, 80, 18385
+    default_units = B
 
     def __init__(self, dev, seed, units=None):
         from turboocr_b200 import kernels as K
@@ -170,36 +171,18 @@ class CtcWorkload:
         self.h_len.copy_(self.out.lengths, non_blocking=True)
         self.h_sc.copy_(self.out.scores, non_blocking=True)
 
-    def cpu_baseline(self, cores, budget_s=15.0):
-        """Reference ctc_decode.cpp (decode_raw + max-softmax beside it) on
-        fp32-converted lines over `cores` std::threads, bounded sample."""
-        from oracle import ctc_oracle as co
-        n = max(cores * 2, 16)
-        sample = self.x[:n].float().cpu().numpy()
-        t0 = time.perf_counter()
-        reps = 0
-        while True:
-            co.ref_decode_batch(sample, self.V, cores, simd=True)
-            reps += 1
-            if time.perf_counter() - t0 > budget_s or reps >= 50:
-                break
-        dt = time.perf_counter() - t0
-        return {"value": n * reps / dt, "unit": self.unit, "cores": cores, "kind": "reference",
-                "sample": f"{n} lines x {reps} reps of the config-2 logits, SIMD_CTC=1, "
-                          "fp16->fp32 conversion untimed"}
-
-
 class PreprocessWorkload:
     """batched resize/letterbox/normalise to fp16 NCHW."""
     name = "preprocess_256img_600-2000_to_960x960_f16"
     # DRAM bytes per image of preprocess_batch_kernel (32-image ncu capture, scaled;
     # part of the output is still in L2 when that short launch ends)
     traffic_per_unit = (160_950_016 + 131_166_976) / 32
-    traffic_source = "profiles/preprocess_256img_960_f16.md"
+    traffic_source = "ncu dram__bytes_read/write.sum, 32-image capture scaled per image"
     metric = "images/sec batched det preprocessing (256 u8 images -> fp16 960x960 NCHW)"
     unit = "images/s"
     dtype = "f32"
     N, H, W = 256, 960, 960
+    default_units = N
     launches_per_step = 1
     l2_note = "inputs 1.3 GB + outputs 1.4 GB > 126 MB L2 (no flush needed)"
 
@@ -256,53 +239,18 @@ class PreprocessWorkload:
         self.K.preprocess_batch(self.meta, self.out)
         self.h_out.copy_(self.out, non_blocking=True)
 
-    def cpu_baseline(self, cores, budget_s=15.0):
-        """cpu_paddle_det.cpp:53-94 restated with cv2 (INTER_LINEAR resize,
-        per-channel normalise, letterbox), images over `cores` threads."""
-        import cv2
-        from concurrent.futures import ThreadPoolExecutor
-        cv2.setNumThreads(1)
-        n = min(self.N, max(cores * 2, 16))
-        host = self.src.cpu().numpy()
-        imgs = [host[int(self.offs[i]):int(self.offs[i]) + self.dims[i][0] * self.dims[i][1] * 3]
-                .reshape(self.dims[i][0], self.dims[i][1], 3) for i in range(n)]
-        mean = np.array([0.485, 0.456, 0.406], np.float32)
-        istd = 1.0 / np.array([0.229, 0.224, 0.225], np.float32)
-
-        def one(i):
-            ch, cw = self.content[i]
-            r = cv2.resize(imgs[i], (cw, ch), interpolation=cv2.INTER_LINEAR)
-            f = (r.astype(np.float32) * (1 / 255.0) - mean) * istd
-            canvas = np.empty((3, self.H, self.W), np.float16)
-            canvas[:] = ((0 - mean) * istd).astype(np.float16)[:, None, None]
-            canvas[:, :ch, :cw] = f.transpose(2, 0, 1)
-            return canvas
-
-        t0 = time.perf_counter()
-        reps = 0
-        with ThreadPoolExecutor(cores) as ex:
-            while True:
-                list(ex.map(one, range(n)))
-                reps += 1
-                if time.perf_counter() - t0 > budget_s or reps >= 20:
-                    break
-        dt = time.perf_counter() - t0
-        return {"value": n * reps / dt, "unit": self.unit, "cores": cores, "kind": "port",
-                "sample": f"{n} images x {reps} reps (cv2 {cv2.__version__} resize+normalise "
-                          "restatement of cpu_paddle_det.cpp:53-94 with letterbox)"}
-
-
 class DwPwWorkload:
     """fused DW3x3 + PW1x1 block, INT8 PW weights on tcgen05."""
     name = "dwpw_block_32x128x240x240_to_256_int8"
     # DRAM bytes per image of dwpw_kernel (8-image ncu capture, scaled; part of
     # the output is still in L2 when that short launch ends)
     traffic_per_unit = (118_064_128 + 177_737_728) / 8
-    traffic_source = "profiles/dwpw_int8_32x240x240_128to256.md"
+    traffic_source = "ncu dram__bytes_read/write.sum, 8-image capture scaled per image"
     metric = "images/sec fused dw3x3+pw1x1 block (32x128x240x240 fp16 -> 256ch, INT8 PW)"
     unit = "images/s"
     dtype = "i8 (PW on tcgen05 kind::i8, DW fp16x2)"
     N, H, W, C, CO = 32, 240, 240, 128, 256
+    default_units = N
     launches_per_step = 1
     l2_note = "input 472 MB + output 944 MB per step > 126 MB L2 (no flush needed)"
     kind = 0
@@ -348,39 +296,11 @@ class DwPwWorkload:
         self.blk(self.x, self.y)
         self.h_y.copy_(self.y, non_blocking=True)
 
-    def cpu_baseline(self, cores, budget_s=15.0):
-        """The same block in torch fp32 on the host (mkldnn), all threads."""
-        torch.set_num_threads(cores)
-        x = self.x[:1].float().cpu()
-        t0 = time.perf_counter()
-        reps = 0
-        with torch.no_grad():
-            while True:
-                self.bb.reference_block(x, self.params, 1)
-                reps += 1
-                if time.perf_counter() - t0 > budget_s or reps >= 30:
-                    break
-        dt = time.perf_counter() - t0
-        return {"value": reps / dt, "unit": self.unit, "cores": cores, "kind": "port",
-                "sample": f"{reps} single-image passes of the block in torch fp32 "
-                          f"({torch.__version__}, {cores} threads)"}
-
-
 def det_resize_max960(h, w):
-    """compute_det_resize with {"max", 960, 960} (det_config.h:58-81)."""
-    ratio = np.float32(1.0)
-    longest = max(h, w)
-    if longest > 960:
-        ratio = np.float32(960) / np.float32(longest)
-
-    def r32(v):
-        return max(int(round(float(v) / 32.0) * 32), 32)
-    rh, rw = r32(np.float32(h) * ratio), r32(np.float32(w) * ratio)
-    lo = max(rh, rw)
-    if lo > 960:
-        rs = 960 / lo
-        rh, rw = r32(rh * rs), r32(rw * rs)
-    return rh, rw
+    """compute_det_resize with {"max", 960, 960} (det_config.h:58-81), as the
+    library computes it (config 3's DET_LIMIT_TYPE=max, 960, 960)."""
+    from turboocr_b200.det_config import DetResizeParams, compute_det_resize
+    return compute_det_resize(h, w, DetResizeParams("max", 960, 960))
 
 
 def touched_source_bytes(dims, content):
@@ -409,6 +329,7 @@ class DbWorkload:
     unit = "maps/s"
     dtype = "f32 map / int geometry"
     N, H, W = 8, 960, 960
+    default_units = N
     launches_per_step = 16
     l2_note = ("8 maps = 29.5 MB < L2: every step first writes a 256 MB buffer to flush L2 "
                "(inside the timed step; the roofline time excludes it)")
@@ -463,32 +384,6 @@ class DbWorkload:
         for h, d in zip(self.h_out, (self.db.boxes, self.db.scores, self.db.counts)):
             h.copy_(d, non_blocking=True)
 
-    def cpu_baseline(self, cores, budget_s=15.0):
-        """The CPU restatement of extract_boxes_from_bitmap (cv2 + the
-        reference's Clipper, with cv2.compare-style threshold), one process per
-        map over all host cores."""
-        from concurrent.futures import ProcessPoolExecutor
-        import multiprocessing as mpc
-        n = self.N
-        reps = 0
-        with ProcessPoolExecutor(min(cores, n), mp_context=mpc.get_context("spawn")) as ex:
-            list(ex.map(_db_map_cpu, [self.host_maps[0]]))  # warm the workers
-            t0 = time.perf_counter()
-            while True:
-                list(ex.map(_db_map_cpu, list(self.host_maps)))
-                reps += 1
-                if time.perf_counter() - t0 > budget_s or reps >= 20:
-                    break
-        dt = time.perf_counter() - t0
-        return {"value": n * reps / dt, "unit": self.unit, "cores": min(cores, n), "kind": "port",
-                "sample": f"{n} maps x {reps} reps, one process per map (cv2 + reference Clipper)"}
-
-
-def _db_map_cpu(m):
-    from oracle import db_oracle as do
-    return len(do.db_postprocess(m))
-
-
 class E2eWorkload:
     """BASELINE config 5 (the headline metric): 4096 synthetic 960x960 pages
     through preprocess + stem -> 8 INT8 DW+PW blocks -> head -> DB -> crops
@@ -506,9 +401,9 @@ class E2eWorkload:
     # each holds about 13 GB (mostly the stand-in logits of 4096 crop slots)
     NP = 6
     # DRAM bytes of the dominant launch (the CTC decode of pages 0..31's crops),
-    # from the ncu capture summarised in profiles/e2e_4096pages_960x960.md
+    # from one ncu capture of that launch (dram__bytes_read.sum + write.sum)
     traffic_per_launch = 5_026_007_296 + 3_558_912
-    traffic_source = "profiles/e2e_4096pages_960x960.md"
+    traffic_source = "ncu dram__bytes_read/write.sum of that launch"
     l2_note = "pages 2.76 MB each, >= 1.4 GB of input per rank per step > 126 MB L2 (no flush needed)"
     world = 1
     rank = 0
@@ -639,83 +534,26 @@ class E2eWorkload:
                     h.copy_(d, non_blocking=True)
         self._join()
 
-    def cpu_baseline(self, cores, budget_s=20.0):
-        """The path on the host, stage by stage on one page of the job, all
-        threads: det preprocessing (cv2 restatement of cpu_paddle_det.cpp:53-94),
-        the backbone in torch fp32 (stem + 8 blocks; the reference's CPU backend
-        runs its network in ORT, absent here), DB on the same probability map
-        (cv2 + the reference's Clipper, det_postprocess.cpp:145-222),
-        cv2.warpPerspective crops with the reference's crop transform
-        (cpu_paddle_rec.cpp:80-85), the reference's ctc_decode.cpp on the same
-        logits. Pages/s = 1 / the summed stage times."""
-        import cv2
-        from oracle import ctc_oracle as co
-        from oracle import db_oracle as do
-        from turboocr_b200 import backbone as bb
-        torch.set_num_threads(cores)
-        cv2.setNumThreads(cores)
-        pl = self.pl
-        p = self.pipe
-        p.run(self.pages[:self.MB])
-        torch.cuda.synchronize()
-        page = self.pages[0].cpu().numpy()
-        prob = p.prob[0].cpu().numpy()
-        k0 = int(p.db.counts[0].item())
-        logits = p.logits[:k0].float().cpu().numpy()
-        boxes = p.db.boxes[0, :k0].cpu().numpy()
-        mean = np.array([0.485, 0.456, 0.406], np.float32)
-        istd = 1.0 / np.array([0.229, 0.224, 0.225], np.float32)
-        times = {}
-        t_end = time.perf_counter() + budget_s
-        reps = 0
-        while reps < 1 or (time.perf_counter() < t_end and reps < 3):
-            t = time.perf_counter()
-            x = cv2.resize(page, (960, 960), interpolation=cv2.INTER_LINEAR)
-            x = ((x.astype(np.float32) * (1 / 255.0) - mean) * istd).transpose(2, 0, 1)[None]
-            t1 = time.perf_counter()
-            with torch.no_grad():
-                y = torch.from_numpy(np.ascontiguousarray(x))
-                y = torch.nn.functional.hardswish(torch.nn.functional.conv2d(
-                    y, torch.from_numpy(p.stem_w), torch.from_numpy(p.stem_b), stride=2, padding=1))
-                y = y.permute(0, 2, 3, 1)
-                for blk in p.blocks:
-                    y = bb.reference_block(y, blk.params, blk.stride)
-                head = torch.sigmoid(y @ p.head_w.cpu())
-            t2 = time.perf_counter()
-            dets = do.db_postprocess(prob)
-            t3 = time.perf_counter()
-            for q in boxes:
-                m, cw, _ = _crop_ref(q)
-                cv2.warpPerspective(page, m.reshape(3, 3), (pl.REC_W, pl.REC_H),
-                                    flags=cv2.INTER_LINEAR | cv2.WARP_INVERSE_MAP,
-                                    borderMode=cv2.BORDER_REPLICATE)
-            t4 = time.perf_counter()
-            co.ref_decode_batch(logits, pl.REC_V, cores, simd=True)
-            t5 = time.perf_counter()
-            for k, v in (("preprocess", t1 - t), ("backbone", t2 - t1), ("db", t3 - t2),
-                         ("crops", t4 - t3), ("ctc", t5 - t4)):
-                times[k] = times.get(k, 0.0) + v
-            reps += 1
-            del head, dets
-        per_page = sum(times.values()) / reps
-        return {"value": 1.0 / per_page, "unit": self.unit, "cores": cores, "kind": "port",
-                "sample": f"page 0 x {reps} reps, {k0} crops; stage s/page: " +
-                          ", ".join(f"{k} {v / reps:.3f}" for k, v in times.items())}
+def workload_config(Wl, world: int, units: int) -> dict:
+    """The `config` object of both arms (computed without a GPU, so the
+    reference arm prints the same one)."""
+    cfg = {"workload": Wl.name, "l2": Wl.l2_note,
+           "parallelism": f"dp{world} (independent shards)"}
+    if Wl is E2eWorkload:
+        per = -(-Wl.TOTAL // world)
+        per = -(-per // Wl.MB) * Wl.MB
+        cfg.update({
+            "pages_total": Wl.TOTAL, "pages_per_gpu": units or per, "micro_batch": Wl.MB,
+            "backbone": "stem 3->32 s2; " + ", ".join(f"{c}->{co} s{st}" for c, co, st in
+                                                     E2E_SCHEDULE),
+            "rec": "stand-in logits 80 x 18385 per crop (rec network out of scope)"})
+    else:
+        cfg["units_per_gpu_per_step"] = units or Wl.default_units
+    return cfg
 
 
-def _crop_ref(box):
-    """The reference's compute_crop_transform (oracle/_ref/libcrop_ref.so)."""
-    import ctypes as C
-    from oracle._loader import load
-    L = load("_ref/libcrop_ref.so")
-    L.crop_ref_transform.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
-                                     C.c_void_p]
-    b = np.ascontiguousarray(np.asarray(box, np.int32).reshape(8))
-    m = np.zeros(9, np.float32)
-    cw, v = C.c_int(), C.c_int()
-    L.crop_ref_transform(b.ctypes.data, 48, 320, m.ctypes.data, C.byref(cw), C.byref(v))
-    return m, cw.value, v.value
-
+E2E_SCHEDULE = [(32, 64, 1), (64, 64, 2), (64, 128, 1), (128, 128, 2),
+                (128, 128, 1), (128, 128, 2), (128, 128, 1), (128, 256, 1)]
 
 WORKLOADS = {"db": DbWorkload, "ctc": CtcWorkload, "preprocess": PreprocessWorkload,
              "dwpw": DwPwWorkload,
@@ -743,26 +581,24 @@ def main():
     Wl = WORKLOADS[args.workload]
     cores = len(os.sched_getaffinity(0))
 
+    config = workload_config(Wl, world, args.units)
     if args.impl == "reference":
-        # The reference's CPU implementation of the path, rank 0 only.
+        # The reference's CPU implementation of the path on this host's cores,
+        # rank 0 only; no GPU and none of this repository's libraries.
         if rank != 0:
             return
-        dev = torch.device("cuda", local) if torch.cuda.is_available() else None
-        Wl.world, Wl.rank = 1, 0
-        if args.workload == "e2e":
-            args.units = args.units or Wl.MB
-        wl = Wl(dev, 0x7EC00000 + SEEDS[args.workload], args.units)
-        vals = []
-        for i in range(args.warmup + args.steps):
-            cb = wl.cpu_baseline(cores, budget_s=2.0)
-            if i >= args.warmup:
-                vals.append(cb["value"])
-        v = statistics.median(vals)
+        from oracle.cpu_baselines import BASELINES
+        vals, desc = BASELINES[args.workload](cores, args.warmup + args.steps)
+        v = statistics.median(vals[args.warmup:])
+        units = desc.pop("units_per_step")
         print(json.dumps({"impl": "reference", "metric": Wl.metric, "value": v, "unit": Wl.unit,
                           "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-                          "higher_is_better": True, "dtype": Wl.dtype, "data": "synthetic",
-                          "config": {"workload": Wl.name},
-                          "cpu_baseline": dict(cb, value=v),
+                          "ms_per_step": 1e3 * units / v,
+                          "higher_is_better": True, "scaling": getattr(Wl, "scaling", "weak"),
+                          "vs_baseline": None, "dtype": Wl.dtype,
+                          "data": "synthetic (seeded generator, BASELINE config shapes)",
+                          "config": config,
+                          "cpu_baseline": dict(desc, value=v, unit=Wl.unit),
                           "e2e": {"value": v, "unit": Wl.unit, "h2d_bytes_per_step": 0,
                                   "d2h_bytes_per_step": 0}}), flush=True)
         return
@@ -832,8 +668,7 @@ def main():
             "higher_is_better": True, "scaling": getattr(Wl, "scaling", "weak"),
             "vs_baseline": None,
             "dtype": Wl.dtype, "data": "synthetic (seeded generator, BASELINE config shapes)",
-            "config": {"workload": Wl.name, "units_per_gpu_per_step": wl.units_per_step,
-                       "l2": Wl.l2_note, "parallelism": f"dp{world} (independent shards)"},
+            "config": config,
             "gpu_launches": wl.launches_per_step * args.steps,
             "e2e": {"value": wl.units_per_step * world / (ms_e2e / 1e3), "unit": Wl.unit,
                     "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h},
@@ -849,12 +684,7 @@ def main():
         if hasattr(wl, "dominant"):
             line["roofline"]["kernel"] = wl.dominant
         if args.workload == "e2e":
-            from turboocr_b200.pipeline import SCHEDULE
-            line["config"].update({
-                "pages_total": wl.n_pages * world, "pages_per_gpu": wl.n_pages,
-                "micro_batch": wl.MB, "crops_per_page": round(wl.crops_per_page, 2),
-                "backbone": "stem 3->32 s2; " + ", ".join(f"{c}->{co} s{st}" for c, co, st in SCHEDULE),
-                "rec": "stand-in logits 80 x 18385 per crop (rec network out of scope)"})
+            line["crops_per_page"] = round(wl.crops_per_page, 2)
             bpp = wl.path_bytes_per_page()
             ach = bpp * value / world / 1e9
             line["roofline_path"] = {"bound": "hbm", "bytes_per_page": bpp,
@@ -862,7 +692,10 @@ def main():
                                      "frac": ach / peak,
                                      "note": "algorithmic bytes of every stage per page x pages/s per GPU"}
         if not args.no_cpu_baseline and world == 1:  # rank 0 at N=1 only
-            line["cpu_baseline"] = wl.cpu_baseline(cores)
+            from oracle.cpu_baselines import BASELINES
+            vals, desc = BASELINES[args.workload](cores, 2)
+            desc.pop("units_per_step")
+            line["cpu_baseline"] = dict(desc, value=vals[-1], unit=Wl.unit)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -55,6 +55,26 @@ TOCR_API void tocr_debug_inject_error(int status, int count);
  * not depend on it. */
 TOCR_API void tocr_debug_db_shared_columns(int columns);
 
+/* ---- detection resize policy (host) ------------------------------------ */
+
+/* Replaces turbo_ocr::detection::compute_det_resize
+ *   (include/turbo_ocr/detection/det_config.h:58-81): the /32-rounded det
+ * input size of an h x w image under limit type "max" (limit_max = 1: shrink
+ * the longer side to limit_side_len) or "min" (0: grow the shorter side),
+ * with the longer output side capped at max_side_limit. Host only. */
+TOCR_API int tocr_compute_det_resize(int h, int w, int limit_max, int limit_side_len,
+                                     int max_side_limit, int *out_h, int *out_w);
+/* read_det_resize (det_config.h:89-127): applies DET_LIMIT_TYPE,
+ * DET_LIMIT_SIDE_LEN, DET_MAX_SIDE_LIMIT and DET_MAX_SIDE to the base passed
+ * in the three in/out arguments. */
+TOCR_API int tocr_read_det_resize(int *limit_max, int *limit_side_len, int *max_side_limit);
+/* effective_det_max_side (det_config.h:158-163): the buffer side for a
+ * max_side_limit (DET_MAX_SIDE wins), clamped to [32, 4096], rounded up to /32. */
+TOCR_API int tocr_effective_det_max_side(int max_side_limit);
+/* read_db_params (det_config.h:132-141): DET_DB_THRESH, DET_BOX_THRESH and
+ * DET_UNCLIP over the in/out base values. */
+TOCR_API int tocr_read_db_params(float *thresh, float *box_thresh, float *unclip_ratio);
+
 /* ---- subsystem 4: CTC greedy decode ------------------------------------ */
 
 /* Replaces turbo_ocr::kernels::cuda_argmax
@@ -84,13 +104,17 @@ TOCR_API int tocr_ctc_greedy_f16(const void *d_logits, int batch_size,
                                  float *d_step_prob, void *stream);
 
 /* Allocation-free variant of tocr_ctc_greedy_f16 (no counterpart in the
- * reference): same kernels and results, but the per-step scratch lives in a
- * static device array of 2^20 steps (8 MiB), so batch_size * seq_len must
- * not exceed 1048576 (TOCR_ERR_INVALID otherwise). Nothing is allocated.
- * The first call on each device looks up the array's address
- * (cudaGetSymbolAddress) and may load the module: make it before any stream
- * capture. Calls that overlap on one device share the scratch and race:
- * serialise them (one stream, or events). */
+ * reference). It is for callers that may not call cudaMalloc at all: plugins
+ * hosted by an engine that owns every device allocation, or serving
+ * processes whose allocator reserved the GPU's memory at start-up and gives
+ * none to third-party code. Same kernels and results, but the per-step
+ * scratch lives in a static device array of 2^20 steps (8 MiB, held by every
+ * GPU that loads the library until exit), so batch_size * seq_len must not
+ * exceed 1048576 (TOCR_ERR_INVALID otherwise). Nothing is allocated. Every
+ * call looks up the array's address in the current context
+ * (cudaGetSymbolAddress); the first call on a device may load the module, so
+ * make it before any stream capture. Calls that overlap on one device share
+ * the scratch and race: serialise them (one stream, or events). */
 TOCR_API int tocr_ctc_greedy_f16_noalloc(const void *d_logits, int batch_size,
                                          int seq_len, int num_classes, int num_labels,
                                          int *d_tokens, int *d_lengths,

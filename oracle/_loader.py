@@ -4,12 +4,28 @@ travelled with the snapshot are used."""
 from __future__ import annotations
 
 import ctypes as C
+import json
 import os
 import subprocess
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("TOCR_REFERENCE", "/root/reference"))
+
+
+def _reference_root() -> Path:
+    """The reference checkout: $TOCR_REFERENCE, else BASELINE.json's
+    reference_path. It exists only where the oracle is built, not on a GPU
+    box (which uses the prebuilt files)."""
+    env = os.environ.get("TOCR_REFERENCE")
+    if env:
+        return Path(env)
+    try:
+        return Path(json.loads((HERE.parent / "BASELINE.json").read_text())["reference_path"])
+    except (OSError, KeyError, ValueError):
+        return HERE / "_no_reference"
+
+
+REF = _reference_root()
 
 
 def build(verbose: bool = False) -> None:

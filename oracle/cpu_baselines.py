@@ -1,0 +1,179 @@
+"""ORACLE-side CPU baselines of the five BASELINE configs, for bench.py's
+reference arm (`--impl reference`) and its `cpu_baseline` key only. Nothing
+here loads this repository's native libraries or touches a GPU: inputs are
+made on the host by oracle/synth_host.py, the work runs on the host cores.
+
+Each function runs `n_steps` bounded samples of its workload and returns
+(list of per-step values in the workload's unit, a dict describing the
+sample: kind, cores, units_per_step, sample).
+"""
+from __future__ import annotations
+
+import multiprocessing as mp
+import time
+
+import numpy as np
+
+from . import synth_host as sh
+
+SEED = 0x7EC00000
+
+
+def e2e(cores: int, n_steps: int, pages_per_worker: int = 1):
+    """Config 5: one single-threaded worker process per core, each with its
+    own pages (oracle/cpu_path.py); a step = every worker's pages once."""
+    from . import cpu_path as cp
+    rows = cp.run_throughput(n_steps, cores, pages_per_worker)
+    pages = rows[0][2]
+    stage = {}
+    for _, times, p in rows:
+        for k, v in times.items():
+            stage[k] = stage.get(k, 0.0) + v / p / len(rows)
+    return [r[0] for r in rows], {
+        "kind": "port", "cores": cores, "units_per_step": pages,
+        "sample": f"{pages} pages per step ({pages_per_worker} per worker process x {cores} "
+                  "single-threaded processes); stage s/page/core: " +
+                  ", ".join(f"{k} {v:.3f}" for k, v in stage.items()) +
+                  "; CTC = the reference's ctc_decode.cpp, DB = cv2 + the reference's Clipper, "
+                  "backbone = torch fp32 (ORT absent)"}
+
+
+def ctc(cores: int, n_steps: int, lines: int = 0):
+    """Config 2: the reference's ctc_decode.cpp (ctc_greedy_decode_raw, SIMD_CTC=1)
+    plus the max-softmax beside it, on fp32 rows, lines over `cores` threads."""
+    from . import ctc_oracle as co
+    T, V = 80, 18385
+    n = lines or max(2 * cores, 16)
+    x = sh.ctc_logits(n, T, V, SEED + 1, dtype=np.float32)
+    co.ref_decode_batch(x[:cores], V, cores, simd=True)
+    vals = []
+    for _ in range(n_steps):
+        t0 = time.perf_counter()
+        co.ref_decode_batch(x, V, cores, simd=True)
+        vals.append(n / (time.perf_counter() - t0))
+    return vals, {"kind": "reference", "cores": cores, "units_per_step": n,
+                  "sample": f"{n} lines of 80 x 18385 per step (config-2 generator on the host), "
+                            "fp32 rows, std::thread over lines"}
+
+
+def _pre_images(n: int):
+    """The first n images of the config-3 batch, as the device generator lays
+    them out (one byte stream, each image at a 256-byte aligned offset)."""
+    seed = SEED + 2
+    dims = sh.preprocess_dims(n, seed)
+    sizes = [h * w * 3 for h, w in dims]
+    offs = np.concatenate([[0], np.cumsum([(s + 255) // 256 * 256 for s in sizes])])
+    buf = sh.fill_u8(int(offs[-1]), seed, 3)
+    return dims, [buf[int(offs[i]):int(offs[i]) + sizes[i]].reshape(h, w, 3)
+                  for i, (h, w) in enumerate(dims)]
+
+
+def round32_floor(v: float) -> int:
+    """det_config.h:50-52: std::round (half away from zero) of v / 32, x32, floor 32."""
+    q = v / 32.0
+    f = np.floor(q)
+    r = f + 1.0 if q - f >= 0.5 else f
+    return max(int(r) * 32, 32)
+
+
+def det_resize_max(h: int, w: int, L: int = 960, max_side: int = 960):
+    """compute_det_resize with {"max", L, max_side} (det_config.h:58-81)."""
+    ratio = np.float32(1.0)
+    if max(h, w) > L:
+        ratio = np.float32(np.float32(L) / np.float32(max(h, w)))
+    rh = round32_floor(float(np.float32(np.float32(h) * ratio)))
+    rw = round32_floor(float(np.float32(np.float32(w) * ratio)))
+    lo = max(rh, rw)
+    if lo > max_side:
+        rs = max_side / lo
+        rh, rw = round32_floor(rh * rs), round32_floor(rw * rs)
+    return rh, rw
+
+
+def preprocess(cores: int, n_steps: int, n_images: int = 0):
+    """Config 3: cpu_paddle_det.cpp:53-94 restated with cv2 (INTER_LINEAR
+    resize, normalise, letterbox into 960x960 fp16), images over threads."""
+    import cv2
+    from concurrent.futures import ThreadPoolExecutor
+    cv2.setNumThreads(1)
+    n = n_images or max(2 * cores, 16)
+    dims, imgs = _pre_images(n)
+    content = [det_resize_max(h, w) for h, w in dims]
+    mean = np.array([0.485, 0.456, 0.406], np.float32)
+    istd = 1.0 / np.array([0.229, 0.224, 0.225], np.float32)
+    pad = ((0 - mean) * istd).astype(np.float16)[:, None, None]
+
+    def one(i):
+        ch, cw = content[i]
+        r = cv2.resize(imgs[i], (cw, ch), interpolation=cv2.INTER_LINEAR)
+        f = (r.astype(np.float32) * np.float32(1 / 255.0) - mean) * istd
+        canvas = np.empty((3, 960, 960), np.float16)
+        canvas[:] = pad
+        canvas[:, :ch, :cw] = f.transpose(2, 0, 1)
+        return canvas
+
+    vals = []
+    with ThreadPoolExecutor(cores) as ex:
+        list(ex.map(one, range(min(n, cores))))
+        for _ in range(n_steps):
+            t0 = time.perf_counter()
+            list(ex.map(one, range(n)))
+            vals.append(n / (time.perf_counter() - t0))
+    return vals, {"kind": "port", "cores": cores, "units_per_step": n,
+                  "sample": f"{n} images per step (sides 600..2000), cv2 {cv2.__version__} "
+                            "resize + normalise + letterbox, threads over images"}
+
+
+def dwpw(cores: int, n_steps: int, images: int = 1):
+    """Config 4: the block (DW3x3 + hardswish, PW1x1 + hardswish, BN folded)
+    in torch fp32 on the host (mkldnn), all threads."""
+    import torch
+    torch.set_num_threads(cores)
+    rng = np.random.default_rng(SEED + 4)
+    C, CO = 128, 256
+    wdw = rng.normal(0, 0.05, (C, 1, 3, 3)).astype(np.float32)
+    bdw = rng.normal(0, 0.1, C).astype(np.float32)
+    wpw = rng.normal(0, 0.05, (CO, C, 1, 1)).astype(np.float32)
+    bpw = rng.normal(0, 0.1, CO).astype(np.float32)
+    x = torch.from_numpy(rng.standard_normal((images, C, 240, 240), dtype=np.float32))
+    F = torch.nn.functional
+    t = [torch.from_numpy(a) for a in (wdw, bdw, wpw, bpw)]
+
+    def block():
+        with torch.no_grad():
+            y = F.hardswish(F.conv2d(x, t[0], t[1], padding=1, groups=C))
+            return F.hardswish(F.conv2d(y, t[2], t[3]))
+
+    block()
+    vals = []
+    for _ in range(n_steps):
+        t0 = time.perf_counter()
+        block()
+        vals.append(images / (time.perf_counter() - t0))
+    return vals, {"kind": "port", "cores": cores, "units_per_step": images,
+                  "sample": f"{images} image(s) of 128x240x240 per step, torch {torch.__version__} "
+                            f"fp32, {cores} threads"}
+
+
+def _db_one(m):
+    from . import db_oracle as do
+    return len(do.db_postprocess(m))
+
+
+def db(cores: int, n_steps: int, maps: int = 8):
+    """Config 1: the cv2 + reference-Clipper restatement of
+    extract_boxes_from_bitmap, one process per map over the host cores."""
+    from concurrent.futures import ProcessPoolExecutor
+    host = [sh.db_map(960, 960, 40, 200, SEED, i) for i in range(maps)]
+    vals = []
+    with ProcessPoolExecutor(min(cores, maps), mp_context=mp.get_context("spawn")) as ex:
+        list(ex.map(_db_one, host[:min(cores, maps)]))
+        for _ in range(n_steps):
+            t0 = time.perf_counter()
+            list(ex.map(_db_one, host))
+            vals.append(maps / (time.perf_counter() - t0))
+    return vals, {"kind": "port", "cores": min(cores, maps), "units_per_step": maps,
+                  "sample": f"{maps} maps per step, one process per map (cv2 + reference Clipper)"}
+
+
+BASELINES = {"e2e": e2e, "ctc": ctc, "preprocess": preprocess, "dwpw": dwpw, "db": db}

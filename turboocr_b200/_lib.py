@@ -79,6 +79,10 @@ SIGNATURES: dict[str, tuple] = {
     "tocr_roi_warp_f16": (_i, [_vp, _ll, _i, _i, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _f,
                                _vp, _vp]),
     "tocr_ctc_greedy_f16_dev": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "tocr_compute_det_resize": (_i, [_i, _i, _i, _i, _i, _vp, _vp]),
+    "tocr_read_det_resize": (_i, [_vp, _vp, _vp]),
+    "tocr_effective_det_max_side": (_i, [_i]),
+    "tocr_read_db_params": (_i, [_vp, _vp, _vp]),
 }
 
 SYNTH_SIGNATURES: dict[str, tuple] = {

@@ -36,7 +36,7 @@ LIBS = {
 }
 # C++ host sources (reference-signature shims), built into libtocr_b200.so.
 HOST_SOURCES = {
-    "libtocr_b200.so": ["shim_kernels.cpp", "shim_ctc.cpp"],
+    "libtocr_b200.so": ["shim_kernels.cpp", "shim_ctc.cpp", "det_config_capi.cpp"],
 }
 HEADERS = sorted(list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list(INCLUDE.rglob("*.h")))
 

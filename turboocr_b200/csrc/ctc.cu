@@ -16,7 +16,6 @@
 #include "tocr_common.cuh"
 
 #include <cmath>
-#include <mutex>
 
 namespace tocr {
 namespace {
@@ -362,7 +361,6 @@ TOCR_API int tocr_ctc_greedy_f16_dev(const void *d_logits, const int *d_batch, i
 namespace {
 
 constexpr long long kNoAllocMaxSteps = 1ll << 20;  // 4 MiB of indices + 4 MiB of probabilities
-constexpr int kNoAllocMaxDevices = 64;
 
 __device__ __align__(256) int g_noalloc_step_idx[kNoAllocMaxSteps];
 __device__ __align__(256) float g_noalloc_step_prob[kNoAllocMaxSteps];
@@ -372,30 +370,20 @@ struct NoAllocScratch {
   float *prob = nullptr;
 };
 
-std::mutex g_noalloc_mu;
-NoAllocScratch g_noalloc[kNoAllocMaxDevices];
-
-// Device addresses of the scratch arrays on the current device, looked up
-// once per device (the first lookup may load the module).
+// Device addresses of the scratch arrays in the current context. They are
+// looked up on every call rather than cached: a device reset or a new
+// primary context reloads the module at another address, and after the
+// first call (which may load the module) the lookup is cheap.
 int noalloc_scratch(NoAllocScratch *out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return set_error(TOCR_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
-  TOCR_REQUIRE(dev >= 0 && dev < kNoAllocMaxDevices, "no-alloc CTC: device %d out of range", dev);
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  NoAllocScratch &s = g_noalloc[dev];
-  if (!s.idx) {
-    void *pi = nullptr, *pp = nullptr;
-    e = cudaGetSymbolAddress(&pi, g_noalloc_step_idx);
-    if (e != cudaSuccess)
-      return set_error(TOCR_ERR_CUDA, "cudaGetSymbolAddress(step_idx): %s", cudaGetErrorString(e));
-    e = cudaGetSymbolAddress(&pp, g_noalloc_step_prob);
-    if (e != cudaSuccess)
-      return set_error(TOCR_ERR_CUDA, "cudaGetSymbolAddress(step_prob): %s", cudaGetErrorString(e));
-    s.idx = static_cast<int *>(pi);
-    s.prob = static_cast<float *>(pp);
-  }
-  *out = s;
+  void *pi = nullptr, *pp = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&pi, g_noalloc_step_idx);
+  if (e != cudaSuccess)
+    return set_error(TOCR_ERR_CUDA, "cudaGetSymbolAddress(step_idx): %s", cudaGetErrorString(e));
+  e = cudaGetSymbolAddress(&pp, g_noalloc_step_prob);
+  if (e != cudaSuccess)
+    return set_error(TOCR_ERR_CUDA, "cudaGetSymbolAddress(step_prob): %s", cudaGetErrorString(e));
+  out->idx = static_cast<int *>(pi);
+  out->prob = static_cast<float *>(pp);
   return TOCR_OK;
 }
 

@@ -43,8 +43,11 @@ TOCR_SHIM_API bool load_label_dict(const std::string &dict_path,
   if (!in) return false;
   std::string line;
   while (std::getline(in, line)) {
-    while (!line.empty() && (line.back() == '\n' || line.back() == '\r')) line.pop_back();
-    label_list.push_back(line);
+    // At most one '\n', then at most one '\r' (a "\r\r" line keeps one '\r'),
+    // as the reference loader does (src/recognition/ctc_decode.cpp:150-154).
+    if (!line.empty() && line.back() == '\n') line.pop_back();
+    if (!line.empty() && line.back() == '\r') line.pop_back();
+    label_list.push_back(std::move(line));
   }
   label_list.emplace_back(" ");
   return true;

@@ -1,5 +1,8 @@
-// Seeded synthetic inputs for the parity tests and bench.py (test
-// infrastructure, built as libtocr_synth.so, never linked into the product).
+// Seeded synthetic inputs for the parity tests and bench.py, built as
+// libtocr_synth.so beside the product library. The end-to-end page pipeline
+// (turboocr_b200/pipeline.py) loads it for one stage: the recognition network
+// is out of scope, so tocr_synth_rec_logits writes stand-in CTC logits per
+// crop. Every other entry here only makes test and benchmark inputs.
 //
 // One counter-based generator everywhere: value i of stream s under seed k is
 // mix64(k + golden * (mix64(s) + i + 1)) (splitmix64 finaliser), so any
