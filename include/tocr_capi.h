@@ -170,14 +170,20 @@ TOCR_API int tocr_threshold_u8(const float *d_src, uint8_t *d_dst, int w,
  * ([n_maps][max_boxes]) and counts ([n_maps]) in contour order.
  * d_geometry: NULL (identity) or int [n_maps][4] = orig_h, orig_w, resize_h,
  * resize_w for the scaling of det_postprocess.cpp:205-210.
+ * unclip is the reference's: Clipper's round-join offset and then Clipper's
+ * union of that path (positive fill), largest ring kept, so the boxes are
+ * bit-exact with the reference's CPU path.
  * point_cap bounds the traced contour points of a call; offset_cap sizes a
- * scratch pool (64 bytes per point) used only by point sets (contours,
- * unclip rings) wider than the shared-memory geometry takes (6144 columns);
- * <= 0: defaults. The workspace (256-byte aligned) must hold
+ * scratch pool (256 bytes per point) that holds every unclip's offset ring,
+ * union sweep and hull work space, and the rare point sets wider than the
+ * shared-memory geometry takes (6144 columns); <= 0: defaults (h*w/4 + 4096
+ * points per map for both). The workspace (256-byte aligned) must hold
  * tocr_db_workspace_bytes(n_maps, h, w, point_cap, offset_cap) bytes.
  * d_status (device int) receives 0 or a bit set: 1 point pool full, 2 a
  * border walk exceeded its bound, 4 scratch pool full, 8 more than max_boxes
- * kept (truncated). Enqueued on `stream`; no synchronisation, no allocation. */
+ * kept (truncated), 16 a union sweep exceeded its bounds (that box was built
+ * from the raw offset ring). Enqueued on `stream`; no synchronisation, no
+ * allocation. */
 TOCR_API size_t tocr_db_workspace_bytes(int n_maps, int h, int w, long long point_cap,
                                         long long offset_cap);
 TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,

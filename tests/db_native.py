@@ -10,6 +10,7 @@ import numpy as np
 ROOT = Path(__file__).resolve().parents[1]
 SRC = ROOT / "tests" / "native" / "db_geom_host.cpp"
 HDR = ROOT / "turboocr_b200" / "csrc" / "db_geom.cuh"
+UNION_HDR = ROOT / "turboocr_b200" / "csrc" / "clipper_union.cuh"
 OUT = ROOT / "tests" / "native" / "_build" / "libdbgeom_host.so"
 
 _lib = None
@@ -41,7 +42,8 @@ def lib():
     if _lib is not None:
         return _lib
     OUT.parent.mkdir(exist_ok=True)
-    if not OUT.exists() or OUT.stat().st_mtime < max(SRC.stat().st_mtime, HDR.stat().st_mtime):
+    if not OUT.exists() or OUT.stat().st_mtime < max(SRC.stat().st_mtime, HDR.stat().st_mtime,
+                                                     UNION_HDR.stat().st_mtime):
         subprocess.run(["g++", "-std=c++17", "-O2", "-ffp-contract=off", "-fPIC", "-shared",
                         f"-I{HDR.parent}", "-o", str(OUT), str(SRC)], check=True)
     L = C.CDLL(str(OUT))
@@ -59,6 +61,8 @@ def lib():
     L.dbh_arclen.argtypes = [vp, i]
     L.dbh_arclen.restype = d
     L.dbh_offset_raw.argtypes = [vp, i, d, vp, i]
+    L.dbh_unclip_union.argtypes = [vp, i, d, vp, i]
+    L.dbh_sort_check.argtypes = [vp, i, vp, vp]
     L.dbh_poly_mask.argtypes = [vp, i, i, i, i, i, vp]
     L.dbh_poly_mask_parity.argtypes = [vp, i, i, i, i, i, vp]
     _lib = L
@@ -152,3 +156,23 @@ def poly_mask(p, x0, y0, w, h, parity=False):
     fn = lib().dbh_poly_mask_parity if parity else lib().dbh_poly_mask
     fn(p.ctypes.data, len(p), x0, y0, w, h, m.ctypes.data)
     return m
+
+
+def unclip_union(p, delta):
+    """The largest ring of Clipper's union of the raw offset (clipper_union.cuh)."""
+    p = _pts(p)
+    cap = 1 << 20
+    out = np.zeros(2 * cap, dtype=np.int32)
+    n = lib().dbh_unclip_union(p.ctypes.data, len(p), delta, out.ctypes.data, cap)
+    if n < 0:
+        raise RuntimeError(f"union sweep failed ({n})")
+    return out[: 2 * n].reshape(n, 2)
+
+
+def sort_check(keys):
+    """(std::sort permutation, std_sort permutation) of keys by descending value."""
+    k = np.ascontiguousarray(keys, dtype=np.int32)
+    a = np.zeros(len(k), np.int32)
+    b = np.zeros(len(k), np.int32)
+    assert lib().dbh_sort_check(k.ctypes.data, len(k), a.ctypes.data, b.ctypes.data) == 0
+    return a, b

@@ -6,6 +6,7 @@
 #include <cstring>
 #include <vector>
 
+#include "clipper_union.cuh"
 #include "db_geom.cuh"
 
 using namespace tocr::db;
@@ -175,3 +176,56 @@ int dbh_offset_raw(const int *pts, int n, double delta, int *out, int cap) {
 }
 
 }  // extern "C"
+
+// unclip() with Clipper's union (clipper_union.cuh) on the raw offset: the
+// largest output ring in path order. Returns its length, 0 for an empty
+// solution, -1 when the sweep failed, -2 when out is too small.
+extern "C" int dbh_unclip_union(const int *pts, int n, double delta, int *out, int cap) {
+  std::vector<P2> q(n + 1);
+  const int m = offset_prepare(reinterpret_cast<const P2 *>(pts), n, q.data());
+  if (m == 0) return 0;
+  const int rn = offset_raw(q.data(), m, delta, nullptr, 0);
+  if (rn <= 0) return 0;
+  std::vector<P2> ring(rn);
+  offset_raw(q.data(), m, delta, ring.data(), rn);
+  std::vector<char> arena(cu::arena_bytes(rn) + 64);
+  cu::Sweep s;
+  s.init(arena.data(), rn);
+  if (!s.execute(ring.data(), rn)) return -1;
+  const int k = s.best_ring(reinterpret_cast<P2 *>(out), cap);
+  return k < 0 ? (s.fail ? -1 : -2) : k;
+}
+
+// Peak use of the sweep's arrays for one unclip (test of the capacities).
+extern "C" int dbh_union_usage(const int *pts, int n, double delta, int *use) {
+  std::vector<P2> q(n + 1);
+  const int m = offset_prepare(reinterpret_cast<const P2 *>(pts), n, q.data());
+  if (m == 0) return 0;
+  std::vector<P2> ring(1 << 20);
+  const int rn = offset_raw(q.data(), m, delta, ring.data(), 1 << 20);
+  if (rn <= 0) return 0;
+  std::vector<char> arena(cu::arena_bytes(rn) + 64);
+  cu::Sweep s;
+  s.init(arena.data(), rn);
+  const bool ok = s.execute(ring.data(), rn);
+  use[0] = rn; use[1] = s.n_lm; use[2] = s.n_op; use[3] = s.n_or; use[4] = s.n_jn;
+  use[5] = (int)s.guard;
+  return ok ? 1 : -1;
+}
+
+// std_sort (libstdc++'s introsort restated in clipper_union.cuh) against the
+// host's std::sort on the same keys: both permutations of 0..n-1, keys
+// compared by descending value as Clipper's sorts do.
+#include <algorithm>
+extern "C" int dbh_sort_check(const int *keys, int n, int *perm_std, int *perm_own) {
+  struct K { int key, id; };
+  std::vector<K> a(n), b(n);
+  for (int i = 0; i < n; ++i) a[i] = b[i] = K{keys[i], i};
+  auto less = [](const K &x, const K &y) { return y.key < x.key; };
+  std::sort(a.begin(), a.end(), less);
+  std::vector<int> stk(3 * 64);
+  bool fail = false;
+  cu::std_sort(b.data(), n, less, stk.data(), 64, &fail);
+  for (int i = 0; i < n; ++i) { perm_std[i] = a[i].id; perm_own[i] = b[i].id; }
+  return fail ? -1 : 0;
+}

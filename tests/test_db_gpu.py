@@ -2,19 +2,15 @@
 restatement of extract_boxes_from_bitmap (oracle/db_oracle.py: cv2 4.13 +
 the reference's Clipper).
 
-Two bars:
-- bit-exact boxes, in contour order, against the oracle whose unclip ring
-  is Clipper's raw round-join offset (the offset before Clipper's union, as
-  the device computes it). This pins every device stage: threshold,
-  labelling, contour order and the 3000 cap, border following, both
-  min-area boxes, the polygon-mask score, the offset, scaling and filters.
-  Scores within 1e-3 (measured: equal to float rounding).
-- against the full oracle (Clipper's union): the union re-rounds vertices
-  where the offset path crosses itself, which moves a mini-box corner by a
-  pixel for about 2 % of the boxes; the test bounds that rate and the size
-  of the differences.
-The labelling stage is also checked on its own (tocr_db_components) as a
-partition against scipy's 8-/4-connected labelling."""
+The bar: bit-exact boxes, in contour order, against the unmodified oracle,
+whose unclip is the reference's own Clipper (offset and union), on the
+config-1 maps and on other seeds, sizes and shapes. This pins every device
+stage: threshold, labelling, contour order and the 3000 cap, border
+following, both min-area boxes, the polygon-mask score, the round-join
+offset, Clipper's union sweep, scaling and filters. Scores within 1e-3
+(measured: equal to float rounding). The labelling stage is also checked on
+its own (tocr_db_components) as a partition against scipy's 8-/4-connected
+labelling."""
 import numpy as np
 import pytest
 import torch
@@ -35,15 +31,6 @@ def synth_maps(n, h, w, kmin=40, kmax=200, seed=0x7EC00000, first=0):
     for i in range(n):
         synth().tocr_synth_db_map_host(out[i].ctypes.data, h, w, kmin, kmax, seed, first + i)
     return out
-
-
-def raw_unclip(contour, ratio):
-    import db_native as dn
-    d = do.unclip_distance(contour, ratio)
-    if d is None:
-        return contour
-    raw = dn.offset_raw(contour, d)
-    return np.array(raw, np.int32) if raw else contour
 
 
 def run_gpu(cuda, maps, **kw):
@@ -104,7 +91,7 @@ def test_db_config1_exact(cuda):
     got = run_gpu(cuda, maps)
     n = 0
     for m in range(8):
-        ref = do.db_postprocess(maps[m], unclip_fn=raw_unclip)
+        ref = do.db_postprocess(maps[m])
         compare_exact(got[m], ref)
         n += len(ref)
     assert n > 60
@@ -115,7 +102,7 @@ def test_db_small_maps_exact(cuda, hw, k):
     maps = synth_maps(4, hw[0], hw[1], k[0], k[1], first=100)
     got = run_gpu(cuda, maps)
     for m in range(4):
-        compare_exact(got[m], do.db_postprocess(maps[m], unclip_fn=raw_unclip))
+        compare_exact(got[m], do.db_postprocess(maps[m]))
 
 
 def test_db_noise_and_holes_exact(cuda):
@@ -125,7 +112,7 @@ def test_db_noise_and_holes_exact(cuda):
     maps = np.clip((maps - 0.45) * 4, 0, 1).astype(np.float32)
     got = run_gpu(cuda, maps, box_thresh=0.5)
     for m in range(6):
-        compare_exact(got[m], do.db_postprocess(maps[m], box_thresh=0.5, unclip_fn=raw_unclip))
+        compare_exact(got[m], do.db_postprocess(maps[m], box_thresh=0.5))
 
 
 def test_db_edge_cases(cuda):
@@ -138,7 +125,7 @@ def test_db_edge_cases(cuda):
     got = run_gpu(cuda, maps)
     assert got[0] == []
     for m in range(1, 4):
-        compare_exact(got[m], do.db_postprocess(maps[m], unclip_fn=raw_unclip))
+        compare_exact(got[m], do.db_postprocess(maps[m]))
     assert len(got[1]) == 1
 
 
@@ -154,7 +141,7 @@ def test_db_3000_cap(cuda):
     total = len(do.find_contours(do.threshold(m, 0.3)))
     assert total > 3000
     got = run_gpu(cuda, maps)
-    ref = do.db_postprocess(m, unclip_fn=raw_unclip)
+    ref = do.db_postprocess(m)
     compare_exact(got[0], ref)
     assert ref == []
     m2 = m.copy()
@@ -174,24 +161,46 @@ def test_db_geometry_scaling(cuda):
     got = db.results()
     for m, (oh, ow) in enumerate([(500, 700), (160, 240)]):
         ref = do.extract_boxes_from_bitmap(maps[m], do.threshold(maps[m], 0.3), oh, ow, 320, 480,
-                                           0.6, 1.5, unclip_fn=raw_unclip)
+                                           0.6, 1.5)
         compare_exact(got[m], ref)
 
 
-def test_db_vs_clipper_union_rate(cuda):
-    """Against the full reference unclip (with Clipper's union)."""
-    maps = synth_maps(8, 960, 960, first=300)
+@pytest.mark.parametrize("first", [300, 600])
+def test_db_more_config1_seeds_exact(cuda, first):
+    """Other config-1 seeds: every box equal to the full reference path."""
+    maps = synth_maps(8, 960, 960, first=first)
     got = run_gpu(cuda, maps)
-    same = total = 0
+    n = 0
     for m in range(8):
         ref = do.db_postprocess(maps[m])
-        assert len(got[m]) == len(ref)
-        for (b1, s1), (b2, s2) in zip(got[m], ref):
-            total += 1
-            same += b1 == b2
-            assert np.abs(np.array(b1) - np.array(b2)).max() <= 6
-            assert abs(s1 - s2) <= SCORE_TOL
-    assert total > 60 and same >= 0.9 * total, (same, total)
+        compare_exact(got[m], ref)
+        n += len(ref)
+    assert n > 60
+
+
+@pytest.mark.parametrize("size,angle", [((480, 640), 15), ((800, 1200), -15), ((256, 256), 45),
+                                        ((600, 900), 75)])
+def test_db_rotated_shapes_exact(cuda, size, angle):
+    """Filled rotated rectangles and ellipses (staircase contours whose
+    offset paths cross themselves at every step) at one angle each."""
+    h, w = size
+    rng = np.random.default_rng(h + angle)
+    maps = np.zeros((3, h, w), np.float32)
+    for m in range(3):
+        bm = np.zeros((h, w), np.uint8)
+        for _ in range(12):
+            cx, cy = rng.uniform(0.1, 0.9) * w, rng.uniform(0.1, 0.9) * h
+            a = angle + rng.uniform(-3, 3)
+            ww, hh = rng.uniform(20, 0.4 * w), rng.uniform(6, 50)
+            if rng.random() < 0.7:
+                box = cv2.boxPoints(((cx, cy), (ww, hh), a)).astype(np.int32)
+                cv2.fillPoly(bm, [box], 1)
+            else:
+                cv2.ellipse(bm, ((cx, cy), (ww, hh), a), 1, -1)
+        maps[m] = bm * rng.uniform(0.65, 1.0, (h, w)).astype(np.float32)
+    got = run_gpu(cuda, maps)
+    for m in range(3):
+        compare_exact(got[m], do.db_postprocess(maps[m]))
 
 
 @pytest.fixture
@@ -212,7 +221,7 @@ def test_db_global_scratch_path_exact(cuda, shared_columns, cap):
     maps = synth_maps(3, 960, 960, first=400)
     got = run_gpu(cuda, maps)
     for m in range(3):
-        compare_exact(got[m], do.db_postprocess(maps[m], unclip_fn=raw_unclip))
+        compare_exact(got[m], do.db_postprocess(maps[m]))
 
 
 def test_db_scratch_pool_full_raises(cuda, shared_columns):
@@ -236,6 +245,6 @@ def test_db_wide_jagged_bar_exact(cuda, shared_columns, cap):
     for x in range(20, 2580, 8):
         m[10:12, x:x + 4] = 0.9               # jagged top edge
     got = run_gpu(cuda, m[None].copy())
-    ref = do.db_postprocess(m, unclip_fn=raw_unclip)
+    ref = do.db_postprocess(m)
     assert len(ref) == 1
     compare_exact(got[0], ref)

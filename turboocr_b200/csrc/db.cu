@@ -39,6 +39,7 @@
 #include "tocr_common.cuh"
 
 #include "db_geom.cuh"
+#include "clipper_union.cuh"
 
 namespace tocr {
 namespace {
@@ -56,6 +57,7 @@ constexpr int kErrPointPool = 1;      // traced points exceed the point pool
 constexpr int kErrTrace = 2;          // a border walk exceeded its step bound
 constexpr int kErrOffsetPool = 4;     // offset points exceed the offset pool
 constexpr int kErrBoxes = 8;          // more kept boxes than max_boxes (truncated)
+constexpr int kErrUnion = 16;         // a union sweep hit its bounds (raw offset ring used)
 
 struct DbParams {
   int n_maps, H, W;
@@ -80,7 +82,10 @@ constexpr size_t kBigFscBytes = sizeof(float) * 3 * kBigHull;
 constexpr size_t kBigSmem = kBigTabBytes + kBigStkBytes + kBigHullBytes + kBigFscBytes;
 // the prepared offset path aliases everything after the table
 constexpr int kBigQPts = (int)((kBigSmem - kBigTabBytes) / sizeof(P2));
-constexpr unsigned long long kPoolBytesPerPoint = 64;
+// Scratch pool bytes per point of offset_cap: per unclip the pool holds the
+// prepared path, the raw offset ring, the union sweep's arrays (about 200
+// bytes per ring point) and the hull work space.
+constexpr unsigned long long kPoolBytesPerPoint = 256;
 static_assert(kBigSmem <= 227 * 1024, "shared memory of the CTA geometry path");
 
 // Counters of the geometry stages: [0] contour list length, [1] ring list
@@ -1034,219 +1039,67 @@ __device__ void finish_box(const RRect &rr, long long c, const int *geo, int *ke
   keep2[c] = 1;
 }
 
-// 7. one thread per surviving contour: the unclip ring (det_postprocess.cpp
-// :190-199, Clipper's raw round-join offset), the second min-area box and
-// finish_box. Contours or rings above kLocalPts points are listed for
-// unclip_big_kernel.
+// 7. one thread per surviving contour slot: unclip (det_postprocess.cpp
+// :57-102) as the reference computes it, i.e. Clipper's raw round-join
+// offset (DoOffset) followed by the union of that path with positive fill
+// (ClipperOffset::Execute, clipper_union.cuh), keeping the output ring of
+// largest area; then the second min-area box and finish_box. The offset
+// ring, the sweep's arrays and the hull work space come from the scratch
+// pool. When the pool or the sweep's bounds run out, the box comes from the
+// raw offset ring instead and status bit kErrUnion is set.
 __global__ void __launch_bounds__(128)
-unclip_kernel(const int *__restrict__ stage2, const int *__restrict__ npts,
-              const long long *__restrict__ pt_off, const P2 *__restrict__ pts,
-              const double *__restrict__ dist, const int *__restrict__ geo,
-              int *__restrict__ keep2, int *__restrict__ boxes, int *__restrict__ list,
-              int *__restrict__ counters, DbParams P) {
+union_kernel(const int *__restrict__ stage2, const int *__restrict__ npts,
+             const long long *__restrict__ pt_off, const P2 *__restrict__ pts,
+             const double *__restrict__ dist, const int *__restrict__ geo,
+             int *__restrict__ keep2, int *__restrict__ boxes, char *__restrict__ pool,
+             int *__restrict__ pool_counters, int *__restrict__ status, DbParams P) {
   const long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= (long long)P.n_maps * kMaxCand) return;
   keep2[c] = 0;
   if (!stage2[c]) return;
   const int n = npts[c];
-  if (n > kLocalPts) {
-    list[atomicAdd(counters + 1, 1)] = (int)c;
-    return;
-  }
   const P2 *p = pts + pt_off[c];
   const double d = dist[c];
-  P2 q[kLocalPts];
-  P2 ring[kLocalPts];
-  const int qm = (d == 0.) ? 0 : db::offset_prepare(p, n, q);
-  int rn;
-  if (qm == 0) {  // no offset: unclip returns the contour itself
-    for (int i = 0; i < n; ++i) ring[i] = p[i];
-    rn = n;
-  } else {
-    rn = db::offset_raw(q, qm, d, ring, kLocalPts);
-    if (rn > kLocalPts) {
-      list[atomicAdd(counters + 1, 1)] = (int)c;
-      return;
+  const P2 *ring = p;  // unclip returns the contour itself when there is no offset
+  int rn = n;
+  if (d != 0.) {
+    P2 *q = reinterpret_cast<P2 *>(
+        pool_alloc(pool, pool_counters, P.pool_bytes, (n + 1ull) * sizeof(P2), status));
+    if (!q) return;
+    const int m = db::offset_prepare(p, n, q);
+    if (m > 0) {
+      const int raw_n = db::offset_raw(q, m, d, nullptr, 0);
+      const int out_cap = 2 * raw_n + 64;
+      const unsigned long long raw_b = ((unsigned long long)raw_n * sizeof(P2) + 15) & ~15ull;
+      const unsigned long long out_b = ((unsigned long long)out_cap * sizeof(P2) + 15) & ~15ull;
+      char *w = pool_alloc(pool, pool_counters, P.pool_bytes,
+                           raw_b + out_b + db::cu::arena_bytes(raw_n), status);
+      if (!w) return;
+      P2 *raw = reinterpret_cast<P2 *>(w);
+      P2 *out = reinterpret_cast<P2 *>(w + raw_b);
+      db::offset_raw(q, m, d, raw, raw_n);
+      db::cu::Sweep sw;
+      sw.init(w + raw_b + out_b, raw_n);
+      int k = -1;
+      if (sw.execute(raw, raw_n)) k = sw.best_ring(out, out_cap);
+      if (k < 0) {  // sweep out of bounds: the raw ring stands in, flagged
+        atomicOr(status, kErrUnion);
+        ring = raw;
+        rn = raw_n;
+      } else if (k > 0) {
+        ring = out;
+        rn = k;
+      }
     }
   }
   if (rn < 3) return;
-  finish_box(rect_local(ring, rn), c, geo, keep2, boxes, P);
-}
-
-// offset_prepare by the whole CTA (same q, same length): the last point that
-// differs from p[0] bounds the path, consecutive repeats are dropped (a point
-// is kept when it differs from its predecessor, which is always the last
-// kept one), and the path is reversed when its shoelace sum is positive. The
-// shoelace terms are integers, so the int64 sum (any order, modular) equals
-// the sequential double sum. Returns the length, 0 when below 3.
-__device__ int cta_offset_prepare(const P2 *p, int n, P2 *q) {
-  __shared__ int s_hi;
-  __shared__ unsigned long long s_area;
-  const int t = threadIdx.x, T = blockDim.x, lane = t & 31;
-  if (t == 0) { s_hi = 0; s_area = 0ull; }
-  __syncthreads();
-  const P2 p0 = p[0];
-  int hi = 0;
-  for (int i = t; i < n; i += T)
-    if (p[i].x != p0.x || p[i].y != p0.y) hi = i;
-  for (int o = 16; o; o >>= 1) hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
-  if (lane == 0) atomicMax(&s_hi, hi);
-  __syncthreads();
-  const int len = s_hi + 1;
-  const int chunk = (len + T - 1) / T;
-  const int i0 = min(len, t * chunk), i1 = min(len, i0 + chunk);
-  auto kept = [&](int i) { return db::prep_kept(p, i); };
-  int cnt = 0;
-  for (int i = i0; i < i1; ++i) cnt += kept(i);
-  int m;
-  int pos = cta_inclusive_sum(cnt, &m) - cnt;
-  for (int i = i0; i < i1; ++i)
-    if (kept(i)) q[pos++] = p[i];
-  if (m < 3) return 0;
-  __syncthreads();
-  long long a = 0;
-  for (int i = t; i < m; i += T) a += db::shoelace_term(q, m, i);
-  for (int o = 16; o; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-  if (lane == 0) atomicAdd(&s_area, (unsigned long long)a);
-  __syncthreads();
-  if ((long long)s_area > 0)
-    for (int i = t; i < m / 2; i += T) {
-      const P2 u = q[i];
-      q[i] = q[m - 1 - i];
-      q[m - 1 - i] = u;
-    }
-  __syncthreads();
-  return m;
-}
-
-// One thread, global scratch: unclip ring of rn points and its min-area box.
-__device__ bool unclip_rect_global(const P2 *p, int n, double d, int rn, char *pool,
-                                   int *counters, unsigned long long pool_bytes, int *status,
-                                   RRect *r) {
-  P2 *q = reinterpret_cast<P2 *>(
-      pool_alloc(pool, counters, pool_bytes, (n + 1ull + rn) * sizeof(P2), status));
-  if (!q) return false;
-  P2 *ring = q + n + 1;
-  const int qm = (d == 0.) ? 0 : db::offset_prepare(p, n, q);
-  if (qm == 0) {
-    for (int i = 0; i < n; ++i) ring[i] = p[i];
-  } else {
-    db::offset_raw(q, qm, d, ring, rn);
+  RRect r;
+  if (rn <= kLocalPts) {
+    r = rect_local(ring, rn);
+  } else if (!rect_global(ring, rn, pool, pool_counters, P.pool_bytes, status, &r)) {
+    return;
   }
-  return rect_global(ring, rn, pool, counters, pool_bytes, status, r);
-}
-
-// 7'. one CTA per listed contour (grid-stride): the unclip ring goes
-// straight into the column table. Its vertices are emitted in parallel (a
-// thread per vertex, ring indices from a prefix sum of the per-vertex counts)
-// unless some joint keeps Clipper's previous vertex k (nearly straight
-// joints, only at distances below 1/sin 45 for contours), in which case
-// thread 0 emits serially. Then the CTA's min-area box and finish_box.
-__global__ void __launch_bounds__(kBigThreads)
-unclip_big_kernel(const int *__restrict__ list, const int *__restrict__ counters,
-                  const int *__restrict__ npts, const long long *__restrict__ pt_off,
-                  const P2 *__restrict__ pts, const int4 *__restrict__ aabb,
-                  const double *__restrict__ dist, const int *__restrict__ geo,
-                  int *__restrict__ keep2, int *__restrict__ boxes, char *__restrict__ pool,
-                  int *__restrict__ pool_counters, int *__restrict__ status, DbParams P) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  __shared__ int s_rn, s_fits;
-  __shared__ P2 *s_q;
-  const BigSmem S = big_smem(smem);
-  const int count = counters[1];
-  for (int li = blockIdx.x; li < count; li += gridDim.x) {
-    const int c = list[li];
-    const int n = npts[c];
-    const P2 *p = pts + pt_off[c];
-    const double d = dist[c];
-    const int4 bb = aabb[c];
-    // the ring stays within d + 1 of the contour's box
-    const bool near = d >= 0. && d < (double)kBigCols;
-    const int pad = near ? (int)ceil(d) + 2 : 0;
-    const int base = bb.x - pad, ncols = bb.z - bb.x + 1 + 2 * pad;
-    const bool in_smem = near && ncols <= P.big_cols;
-    if (threadIdx.x == 0) {
-      P2 *q = S.q;
-      if (d != 0. && n > kBigQPts)
-        q = reinterpret_cast<P2 *>(
-            pool_alloc(pool, pool_counters, P.pool_bytes, n * sizeof(P2), status));
-      s_q = q;
-    }
-    if (in_smem) table_clear(S, ncols);
-    __syncthreads();
-    P2 *q = s_q;
-    if (d != 0. && !q) {  // scratch pool exhausted (status set)
-      __syncthreads();
-      continue;
-    }
-    const int qm = d == 0. ? 0 : cta_offset_prepare(p, n, q);
-    int rn = 0;
-    bool fits = true;
-    if (qm == 0) {  // no offset: the ring is the contour itself
-      rn = n;
-      if (in_smem)
-        for (int i = threadIdx.x; i < n; i += blockDim.x) table_add(S, p[i].x - base, p[i].y, i);
-    } else {
-      const db::OffsetConsts oc = db::offset_consts(d);
-      const int chunk = (qm + blockDim.x - 1) / blockDim.x;
-      const int j0 = min(qm, (int)threadIdx.x * chunk), j1 = min(qm, j0 + chunk);
-      int cnt = 0;
-      bool keeps = false;
-      for (int j = j0; j < j1; ++j) {
-        const bool keep = db::offset_vertex(q, qm, j, j == 0 ? qm - 1 : j - 1, d, oc,
-                                            [&](long long, long long) { ++cnt; });
-        keeps |= keep && j < qm - 1;
-      }
-      const bool serial = __syncthreads_or(keeps || db::offset_is_identity(d)) != 0;
-      if (!serial) {
-        int idx = cta_inclusive_sum(cnt, &rn) - cnt;
-        if (in_smem) {
-          bool ok = true;
-          for (int j = j0; j < j1; ++j)
-            db::offset_vertex(q, qm, j, j == 0 ? qm - 1 : j - 1, d, oc,
-                              [&](long long x, long long y) {
-                                const long long col = x - base;
-                                if (col < 0 || col >= ncols || !db::col_y_fits(y)) ok = false;
-                                else table_add(S, (int)col, (int)y, idx);
-                                ++idx;
-                              });
-          fits = __syncthreads_or(!ok) == 0;
-        }
-      } else {
-        if (threadIdx.x == 0) {
-          bool ok = true;
-          int k = 0;
-          const int total = db::offset_emit(q, qm, d, [&](long long x, long long y) {
-            const long long col = x - base;
-            if (in_smem) {
-              if (col < 0 || col >= ncols || !db::col_y_fits(y)) {
-                ok = false;
-              } else {
-                const uint64_t a = db::col_lo_key((int)y, k), b = db::col_hi_key((int)y, k);
-                if (a < S.lo[col]) S.lo[col] = a;
-                if (b < S.hi[col]) S.hi[col] = b;
-              }
-            }
-            ++k;
-          });
-          s_rn = total;
-          s_fits = ok;
-        }
-        __syncthreads();
-        rn = s_rn;
-        fits = s_fits != 0;
-      }
-    }
-    __syncthreads();
-    RRect r{};
-    bool ok = false;
-    if (rn >= 3 && in_smem && fits) ok = cta_table_rect(S, ncols, base, &r);
-    if (threadIdx.x == 0 && rn >= 3) {
-      if (!ok) ok = unclip_rect_global(p, n, d, rn, pool, pool_counters, P.pool_bytes, status, &r);
-      if (ok) finish_box(r, c, geo, keep2, boxes, P);
-    }
-    __syncthreads();
-  }
+  finish_box(r, c, geo, keep2, boxes, P);
 }
 
 // 8. kept boxes of map m in contour order. grid n_maps, kScanThreads threads.
@@ -1298,7 +1151,7 @@ namespace {
 
 struct DbLayout {
   size_t bitmap, tile_bg, bits, slab, lab, scan_tot, row_count, row_off, n_contours, n_total,
-      starts, npts, pt_off, pts, stage1, aabb, stage2, score, dist, keep2, boxes, list1, list2, list3,
+      starts, npts, pt_off, pts, stage1, aabb, stage2, score, dist, keep2, boxes, list1, list3,
       counters, pool, ovf_first, ovf_next, ovf_pts, ovf_count, part_sum, part_cnt, score_done,
       total;
   int ovf_chunks;
@@ -1335,7 +1188,6 @@ DbLayout db_layout(int n_maps, int h, int w, long long point_cap, long long offs
   L.keep2 = take(C * 4);
   L.boxes = take(C * 8 * 4);
   L.list1 = take(C * 4);
-  L.list2 = take(C * 4);
   L.list3 = take(C * 4);
   L.counters = take(kCounters * 4);
   L.pool_bytes = (unsigned long long)offset_cap * kPoolBytesPerPoint;
@@ -1414,7 +1266,7 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
   P2 *pts = (P2 *)at(L.pts);
   float *score = (float *)at(L.score);
   int *stage1 = (int *)at(L.stage1), *stage2 = (int *)at(L.stage2), *keep2 = (int *)at(L.keep2),
-      *boxes = (int *)at(L.boxes), *list1 = (int *)at(L.list1), *list2 = (int *)at(L.list2),
+      *boxes = (int *)at(L.boxes), *list1 = (int *)at(L.list1),
       *list3 = (int *)at(L.list3),
       *counters = (int *)at(L.counters);
   char *pool = at(L.pool);
@@ -1435,9 +1287,6 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
 
   cudaError_t e = cudaFuncSetAttribute(geom_big_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)kBigSmem);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(unclip_big_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kBigSmem);
   if (e != cudaSuccess) return set_error(TOCR_ERR_CUDA, "db smem attribute: %s", cudaGetErrorString(e));
   e = cudaMemsetAsync(d_status, 0, sizeof(int), st);
   if (e != cudaSuccess) return set_error(TOCR_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
@@ -1463,11 +1312,8 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
   score_kernel<<<dim3((unsigned)(C < 148 * 8 ? C : 148 * 8), kScoreGroups), kScoreThreads, 0, st>>>(
       d_pred, list3, counters, aabb, npts, pt_off, pts, stage2, score, dist, part_sum, part_cnt,
       score_done, P);
-  unclip_kernel<<<cgrid, 128, 0, st>>>(stage2, npts, pt_off, pts, dist, d_geometry, keep2, boxes,
-                                       list2, counters, P);
-  unclip_big_kernel<<<bgrid, kBigThreads, kBigSmem, st>>>(list2, counters, npts, pt_off, pts, aabb,
-                                                          dist, d_geometry, keep2, boxes, pool,
-                                                          counters, d_status, P);
+  union_kernel<<<cgrid, 128, 0, st>>>(stage2, npts, pt_off, pts, dist, d_geometry, keep2, boxes,
+                                      pool, counters, d_status, P);
   compact_kernel<<<n_maps, kScanThreads, 0, st>>>(keep2, boxes, score, d_boxes, d_scores, d_counts,
                                                   d_status, max_boxes);
   return check_launch("tocr_db_postprocess");

@@ -107,7 +107,8 @@ def cuda_batch_threshold_to_u8(src: torch.Tensor, dst: torch.Tensor, w: int, h: 
 # ---- subsystem 3 ------------------------------------------------------------
 
 DB_STATUS_BITS = {1: "point pool full", 2: "border walk exceeded its bound",
-                  4: "geometry scratch pool full", 8: "more boxes than max_boxes (truncated)"}
+                  4: "geometry scratch pool full", 8: "more boxes than max_boxes (truncated)",
+                  16: "union sweep out of bounds (raw offset ring used)"}
 
 
 class DbPostprocess:
@@ -145,7 +146,7 @@ class DbPostprocess:
     def results(self, n: int | None = None) -> list[list[tuple[list[list[int]], float]]]:
         """Per map: [(quad [[x, y] * 4], score)] in contour order (synchronises)."""
         st = int(self.status.item())
-        if st & 7:
+        if st & 23:
             msgs = [m for b, m in DB_STATUS_BITS.items() if st & b]
             raise RuntimeError("tocr_db_postprocess: " + ", ".join(msgs))
         n = self.n_maps if n is None else n

@@ -72,6 +72,8 @@ class PagePipeline:
         self.prob = torch.empty(batch, H, W, dtype=torch.float32, device=device)
         if point_cap <= 0:
             point_cap = batch * 65536
+        if offset_cap <= 0:  # text-line rings: about 1 MB of unclip scratch per page
+            offset_cap = batch * 16384
         self.db = DbPostprocess(batch, H, W, device, max_boxes=max_boxes, point_cap=point_cap,
                                 offset_cap=offset_cap)
         nc = batch * max_boxes
