@@ -82,3 +82,23 @@ def test_union_rotated_shapes_and_blobs():
         for c in sorted(do.find_contours(bm), key=len)[-2:]:
             for ratio in (1.5, 0.6):
                 assert same_ring(c, ratio)
+
+
+def test_axis_rectangle_rings_need_no_union():
+    """The device skips the sweep for axis-aligned rectangle contours (text
+    lines): their round-join offset is a convex rounded rectangle, and its
+    min-area box equals the one of Clipper's union ring."""
+    rng = np.random.default_rng(3)
+    for _ in range(400):
+        bm = np.zeros((120, 200), np.uint8)
+        x0, y0 = rng.integers(2, 100), rng.integers(2, 60)
+        w, h = rng.integers(1, 95), rng.integers(1, 55)
+        bm[y0:y0 + h, x0:x0 + w] = 255
+        for c in do.find_contours(bm):
+            ratio = float(rng.uniform(0.2, 3.0))
+            d = do.unclip_distance(c, ratio)
+            if len(c) != 4 or d is None:
+                continue
+            raw = np.array(dn.offset_raw(c, d), np.int32).reshape(-1, 2)
+            full = np.asarray(do.unclip(c, ratio), np.int32).reshape(-1, 2)
+            assert do.get_mini_boxes(raw) == do.get_mini_boxes(full)

@@ -59,7 +59,7 @@ struct Edge {
   int bx, by, cx, cy, tx, ty;  // Bot, Curr, Top
   double dx;
   int wdelta, wcnt, wcnt2, out_idx, side;
-  int next, prev, next_lml, next_ael, prev_ael, next_sel, prev_sel;
+  int next, prev, next_lml, ael_pos, next_sel, prev_sel;
 };
 struct OutPt {
   int idx;
@@ -86,6 +86,8 @@ struct INode {
 struct Caps {
   int edges, minima, scan, outpts, outrecs, joins, ghosts, inodes, stack;
 };
+// per-scanbeam work arrays of the intersection list: 3 x edges + 1 x inodes
+// ints and a second INode array
 TG Caps caps_for(int n) {
   Caps c;
   // Peak use measured over ~50k contours (noise, rotated shapes, text maps,
@@ -114,7 +116,10 @@ TG unsigned long long arena_bytes(int n) {
          al(sizeof(Join) * (unsigned long long)c.joins) +
          al(sizeof(Join) * (unsigned long long)c.ghosts) +
          al(sizeof(INode) * (unsigned long long)c.inodes) +
-         al(sizeof(int) * 3ull * (unsigned long long)c.stack);
+         al(sizeof(int) * 3ull * (unsigned long long)c.stack) +
+         al(sizeof(int) * 4ull * (unsigned long long)(c.edges + 2)) +
+         al(sizeof(int) * (unsigned long long)c.inodes) +
+         al(sizeof(INode) * (unsigned long long)c.inodes);
 }
 
 // ------------------------------------------------------------ std::sort -------
@@ -238,9 +243,18 @@ struct Sweep {
   Join *GJ;
   INode *IN;
   int *STK;
+  int *ARR, *KEY, *SUF, *PASS;
+  INode *IN2;
   Caps cap;
   int n_edges, n_lm, cur_lm, n_sb, n_op, n_or, n_jn, n_gj, n_in;
-  int active, sorted;  // AEL head, SEL head
+  // The active edge list (AEL) is kept as an array in x order, AEL[0..
+  // ael_n), with each member's index in Edge::ael_pos (-1 when not in it):
+  // Clipper's NextInAEL / PrevInAEL are the neighbours in that array, and its
+  // walks become loops over it. Clipper only reads the links of an edge that
+  // is not in the AEL to learn that it is not there.
+  int *AEL;
+  int ael_n;
+  int sorted;  // SEL head
   long long guard, guard_limit;
   bool fail;
 
@@ -256,9 +270,17 @@ struct Sweep {
     JN = reinterpret_cast<Join *>(p); p += al(sizeof(Join) * (unsigned long long)cap.joins);
     GJ = reinterpret_cast<Join *>(p); p += al(sizeof(Join) * (unsigned long long)cap.ghosts);
     IN = reinterpret_cast<INode *>(p); p += al(sizeof(INode) * (unsigned long long)cap.inodes);
-    STK = reinterpret_cast<int *>(p);
+    STK = reinterpret_cast<int *>(p); p += al(sizeof(int) * 3ull * (unsigned long long)cap.stack);
+    ARR = reinterpret_cast<int *>(p);
+    KEY = ARR + (cap.edges + 2);
+    SUF = KEY + (cap.edges + 2);
+    AEL = SUF + (cap.edges + 2);
+    p += al(sizeof(int) * 4ull * (unsigned long long)(cap.edges + 2));
+    PASS = reinterpret_cast<int *>(p); p += al(sizeof(int) * (unsigned long long)cap.inodes);
+    IN2 = reinterpret_cast<INode *>(p);
     n_edges = n_lm = cur_lm = n_sb = n_op = n_or = n_jn = n_gj = n_in = 0;
-    active = sorted = kNil;
+    ael_n = 0;
+    sorted = kNil;
     fail = false;
     guard = 0;
     // Bound on the total number of loop steps of one sweep: about ten times
@@ -459,7 +481,8 @@ struct Sweep {
       e.out_idx = kUnassigned;
       e.next = i == hi ? 0 : i + 1;
       e.prev = i == 0 ? hi : i - 1;
-      e.next_lml = e.next_ael = e.prev_ael = e.next_sel = e.prev_sel = kNil;
+      e.next_lml = e.next_sel = e.prev_sel = kNil;
+      e.ael_pos = -1;
     }
     n_edges = hi + 1;
     int start = 0, e = 0, stop = 0;
@@ -541,33 +564,47 @@ struct Sweep {
     }
     return E[e2].cx < E[e1].cx;
   }
+  CU_HD int head() const { return ael_n > 0 ? AEL[0] : kNil; }
+  CU_HD int nxt(int e) const {
+    const int p = E[e].ael_pos;
+    return (p >= 0 && p + 1 < ael_n) ? AEL[p + 1] : kNil;
+  }
+  CU_HD int prv(int e) const {
+    const int p = E[e].ael_pos;
+    return p > 0 ? AEL[p - 1] : kNil;
+  }
+  CU_HD void ael_insert_at(int e, int pos) {
+    if (ael_n >= n_edges) { fail = true; return; }
+    for (int k = ael_n - 1; k >= pos; --k) {
+      const int m = AEL[k];
+      AEL[k + 1] = m;
+      E[m].ael_pos = k + 1;
+    }
+    AEL[pos] = e;
+    E[e].ael_pos = pos;
+    ++ael_n;
+  }
   CU_HD void insert_into_ael(int e, int start) {
-    if (active == kNil) {
-      E[e].prev_ael = E[e].next_ael = kNil;
-      active = e;
-    } else if (start == kNil && e2_inserts_before_e1(active, e)) {
-      E[e].prev_ael = kNil;
-      E[e].next_ael = active;
-      E[active].prev_ael = e;
-      active = e;
+    if (ael_n == 0) {
+      ael_insert_at(e, 0);
+    } else if (start == kNil && e2_inserts_before_e1(AEL[0], e)) {
+      ael_insert_at(e, 0);
     } else {
-      if (start == kNil) start = active;
-      while (E[start].next_ael != kNil && !e2_inserts_before_e1(E[start].next_ael, e)) {
-        if (!tick()) return;
-        start = E[start].next_ael;
-      }
-      E[e].next_ael = E[start].next_ael;
-      if (E[start].next_ael != kNil) E[E[start].next_ael].prev_ael = e;
-      E[e].prev_ael = start;
-      E[start].next_ael = e;
+      int k = start == kNil ? 0 : E[start].ael_pos;
+      while (k + 1 < ael_n && !e2_inserts_before_e1(AEL[k + 1], e)) ++k;
+      ael_insert_at(e, k + 1);
     }
   }
   CU_HD void delete_from_ael(int e) {
-    const int p = E[e].prev_ael, n = E[e].next_ael;
-    if (p == kNil && n == kNil && e != active) return;
-    if (p != kNil) E[p].next_ael = n; else active = n;
-    if (n != kNil) E[n].prev_ael = p;
-    E[e].next_ael = E[e].prev_ael = kNil;
+    const int p = E[e].ael_pos;
+    if (p < 0) return;
+    for (int k = p; k + 1 < ael_n; ++k) {
+      const int m = AEL[k + 1];
+      AEL[k] = m;
+      E[m].ael_pos = k;
+    }
+    --ael_n;
+    E[e].ael_pos = -1;
   }
   CU_HD void delete_from_sel(int e) {
     const int p = E[e].prev_sel, n = E[e].next_sel;
@@ -588,42 +625,20 @@ struct Sweep {
     }
   }
   CU_HD void copy_ael_to_sel() {
-    int e = active;
-    sorted = e;
-    while (e != kNil) {
-      if (!tick()) return;
-      E[e].prev_sel = E[e].prev_ael;
-      E[e].next_sel = E[e].next_ael;
-      e = E[e].next_ael;
+    sorted = head();
+    for (int k = 0; k < ael_n; ++k) {
+      const int e = AEL[k];
+      E[e].prev_sel = k > 0 ? AEL[k - 1] : kNil;
+      E[e].next_sel = k + 1 < ael_n ? AEL[k + 1] : kNil;
     }
   }
+  // SwapPositionsInAEL: both edges must be in the AEL (Clipper's test
+  // NextInAEL == PrevInAEL is true only for an edge outside it, or alone).
   CU_HD void swap_in_ael(int a, int b) {
-    if (E[a].next_ael == E[a].prev_ael || E[b].next_ael == E[b].prev_ael) return;
-    if (E[a].next_ael == b) {
-      const int nx = E[b].next_ael, pv = E[a].prev_ael;
-      if (nx != kNil) E[nx].prev_ael = a;
-      if (pv != kNil) E[pv].next_ael = b;
-      E[b].prev_ael = pv; E[b].next_ael = a;
-      E[a].prev_ael = b; E[a].next_ael = nx;
-    } else if (E[b].next_ael == a) {
-      const int nx = E[a].next_ael, pv = E[b].prev_ael;
-      if (nx != kNil) E[nx].prev_ael = b;
-      if (pv != kNil) E[pv].next_ael = a;
-      E[a].prev_ael = pv; E[a].next_ael = b;
-      E[b].prev_ael = a; E[b].next_ael = nx;
-    } else {
-      const int nx = E[a].next_ael, pv = E[a].prev_ael;
-      E[a].next_ael = E[b].next_ael;
-      if (E[a].next_ael != kNil) E[E[a].next_ael].prev_ael = a;
-      E[a].prev_ael = E[b].prev_ael;
-      if (E[a].prev_ael != kNil) E[E[a].prev_ael].next_ael = a;
-      E[b].next_ael = nx;
-      if (E[b].next_ael != kNil) E[E[b].next_ael].prev_ael = b;
-      E[b].prev_ael = pv;
-      if (E[b].prev_ael != kNil) E[E[b].prev_ael].next_ael = b;
-    }
-    if (E[a].prev_ael == kNil) active = a;
-    else if (E[b].prev_ael == kNil) active = b;
+    if (nxt(a) == prv(a) || nxt(b) == prv(b)) return;
+    const int pa = E[a].ael_pos, pb = E[b].ael_pos;
+    AEL[pa] = b; E[b].ael_pos = pa;
+    AEL[pb] = a; E[a].ael_pos = pb;
   }
   CU_HD void swap_in_sel(int a, int b) {
     if (E[a].next_sel == kNil && E[a].prev_sel == kNil) return;
@@ -658,9 +673,11 @@ struct Sweep {
     const int nl = E[e].next_lml;
     if (nl == kNil) { fail = true; return; }
     E[nl].out_idx = E[e].out_idx;
-    const int p = E[e].prev_ael, n = E[e].next_ael;
-    if (p != kNil) E[p].next_ael = nl; else active = nl;
-    if (n != kNil) E[n].prev_ael = nl;
+    const int pos = E[e].ael_pos;
+    if (pos < 0) { fail = true; return; }
+    AEL[pos] = nl;
+    E[nl].ael_pos = pos;
+    E[e].ael_pos = -1;
     E[nl].side = E[e].side;
     E[nl].wdelta = E[e].wdelta;
     E[nl].wcnt = E[e].wcnt;
@@ -668,20 +685,21 @@ struct Sweep {
     e = nl;
     E[e].cx = E[e].bx;
     E[e].cy = E[e].by;
-    E[e].prev_ael = p;
-    E[e].next_ael = n;
     if (!is_horz(e)) sb_push(E[e].ty);
   }
 
   // ---- winding (positive fill, subject only) --------------------------------
   CU_HD void set_winding_count(int ei) {
     Edge &edge = E[ei];
-    int e = edge.prev_ael;
-    while (e != kNil && E[e].wdelta == 0) { if (!tick()) return; e = E[e].prev_ael; }
+    int e = prv(ei), g = 0;
+    while (e != kNil && E[e].wdelta == 0) {
+      if (++g > n_edges) { fail = true; return; }
+      e = prv(e);
+    }
     if (e == kNil) {
       edge.wcnt = edge.wdelta == 0 ? 1 : edge.wdelta;
       edge.wcnt2 = 0;
-      e = active;
+      e = head();
     } else {
       const Edge &pe = E[e];
       if (pe.wcnt * pe.wdelta < 0) {
@@ -697,12 +715,12 @@ struct Sweep {
         else edge.wcnt = pe.wcnt + edge.wdelta;
       }
       edge.wcnt2 = pe.wcnt2;
-      e = pe.next_ael;
+      e = nxt(e);
     }
     while (e != ei) {
-      if (!tick()) return;
+      if (e == kNil || ++g > 2 * n_edges) { fail = true; return; }
       edge.wcnt2 += E[e].wdelta;
-      e = E[e].next_ael;
+      e = nxt(e);
     }
   }
   // positive fill for the subject, union with an empty positive clip side
@@ -710,14 +728,13 @@ struct Sweep {
 
   // ---- output polygons ------------------------------------------------------
   CU_HD void set_hole_state(int e, int orec) {
-    int e2 = E[e].prev_ael, tmp = kNil;
-    while (e2 != kNil) {
-      if (!tick()) return;
+    int tmp = kNil;
+    for (int k = E[e].ael_pos - 1; k >= 0; --k) {
+      const int e2 = AEL[k];
       if (E[e2].out_idx >= 0 && E[e2].wdelta != 0) {
         if (tmp == kNil) tmp = e2;
         else if (E[tmp].out_idx == E[e2].out_idx) tmp = kNil;
       }
-      e2 = E[e2].prev_ael;
     }
     if (tmp == kNil) {
       OR[orec].first_left = kNil;
@@ -766,14 +783,14 @@ struct Sweep {
       E[e1].side = kSideLeft;
       E[e2].side = kSideRight;
       e = e1;
-      prev_e = E[e].prev_ael == e2 ? E[e2].prev_ael : E[e].prev_ael;
+      prev_e = prv(e) == e2 ? prv(e2) : prv(e);
     } else {
       result = add_out_pt(e2, x, y);
       E[e1].out_idx = E[e2].out_idx;
       E[e1].side = kSideRight;
       E[e2].side = kSideLeft;
       e = e2;
-      prev_e = E[e].prev_ael == e1 ? E[e1].prev_ael : E[e].prev_ael;
+      prev_e = prv(e) == e1 ? prv(e1) : prv(e);
     }
     if (prev_e != kNil && E[prev_e].out_idx >= 0 && E[prev_e].ty < y && E[e].ty < y) {
       const long long xp = top_x(prev_e, y), xe = top_x(e, y);
@@ -916,8 +933,8 @@ struct Sweep {
     const int ok = E[e1].out_idx, obsolete = E[e2].out_idx;
     E[e1].out_idx = kUnassigned;
     E[e2].out_idx = kUnassigned;
-    for (int e = active; e != kNil; e = E[e].next_ael) {
-      if (!tick()) return;
+    for (int k = 0; k < ael_n; ++k) {
+      const int e = AEL[k];
       if (E[e].out_idx == obsolete) {
         E[e].out_idx = ok;
         E[e].side = E[e1].side;
@@ -1023,39 +1040,67 @@ struct Sweep {
     *ox = x;
     *oy = y;
   }
+  // Clipper's BuildIntersectList sorts a copy of the AEL (the SEL) by the
+  // edges' x at top_y with a bubble sort and records an intersection for
+  // every adjacent swap, in swap order. Restated exactly but without walking
+  // the whole list once per pass: the list splits into clusters at every
+  // position where the prefix maximum is <= the suffix minimum; no swap
+  // crosses such a position and every pass meets the clusters in list order
+  // (a pass's carrier enters a cluster below all of its keys and leaves it
+  // below all of the next one's), so each cluster is bubble-sorted on its
+  // own, its swaps tagged with their pass, and the records are put in (pass,
+  // cluster, swap) order. Equal keys never swap (strict comparison).
   CU_HD void build_intersect_list(long long top_y) {
-    if (active == kNil) return;
-    int e = active;
-    sorted = e;
-    while (e != kNil) {
-      if (!tick()) return;
-      E[e].prev_sel = E[e].prev_ael;
-      E[e].next_sel = E[e].next_ael;
-      E[e].cx = (int)top_x(e, top_y);
-      e = E[e].next_ael;
+    if (ael_n == 0) return;
+    int L = 0;
+    for (int k = 0; k < ael_n; ++k) {
+      const int e = AEL[k];
+      const int x = (int)top_x(e, top_y);
+      E[e].cx = x;
+      ARR[L] = e;
+      KEY[L] = x;
+      ++L;
     }
-    bool modified;
-    do {
-      modified = false;
-      e = sorted;
-      while (E[e].next_sel != kNil) {
-        if (!tick()) return;
-        const int en = E[e].next_sel;
-        if (E[e].cx > E[en].cx) {
-          long long px, py;
-          intersect_point(e, en, &px, &py);
-          if (py < top_y) { px = top_x(e, top_y); py = top_y; }
-          if (n_in >= cap.inodes) { fail = true; return; }
-          IN[n_in++] = INode{e, en, (int)px, (int)py};
-          swap_in_sel(e, en);
-          modified = true;
-        } else {
-          e = en;
+    SUF[L - 1] = KEY[L - 1];
+    for (int i = L - 2; i >= 0; --i) SUF[i] = KEY[i] < SUF[i + 1] ? KEY[i] : SUF[i + 1];
+    int n_nodes = 0, max_pass = 0;
+    int s = 0, pmax = KEY[0];
+    for (int i = 0; i < L; ++i) {
+      pmax = KEY[i] > pmax ? KEY[i] : pmax;
+      if (i + 1 < L && pmax > SUF[i + 1]) continue;  // cluster goes on
+      if (i > s) {  // cluster [s, i] (has an inversion): Clipper's passes on it
+        int end = i, pass = 0;
+        for (;;) {
+          bool modified = false;
+          for (int j = s + 1; j <= end; ++j) {
+            if (KEY[j - 1] > KEY[j]) {
+              const int a = ARR[j - 1], b = ARR[j];
+              long long px, py;
+              intersect_point(a, b, &px, &py);
+              if (py < top_y) { px = top_x(a, top_y); py = top_y; }
+              if (n_nodes >= cap.inodes) { fail = true; return; }
+              IN2[n_nodes] = INode{a, b, (int)px, (int)py};
+              PASS[n_nodes] = pass;
+              ++n_nodes;
+              ARR[j - 1] = b; ARR[j] = a;
+              const int k = KEY[j - 1]; KEY[j - 1] = KEY[j]; KEY[j] = k;
+              modified = true;
+            }
+          }
+          if (!tick()) return;
+          if (pass > max_pass) max_pass = pass;
+          ++pass;
+          if (!modified || --end <= s) break;
         }
       }
-      if (E[e].prev_sel != kNil) E[E[e].prev_sel].next_sel = kNil;
-      else break;
-    } while (modified);
+      s = i + 1;
+    }
+    // stable counting sort of the records by pass
+    for (int p2 = 0; p2 <= max_pass + 1; ++p2) SUF[p2] = 0;
+    for (int k = 0; k < n_nodes; ++k) ++SUF[PASS[k] + 1];
+    for (int p2 = 1; p2 <= max_pass + 1; ++p2) SUF[p2] += SUF[p2 - 1];
+    for (int k = 0; k < n_nodes; ++k) IN[SUF[PASS[k]]++] = IN2[k];
+    n_in = n_nodes;
     sorted = kNil;
   }
   CU_HD bool edges_adjacent(const INode &n) const {
@@ -1078,7 +1123,7 @@ struct Sweep {
     return true;
   }
   CU_HD bool process_intersections(long long top_y) {
-    if (active == kNil) return true;
+    if (ael_n == 0) return true;
     n_in = 0;
     build_intersect_list(top_y);
     if (fail) return false;
@@ -1106,7 +1151,7 @@ struct Sweep {
   }
   CU_HD int maxima_pair_ex(int e) const {
     const int r = maxima_pair(e);
-    if (r != kNil && E[r].next_ael == E[r].prev_ael && !is_horz(r)) return kNil;
+    if (r != kNil && nxt(r) == prv(r) && !is_horz(r)) return kNil;
     return r;
   }
   CU_HD static bool horz_overlap(long long a1, long long a2, long long b1, long long b2) {
@@ -1132,9 +1177,9 @@ struct Sweep {
     for (;;) {
       if (!tick()) return;
       const bool is_last = horz == last_h;
-      int e = l2r ? E[horz].next_ael : E[horz].prev_ael;
+      int e = l2r ? nxt(horz) : prv(horz), g = 0;
       while (e != kNil) {
-        if (!tick()) return;
+        if (++g > n_edges) { fail = true; return; }
         if ((l2r && E[e].cx > right) || (!l2r && E[e].cx < left)) break;
         if (E[e].cx == E[horz].tx && E[horz].next_lml != kNil && E[e].dx < E[E[horz].next_lml].dx)
           break;
@@ -1155,7 +1200,7 @@ struct Sweep {
         }
         if (l2r) intersect_edges(horz, e, E[e].cx, E[horz].cy);
         else intersect_edges(e, horz, E[e].cx, E[horz].cy);
-        const int en = l2r ? E[e].next_ael : E[e].prev_ael;
+        const int en = l2r ? nxt(e) : prv(e);
         swap_in_ael(horz, e);
         e = en;
       }
@@ -1180,7 +1225,7 @@ struct Sweep {
         update_edge_into_ael(horz);
         if (fail) return;
         if (E[horz].wdelta == 0) return;
-        const int ep = E[horz].prev_ael, en = E[horz].next_ael;
+        const int ep = prv(horz), en = nxt(horz);
         if (ep != kNil && E[ep].cx == E[horz].bx && E[ep].cy == E[horz].by && E[ep].wdelta != 0 &&
             E[ep].out_idx >= 0 && E[ep].cy > E[ep].ty && slopes_edges(horz, ep)) {
           const int op2 = add_out_pt(ep, E[horz].bx, E[horz].by);
@@ -1236,27 +1281,27 @@ struct Sweep {
             add_join(g.op1, op1, g.offx, g.offy);
         }
       }
-      const int lp = E[lb].prev_ael;
+      const int lp = prv(lb);
       if (E[lb].out_idx >= 0 && lp != kNil && E[lp].cx == E[lb].bx && E[lp].out_idx >= 0 &&
           slopes4(E[lp].bx, E[lp].by, E[lp].tx, E[lp].ty, E[lb].cx, E[lb].cy, E[lb].tx, E[lb].ty) &&
           E[lb].wdelta != 0 && E[lp].wdelta != 0) {
         const int op2 = add_out_pt(lp, E[lb].bx, E[lb].by);
         add_join(op1, op2, E[lb].tx, E[lb].ty);
       }
-      if (E[lb].next_ael != rb) {
-        const int rp = E[rb].prev_ael;
+      if (nxt(lb) != rb) {
+        const int rp = prv(rb);
         if (E[rb].out_idx >= 0 && E[rp].out_idx >= 0 &&
             slopes4(E[rp].cx, E[rp].cy, E[rp].tx, E[rp].ty, E[rb].cx, E[rb].cy, E[rb].tx, E[rb].ty) &&
             E[rb].wdelta != 0 && E[rp].wdelta != 0) {
           const int op2 = add_out_pt(rp, E[rb].bx, E[rb].by);
           add_join(op1, op2, E[rb].tx, E[rb].ty);
         }
-        int e = E[lb].next_ael;
+        int e = nxt(lb);
         if (e != kNil) {
           while (e != rb) {
-            if (!tick()) return;
+            if (e == kNil || !tick()) { fail = true; return; }
             intersect_edges(rb, e, E[lb].cx, E[lb].cy);
-            e = E[e].next_ael;
+            e = nxt(e);
           }
         }
       }
@@ -1271,12 +1316,12 @@ struct Sweep {
       delete_from_ael(e);
       return;
     }
-    int en = E[e].next_ael;
+    int en = nxt(e);
     while (en != kNil && en != mp) {
       if (!tick()) return;
       intersect_edges(e, en, E[e].tx, E[e].ty);
       swap_in_ael(e, en);
-      en = E[e].next_ael;
+      en = nxt(e);
     }
     if (E[e].out_idx == kUnassigned && E[mp].out_idx == kUnassigned) {
       delete_from_ael(e);
@@ -1289,44 +1334,45 @@ struct Sweep {
       fail = true;  // Clipper throws "DoMaxima error"
     }
   }
+  // ProcessEdgesAtTopOfScanbeam, walking the AEL array by index: after
+  // DoMaxima Clipper resumes at ePrev->NextInAEL, which is the same index
+  // (DoMaxima only moves and removes edges from e onwards).
   CU_HD void process_edges_at_top(long long top_y) {
-    int e = active;
-    while (e != kNil) {
-      if (!tick()) return;
+    int k = 0, g = 0;
+    while (k < ael_n) {
+      if (++g > 2 * n_edges + 16) { fail = true; return; }
+      int e = AEL[k];
       bool is_max = E[e].ty == top_y && E[e].next_lml == kNil;
       if (is_max) {
         const int mp = maxima_pair_ex(e);
         is_max = mp == kNil || !is_horz(mp);
       }
       if (is_max) {
-        const int ep = E[e].prev_ael;
         do_maxima(e);
         if (fail) return;
-        e = ep == kNil ? active : E[ep].next_ael;
-      } else {
-        if (E[e].ty == top_y && E[e].next_lml != kNil && is_horz(E[e].next_lml)) {
-          update_edge_into_ael(e);
-          if (fail) return;
-          if (E[e].out_idx >= 0) add_out_pt(e, E[e].bx, E[e].by);
-          add_to_sel(e);
-        } else {
-          E[e].cx = (int)top_x(e, top_y);
-          E[e].cy = (int)top_y;
-        }
-        e = E[e].next_ael;
+        continue;
       }
+      if (E[e].ty == top_y && E[e].next_lml != kNil && is_horz(E[e].next_lml)) {
+        update_edge_into_ael(e);
+        if (fail) return;
+        if (E[e].out_idx >= 0) add_out_pt(e, E[e].bx, E[e].by);
+        add_to_sel(e);
+      } else {
+        E[e].cx = (int)top_x(e, top_y);
+        E[e].cy = (int)top_y;
+      }
+      ++k;
     }
     process_horizontals();
     if (fail) return;
-    e = active;
-    while (e != kNil) {
-      if (!tick()) return;
+    for (k = 0; k < ael_n; ++k) {
+      int e = AEL[k];
       if (E[e].ty == top_y && E[e].next_lml != kNil) {
         int op = kNil;
         if (E[e].out_idx >= 0) op = add_out_pt(e, E[e].tx, E[e].ty);
         update_edge_into_ael(e);
         if (fail) return;
-        const int ep = E[e].prev_ael, en = E[e].next_ael;
+        const int ep = prv(e), en = nxt(e);
         if (ep != kNil && E[ep].cx == E[e].bx && E[ep].cy == E[e].by && op != kNil &&
             E[ep].out_idx >= 0 && E[ep].cy > E[ep].ty &&
             slopes4(E[e].cx, E[e].cy, E[e].tx, E[e].ty, E[ep].cx, E[ep].cy, E[ep].tx, E[ep].ty) &&
@@ -1342,7 +1388,6 @@ struct Sweep {
           add_join(op, op2, E[e].tx, E[e].ty);
         }
       }
-      e = E[e].next_ael;
     }
   }
 
@@ -1681,7 +1726,7 @@ struct Sweep {
       E[l].cx = E[l].bx; E[l].cy = E[l].by; E[l].side = kSideLeft; E[l].out_idx = kUnassigned;
       E[r].cx = E[r].bx; E[r].cy = E[r].by; E[r].side = kSideRight; E[r].out_idx = kUnassigned;
     }
-    active = kNil;
+    ael_n = 0;
     sorted = kNil;
     long long bot_y, top_y;
     if (!pop_scanbeam(&bot_y)) return !fail;

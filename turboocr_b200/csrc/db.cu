@@ -1039,6 +1039,15 @@ __device__ void finish_box(const RRect &rr, long long c, const int *geo, int *ke
   keep2[c] = 1;
 }
 
+// True when the prepared path is an axis-aligned rectangle (4 points, edges
+// alternately horizontal and vertical): text-line contours.
+__device__ __forceinline__ bool axis_rect(const P2 *q, int m) {
+  if (m != 4) return false;
+  const bool h0 = q[0].y == q[1].y && q[2].y == q[3].y && q[1].x == q[2].x && q[3].x == q[0].x;
+  const bool v0 = q[0].x == q[1].x && q[2].x == q[3].x && q[1].y == q[2].y && q[3].y == q[0].y;
+  return h0 || v0;
+}
+
 // 7. one thread per surviving contour slot: unclip (det_postprocess.cpp
 // :57-102) as the reference computes it, i.e. Clipper's raw round-join
 // offset (DoOffset) followed by the union of that path with positive fill
@@ -1078,17 +1087,24 @@ union_kernel(const int *__restrict__ stage2, const int *__restrict__ npts,
       P2 *raw = reinterpret_cast<P2 *>(w);
       P2 *out = reinterpret_cast<P2 *>(w + raw_b);
       db::offset_raw(q, m, d, raw, raw_n);
-      db::cu::Sweep sw;
-      sw.init(w + raw_b + out_b, raw_n);
-      int k = -1;
-      if (sw.execute(raw, raw_n)) k = sw.best_ring(out, out_cap);
-      if (k < 0) {  // sweep out of bounds: the raw ring stands in, flagged
-        atomicOr(status, kErrUnion);
+      if (axis_rect(q, m)) {
+        // an axis-aligned rectangle's offset is a convex rounded rectangle:
+        // the union only drops collinear points, which moves no box corner
         ring = raw;
         rn = raw_n;
-      } else if (k > 0) {
-        ring = out;
-        rn = k;
+      } else {
+        db::cu::Sweep sw;
+        sw.init(w + raw_b + out_b, raw_n);
+        int k = -1;
+        if (sw.execute(raw, raw_n)) k = sw.best_ring(out, out_cap);
+        if (k < 0) {  // sweep out of bounds: the raw ring stands in, flagged
+          atomicOr(status, kErrUnion);
+          ring = raw;
+          rn = raw_n;
+        } else if (k > 0) {
+          ring = out;
+          rn = k;
+        }
       }
     }
   }
