@@ -148,6 +148,18 @@ TOCR_API int tocr_preprocess_batch_f32(
     int dst_w, int dst_h, int batch_size, const float *mean3,
     const float *inv_std3, void *stream);
 
+/* Replaces cuda_fused_resize_normalize_det (include/turbo_ocr/kernels/
+ * kernels.h:33-35, src/kernels/preprocess_kernels.cu:58-97): one u8 HWC image
+ * (pitch src_step) resized to the whole dst_h x dst_w canvas (no letterbox),
+ * normalised, CHW. The image descriptor is passed by value to the kernel, so
+ * nothing is staged in device memory. dst_w must be a multiple of 8. */
+TOCR_API int tocr_preprocess_one_f32(const void *d_src, int src_step, int src_h, int src_w,
+                                     float *dst_f32, int dst_w, int dst_h, const float *mean3,
+                                     const float *inv_std3, void *stream);
+TOCR_API int tocr_preprocess_one_f16(const void *d_src, int src_step, int src_h, int src_w,
+                                     void *dst_f16, int dst_w, int dst_h, const float *mean3,
+                                     const float *inv_std3, void *stream);
+
 /* ---- DB threshold (replaces cuda_batch_threshold_to_u8) ----------------- */
 
 /* src/kernels/reduce_kernels.cu:97-151: dst = src > thresh ? 255 : 0 over
@@ -206,6 +218,22 @@ TOCR_API size_t tocr_db_components_scratch_bytes(int n_maps, int h, int w);
 TOCR_API int tocr_db_components(const float *d_pred, int n_maps, int h, int w, float thresh,
                                 int *d_labels, uint8_t *d_bitmap, void *d_scratch, void *stream);
 
+/* Replaces cuda_gpu_ccl_detect (include/turbo_ocr/kernels/kernels.h:131-145,
+ * src/kernels/ccl_kernels.cu:387-493): 8-connected components of the 255/0
+ * bitmap [h][w], per component the box, pixel count and mean of d_pred, kept
+ * when pixel_count >= 3, both sides >= 3 and mean >= box_thresh. Components
+ * are numbered in raster order of their first pixel (at most 3000); kept
+ * boxes (56-byte GpuDetBox records) in that order. Caller buffers as the
+ * reference: d_labels / d_compact_ids int[w*h], d_id_counter int[1],
+ * d_bboxes 2*3000 records, d_num_boxes int[1]; h_boxes >= 3000 records
+ * (pinned). Synchronises `stream` once (the reference's contract);
+ * *h_num_boxes = kept count, *h_num_total (optional) = components found. */
+TOCR_API int tocr_gpu_ccl_detect(const uint8_t *d_bitmap, const float *d_pred, int w, int h,
+                                 float box_thresh, int *d_labels, int *d_compact_ids,
+                                 int *d_id_counter, void *d_bboxes, int *d_num_boxes,
+                                 void *h_boxes, int *h_num_boxes, int *h_num_total,
+                                 void *stream);
+
 /* ---- recognition crops (replace the host-side crop loop of PaddleRec) ----- */
 
 /* compute_crop_transform (include/turbo_ocr/common/geometry/perspective.h:25-67,
@@ -230,6 +258,36 @@ TOCR_API int tocr_roi_warp_f16(const uint8_t *d_pages, long long page_stride, in
                                const int *d_crop_page, const int *d_n_crops, int max_crops,
                                int dst_h, int dst_w, const float *mean3, const float *inv_std3,
                                float inv_scale, void *d_dst, void *stream);
+
+/* Replaces cuda_batch_roi_warp (include/turbo_ocr/kernels/kernels.h:19-25,
+ * src/kernels/preprocess_kernels.cu:211-344) with its signature's meaning:
+ * batch_size crops of ONE u8 HWC image (pitch src_step), transforms d_minv
+ * [batch][9] and widths d_crop_w [batch], fp32 output [batch][3][dst_h]
+ * [dst_w] = (p * inv_scale - mean_c) * inv_std_c in RGB order, zero beyond
+ * each crop's width. mean3 / inv_std3 NULL: 0.5 / 2.0 (recognition). */
+TOCR_API int tocr_roi_warp_f32(const uint8_t *d_src, int src_h, int src_w, int src_step,
+                               const float *d_minv, const int *d_crop_w, int batch_size,
+                               int dst_h, int dst_w, const float *mean3, const float *inv_std3,
+                               float inv_scale, float *d_dst, void *stream);
+
+/* ---- stand-in network heads (no trained weights in this build) ------------- */
+
+/* The detection module's stand-in for the trained DB network (the synthetic
+ * pages' probability map): from the normalised fp32 canvas [n][3][h][w],
+ * ink = 1 - mean of the de-normalised channels (0 outside each image's
+ * letterbox content d_content_hw [n][2], NULL = whole canvas), 15-pixel
+ * horizontal max, prob = sigmoid(gain * (max - 0.5)) into d_prob [n][h][w].
+ * mean3 / inv_std3 NULL: the det normalisation. */
+TOCR_API int tocr_det_standin_prob_f32(const float *d_chw, int n, int h, int w,
+                                       const int *d_content_hw, const float *mean3,
+                                       const float *inv_std3, float gain, float *d_prob,
+                                       void *stream);
+/* The recognition module's stand-in for the trained CRNN: fp16 logits
+ * [n][seq_len][num_classes], 0 except 16.0 at one class per step; crop c's
+ * class at step t is drawn from (seed, id = d_ids[c] or c when NULL, t / 3):
+ * blank with probability 1/2, else uniform over 1..num_classes-1. */
+TOCR_API int tocr_rec_standin_logits_f16(void *d_logits, const int *d_ids, int n, int seq_len,
+                                         int num_classes, uint64_t seed, void *stream);
 
 /* tocr_ctc_greedy_f16 for a line count that lives on the device: lines
  * [0, min(*d_batch, max_batch)) of d_logits [max_batch][seq_len][num_classes]

@@ -8,11 +8,22 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include "turbo_ocr/common/geometry/perspective_math.h"
 #include "turbo_ocr/decode/gpu_image.h"
 
 namespace turbo_ocr::kernels {
 
 using decode::GpuImage;
+
+// kernels.h:19-25 — ROI warp of batch_size crops of one source image into
+// [batch][3][dst_h][dst_w] fp32: inverse-perspective bilinear sample, BGR->RGB,
+// (p * inv_scale - mean_c) * inv_std_c, zero beyond each crop's width. The
+// defaults are the recognizer's (p / 255 - 0.5) / 0.5.
+void cuda_batch_roi_warp(const GpuImage &src, const float *d_M_invs, const int *d_crop_widths,
+                         float *d_dst_batch, int batch_size, int dst_h, int dst_w,
+                         cudaStream_t stream = 0, float mean0 = 0.5f, float mean1 = 0.5f,
+                         float mean2 = 0.5f, float inv_std0 = 2.0f, float inv_std1 = 2.0f,
+                         float inv_std2 = 2.0f, float inv_scale = 1.0f / 255.0f);
 
 // kernels.h:27-30 — per-row max value + lowest index of the max.
 void cuda_argmax(const float *input_probs, int *output_indices, float *output_scores,
@@ -37,5 +48,35 @@ void cuda_batch_threshold_to_u8(const float *src, uint8_t *dst, int w, int h, in
 // kernels.h:110-111
 void cuda_threshold_to_u8(const float *src, uint8_t *dst, int w, int h, float thresh,
                           cudaStream_t stream = 0);
+
+// kernels.h:114-118 — forwards to turbo_ocr::compute_perspective_inv.
+inline void compute_perspective_inv(const float *dst_pts, const float *src_pts, float *M_inv) {
+  turbo_ocr::compute_perspective_inv(dst_pts, src_pts, M_inv);
+}
+
+// kernels.h:118-130 — one connected component (resize coordinates).
+struct GpuDetBox {
+  int xmin, ymin, xmax, ymax;
+  float score;      // mean prediction over the component's pixels
+  int pixel_count;
+  float ox[4], oy[4];  // oriented corners; not filled by cuda_gpu_ccl_detect
+};
+static constexpr int kMaxGpuComponents = 3000;
+
+// kernels.h:131-145 — 8-connected labelling of the 255/0 bitmap, per-component
+// box, pixel count and mean prediction, kept when pixel_count >= 3, both box
+// sides >= 3 and mean >= box_thresh. Synchronises `stream` once; returns the
+// kept count (also in *h_num_boxes), boxes in h_boxes (at least
+// kMaxGpuComponents entries, pinned). Components are numbered in raster order
+// of their first pixel, at most kMaxGpuComponents (the reference numbers them
+// in an unspecified order, so its output order is unspecified too).
+// Buffers: d_labels / d_compact_ids int[w*h], d_id_counter int[1],
+// d_bboxes GpuDetBox[2 * kMaxGpuComponents], d_num_boxes int[1]; all
+// allocated by the caller. *h_num_total (optional) receives the number of
+// components before the cap and the filter.
+int cuda_gpu_ccl_detect(const uint8_t *d_bitmap, const float *d_pred_map, int w, int h,
+                        float box_thresh, int *d_labels, int *d_compact_ids, int *d_id_counter,
+                        GpuDetBox *d_bboxes, int *d_num_boxes, GpuDetBox *h_boxes,
+                        int *h_num_boxes, cudaStream_t stream, int *h_num_total = nullptr);
 
 }  // namespace turbo_ocr::kernels

@@ -18,6 +18,12 @@ namespace turbo_ocr::recognition {
     const int *indices, const float *scores, int seq_len,
     const std::vector<std::string> &label_list);
 
+// ctc_decode.h:15-17 — per step the argmax of raw scores (first maximum), then
+// the same collapse; the line score is the mean emitted maximum.
+[[nodiscard]] std::pair<std::string, float> ctc_greedy_decode_raw(
+    const float *logits, int seq_len, int num_classes,
+    const std::vector<std::string> &label_list);
+
 // Text of an already-collapsed token list (the GPU decode's output).
 [[nodiscard]] std::string ctc_tokens_to_text(const int *tokens, int n_tokens,
                                              const std::vector<std::string> &label_list);

@@ -16,6 +16,11 @@ def lib():
         L.refk_argmax.argtypes = [C.c_void_p] * 3 + [C.c_int] * 3 + [C.c_void_p]
         L.refk_threshold.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                      C.c_float, C.c_void_p]
+        L.refk_roi_warp.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_longlong, C.c_void_p,
+                                    C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
+                                    C.c_void_p]
+        L.refk_fused_single.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_longlong, C.c_void_p,
+                                        C.c_int, C.c_int, C.c_void_p]
         L._tocr_ready = True
     return L
 

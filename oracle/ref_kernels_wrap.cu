@@ -59,4 +59,20 @@ int refk_roi_warp(const void *src, int rows, int cols, long long step, const flo
   }
   return 0;
 }
+
+int refk_fused_single(const void *src, int rows, int cols, long long step, float *dst, int dst_w,
+                      int dst_h, void *stream) {
+  try {
+    turbo_ocr::GpuImage img;
+    img.data = const_cast<void *>(src);
+    img.step = (std::size_t)step;
+    img.rows = rows;
+    img.cols = cols;
+    turbo_ocr::kernels::cuda_fused_resize_normalize_det(img, dst, dst_w, dst_h,
+                                                        (cudaStream_t)stream);
+  } catch (const std::exception &) {
+    return 2;
+  }
+  return 0;
+}
 }

@@ -79,6 +79,13 @@ SIGNATURES: dict[str, tuple] = {
     "tocr_roi_warp_f16": (_i, [_vp, _ll, _i, _i, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _f,
                                _vp, _vp]),
     "tocr_ctc_greedy_f16_dev": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "tocr_preprocess_one_f32": (_i, [_vp, _i, _i, _i, _vp, _i, _i, _vp, _vp, _vp]),
+    "tocr_preprocess_one_f16": (_i, [_vp, _i, _i, _i, _vp, _i, _i, _vp, _vp, _vp]),
+    "tocr_roi_warp_f32": (_i, [_vp, _i, _i, _i, _vp, _vp, _i, _i, _i, _vp, _vp, _f, _vp, _vp]),
+    "tocr_det_standin_prob_f32": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp, _f, _vp, _vp]),
+    "tocr_rec_standin_logits_f16": (_i, [_vp, _vp, _i, _i, _i, _u64, _vp]),
+    "tocr_gpu_ccl_detect": (_i, [_vp, _vp, _i, _i, _f, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                 _vp]),
     "tocr_compute_det_resize": (_i, [_i, _i, _i, _i, _i, _vp, _vp]),
     "tocr_read_det_resize": (_i, [_vp, _vp, _vp]),
     "tocr_effective_det_max_side": (_i, [_i]),

@@ -36,7 +36,7 @@ LIBS = {
 }
 # C++ host sources (reference-signature shims), built into libtocr_b200.so.
 HOST_SOURCES = {
-    "libtocr_b200.so": ["shim_kernels.cpp", "shim_ctc.cpp", "det_config_capi.cpp"],
+    "libtocr_b200.so": ["shim_kernels.cpp", "shim_ctc.cpp", "det_config_capi.cpp", "modules.cpp"],
 }
 HEADERS = sorted(list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list(INCLUDE.rglob("*.h")))
 
@@ -48,7 +48,8 @@ def _newest_header() -> float:
 # Per-file extra flags. db.cu and crop.cu must not contract multiply-adds:
 # they reproduce the floating-point operation order of OpenCV, Clipper and
 # the reference's host geometry (explicit fma() where those contract).
-EXTRA = {"db.cu": ["-fmad=false"], "crop.cu": ["-fmad=false"]}
+EXTRA = {"db.cu": ["-fmad=false"], "crop.cu": ["-fmad=false"],
+         "modules.cpp": ["-Xcompiler", "-ffp-contract=off"]}
 
 
 def _compile(src: Path, obj: Path, verbose: bool) -> None:

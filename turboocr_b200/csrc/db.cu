@@ -144,7 +144,8 @@ __device__ __forceinline__ void union_s(int *par, int a, int b) {
   }
 }
 
-// 1. threshold + tile-local labelling, run based: a warp owns a tile row, the
+// 1. threshold (pred non-null; else the bitmap is the input) + tile-local
+// labelling, run based: a warp owns a tile row, the
 // row's foreground mask is one ballot, and every pixel starts out pointing at
 // the first pixel of its same-colour run. Unions are then only made where runs
 // of consecutive rows meet: at the first pixel of an overlap (one of the two
@@ -168,8 +169,12 @@ ccl_local_kernel(const float *__restrict__ pred, uint8_t *__restrict__ bitmap, i
     const int y = ty0 + ly;
     bool f = false;
     if (x < W && y < H) {
-      f = pred[base + (size_t)y * W + x] > thresh;
-      bitmap[base + (size_t)y * W + x] = f ? 255 : 0;
+      if (pred) {  // threshold the map; else label the given bitmap
+        f = pred[base + (size_t)y * W + x] > thresh;
+        bitmap[base + (size_t)y * W + x] = f ? 255 : 0;
+      } else {
+        f = bitmap[base + (size_t)y * W + x] != 0;
+      }
     }
     const unsigned fg = __ballot_sync(0xffffffffu, f) & in_row;
     // run starts: first pixel of the tile row, or colour differs from the left
@@ -1158,6 +1163,168 @@ compact_kernel(const int *__restrict__ keep2, const int *__restrict__ boxes,
   }
 }
 
+// ---- cuda_gpu_ccl_detect (ccl_kernels.cu:241-493): per-component boxes ------
+// GpuDetBox of include/turbo_ocr/kernels/kernels.h:118-126.
+struct CclBox {
+  int xmin, ymin, xmax, ymax;
+  float score;
+  int pixel_count;
+  float ox[4], oy[4];
+};
+constexpr int kMaxGpuComponents = 3000;
+
+// Foreground roots per row (a root is a pixel labelled with itself).
+__global__ void __launch_bounds__(256)
+ccl_root_count_kernel(const uint8_t *__restrict__ bitmap, const int *__restrict__ lab, int H, int W,
+                      int *__restrict__ row_count) {
+  __shared__ int s;
+  if (threadIdx.x == 0) s = 0;
+  __syncthreads();
+  const int y = blockIdx.x;
+  int c = 0;
+  for (int x = threadIdx.x; x < W; x += blockDim.x) {
+    const int p = y * W + x;
+    c += bitmap[p] != 0 && lab[p] == p + 1;
+  }
+  for (int o = 16; o; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+  if ((threadIdx.x & 31) == 0) atomicAdd(&s, c);
+  __syncthreads();
+  if (threadIdx.x == 0) row_count[y] = s;
+}
+
+// Exclusive scan of the row counts (one CTA), total into *total.
+__global__ void __launch_bounds__(1024)
+ccl_root_scan_kernel(int *__restrict__ row, int H, int *__restrict__ total) {
+  __shared__ int s_w[32];
+  __shared__ int s_carry;
+  if (threadIdx.x == 0) s_carry = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  for (int y0 = 0; y0 < H; y0 += 1024) {
+    const int y = y0 + threadIdx.x;
+    const int v = y < H ? row[y] : 0;
+    int x = v;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += t;
+    }
+    if (lane == 31) s_w[wid] = x;
+    __syncthreads();
+    if (wid == 0) {
+      int w = s_w[lane];
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += t;
+      }
+      s_w[lane] = w;
+    }
+    __syncthreads();
+    const int incl = x + (wid > 0 ? s_w[wid - 1] : 0) + s_carry;
+    if (y < H) row[y] = incl - v;
+    __syncthreads();
+    if (threadIdx.x == 1023) s_carry = incl;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *total = s_carry;
+}
+
+// Compact id of every root in raster order (ids >= 3000 become -1), written
+// at the root pixel. One CTA per row, 256-pixel chunks.
+__global__ void __launch_bounds__(256)
+ccl_root_ids_kernel(const uint8_t *__restrict__ bitmap, const int *__restrict__ lab, int H, int W,
+                    const int *__restrict__ row_off, int *__restrict__ cid) {
+  __shared__ int s_w[8];
+  __shared__ int s_carry;
+  const int y = blockIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (threadIdx.x == 0) s_carry = row_off[y];
+  __syncthreads();
+  for (int x0 = 0; x0 < W; x0 += 256) {
+    const int x = x0 + threadIdx.x, p = y * W + x;
+    const bool root = x < W && bitmap[p] != 0 && lab[p] == p + 1;
+    const unsigned b = __ballot_sync(0xffffffffu, root);
+    if (lane == 0) s_w[wid] = __popc(b);
+    __syncthreads();
+    int before = s_carry;
+    for (int k = 0; k < wid; ++k) before += s_w[k];
+    if (root) {
+      const int id = before + __popc(b & ((1u << lane) - 1u));
+      cid[p] = id < kMaxGpuComponents ? id : -1;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0)
+      for (int k = 0; k < 8; ++k) s_carry += s_w[k];
+    __syncthreads();
+  }
+}
+
+// Every pixel: its root's compact id (-1 for background); and the per-id
+// box / pixel count / prediction sum.
+__global__ void __launch_bounds__(256)
+ccl_extract_kernel(const uint8_t *__restrict__ bitmap, const int *__restrict__ lab,
+                   const float *__restrict__ pred, int H, int W, int *__restrict__ cid,
+                   CclBox *__restrict__ boxes) {
+  const long long n = (long long)H * W;
+  for (long long p = (long long)blockIdx.x * blockDim.x + threadIdx.x; p < n;
+       p += (long long)gridDim.x * blockDim.x) {
+    if (bitmap[p] == 0) { cid[p] = -1; continue; }
+    const int r = lab[p] - 1;
+    const int id = cid[r];  // the root's entry (roots write only their own value)
+    if (r != p) cid[p] = id;
+    if (id < 0) continue;
+    const int x = (int)(p % W), y = (int)(p / W);
+    CclBox &b = boxes[id];
+    atomicMin(&b.xmin, x);
+    atomicMax(&b.xmax, x);
+    atomicMin(&b.ymin, y);
+    atomicMax(&b.ymax, y);
+    atomicAdd(&b.pixel_count, 1);
+    atomicAdd(&b.score, pred[p]);
+  }
+}
+
+__global__ void ccl_box_init_kernel(CclBox *__restrict__ boxes) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= kMaxGpuComponents) return;
+  CclBox b{};
+  b.xmin = b.ymin = INT_MAX;
+  boxes[i] = b;
+}
+
+// The reference filter (ccl_kernels.cu:346-368): pixel_count >= 3, box sides
+// >= 3, mean >= box_thresh; kept boxes in compact-id order (one CTA).
+__global__ void __launch_bounds__(1024)
+ccl_box_filter_kernel(const CclBox *__restrict__ in, float box_thresh, CclBox *__restrict__ out,
+                      int *__restrict__ count) {
+  __shared__ int s_w[32];
+  __shared__ int s_carry;
+  if (threadIdx.x == 0) s_carry = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  for (int i0 = 0; i0 < kMaxGpuComponents; i0 += 1024) {
+    const int i = i0 + threadIdx.x;
+    CclBox b{};
+    bool keep = false;
+    if (i < kMaxGpuComponents) {
+      b = in[i];
+      if (b.pixel_count >= 3 && b.xmax - b.xmin + 1 >= 3 && b.ymax - b.ymin + 1 >= 3) {
+        b.score = b.score / (float)b.pixel_count;
+        keep = !(b.score < box_thresh);
+      }
+    }
+    const unsigned bal = __ballot_sync(0xffffffffu, keep);
+    if (lane == 0) s_w[wid] = __popc(bal);
+    __syncthreads();
+    int before = s_carry;
+    for (int k = 0; k < wid; ++k) before += s_w[k];
+    if (keep) out[before + __popc(bal & ((1u << lane) - 1u))] = b;
+    __syncthreads();
+    if (threadIdx.x == 0)
+      for (int k = 0; k < 32; ++k) s_carry += s_w[k];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *count = s_carry;
+}
+
 }  // namespace
 }  // namespace tocr
 
@@ -1370,6 +1537,55 @@ TOCR_API int tocr_db_components(const float *d_pred, int n_maps, int h, int w, f
   if (root_flag) ccl_roots_kernel<<<tiles, 256, 0, st>>>(d_labels, root_flag, h, w);
   ccl_rows_kernel<<<dim3(h, n_maps), 256, 0, st>>>(d_labels, nullptr, h, w, true);
   return check_launch("tocr_db_components");
+}
+
+// cuda_gpu_ccl_detect (include/turbo_ocr/kernels/kernels.h:131-145): labels
+// (8-connected) of the 255/0 bitmap, compact ids in raster order of each
+// component's first pixel (at most 3000), per-id box / pixel count / mean
+// prediction, the reference's filter, kept boxes in id order; one
+// synchronisation, then *h_num_boxes boxes in h_boxes.
+TOCR_API int tocr_gpu_ccl_detect(const uint8_t *d_bitmap, const float *d_pred, int w, int h,
+                                 float box_thresh, int *d_labels, int *d_compact_ids,
+                                 int *d_id_counter, void *d_bboxes, int *d_num_boxes,
+                                 void *h_boxes, int *h_num_boxes, int *h_num_total,
+                                 void *stream) {
+  TOCR_ENTRY();
+  TOCR_REQUIRE(w > 0 && h > 0 && (long long)w * h < (1ll << 30) && h <= (int)(
+                   (2 * kMaxGpuComponents * sizeof(CclBox)) / (2 * sizeof(int))),
+               "tocr_gpu_ccl_detect: bad sizes %dx%d", w, h);
+  TOCR_REQUIRE(d_bitmap && d_pred && d_labels && d_compact_ids && d_id_counter && d_bboxes &&
+                   d_num_boxes && h_boxes && h_num_boxes,
+               "tocr_gpu_ccl_detect: null pointer");
+  cudaStream_t st = as_stream(stream);
+  const dim3 tiles((w + kTileW - 1) / kTileW, (h + kTileH - 1) / kTileH, 1);
+  CclBox *boxes = static_cast<CclBox *>(d_bboxes);
+  int *row = reinterpret_cast<int *>(boxes);  // row offsets, before the boxes are used
+  ccl_local_kernel<<<tiles, 256, 0, st>>>(nullptr, const_cast<uint8_t *>(d_bitmap), d_labels,
+                                          nullptr, nullptr, nullptr, h, w, 0.f);
+  ccl_merge_kernel<<<tiles, 128, 0, st>>>(d_bitmap, d_labels, nullptr, h, w);
+  ccl_rows_kernel<<<dim3(h, 1), 256, 0, st>>>(d_labels, nullptr, h, w, true);
+  ccl_root_count_kernel<<<h, 256, 0, st>>>(d_bitmap, d_labels, h, w, row);
+  ccl_root_scan_kernel<<<1, 1024, 0, st>>>(row, h, d_id_counter);
+  ccl_root_ids_kernel<<<h, 256, 0, st>>>(d_bitmap, d_labels, h, w, row, d_compact_ids);
+  ccl_box_init_kernel<<<(kMaxGpuComponents + 255) / 256, 256, 0, st>>>(boxes);
+  const long long n = (long long)w * h;
+  const unsigned grid = (unsigned)std::min<long long>((n + 255) / 256, (long long)sm_count() * 16);
+  ccl_extract_kernel<<<grid, 256, 0, st>>>(d_bitmap, d_labels, d_pred, h, w, d_compact_ids, boxes);
+  ccl_box_filter_kernel<<<1, 1024, 0, st>>>(boxes, box_thresh, boxes + kMaxGpuComponents,
+                                            d_num_boxes);
+  int rc = check_launch("tocr_gpu_ccl_detect");
+  if (rc != TOCR_OK) return rc;
+  cudaError_t e = cudaMemcpyAsync(h_num_boxes, d_num_boxes, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess && h_num_total)
+    e = cudaMemcpyAsync(h_num_total, d_id_counter, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(h_boxes, boxes + kMaxGpuComponents, kMaxGpuComponents * sizeof(CclBox),
+                        cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess)
+    return set_error(TOCR_ERR_CUDA, "tocr_gpu_ccl_detect: %s", cudaGetErrorString(e));
+  if (*h_num_boxes > kMaxGpuComponents) *h_num_boxes = kMaxGpuComponents;
+  return TOCR_OK;
 }
 
 }  // extern "C"

@@ -373,13 +373,13 @@ struct RecNorm {
   float mean[3], inv_std[3], inv_scale;
 };
 
-// One output pixel of crop b (r, g, b planes as fp16), arithmetic as
+// One output pixel of crop b (r, g, b planes), arithmetic as
 // batch_roi_warp_kernel: zero beyond the crop width or for a non-finite
 // source position.
 __device__ __forceinline__ void roi_warp_px(const uint8_t *src, int src_h, int src_w, int src_step,
                                             const float *M, int cw, int x, int y,
-                                            const RecNorm &nm, __half o[3]) {
-  o[0] = o[1] = o[2] = __float2half_rn(0.f);
+                                            const RecNorm &nm, float o[3]) {
+  o[0] = o[1] = o[2] = 0.f;
   if (x >= cw) return;
   float denom = M[6] * x + M[7] * y + M[8];
   denom = copysignf(fmaxf(fabsf(denom), 1e-7f), denom);
@@ -404,53 +404,172 @@ __device__ __forceinline__ void roi_warp_px(const uint8_t *src, int src_h, int s
   const float r = w00 * p00.x + w10 * p10.x + w01 * p01.x + w11 * p11.x;
   const float g = w00 * p00.y + w10 * p10.y + w01 * p01.y + w11 * p11.y;
   const float bl = w00 * p00.z + w10 * p10.z + w01 * p01.z + w11 * p11.z;
-  o[0] = __float2half_rn((r * nm.inv_scale - nm.mean[0]) * nm.inv_std[0]);
-  o[1] = __float2half_rn((g * nm.inv_scale - nm.mean[1]) * nm.inv_std[1]);
-  o[2] = __float2half_rn((bl * nm.inv_scale - nm.mean[2]) * nm.inv_std[2]);
+  o[0] = (r * nm.inv_scale - nm.mean[0]) * nm.inv_std[0];
+  o[1] = (g * nm.inv_scale - nm.mean[1]) * nm.inv_std[1];
+  o[2] = (bl * nm.inv_scale - nm.mean[2]) * nm.inv_std[2];
 }
 
+template <typename OutT>
+struct WarpStore;
+template <>
+struct WarpStore<__half> {
+  static __device__ __forceinline__ void one(__half *p, float v) { *p = __float2half_rn(v); }
+  static __device__ __forceinline__ void two(__half *p, float a, float b) {
+    *reinterpret_cast<__half2 *>(p) = __floats2half2_rn(a, b);
+  }
+};
+template <>
+struct WarpStore<float> {
+  static __device__ __forceinline__ void one(float *p, float v) { *p = v; }
+  static __device__ __forceinline__ void two(float *p, float a, float b) {
+    *reinterpret_cast<float2 *>(p) = make_float2(a, b);
+  }
+};
+
 // grid (ceil(dst_w/64), ceil(dst_h/8), z), block (32, 8): the z slices stride
-// over the crops that exist (*n_crops, at most max_crops), so no CTA is spent
-// on empty crop slots. A thread writes two neighbouring pixels (half2 per
-// plane when the width is even).
+// over the crops that exist (*n_crops when given, else n_crops_value, at most
+// max_crops), so no CTA is spent on empty crop slots. crop_page NULL: every
+// crop comes from page 0. A thread writes two neighbouring pixels (one
+// 2-element store per plane when the width is even).
+template <typename OutT>
 __global__ void __launch_bounds__(256)
 roi_warp_kernel(const uint8_t *__restrict__ pages, long long page_stride, int src_h, int src_w,
                 int src_step, const float *__restrict__ minv, const int *__restrict__ crop_w,
-                const int *__restrict__ crop_page, const int *__restrict__ n_crops, int max_crops,
-                __half *__restrict__ dst, int dst_h, int dst_w, RecNorm nm) {
+                const int *__restrict__ crop_page, const int *__restrict__ n_crops,
+                int n_crops_value, int max_crops, OutT *__restrict__ dst, int dst_h, int dst_w,
+                RecNorm nm) {
   __shared__ float s_M[9];
   __shared__ int s_crop_w, s_page;
-  const int nc = min(*n_crops, max_crops);
+  const int nc = min(n_crops ? *n_crops : n_crops_value, max_crops);
   const int tid = threadIdx.y * blockDim.x + threadIdx.x;
   const int x0 = (blockIdx.x * blockDim.x + threadIdx.x) * 2;
   const int y = blockIdx.y * blockDim.y + threadIdx.y;
   const long long plane = (long long)dst_h * dst_w;
-  const bool pair = (dst_w & 1) == 0 && (reinterpret_cast<uintptr_t>(dst) & 3) == 0;
+  const bool pair = (dst_w & 1) == 0 && (reinterpret_cast<uintptr_t>(dst) & (2 * sizeof(OutT) - 1)) == 0;
   for (int b = blockIdx.z; b < nc; b += gridDim.z) {
     __syncthreads();
     if (tid < 9) s_M[tid] = minv[(long long)b * 9 + tid];
-    if (tid == 0) { s_crop_w = crop_w[b]; s_page = crop_page[b]; }
+    if (tid == 0) { s_crop_w = crop_w[b]; s_page = crop_page ? crop_page[b] : 0; }
     __syncthreads();
     if (x0 >= dst_w || y >= dst_h) continue;
     const uint8_t *src = pages + (long long)s_page * page_stride;
-    __half v0[3], v1[3];
+    float v0[3], v1[3];
     roi_warp_px(src, src_h, src_w, src_step, s_M, s_crop_w, x0, y, nm, v0);
-    __half *o = dst + (long long)b * 3 * plane + (long long)y * dst_w + x0;
+    OutT *o = dst + (long long)b * 3 * plane + (long long)y * dst_w + x0;
     if (pair) {
       roi_warp_px(src, src_h, src_w, src_step, s_M, s_crop_w, x0 + 1, y, nm, v1);
 #pragma unroll
-      for (int c = 0; c < 3; ++c)
-        *reinterpret_cast<__half2 *>(o + c * plane) = __halves2half2(v0[c], v1[c]);
+      for (int c = 0; c < 3; ++c) WarpStore<OutT>::two(o + c * plane, v0[c], v1[c]);
     } else {
 #pragma unroll
-      for (int c = 0; c < 3; ++c) o[c * plane] = v0[c];
+      for (int c = 0; c < 3; ++c) WarpStore<OutT>::one(o + c * plane, v0[c]);
       if (x0 + 1 < dst_w) {
         roi_warp_px(src, src_h, src_w, src_step, s_M, s_crop_w, x0 + 1, y, nm, v1);
 #pragma unroll
-        for (int c = 0; c < 3; ++c) o[c * plane + 1] = v1[c];
+        for (int c = 0; c < 3; ++c) WarpStore<OutT>::one(o + c * plane + 1, v1[c]);
       }
     }
   }
+}
+
+// ---------------------------------------------------- stand-in network heads --
+// The trained detection and recognition networks are not available, so the
+// modules (PaddleDet / PaddleRec) run these stand-ins where the reference
+// runs its TensorRT engines:
+//   det: the synthetic page's DB probability map computed from the
+//        normalised canvas: ink = 1 - mean of the de-normalised channels
+//        (0 outside the letterbox content), 15-pixel horizontal max,
+//        sigmoid(gain * (max - 0.5));
+//   rec: CTC logits [n][T][V] fp16, 0 except 16.0 at one class per step, the
+//        class of crop id and step t being hash-drawn per 3 steps (blank with
+//        probability 1/2, else uniform over 1..V-1).
+constexpr int kHeadTile = 256, kHeadRadius = 7;
+
+__global__ void __launch_bounds__(kHeadTile)
+det_standin_kernel(const float *__restrict__ chw, int H, int W, const int *__restrict__ content,
+                   float s0, float s1, float s2, float m0, float m1, float m2, float gain,
+                   float *__restrict__ prob) {
+  __shared__ float s_ink[kHeadTile + 2 * kHeadRadius];
+  const int b = blockIdx.z, y = blockIdx.y, x0 = blockIdx.x * kHeadTile;
+  const int ch = content ? content[2 * b] : H, cw = content ? content[2 * b + 1] : W;
+  const long long plane = (long long)H * W;
+  const float *img = chw + (long long)b * 3 * plane + (long long)y * W;
+  for (int i = threadIdx.x; i < kHeadTile + 2 * kHeadRadius; i += blockDim.x) {
+    const int x = x0 - kHeadRadius + i;
+    float v = 0.f;
+    if (x >= 0 && x < W && x < cw && y < ch) {
+      const float r = img[x] * s0 + m0, g = img[plane + x] * s1 + m1, bl = img[2 * plane + x] * s2 + m2;
+      v = 1.f - (r + g + bl) * (1.f / 3.f);
+    }
+    s_ink[i] = v;
+  }
+  __syncthreads();
+  const int x = x0 + threadIdx.x;
+  if (x >= W) return;
+  float m = 0.f;
+#pragma unroll
+  for (int d = 0; d <= 2 * kHeadRadius; ++d) m = fmaxf(m, s_ink[threadIdx.x + d]);
+  prob[(long long)b * plane + (long long)y * W + x] = 1.f / (1.f + __expf(-gain * (m - 0.5f)));
+}
+
+__device__ __forceinline__ uint64_t standin_mix(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+  return z ^ (z >> 31);
+}
+__device__ __forceinline__ int standin_token(uint64_t seed, long long id, int t, int V) {
+  const uint64_t h = standin_mix(seed + 0x9E3779B97F4A7C15ULL *
+                                 (standin_mix(7000 + (uint64_t)id) + (uint64_t)(t / 3) + 1));
+  return (h & 1) ? 0 : 1 + (int)((h >> 32) % (uint64_t)(V - 1));
+}
+
+// grid-stride over the n*T rows; one warp per row: zero the row,
+// then plant 16.0 (p_max near 1, so results pass the drop score).
+__global__ void __launch_bounds__(256)
+rec_standin_kernel(__half *__restrict__ logits, const int *__restrict__ ids, long long rows, int T,
+                   int V, uint64_t seed) {
+  const int lane = threadIdx.x & 31;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long r = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
+    __half *row = logits + r * V;
+    for (int j = lane; j < V; j += 32) row[j] = __float2half_rn(0.f);
+    __syncwarp();
+    if (lane == 0) {
+      const long long c = r / T;
+      const int t = (int)(r % T);
+      row[standin_token(seed, ids ? ids[c] : c, t, V)] = __float2half_rn(16.f);
+    }
+  }
+}
+
+RecNorm rec_norm(const float *mean3, const float *inv_std3, float inv_scale) {
+  RecNorm nm;
+  for (int c = 0; c < 3; ++c) {
+    nm.mean[c] = mean3 ? mean3[c] : 0.5f;
+    nm.inv_std[c] = inv_std3 ? inv_std3[c] : 2.0f;
+  }
+  nm.inv_scale = inv_scale;
+  return nm;
+}
+
+template <typename OutT>
+int launch_roi_warp(const uint8_t *d_pages, long long page_stride, int src_h, int src_w,
+                    int src_step, const float *d_minv, const int *d_crop_w, const int *d_crop_page,
+                    const int *d_n_crops, int n_crops_value, int max_crops, int dst_h, int dst_w,
+                    const RecNorm &nm, OutT *d_dst, void *stream, const char *name) {
+  TOCR_REQUIRE(max_crops >= 0 && dst_h > 0 && dst_w > 0 && src_h > 0 && src_w > 0,
+               "%s: bad sizes", name);
+  if (max_crops == 0) return TOCR_OK;
+  TOCR_REQUIRE(d_pages && d_minv && d_crop_w && d_dst, "%s: null pointer", name);
+  const dim3 block(32, 8);
+  const unsigned gx = (dst_w + 63) / 64, gy = (dst_h + 7) / 8;
+  // about 16 CTAs per SM in flight; each z slice strides over the crops
+  const unsigned zmax = (unsigned)std::max(1, sm_count() * 16 / (int)(gx * gy));
+  const dim3 grid(gx, gy, std::min<unsigned>((unsigned)max_crops, std::min(zmax, 65535u)));
+  roi_warp_kernel<OutT><<<grid, block, 0, as_stream(stream)>>>(
+      d_pages, page_stride, src_h, src_w, src_step, d_minv, d_crop_w, d_crop_page, d_n_crops,
+      n_crops_value, max_crops, d_dst, dst_h, dst_w, nm);
+  return check_launch(name);
 }
 
 }  // namespace
@@ -564,25 +683,61 @@ TOCR_API int tocr_roi_warp_f16(const uint8_t *d_pages, long long page_stride, in
                                int dst_h, int dst_w, const float *mean3, const float *inv_std3,
                                float inv_scale, void *d_dst, void *stream) {
   TOCR_ENTRY();
-  TOCR_REQUIRE(max_crops >= 0 && dst_h > 0 && dst_w > 0 && src_h > 0 && src_w > 0,
-               "tocr_roi_warp_f16: bad sizes");
+  TOCR_REQUIRE(max_crops >= 0, "tocr_roi_warp_f16: bad sizes");
   if (max_crops == 0) return TOCR_OK;
-  RecNorm nm;
+  TOCR_REQUIRE(d_crop_page && d_n_crops, "tocr_roi_warp_f16: null pointer");
+  return launch_roi_warp<__half>(d_pages, page_stride, src_h, src_w, src_step, d_minv, d_crop_w,
+                                 d_crop_page, d_n_crops, 0, max_crops, dst_h, dst_w,
+                                 rec_norm(mean3, inv_std3, inv_scale),
+                                 static_cast<__half *>(d_dst), stream, "tocr_roi_warp_f16");
+}
+
+TOCR_API int tocr_det_standin_prob_f32(const float *d_chw, int n, int h, int w,
+                                       const int *d_content_hw, const float *mean3,
+                                       const float *inv_std3, float gain, float *d_prob,
+                                       void *stream) {
+  TOCR_ENTRY();
+  TOCR_REQUIRE(n >= 0 && h > 0 && w > 0 && h <= 65535 && n <= 65535,
+               "tocr_det_standin_prob_f32: bad sizes n=%d h=%d w=%d", n, h, w);
+  if (n == 0) return TOCR_OK;
+  TOCR_REQUIRE(d_chw && d_prob, "tocr_det_standin_prob_f32: null pointer");
+  const float dm[3] = {0.485f, 0.456f, 0.406f}, ds[3] = {0.229f, 0.224f, 0.225f};
+  float m[3], sd[3];
   for (int c = 0; c < 3; ++c) {
-    nm.mean[c] = mean3 ? mean3[c] : 0.5f;
-    nm.inv_std[c] = inv_std3 ? inv_std3[c] : 2.0f;
+    m[c] = mean3 ? mean3[c] : dm[c];
+    sd[c] = inv_std3 ? 1.f / inv_std3[c] : ds[c];
   }
-  nm.inv_scale = inv_scale;
-  const dim3 block(32, 8);
-  const unsigned gx = (dst_w + 63) / 64, gy = (dst_h + 7) / 8;
-  // about 16 CTAs per SM in flight; each z slice strides over the crops
-  const unsigned zmax = (unsigned)std::max(1, sm_count() * 16 / (int)(gx * gy));
-  const dim3 grid(gx, gy, std::min<unsigned>((unsigned)max_crops, std::min(zmax, 65535u)));
-  roi_warp_kernel<<<grid, block, 0, as_stream(stream)>>>(d_pages, page_stride, src_h, src_w,
-                                                         src_step, d_minv, d_crop_w, d_crop_page,
-                                                         d_n_crops, max_crops, (__half *)d_dst,
-                                                         dst_h, dst_w, nm);
-  return check_launch("roi_warp_kernel");
+  const dim3 grid((w + kHeadTile - 1) / kHeadTile, h, n);
+  det_standin_kernel<<<grid, kHeadTile, 0, as_stream(stream)>>>(d_chw, h, w, d_content_hw, sd[0],
+                                                                 sd[1], sd[2], m[0], m[1], m[2],
+                                                                 gain, d_prob);
+  return check_launch("det_standin_kernel");
+}
+
+TOCR_API int tocr_rec_standin_logits_f16(void *d_logits, const int *d_ids, int n, int seq_len,
+                                         int num_classes, uint64_t seed, void *stream) {
+  TOCR_ENTRY();
+  TOCR_REQUIRE(n >= 0 && seq_len > 0 && num_classes > 1,
+               "tocr_rec_standin_logits_f16: bad sizes n=%d T=%d V=%d", n, seq_len, num_classes);
+  if (n == 0) return TOCR_OK;
+  TOCR_REQUIRE(d_logits, "tocr_rec_standin_logits_f16: null pointer");
+  const long long rows = (long long)n * seq_len;
+  const unsigned grid = (unsigned)std::min<long long>((rows + 7) / 8, (long long)sm_count() * 16);
+  rec_standin_kernel<<<grid, 256, 0, as_stream(stream)>>>(static_cast<__half *>(d_logits), d_ids,
+                                                          rows, seq_len, num_classes, seed);
+  return check_launch("rec_standin_kernel");
+}
+
+TOCR_API int tocr_roi_warp_f32(const uint8_t *d_src, int src_h, int src_w, int src_step,
+                               const float *d_minv, const int *d_crop_w, int batch_size,
+                               int dst_h, int dst_w, const float *mean3, const float *inv_std3,
+                               float inv_scale, float *d_dst, void *stream) {
+  TOCR_ENTRY();
+  TOCR_REQUIRE(batch_size >= 0, "tocr_roi_warp_f32: bad batch size %d", batch_size);
+  return launch_roi_warp<float>(d_src, 0, src_h, src_w, src_step, d_minv, d_crop_w, nullptr,
+                                nullptr, batch_size, batch_size, dst_h, dst_w,
+                                rec_norm(mean3, inv_std3, inv_scale), d_dst, stream,
+                                "tocr_roi_warp_f32");
 }
 
 }  // extern "C"

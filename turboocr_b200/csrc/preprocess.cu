@@ -50,6 +50,16 @@ struct Norm {
   float inv_std[3];
 };
 
+// One image's source and letterbox content size.
+struct SrcDesc {
+  const void *ptr;
+  int step, h, w, dh, dw;
+};
+
+template <typename OutT>
+__device__ __forceinline__ void preprocess_image_rows(const SrcDesc d, int b, OutT *__restrict__ dst,
+                                                      int W, int H, const Norm &nm);
+
 template <typename OutT>
 __global__ void __launch_bounds__(kPrepThreads)
 preprocess_batch_kernel(const void *const *__restrict__ src_ptrs,
@@ -58,16 +68,31 @@ preprocess_batch_kernel(const void *const *__restrict__ src_ptrs,
                         const int *__restrict__ dst_ws, OutT *__restrict__ dst, int W, int H,
                         Norm nm) {
   const int b = blockIdx.z;
+  if ((blockIdx.x * kPrepThreads + threadIdx.x) * kPrepCols >= W) return;
+  const SrcDesc d{src_ptrs[b], src_steps[b], src_hs[b], src_ws[b], dst_hs[b], dst_ws[b]};
+  preprocess_image_rows<OutT>(d, b, dst, W, H, nm);
+}
+
+// The single-image form (cuda_fused_resize_normalize_det): the descriptor is
+// a kernel parameter, so nothing is staged in device memory.
+template <typename OutT>
+__global__ void __launch_bounds__(kPrepThreads)
+preprocess_one_kernel(SrcDesc d, OutT *__restrict__ dst, int W, int H, Norm nm) {
+  if ((blockIdx.x * kPrepThreads + threadIdx.x) * kPrepCols >= W) return;
+  preprocess_image_rows<OutT>(d, 0, dst, W, H, nm);
+}
+
+template <typename OutT>
+__device__ __forceinline__ void preprocess_image_rows(const SrcDesc d, int b, OutT *__restrict__ dst,
+                                                      int W, int H, const Norm &nm) {
   const int gx = blockIdx.x * kPrepThreads + threadIdx.x;
   const int x_base = gx * kPrepCols;
-  if (x_base >= W) return;
-
-  const unsigned char *src = static_cast<const unsigned char *>(src_ptrs[b]);
-  const int src_step = src_steps[b];
-  const int src_h = src_hs[b];
-  const int src_w = src_ws[b];
-  const int content_h = dst_hs[b];
-  const int content_w = dst_ws[b];
+  const unsigned char *src = static_cast<const unsigned char *>(d.ptr);
+  const int src_step = d.step;
+  const int src_h = d.h;
+  const int src_w = d.w;
+  const int content_h = d.dh;
+  const int content_w = d.dw;
 
   const float inv_255 = 1.0f / 255.0f;
   const float pad0 = (0.0f - nm.mean[0]) * nm.inv_std[0];
@@ -177,6 +202,27 @@ int launch_preprocess(const void *const *d_src_ptrs, const int *d_src_steps,
   return check_launch(name);
 }
 
+template <typename OutT>
+int launch_preprocess_one(const void *src, int step, int h, int w, OutT *dst, int dst_w,
+                          int dst_h, const float *mean3, const float *inv_std3, void *stream,
+                          const char *name) {
+  TOCR_REQUIRE(dst_w >= 0 && dst_h >= 0 && h >= 0 && w >= 0 && step >= 0, "%s: negative size",
+               name);
+  if (dst_w == 0 || dst_h == 0) return TOCR_OK;
+  TOCR_REQUIRE(dst_w % 8 == 0, "%s: dst_w %d must be a multiple of 8", name, dst_w);
+  TOCR_REQUIRE(dst && (src || h == 0 || w == 0), "%s: null pointer", name);
+  TOCR_REQUIRE(aligned(dst, 16), "%s: dst must be 16-byte aligned", name);
+  if ((size_t)dst_w * dst_h > (size_t)INT_MAX)
+    return set_error(TOCR_ERR_OVERFLOW, "%s: canvas %dx%d too large", name, dst_w, dst_h);
+  dim3 grid((dst_w / kPrepCols + kPrepThreads - 1) / kPrepThreads, (dst_h + kPrepRows - 1) / kPrepRows,
+            1);
+  TOCR_REQUIRE(grid.y <= 65535, "%s: dst_h %d too large", name, dst_h);
+  const SrcDesc d{src, step, h, w, dst_h, dst_w};
+  preprocess_one_kernel<OutT><<<grid, kPrepThreads, 0, as_stream(stream)>>>(
+      d, dst, dst_w, dst_h, make_norm(mean3, inv_std3));
+  return check_launch(name);
+}
+
 }  // namespace
 }  // namespace tocr
 
@@ -208,6 +254,23 @@ TOCR_API int tocr_preprocess_batch_f32(const void *const *d_src_ptrs, const int 
                                   d_dst_heights, d_dst_widths, dst_f32, dst_w, dst_h,
                                   batch_size, mean3, inv_std3, stream,
                                   "tocr_preprocess_batch_f32");
+}
+
+TOCR_API int tocr_preprocess_one_f32(const void *d_src, int src_step, int src_h, int src_w,
+                                     float *dst_f32, int dst_w, int dst_h, const float *mean3,
+                                     const float *inv_std3, void *stream) {
+  TOCR_ENTRY();
+  return launch_preprocess_one<float>(d_src, src_step, src_h, src_w, dst_f32, dst_w, dst_h, mean3,
+                                      inv_std3, stream, "tocr_preprocess_one_f32");
+}
+
+TOCR_API int tocr_preprocess_one_f16(const void *d_src, int src_step, int src_h, int src_w,
+                                     void *dst_f16, int dst_w, int dst_h, const float *mean3,
+                                     const float *inv_std3, void *stream) {
+  TOCR_ENTRY();
+  return launch_preprocess_one<__half>(d_src, src_step, src_h, src_w,
+                                       static_cast<__half *>(dst_f16), dst_w, dst_h, mean3,
+                                       inv_std3, stream, "tocr_preprocess_one_f16");
 }
 
 }  // extern "C"

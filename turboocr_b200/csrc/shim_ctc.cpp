@@ -28,6 +28,33 @@ TOCR_SHIM_API std::pair<std::string, float> ctc_greedy_decode(
   return {text, emitted > 0 ? total / emitted : 0.0f};
 }
 
+TOCR_SHIM_API std::pair<std::string, float> ctc_greedy_decode_raw(
+    const float *logits, int seq_len, int num_classes,
+    const std::vector<std::string> &label_list) {
+  std::string text;
+  float total = 0.0f;
+  int emitted = 0;
+  int prev = -1;
+  const int n_labels = static_cast<int>(label_list.size());
+  for (int t = 0; t < seq_len; ++t) {
+    const float *row = logits + static_cast<size_t>(t) * num_classes;
+    int idx = 0;
+    float best = row[0];
+    for (int j = 1; j < num_classes; ++j)
+      if (row[j] > best) {
+        best = row[j];
+        idx = j;
+      }
+    if (idx != prev && idx != 0 && idx < n_labels) {
+      text.append(label_list[idx]);
+      total += best;
+      ++emitted;
+    }
+    prev = idx;
+  }
+  return {text, emitted > 0 ? total / emitted : 0.0f};
+}
+
 TOCR_SHIM_API std::string ctc_tokens_to_text(const int *tokens, int n_tokens,
                                              const std::vector<std::string> &label_list) {
   std::string text;

@@ -50,40 +50,39 @@ TOCR_SHIM_API void cuda_batch_fused_resize_normalize_det(
 TOCR_SHIM_API void cuda_fused_resize_normalize_det(const GpuImage &src, float *dst_chw,
                                                    int dst_w, int dst_h,
                                                    cudaStream_t stream) {
-  // One-image batch: the descriptor arrays live in a small device block that
-  // is written with a stream-ordered copy from this call's stack frame, so the
-  // call stays asynchronous without any allocation per call.
-  struct Meta {
-    const void *ptr;
-    int step, h, w, dh, dw;
-  };
-  thread_local void *d_meta = nullptr;
-  thread_local int meta_dev = -1;
-  int dev = 0;
-  throw_on_status(cudaGetDevice(&dev) == cudaSuccess ? TOCR_OK : TOCR_ERR_CUDA,
-                  "cuda_fused_resize_normalize_det");
-  if (d_meta == nullptr || meta_dev != dev) {
-    // One-time per thread and device; freed at process exit.
-    if (cudaMalloc(&d_meta, 64) != cudaSuccess)
-      throw CudaError("cuda_fused_resize_normalize_det: metadata allocation failed");
-    meta_dev = dev;
-  }
+  // The descriptor travels as a kernel parameter: no device staging, no
+  // allocation, nothing shared between calls or streams.
   if (src.step > (size_t)INT_MAX) throw CudaError("cuda_fused_resize_normalize_det: step too large");
-  const void *ptrs[1] = {src.data};
-  const int ints[5] = {(int)src.step, src.rows, src.cols, dst_h, dst_w};
-  char host[64];
-  __builtin_memcpy(host, ptrs, sizeof(ptrs));
-  __builtin_memcpy(host + 8, ints, sizeof(ints));
-  // cudaMemcpyAsync from pageable memory is staged synchronously w.r.t. the
-  // host buffer, so `host` may go out of scope after the call returns.
-  if (cudaMemcpyAsync(d_meta, host, 28, cudaMemcpyHostToDevice, stream) != cudaSuccess)
-    throw CudaError("cuda_fused_resize_normalize_det: metadata copy failed");
-  char *m = static_cast<char *>(d_meta);
-  const int *di = reinterpret_cast<const int *>(m + 8);
-  throw_on_status(tocr_preprocess_batch_f32(reinterpret_cast<const void *const *>(m), di,
-                                            di + 1, di + 2, di + 3, di + 4, dst_chw, dst_w,
-                                            dst_h, 1, nullptr, nullptr, stream),
+  throw_on_status(tocr_preprocess_one_f32(src.data, (int)src.step, src.rows, src.cols, dst_chw,
+                                          dst_w, dst_h, nullptr, nullptr, stream),
                   "cuda_fused_resize_normalize_det");
+}
+
+TOCR_SHIM_API void cuda_batch_roi_warp(const GpuImage &src, const float *d_M_invs,
+                                       const int *d_crop_widths, float *d_dst_batch,
+                                       int batch_size, int dst_h, int dst_w,
+                                       cudaStream_t stream, float mean0, float mean1,
+                                       float mean2, float inv_std0, float inv_std1,
+                                       float inv_std2, float inv_scale) {
+  if (src.step > (size_t)INT_MAX) throw CudaError("cuda_batch_roi_warp: step too large");
+  const float mean[3] = {mean0, mean1, mean2}, inv_std[3] = {inv_std0, inv_std1, inv_std2};
+  throw_on_status(tocr_roi_warp_f32(static_cast<const uint8_t *>(src.data), src.rows, src.cols,
+                                    (int)src.step, d_M_invs, d_crop_widths, batch_size, dst_h,
+                                    dst_w, mean, inv_std, inv_scale, d_dst_batch, stream),
+                  "cuda_batch_roi_warp");
+}
+
+TOCR_SHIM_API int cuda_gpu_ccl_detect(const uint8_t *d_bitmap, const float *d_pred_map, int w,
+                                      int h, float box_thresh, int *d_labels,
+                                      int *d_compact_ids, int *d_id_counter,
+                                      GpuDetBox *d_bboxes, int *d_num_boxes,
+                                      GpuDetBox *h_boxes, int *h_num_boxes,
+                                      cudaStream_t stream, int *h_num_total) {
+  throw_on_status(tocr_gpu_ccl_detect(d_bitmap, d_pred_map, w, h, box_thresh, d_labels,
+                                      d_compact_ids, d_id_counter, d_bboxes, d_num_boxes,
+                                      h_boxes, h_num_boxes, h_num_total, stream),
+                  "cuda_gpu_ccl_detect");
+  return *h_num_boxes;
 }
 
 TOCR_SHIM_API void cuda_batch_threshold_to_u8(const float *src, uint8_t *dst, int w, int h,
