@@ -1,10 +1,27 @@
 """Subsystem 2 parity on the GPU: the fused tcgen05 DW+PW block against a
-torch fp32 reference of the same block (TF32 off). The reference uses the
-dequantised PW weights the block carries (the fp32 execution of the QDQ
-model). Tolerance: 3e-2 relative, normwise per (n, c_out) plane, for INT8 and
-FP8. Elementwise, |y - ref| is bounded against the plane's max |ref|: 3e-2 for
-FP8 (hi/lo activation split) and 5e-2 for INT8, whose per-pixel activation
-quantisation has a heavier error tail (worst element ~4e-2 over 59M values)."""
+torch fp32 reference of the same block (TF32 off).
+
+Two references: the block with the ORIGINAL fp32 weights (the model before
+quantisation), and the block with the dequantised PW weights the kernel
+carries (the fp32 execution of the quantised model). Measured at full
+config-4 size (32 x 240 x 240 x 128 -> 256, 472M outputs), worst plane:
+
+                       kernel vs original   kernel vs dequant   dequant model vs original
+  INT8 normwise             2.55e-2              1.52e-2              2.19e-2
+  FP8  normwise             4.98e-2              1.48e-3              4.96e-2
+  FP8  elementwise*         2.0e-1               8.9e-3               2.0e-1
+  (* |y - ref| / max(|ref|, plane rms))
+
+So the FP8 kernel reproduces the FP8 model to 1.5e-3, and all of its 5e-2
+distance from the original weights is E4M3's 3-bit mantissa on the weights
+(no scale choice removes a relative rounding error): the 3e-2 budget against
+the original weights holds for INT8 (normwise) and cannot hold for any plain
+E4M3 weight quantisation. The tests therefore bound: INT8 normwise 3e-2
+against the original weights at full size; FP8 normwise 3e-3 and
+elementwise 3e-2 (against max(|ref|, plane rms)) against its dequantised
+model at full size; both kinds against the dequantised model on the
+backbone's other shapes (normwise 3e-2; elementwise against the plane max,
+5e-2 for INT8, whose per-pixel activation scales have a heavier tail)."""
 import numpy as np
 import pytest
 import torch
@@ -82,10 +99,17 @@ def test_fp8_hi_lo_is_tight(cuda):
     assert nw < 5e-3, nw
 
 
+def elementwise_vs_rms(y: torch.Tensor, ref: torch.Tensor) -> float:
+    """max |y - ref| / max(|ref|, rms of ref's (n, c) plane)."""
+    rms = ref.pow(2).mean(dim=(1, 2), keepdim=True).sqrt()
+    return float(((y.float() - ref).abs() / torch.maximum(ref.abs(), rms).clamp_min(1e-12)).amax())
+
+
 @pytest.mark.parametrize("kind", [bb.KIND_INT8, bb.KIND_FP8])
 def test_config4_full_size(cuda, kind):
     """BASELINE config 4 at full size: x [32, 240, 240, 128] fp16 N(0,1),
-    C_out 256. Every image is compared against the fp32 reference."""
+    C_out 256, every image. INT8 against the original fp32 weights; FP8
+    against its dequantised model (see the module docstring)."""
     N, H, W, C, CO = 32, 240, 240, 128, 256
     params = bb.make_block_params(C, CO, 0x7EC00004)
     blk = bb.DwPwBlock(params, kind, 1, cuda)
@@ -95,12 +119,20 @@ def test_config4_full_size(cuda, kind):
     torch.cuda.synchronize()
     assert int(blk.err.item()) == 0
     wq = blk.dequantized_pw()
-    worst = (0.0, 0.0)
+    worst_nw, worst_el = 0.0, 0.0
     for n0 in range(0, N, 4):
-        ref = bb.reference_block(x[n0:n0 + 4], params, 1, wpw=wq)
-        nw, el = plane_errors(y[n0:n0 + 4], ref)
-        worst = (max(worst[0], nw), max(worst[1], el))
-    assert worst[0] <= TOL and worst[1] <= EL_TOL[kind], worst
+        if kind == bb.KIND_INT8:
+            ref = bb.reference_block(x[n0:n0 + 4], params, 1)
+        else:
+            ref = bb.reference_block(x[n0:n0 + 4], params, 1, wpw=wq)
+        nw, _ = plane_errors(y[n0:n0 + 4], ref)
+        worst_nw = max(worst_nw, nw)
+        worst_el = max(worst_el, elementwise_vs_rms(y[n0:n0 + 4], ref))
+        del ref
+    if kind == bb.KIND_INT8:
+        assert worst_nw <= TOL, worst_nw
+    else:
+        assert worst_nw <= 3e-3 and worst_el <= TOL, (worst_nw, worst_el)
 
 
 def test_int8_model_level_error_vs_unquantised_weights(cuda):
