@@ -44,8 +44,8 @@ def lib():
     OUT.parent.mkdir(exist_ok=True)
     if not OUT.exists() or OUT.stat().st_mtime < max(SRC.stat().st_mtime, HDR.stat().st_mtime,
                                                      UNION_HDR.stat().st_mtime):
-        subprocess.run(["g++", "-std=c++17", "-O2", "-ffp-contract=off", "-fPIC", "-shared",
-                        f"-I{HDR.parent}", "-o", str(OUT), str(SRC)], check=True)
+        subprocess.run(["g++", "-std=c++20", "-O2", "-ffp-contract=off", "-fPIC", "-shared",
+                        "-pthread", f"-I{HDR.parent}", "-o", str(OUT), str(SRC)], check=True)
     L = C.CDLL(str(OUT))
     vp, i, d = C.c_void_p, C.c_int, C.c_double
     L.dbh_trace.argtypes = [vp, i, i, i, i, i, vp, i]
@@ -63,6 +63,7 @@ def lib():
     L.dbh_offset_raw.argtypes = [vp, i, d, vp, i]
     L.dbh_unclip_union.argtypes = [vp, i, d, vp, i]
     L.dbh_sort_check.argtypes = [vp, i, vp, vp]
+    L.dbh_set_union_lanes.argtypes = [i]
     L.dbh_poly_mask.argtypes = [vp, i, i, i, i, i, vp]
     L.dbh_poly_mask_parity.argtypes = [vp, i, i, i, i, i, vp]
     _lib = L

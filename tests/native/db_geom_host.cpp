@@ -229,3 +229,66 @@ extern "C" int dbh_sort_check(const int *keys, int n, int *perm_std, int *perm_o
   for (int i = 0; i < n; ++i) { perm_std[i] = a[i].id; perm_own[i] = b[i].id; }
   return fail ? -1 : 0;
 }
+
+// ---- warp emulation for the union sweep's list-wide steps -------------------
+// dbh_set_union_lanes(n): with n > 1, every list-wide step of the sweep runs
+// on n threads (this one is lane 0) that meet at a std::barrier wherever the
+// device's lanes meet at __syncwarp, so the CPU tests cover the split of each
+// step over the 32 lanes of a warp. n <= 1 restores the single-thread steps.
+#include <barrier>
+#include <memory>
+#include <thread>
+
+namespace {
+struct LanePool {
+  int n = 0;
+  std::unique_ptr<std::barrier<>> bar;
+  std::vector<std::thread> th;
+  cu::BulkArgs *job = nullptr;
+  bool stop = false;
+  void start(int lanes) {
+    n = lanes;
+    bar = std::make_unique<std::barrier<>>(lanes);
+    for (int l = 1; l < lanes; ++l)
+      th.emplace_back([this, l] {
+        for (;;) {
+          bar->arrive_and_wait();  // job posted
+          if (stop) return;
+          cu::bulk_exec(*job, l, n);
+          bar->arrive_and_wait();  // job done
+        }
+      });
+  }
+  void run(cu::BulkArgs *a) {
+    job = a;
+    bar->arrive_and_wait();
+    cu::bulk_exec(*a, 0, n);
+    bar->arrive_and_wait();
+  }
+  void shutdown() {
+    if (!bar) return;
+    stop = true;
+    bar->arrive_and_wait();
+    for (auto &t : th) t.join();
+    th.clear();
+    bar.reset();
+    stop = false;
+    n = 0;
+  }
+};
+LanePool g_pool;
+}  // namespace
+
+extern "C" void dbh_set_union_lanes(int n) {
+  g_pool.shutdown();
+  if (n <= 1) {
+    cu::g_host_lanes = 1;
+    cu::g_host_runner = nullptr;
+    cu::g_host_barrier = nullptr;
+    return;
+  }
+  g_pool.start(n);
+  cu::g_host_lanes = n;
+  cu::g_host_runner = [](cu::BulkArgs *a, int) { g_pool.run(a); };
+  cu::g_host_barrier = [] { g_pool.bar->arrive_and_wait(); };
+}

@@ -102,3 +102,27 @@ def test_axis_rectangle_rings_need_no_union():
             raw = np.array(dn.offset_raw(c, d), np.int32).reshape(-1, 2)
             full = np.asarray(do.unclip(c, ratio), np.int32).reshape(-1, 2)
             assert do.get_mini_boxes(raw) == do.get_mini_boxes(full)
+
+
+@pytest.mark.parametrize("lanes", [32, 5])
+def test_union_list_steps_split_over_lanes(lanes):
+    """The sweep's list-wide steps split over the lanes of a warp (emulated
+    by threads meeting at a barrier where the device's lanes meet at
+    __syncwarp) give the reference's ring point for point."""
+    lib = dn.lib()
+    lib.dbh_set_union_lanes(lanes)
+    try:
+        n = 0
+        pred = sh.db_map(960, 960, 40, 200, 0x7EC00000, 3)
+        for c in do.find_contours(do.threshold(pred, 0.3)):
+            if len(c) > 2:
+                assert same_ring(c, 1.5), len(c)
+                n += 1
+        assert n > 20
+        rng = np.random.default_rng(4)
+        f = cv2.GaussianBlur(rng.random((300, 400)).astype(np.float32), (0, 0), 4)
+        bm = (f > np.median(f)).astype(np.uint8) * 255
+        for c in sorted(do.find_contours(bm), key=len)[-2:]:
+            assert same_ring(c, 1.5)
+    finally:
+        lib.dbh_set_union_lanes(1)

@@ -119,7 +119,8 @@ TG unsigned long long arena_bytes(int n) {
          al(sizeof(int) * 3ull * (unsigned long long)c.stack) +
          al(sizeof(int) * 4ull * (unsigned long long)(c.edges + 2)) +
          al(sizeof(int) * (unsigned long long)c.inodes) +
-         al(sizeof(INode) * (unsigned long long)c.inodes);
+         al(sizeof(INode) * (unsigned long long)c.inodes) +
+         al(sizeof(int) * 3ull * (unsigned long long)(c.edges + 2));
 }
 
 // ------------------------------------------------------------ std::sort -------
@@ -232,6 +233,274 @@ CU_HD void std_sort(T *a, int n, Less less, int *stk, int stk_cap, bool *fail) {
   }
 }
 
+// ------------------------------------------------------- list-wide steps -------
+// The sweep's per-scanbeam passes over the whole active edge list (AEL): the
+// edges' x at the scanbeam top, the clusters of the intersection sort, the
+// update of every edge at the top, the list of edges that end there, the
+// SEL copy, the array shifts of insertions and deletions and the linear
+// searches. Each is a pure data-parallel step with a fixed result, written
+// once for nl lanes: the host runs it with one lane; on the device the
+// warp that owns a ring runs it with 32 lanes while lane 0 keeps Clipper's
+// sequential logic (bulk_step). Chunks are contiguous, lane order is list
+// order, and partial results meet in the per-lane arrays, so the outcome
+// does not depend on nl.
+enum BulkOp : int {
+  kOpStop = 0, kOpKeys, kOpTop, kOpPromote, kOpSel, kOpInsert, kOpDelete, kOpFindIns, kOpFindOut
+};
+constexpr int kMaxLanes = 32;
+struct BulkArgs {
+  int op, a, b, n, result;
+  long long y;
+  Edge *E;
+  int *AEL, *ARR, *KEY, *SUF, *SPL, *CLS;
+  int p0[kMaxLanes], p1[kMaxLanes], p2[kMaxLanes], p3[kMaxLanes];
+};
+
+TG long long round_half_away_ll(double v) { return v < 0 ? (long long)(v - 0.5) : (long long)(v + 0.5); }
+TG long long edge_top_x(const Edge &e, long long y) {
+  return y == e.ty ? (long long)e.tx : (long long)e.bx + round_half_away_ll(e.dx * (double)(y - e.by));
+}
+// Clipper's E2InsertsBeforeE1
+TG bool inserts_before(const Edge *E, int e1, int e2) {
+  if (E[e2].cx == E[e1].cx) {
+    if (E[e2].ty > E[e1].ty) return E[e2].tx < edge_top_x(E[e1], E[e2].ty);
+    return E[e1].tx > edge_top_x(E[e2], E[e1].ty);
+  }
+  return E[e2].cx < E[e1].cx;
+}
+
+#if !defined(__CUDA_ARCH__)
+// Host emulation of the warp (tests): g_host_lanes lanes run each step as
+// threads through g_host_runner and meet at g_host_barrier.
+inline int g_host_lanes = 1;
+inline void (*g_host_runner)(BulkArgs *, int) = nullptr;
+inline void (*g_host_barrier)() = nullptr;
+#endif
+
+TG void bulk_sync(int nl) {
+#if defined(__CUDA_ARCH__)
+  if (nl > 1) __syncwarp();
+#else
+  if (nl > 1 && g_host_barrier) g_host_barrier();
+#endif
+}
+
+// First list position p >= p0 (p < n) where pred(p) holds, else n; rounds of
+// nl positions.
+template <class PRED>
+TG int bulk_find(BulkArgs &A, int lane, int nl, int p0, int n, PRED pred) {
+  for (int base = p0; base < n; base += nl) {
+    const int p = base + lane;
+    A.p0[lane] = (p < n && pred(p)) ? 1 : 0;
+    bulk_sync(nl);
+    int hit = -1;
+    for (int j = 0; j < nl; ++j)
+      if (A.p0[j]) { hit = base + j; break; }
+    bulk_sync(nl);
+    if (hit >= 0) return hit;
+  }
+  return n;
+}
+
+// Exclusive sum of v over the lanes (all lanes get their offset; *total the sum).
+TG int bulk_offset(BulkArgs &A, int lane, int nl, int v, int *total) {
+  A.p2[lane] = v;
+  bulk_sync(nl);
+  int off = 0, all = 0;
+  for (int j = 0; j < nl; ++j) {
+    if (j < lane) off += A.p2[j];
+    all += A.p2[j];
+  }
+  bulk_sync(nl);
+  *total = all;
+  return off;
+}
+
+TG void bulk_exec(BulkArgs &A, int lane, int nl) {
+  Edge *E = A.E;
+  int *AEL = A.AEL;
+  const int n = A.n;
+  const int ch = (n + nl - 1) / nl;
+  const int lo = lane * ch < n ? lane * ch : n;
+  const int hi = lo + ch < n ? lo + ch : n;
+  switch (A.op) {
+    case kOpKeys: {
+      // x at the top of every edge (Curr.X), the sort copy (ARR, KEY); then
+      // the clusters of the bubble sort: cut after position i when every key
+      // up to i is <= every key after i; clusters of two or more positions
+      // (they hold an inversion) go to CLS as (first, last) in list order.
+      const long long y = A.y;
+      int cmin = 0x7fffffff, cmax = (int)0x80000000;
+      for (int k = lo; k < hi; ++k) {
+        const int e = AEL[k];
+        const int x = (int)edge_top_x(E[e], y);
+        E[e].cx = x;
+        A.ARR[k] = e;
+        A.KEY[k] = x;
+        cmin = x < cmin ? x : cmin;
+        cmax = x > cmax ? x : cmax;
+      }
+      A.p0[lane] = cmin;
+      A.p1[lane] = cmax;
+      bulk_sync(nl);
+      int desc = 0;
+      for (int k = lo; k < hi; ++k)
+        if (k + 1 < n && A.KEY[k] > A.KEY[k + 1]) { desc = 1; break; }
+      int any = 0;
+      bulk_offset(A, lane, nl, desc, &any);
+      if (any == 0) {
+        if (lane == 0) A.result = 0;
+        return;
+      }
+      int pm_in = (int)0x80000000, sm_in = 0x7fffffff;
+      for (int j = 0; j < nl; ++j) {
+        if (j < lane) pm_in = A.p1[j] > pm_in ? A.p1[j] : pm_in;
+        if (j > lane) sm_in = A.p0[j] < sm_in ? A.p0[j] : sm_in;
+      }
+      {  // suffix minima of the chunk, seeded with the later chunks' minimum
+        int sm = sm_in;
+        for (int k = hi - 1; k >= lo; --k) {
+          sm = A.KEY[k] < sm ? A.KEY[k] : sm;
+          A.SUF[k] = sm;
+        }
+      }
+      // cut flags (i is a cut when max KEY[0..i] <= min KEY[i+1..n)); the
+      // last cut of each chunk, for the cluster starts of the next chunks
+      auto suf_after = [&](int i) { return i + 1 < hi ? A.SUF[i + 1] : sm_in; };
+      int last_cut = -1, pm = pm_in;
+      for (int i = lo; i < hi; ++i) {
+        pm = A.KEY[i] > pm ? A.KEY[i] : pm;
+        if (i == n - 1 || pm <= suf_after(i)) last_cut = i;
+      }
+      A.p3[lane] = last_cut;
+      bulk_sync(nl);
+      int prev = -1;
+      for (int j = 0; j < lane; ++j) prev = A.p3[j] > prev ? A.p3[j] : prev;
+      int cnt = 0;
+      {
+        int pv = prev, p2 = pm_in;
+        for (int i = lo; i < hi; ++i) {
+          p2 = A.KEY[i] > p2 ? A.KEY[i] : p2;
+          if (i == n - 1 || p2 <= suf_after(i)) {
+            if (i > pv + 1) ++cnt;
+            pv = i;
+          }
+        }
+      }
+      int total = 0;
+      int off = bulk_offset(A, lane, nl, cnt, &total);
+      {
+        int pv = prev, p2 = pm_in;
+        for (int i = lo; i < hi; ++i) {
+          p2 = A.KEY[i] > p2 ? A.KEY[i] : p2;
+          if (i == n - 1 || p2 <= suf_after(i)) {
+            if (i > pv + 1) {
+              A.CLS[2 * off] = pv + 1;
+              A.CLS[2 * off + 1] = i;
+              ++off;
+            }
+            pv = i;
+          }
+        }
+      }
+      if (lane == 0) A.result = total;
+      return;
+    }
+    case kOpTop:
+    case kOpPromote: {
+      // kOpTop: every edge that does not end at y gets its x and y at y
+      // (Curr); the edges that end at y are listed in SPL in list order.
+      // kOpPromote: the edges that end at y and go on (NextInLML) are listed.
+      const long long y = A.y;
+      int cnt = 0;
+      for (int k = lo; k < hi; ++k) {
+        const int e = AEL[k];
+        const bool ends = E[e].ty == y;
+        if (A.op == kOpTop) {
+          if (!ends) {
+            E[e].cx = (int)edge_top_x(E[e], y);
+            E[e].cy = (int)y;
+          } else {
+            ++cnt;
+          }
+        } else if (ends && E[e].next_lml != kNil) {
+          ++cnt;
+        }
+      }
+      int total = 0;
+      int off = bulk_offset(A, lane, nl, cnt, &total);
+      for (int k = lo; k < hi; ++k) {
+        const int e = AEL[k];
+        if (E[e].ty == y && (A.op == kOpTop || E[e].next_lml != kNil)) A.SPL[off++] = e;
+      }
+      if (lane == 0) A.result = total;
+      return;
+    }
+    case kOpSel:
+      for (int k = lo; k < hi; ++k) {
+        const int e = AEL[k];
+        E[e].prev_sel = k > 0 ? AEL[k - 1] : kNil;
+        E[e].next_sel = k + 1 < n ? AEL[k + 1] : kNil;
+      }
+      return;
+    case kOpInsert: {  // positions [a, n) move up by one (from the top down)
+      const int pos = A.a;
+      for (int base = n - 1; base >= pos; base -= nl) {
+        const int k = base - lane;
+        const int m = k >= pos ? AEL[k] : kNil;
+        bulk_sync(nl);
+        if (k >= pos) {
+          AEL[k + 1] = m;
+          E[m].ael_pos = k + 1;
+        }
+        bulk_sync(nl);
+      }
+      return;
+    }
+    case kOpDelete: {  // positions (a, n) move down by one (from the bottom up)
+      const int pos = A.a;
+      for (int base = pos; base + 1 < n; base += nl) {
+        const int k = base + lane;
+        const int m = k + 1 < n ? AEL[k + 1] : kNil;
+        bulk_sync(nl);
+        if (k + 1 < n) {
+          AEL[k] = m;
+          E[m].ael_pos = k;
+        }
+        bulk_sync(nl);
+      }
+      return;
+    }
+    case kOpFindIns: {  // first p >= a where edge b inserts before AEL[p]
+      const int e = A.b;
+      const int r = bulk_find(A, lane, nl, A.a, n, [&](int p) { return inserts_before(E, AEL[p], e); });
+      if (lane == 0) A.result = r;
+      return;
+    }
+    case kOpFindOut: {  // first p with OutIdx == a
+      const int o = A.a;
+      const int r = bulk_find(A, lane, nl, 0, n, [&](int p) { return E[AEL[p]].out_idx == o; });
+      if (lane == 0) A.result = r;
+      return;
+    }
+    default:
+      return;
+  }
+}
+
+#if defined(__CUDACC__)
+// One step of the warp that owns a ring: lane 0 has written the command;
+// every lane runs its share. False once the command is kOpStop. Not inlined,
+// so that every lane meets the same barrier instructions.
+__device__ __noinline__ bool bulk_step(BulkArgs *A, int lane) {
+  __syncwarp();
+  if (*(volatile int *)&A->op == kOpStop) return false;
+  bulk_exec(*A, lane, 32);
+  __syncwarp();
+  return true;
+}
+#endif
+
 // ------------------------------------------------------------ the sweep -------
 struct Sweep {
   Edge *E;
@@ -245,6 +514,9 @@ struct Sweep {
   int *STK;
   int *ARR, *KEY, *SUF, *PASS;
   INode *IN2;
+  int *SPL, *CLS;       // list-wide step outputs: edge lists, bubble-sort clusters
+  BulkArgs *bk;         // list-wide step arguments (per warp on the device)
+  int bk_lanes;
   Caps cap;
   int n_edges, n_lm, cur_lm, n_sb, n_op, n_or, n_jn, n_gj, n_in;
   // The active edge list (AEL) is kept as an array in x order, AEL[0..
@@ -277,7 +549,11 @@ struct Sweep {
     AEL = SUF + (cap.edges + 2);
     p += al(sizeof(int) * 4ull * (unsigned long long)(cap.edges + 2));
     PASS = reinterpret_cast<int *>(p); p += al(sizeof(int) * (unsigned long long)cap.inodes);
-    IN2 = reinterpret_cast<INode *>(p);
+    IN2 = reinterpret_cast<INode *>(p); p += al(sizeof(INode) * (unsigned long long)cap.inodes);
+    SPL = reinterpret_cast<int *>(p);
+    CLS = SPL + (cap.edges + 2);
+    bk = nullptr;
+    bk_lanes = 1;
     n_edges = n_lm = cur_lm = n_sb = n_op = n_or = n_jn = n_gj = n_in = 0;
     ael_n = 0;
     sorted = kNil;
@@ -291,6 +567,30 @@ struct Sweep {
   CU_HD bool tick() {
     if (++guard > guard_limit) fail = true;
     return !fail;
+  }
+  // The list-wide steps: arguments to bk, then every lane of the owning warp
+  // (device, bk_lanes 32) or this thread alone runs bulk_exec.
+  CU_HD void set_bulk(BulkArgs *a, int lanes) {
+    bk = a;
+    bk_lanes = lanes;
+  }
+  CU_HD int bulk(int op, int a = 0, int b = 0, long long y = 0) {
+    BulkArgs &A = *bk;
+    A.op = op; A.a = a; A.b = b; A.y = y; A.n = ael_n; A.result = 0;
+    A.E = E; A.AEL = AEL; A.ARR = ARR; A.KEY = KEY; A.SUF = SUF; A.SPL = SPL; A.CLS = CLS;
+#if defined(__CUDA_ARCH__)
+    if (bk_lanes > 1) {
+      bulk_step(bk, 0);
+      return A.result;
+    }
+#else
+    if (bk_lanes > 1 && g_host_runner) {
+      g_host_runner(bk, bk_lanes);
+      return A.result;
+    }
+#endif
+    bulk_exec(A, 0, 1);
+    return A.result;
   }
 
   // ---- small helpers -----------------------------------------------------
@@ -575,11 +875,7 @@ struct Sweep {
   }
   CU_HD void ael_insert_at(int e, int pos) {
     if (ael_n >= n_edges) { fail = true; return; }
-    for (int k = ael_n - 1; k >= pos; --k) {
-      const int m = AEL[k];
-      AEL[k + 1] = m;
-      E[m].ael_pos = k + 1;
-    }
+    if (pos < ael_n) bulk(kOpInsert, pos);
     AEL[pos] = e;
     E[e].ael_pos = pos;
     ++ael_n;
@@ -590,19 +886,15 @@ struct Sweep {
     } else if (start == kNil && e2_inserts_before_e1(AEL[0], e)) {
       ael_insert_at(e, 0);
     } else {
-      int k = start == kNil ? 0 : E[start].ael_pos;
-      while (k + 1 < ael_n && !e2_inserts_before_e1(AEL[k + 1], e)) ++k;
-      ael_insert_at(e, k + 1);
+      // first position after start where e inserts before the edge there
+      const int k = start == kNil ? 0 : E[start].ael_pos;
+      ael_insert_at(e, bulk(kOpFindIns, k + 1, e));
     }
   }
   CU_HD void delete_from_ael(int e) {
     const int p = E[e].ael_pos;
     if (p < 0) return;
-    for (int k = p; k + 1 < ael_n; ++k) {
-      const int m = AEL[k + 1];
-      AEL[k] = m;
-      E[m].ael_pos = k;
-    }
+    if (p + 1 < ael_n) bulk(kOpDelete, p);
     --ael_n;
     E[e].ael_pos = -1;
   }
@@ -626,11 +918,7 @@ struct Sweep {
   }
   CU_HD void copy_ael_to_sel() {
     sorted = head();
-    for (int k = 0; k < ael_n; ++k) {
-      const int e = AEL[k];
-      E[e].prev_sel = k > 0 ? AEL[k - 1] : kNil;
-      E[e].next_sel = k + 1 < ael_n ? AEL[k + 1] : kNil;
-    }
+    if (ael_n > 0) bulk(kOpSel);
   }
   // SwapPositionsInAEL: both edges must be in the AEL (Clipper's test
   // NextInAEL == PrevInAEL is true only for an edge outside it, or alone).
@@ -933,13 +1221,11 @@ struct Sweep {
     const int ok = E[e1].out_idx, obsolete = E[e2].out_idx;
     E[e1].out_idx = kUnassigned;
     E[e2].out_idx = kUnassigned;
-    for (int k = 0; k < ael_n; ++k) {
+    const int k = bulk(kOpFindOut, obsolete);
+    if (k < ael_n) {
       const int e = AEL[k];
-      if (E[e].out_idx == obsolete) {
-        E[e].out_idx = ok;
-        E[e].side = E[e1].side;
-        break;
-      }
+      E[e].out_idx = ok;
+      E[e].side = E[e1].side;
     }
     OR[r2].idx = OR[r1].idx;
   }
@@ -1052,23 +1338,12 @@ struct Sweep {
   // cluster, swap) order. Equal keys never swap (strict comparison).
   CU_HD void build_intersect_list(long long top_y) {
     if (ael_n == 0) return;
-    int L = 0;
-    for (int k = 0; k < ael_n; ++k) {
-      const int e = AEL[k];
-      const int x = (int)top_x(e, top_y);
-      E[e].cx = x;
-      ARR[L] = e;
-      KEY[L] = x;
-      ++L;
-    }
-    SUF[L - 1] = KEY[L - 1];
-    for (int i = L - 2; i >= 0; --i) SUF[i] = KEY[i] < SUF[i + 1] ? KEY[i] : SUF[i + 1];
+    // keys at the top and the clusters with an inversion (kOpKeys)
+    const int n_cl = bulk(kOpKeys, 0, 0, top_y);
     int n_nodes = 0, max_pass = 0;
-    int s = 0, pmax = KEY[0];
-    for (int i = 0; i < L; ++i) {
-      pmax = KEY[i] > pmax ? KEY[i] : pmax;
-      if (i + 1 < L && pmax > SUF[i + 1]) continue;  // cluster goes on
-      if (i > s) {  // cluster [s, i] (has an inversion): Clipper's passes on it
+    for (int ci = 0; ci < n_cl; ++ci) {
+      const int s = CLS[2 * ci], i = CLS[2 * ci + 1];
+      {  // cluster [s, i]: Clipper's passes on it
         int end = i, pass = 0;
         for (;;) {
           bool modified = false;
@@ -1093,7 +1368,6 @@ struct Sweep {
           if (!modified || --end <= s) break;
         }
       }
-      s = i + 1;
     }
     // stable counting sort of the records by pass
     for (int p2 = 0; p2 <= max_pass + 1; ++p2) SUF[p2] = 0;
@@ -1338,11 +1612,17 @@ struct Sweep {
   // DoMaxima Clipper resumes at ePrev->NextInAEL, which is the same index
   // (DoMaxima only moves and removes edges from e onwards).
   CU_HD void process_edges_at_top(long long top_y) {
-    int k = 0, g = 0;
-    while (k < ael_n) {
-      if (++g > 2 * n_edges + 16) { fail = true; return; }
-      int e = AEL[k];
-      bool is_max = E[e].ty == top_y && E[e].next_lml == kNil;
+    // kOpTop: every edge that does not end at top_y gets its Curr at top_y
+    // (nothing below reads the Curr of another edge before the horizontals),
+    // the edges that end there are listed in list order; the walk over them
+    // below meets them in the order of Clipper's walk over the whole AEL
+    // (DoMaxima only moves and removes edges from e onwards).
+    const int n_end = bulk(kOpTop, 0, 0, top_y);
+    for (int j = 0; j < n_end; ++j) {
+      if (!tick()) return;
+      int e = SPL[j];
+      if (E[e].ael_pos < 0) continue;  // removed with an earlier maxima pair
+      bool is_max = E[e].next_lml == kNil;
       if (is_max) {
         const int mp = maxima_pair_ex(e);
         is_max = mp == kNil || !is_horz(mp);
@@ -1352,7 +1632,7 @@ struct Sweep {
         if (fail) return;
         continue;
       }
-      if (E[e].ty == top_y && E[e].next_lml != kNil && is_horz(E[e].next_lml)) {
+      if (E[e].next_lml != kNil && is_horz(E[e].next_lml)) {
         update_edge_into_ael(e);
         if (fail) return;
         if (E[e].out_idx >= 0) add_out_pt(e, E[e].bx, E[e].by);
@@ -1361,13 +1641,14 @@ struct Sweep {
         E[e].cx = (int)top_x(e, top_y);
         E[e].cy = (int)top_y;
       }
-      ++k;
     }
     process_horizontals();
     if (fail) return;
-    for (k = 0; k < ael_n; ++k) {
-      int e = AEL[k];
-      if (E[e].ty == top_y && E[e].next_lml != kNil) {
+    // intermediate vertices at top_y, in list order (kOpPromote)
+    const int n_pro = bulk(kOpPromote, 0, 0, top_y);
+    for (int j = 0; j < n_pro; ++j) {
+      int e = SPL[j];
+      {
         int op = kNil;
         if (E[e].out_idx >= 0) op = add_out_pt(e, E[e].tx, E[e].ty);
         update_edge_into_ael(e);
@@ -1714,6 +1995,19 @@ struct Sweep {
   // capacity/bound failure (result unusable) and true otherwise; the output
   // rings are then the OutRecs with pts != kNil.
   CU_HD bool execute(const P2 *path, int n) {
+#if !defined(__CUDA_ARCH__)
+    if (bk == nullptr) {  // host: the list-wide steps run on this thread
+      BulkArgs local;
+      set_bulk(&local, g_host_runner ? g_host_lanes : 1);
+      const bool ok = execute_impl(path, n);
+      set_bulk(nullptr, 1);
+      return ok;
+    }
+#endif
+    if (bk == nullptr) { fail = true; return false; }
+    return execute_impl(path, n);
+  }
+  CU_HD bool execute_impl(const P2 *path, int n) {
     if (!add_path(path, n)) return !fail;  // nothing added: empty solution
     std_sort(LM, n_lm, [](const LocMin &a, const LocMin &b) { return b.y < a.y; }, STK,
              cap.stack, &fail);

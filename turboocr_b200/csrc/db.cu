@@ -88,9 +88,10 @@ constexpr int kBigQPts = (int)((kBigSmem - kBigTabBytes) / sizeof(P2));
 constexpr unsigned long long kPoolBytesPerPoint = 256;
 static_assert(kBigSmem <= 227 * 1024, "shared memory of the CTA geometry path");
 
-// Counters of the geometry stages: [0] contour list length, [1] ring list
-// length, [2..3] pool bytes used (u64), [4] scored-slot list length.
-constexpr int kCounters = 6;
+// Counters of the geometry stages: [0] contour list length, [1] large-ring
+// list length, [2..3] pool bytes used (u64), [4] scored-slot list length,
+// [5] small-ring list length, [6] next unclip work item.
+constexpr int kCounters = 8;
 
 // ---------------------------------------------------------------- union-find --
 // Root of v with path halving: each visited node is re-pointed at its
@@ -667,11 +668,13 @@ geom_box1_kernel(const int *__restrict__ n_contours, const int *__restrict__ npt
                  const long long *__restrict__ pt_off, const P2 *__restrict__ pts,
                  int *__restrict__ stage1, int4 *__restrict__ aabb, int *__restrict__ list,
                  int *__restrict__ counters, int *__restrict__ score_done,
-                 int *__restrict__ score_list, int *__restrict__ stage2, DbParams P) {
+                 int *__restrict__ score_list, int *__restrict__ stage2,
+                 int *__restrict__ keep2, DbParams P) {
   const long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= (long long)P.n_maps * kMaxCand) return;
   stage1[c] = 0;
   stage2[c] = 0;
+  keep2[c] = 0;
   score_done[c] = 0;
   const int m = (int)(c / kMaxCand), rank = (int)(c % kMaxCand);
   const int n = npts[c];
@@ -881,11 +884,11 @@ constexpr int kScoreGroups = 8;
 
 __global__ void __launch_bounds__(kScoreThreads)
 score_kernel(const float *__restrict__ pred, const int *__restrict__ score_list,
-             const int *__restrict__ counters, const int4 *__restrict__ aabb, const int *__restrict__ npts,
+             int *__restrict__ counters, const int4 *__restrict__ aabb, const int *__restrict__ npts,
              const long long *__restrict__ pt_off, const P2 *__restrict__ pts,
              int *__restrict__ stage2, float *__restrict__ score, double *__restrict__ dist,
              double *__restrict__ part_sum, long long *__restrict__ part_cnt,
-             int *__restrict__ done, DbParams P) {
+             int *__restrict__ done, int *__restrict__ ring_list, DbParams P) {
   __shared__ unsigned s_edge[kBandRows][kMaxWords];
   __shared__ unsigned s_tog[kBandRows][kMaxWords];
   __shared__ double s_sum[kScoreThreads / 32];
@@ -1009,6 +1012,9 @@ score_kernel(const float *__restrict__ pred, const int *__restrict__ score_list,
       // unclip returns the contour itself when the perimeter is 0 (distance 0 here)
       dist[c] = per != 0. ? db::contour_area(p, n) * (double)P.unclip_ratio / per : 0.;
       stage2[c] = 1;
+      // unclip work list: large contours from the front, small ones from the back
+      if (n > kLocalPts) ring_list[atomicAdd(counters + 1, 1)] = (int)c;
+      else ring_list[(long long)P.n_maps * kMaxCand - 1 - atomicAdd(counters + 5, 1)] = (int)c;
     }
   }
   __syncthreads();
@@ -1053,24 +1059,21 @@ __device__ __forceinline__ bool axis_rect(const P2 *q, int m) {
   return h0 || v0;
 }
 
-// 7. one thread per surviving contour slot: unclip (det_postprocess.cpp
-// :57-102) as the reference computes it, i.e. Clipper's raw round-join
-// offset (DoOffset) followed by the union of that path with positive fill
-// (ClipperOffset::Execute, clipper_union.cuh), keeping the output ring of
-// largest area; then the second min-area box and finish_box. The offset
-// ring, the sweep's arrays and the hull work space come from the scratch
-// pool. When the pool or the sweep's bounds run out, the box comes from the
-// raw offset ring instead and status bit kErrUnion is set.
-__global__ void __launch_bounds__(128)
-union_kernel(const int *__restrict__ stage2, const int *__restrict__ npts,
-             const long long *__restrict__ pt_off, const P2 *__restrict__ pts,
-             const double *__restrict__ dist, const int *__restrict__ geo,
-             int *__restrict__ keep2, int *__restrict__ boxes, char *__restrict__ pool,
-             int *__restrict__ pool_counters, int *__restrict__ status, DbParams P) {
-  const long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= (long long)P.n_maps * kMaxCand) return;
-  keep2[c] = 0;
-  if (!stage2[c]) return;
+// 7. unclip of one contour slot (det_postprocess.cpp:57-102) as the reference
+// computes it: Clipper's raw round-join offset (DoOffset), the union of that
+// path with positive fill (ClipperOffset::Execute, clipper_union.cuh), the
+// output ring of largest area; then the second min-area box and finish_box.
+// Runs on lane 0 of a warp whose other lanes serve the sweep's list-wide
+// steps (bk). The offset ring, the sweep's arrays and the hull work space
+// come from the scratch pool. When the pool or the sweep's bounds run out,
+// the box comes from the raw offset ring instead and status bit kErrUnion is
+// set.
+__device__ void unclip_one(long long c, const int *__restrict__ npts,
+                           const long long *__restrict__ pt_off, const P2 *__restrict__ pts,
+                           const double *__restrict__ dist, const int *__restrict__ geo,
+                           int *__restrict__ keep2, int *__restrict__ boxes,
+                           char *__restrict__ pool, int *__restrict__ pool_counters,
+                           int *__restrict__ status, const DbParams &P, db::cu::BulkArgs *bk) {
   const int n = npts[c];
   const P2 *p = pts + pt_off[c];
   const double d = dist[c];
@@ -1100,6 +1103,7 @@ union_kernel(const int *__restrict__ stage2, const int *__restrict__ npts,
       } else {
         db::cu::Sweep sw;
         sw.init(w + raw_b + out_b, raw_n);
+        sw.set_bulk(bk, 32);
         int k = -1;
         if (sw.execute(raw, raw_n)) k = sw.best_ring(out, out_cap);
         if (k < 0) {  // sweep out of bounds: the raw ring stands in, flagged
@@ -1121,6 +1125,39 @@ union_kernel(const int *__restrict__ stage2, const int *__restrict__ npts,
     return;
   }
   finish_box(r, c, geo, keep2, boxes, P);
+}
+
+
+// One warp per unclip work item (large contours first, from the list that
+// score_kernel filled): the sweeps of different rings take different
+// branches, so they do not share a warp.
+__global__ void __launch_bounds__(128)
+union_kernel(const int *__restrict__ ring_list, int *__restrict__ counters,
+             const int *__restrict__ npts, const long long *__restrict__ pt_off,
+             const P2 *__restrict__ pts, const double *__restrict__ dist,
+             const int *__restrict__ geo, int *__restrict__ keep2, int *__restrict__ boxes,
+             char *__restrict__ pool, int *__restrict__ status, DbParams P) {
+  __shared__ db::cu::BulkArgs s_bulk[4];
+  const int lane = threadIdx.x & 31;
+  db::cu::BulkArgs *bk = &s_bulk[threadIdx.x >> 5];
+  const long long C = (long long)P.n_maps * kMaxCand;
+  const int n_big = counters[1];
+  const int n_all = n_big + counters[5];
+  for (;;) {
+    int k = 0;
+    if (lane == 0) k = atomicAdd(counters + 6, 1);
+    k = __shfl_sync(0xffffffffu, k, 0);
+    if (k >= n_all) return;
+    const long long c = k < n_big ? ring_list[k] : ring_list[C - 1 - (k - n_big)];
+    if (lane == 0) {
+      unclip_one(c, npts, pt_off, pts, dist, geo, keep2, boxes, pool, counters, status, P, bk);
+      bk->op = db::cu::kOpStop;
+      db::cu::bulk_step(bk, 0);
+    } else {
+      while (db::cu::bulk_step(bk, lane)) {
+      }
+    }
+  }
 }
 
 // 8. kept boxes of map m in contour order. grid n_maps, kScanThreads threads.
@@ -1488,15 +1525,17 @@ TOCR_API int tocr_db_postprocess(const float *d_pred, int n_maps, int h, int w,
   gather_kernel<<<(unsigned)((C * 32 + 127) / 128), 128, 0, st>>>(
       bits, starts, npts, pt_off, slab, ovf_first, ovf_next, ovf_pts, pts, point_cap, n_maps, h, w);
   geom_box1_kernel<<<cgrid, 128, 0, st>>>(n_contours, npts, pt_off, pts, stage1, aabb, list1,
-                                          counters, score_done, list3, stage2, P);
+                                          counters, score_done, list3, stage2, keep2, P);
   const unsigned bgrid = (unsigned)(C < sm_count() ? C : sm_count());
   geom_big_kernel<<<bgrid, kBigThreads, kBigSmem, st>>>(list1, counters, npts, pt_off, pts, aabb,
                                                         stage1, list3, pool, counters, d_status, P);
   score_kernel<<<dim3((unsigned)(C < 148 * 8 ? C : 148 * 8), kScoreGroups), kScoreThreads, 0, st>>>(
       d_pred, list3, counters, aabb, npts, pt_off, pts, stage2, score, dist, part_sum, part_cnt,
-      score_done, P);
-  union_kernel<<<cgrid, 128, 0, st>>>(stage2, npts, pt_off, pts, dist, d_geometry, keep2, boxes,
-                                      pool, counters, d_status, P);
+      score_done, list1, P);
+  // list1 (geom_big_kernel's large-contour list) is reused for the unclip work list
+  const unsigned ugrid = (unsigned)std::min<long long>((C + 3) / 4, (long long)sm_count() * 16);
+  union_kernel<<<ugrid, 128, 0, st>>>(list1, counters, npts, pt_off, pts, dist, d_geometry, keep2,
+                                      boxes, pool, d_status, P);
   compact_kernel<<<n_maps, kScanThreads, 0, st>>>(keep2, boxes, score, d_boxes, d_scores, d_counts,
                                                   d_status, max_boxes);
   return check_launch("tocr_db_postprocess");
