@@ -234,6 +234,51 @@ TOCR_API int tocr_gpu_ccl_detect(const uint8_t *d_bitmap, const float *d_pred, i
                                  void *h_boxes, int *h_num_boxes, int *h_num_total,
                                  void *stream);
 
+/* ---- mode-2 unclip: per-component disc growth (src/kernels/jfa.cu) -------- */
+
+/* Replaces cuda_accumulate_crack_perimeter (kernels.h:181-189,
+ * src/kernels/jfa.cu:165-185, 458-469): d_perim[id] (num_slots ints, zeroed
+ * here) = number of 4-connected pixel edges of component id (compact-id map
+ * int[h][w], -1 = background) that face background or the image border. */
+TOCR_API int tocr_jfa_crack_perimeter(const int32_t *d_compact_ids, const uint8_t *d_bitmap,
+                                      int w, int h, int num_slots, int *d_perim, void *stream);
+
+/* Replaces cuda_compute_expand_per_comp (kernels.h:191-200, jfa.cu:191-212,
+ * 471-482): per slot of the PRE-filter records of tocr_gpu_ccl_detect (sum
+ * of prediction in `score`), 0 when pixel_count < 3, a box side < 3 or the
+ * mean < box_thresh, else pixel_count * unclip_ratio / perimeter clamped to
+ * [min_expand, max_expand]. */
+TOCR_API int tocr_jfa_expand_per_comp(const void *d_bboxes, const int *d_perim, int num_slots,
+                                      float unclip_ratio, float min_expand, float max_expand,
+                                      float box_thresh, float *d_expand, void *stream);
+
+/* Replaces cuda_jfa_expand_labels (kernels.h:172-179, jfa.cu:75-146,
+ * 436-456): d_labels uint32[h][w] = 1 + the component id a pixel belongs to
+ * after growth (0 = none): foreground keeps its component (when its distance
+ * is positive); background goes to the nearest boundary pixel (foreground
+ * with a background 8-neighbour) whose component's distance e reaches it
+ * (d2 <= e*e), ties to the smaller id. d_keys uint32[h][w] scratch.
+ * d_seed_list: NULL, or uint32[h*w] scratch that receives the compacted
+ * boundary pixels (faster; the reference's unused d_seeds_alt). */
+TOCR_API int tocr_jfa_expand_labels(const uint8_t *d_bitmap, const int32_t *d_compact_ids,
+                                    const float *d_expand, uint32_t *d_labels, int w, int h,
+                                    uint32_t *d_keys, uint32_t *d_seed_list, void *stream);
+
+/* Replaces cuda_jfa_extract_bboxes (kernels.h:202-209, jfa.cu:214-250,
+ * 484-498): per slot (label - 1) the box and pixel count of the grown
+ * region (slots without pixels: pixel_count 0). */
+TOCR_API int tocr_jfa_extract_bboxes(const uint32_t *d_labels, int w, int h, void *d_bboxes,
+                                     int num_slots, void *stream);
+
+/* Replaces cuda_jfa_extract_oriented (kernels.h:210-229, jfa.cu:252-434):
+ * the box, pixel count and the corners of the rectangle aligned with the
+ * principal axis of the grown region (PCA of its pixel coordinates, angle 0
+ * when nearly isotropic) in ox/oy. d_moments uint64[num_slots*6] and
+ * d_orient float[num_slots*6] scratch. */
+TOCR_API int tocr_jfa_extract_oriented(const uint32_t *d_labels, int w, int h, void *d_bboxes,
+                                       int num_slots, unsigned long long *d_moments,
+                                       float *d_orient, void *stream);
+
 /* ---- recognition crops (replace the host-side crop loop of PaddleRec) ----- */
 
 /* compute_crop_transform (include/turbo_ocr/common/geometry/perspective.h:25-67,

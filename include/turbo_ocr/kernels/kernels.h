@@ -79,4 +79,39 @@ int cuda_gpu_ccl_detect(const uint8_t *d_bitmap, const float *d_pred_map, int w,
                         GpuDetBox *d_bboxes, int *d_num_boxes, GpuDetBox *h_boxes,
                         int *h_num_boxes, cudaStream_t stream, int *h_num_total = nullptr);
 
+// kernels.h:172-179 — mode-2 growth of every component by its own distance
+// (d_expand_per_comp, indexed by compact id): d_expanded_labels = 1 + the
+// winning component (0 = none). d_seeds (uint32[w*h]) holds the per-pixel
+// winner keys; d_seeds_alt (uint32[w*h], may be null) receives the compacted
+// boundary pixels. max_expand is not needed (each disc has its own radius).
+void cuda_jfa_expand_labels(const uint8_t *d_bitmap, const int32_t *d_compact_ids,
+                            const float *d_expand_per_comp, uint32_t *d_expanded_labels, int w,
+                            int h, float max_expand, uint32_t *d_seeds, uint32_t *d_seeds_alt,
+                            cudaStream_t stream);
+
+// kernels.h:181-189 — exposed 4-connected crack edges per compact id
+// (d_perim_per_comp zeroed here).
+void cuda_accumulate_crack_perimeter(const int32_t *d_compact_ids, const uint8_t *d_bitmap,
+                                     int w, int h, int num_slots, int *d_perim_per_comp,
+                                     cudaStream_t stream);
+
+// kernels.h:191-200 — per-slot growth distance from the PRE-filter boxes of
+// cuda_gpu_ccl_detect and the crack perimeters.
+void cuda_compute_expand_per_comp(const GpuDetBox *d_bboxes, const int *d_perim_per_comp,
+                                  int num_slots, float unclip_ratio, float min_expand,
+                                  float max_expand, float box_thresh, float *d_expand_per_comp,
+                                  cudaStream_t stream);
+
+// kernels.h:202-209 — box and pixel count of every grown region.
+void cuda_jfa_extract_bboxes(const uint32_t *d_expanded_labels, int w, int h,
+                             GpuDetBox *d_bboxes, int num_slots, cudaStream_t stream);
+
+// kernels.h:210-229 — box, pixel count and principal-axis rectangle corners
+// (ox/oy) of every grown region; d_moments uint64[num_slots*6] and d_orient
+// float[num_slots*6] scratch.
+void cuda_jfa_extract_oriented(const uint32_t *d_expanded_labels, int w, int h,
+                               GpuDetBox *d_bboxes, int num_slots,
+                               unsigned long long *d_moments, float *d_orient,
+                               cudaStream_t stream);
+
 }  // namespace turbo_ocr::kernels

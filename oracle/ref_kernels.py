@@ -1,5 +1,6 @@
 """ORACLE (test infrastructure only): the reference's own CUDA kernels
-(src/kernels/preprocess_kernels.cu, src/kernels/reduce_kernels.cu) compiled
+(src/kernels/preprocess_kernels.cu, src/kernels/reduce_kernels.cu,
+src/kernels/jfa.cu) compiled
 unchanged into oracle/_ref/libref_kernels.so. GPU tests use them to pin the
 fp32 arithmetic of the B200 kernels bit for bit."""
 from __future__ import annotations
@@ -21,6 +22,12 @@ def lib():
                                     C.c_void_p]
         L.refk_fused_single.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_longlong, C.c_void_p,
                                         C.c_int, C.c_int, C.c_void_p]
+        vp, i, f = C.c_void_p, C.c_int, C.c_float
+        L.refk_jfa_crack.argtypes = [vp, vp, i, i, i, vp, vp]
+        L.refk_jfa_expand_per_comp.argtypes = [vp, vp, i, f, f, f, f, vp, vp]
+        L.refk_jfa_expand_labels.argtypes = [vp, vp, vp, vp, i, i, f, vp, vp, vp]
+        L.refk_jfa_extract_bboxes.argtypes = [vp, i, i, vp, i, vp]
+        L.refk_jfa_extract_oriented.argtypes = [vp, i, i, vp, i, vp, vp, vp]
         L._tocr_ready = True
     return L
 

@@ -1,7 +1,7 @@
 // Test-infrastructure wrapper (oracle only): C entry points over the
-// REFERENCE's own CUDA kernels (src/kernels/preprocess_kernels.cu and
-// src/kernels/reduce_kernels.cu, compiled unchanged from the reference tree
-// by oracle/Makefile). Used on the GPU box by tests/ to pin the fp32
+// REFERENCE's own CUDA kernels (src/kernels/preprocess_kernels.cu,
+// src/kernels/reduce_kernels.cu and src/kernels/jfa.cu, compiled unchanged
+// from the reference tree by oracle/Makefile). Used on the GPU box by tests/ to pin the fp32
 // arithmetic of the B200 kernels to the reference kernel's bits.
 #include <exception>
 
@@ -70,6 +70,67 @@ int refk_fused_single(const void *src, int rows, int cols, long long step, float
     img.cols = cols;
     turbo_ocr::kernels::cuda_fused_resize_normalize_det(img, dst, dst_w, dst_h,
                                                         (cudaStream_t)stream);
+  } catch (const std::exception &) {
+    return 2;
+  }
+  return 0;
+}
+
+// src/kernels/jfa.cu: the mode-2 unclip stages, one call each.
+int refk_jfa_crack(const int *cid, const unsigned char *bm, int w, int h, int slots, int *perim,
+                   void *stream) {
+  try {
+    turbo_ocr::kernels::cuda_accumulate_crack_perimeter(cid, bm, w, h, slots, perim,
+                                                        (cudaStream_t)stream);
+  } catch (const std::exception &) {
+    return 2;
+  }
+  return 0;
+}
+
+int refk_jfa_expand_per_comp(const void *boxes, const int *perim, int slots, float ratio,
+                             float emin, float emax, float box_thresh, float *expand,
+                             void *stream) {
+  try {
+    turbo_ocr::kernels::cuda_compute_expand_per_comp(
+        static_cast<const turbo_ocr::kernels::GpuDetBox *>(boxes), perim, slots, ratio, emin,
+        emax, box_thresh, expand, (cudaStream_t)stream);
+  } catch (const std::exception &) {
+    return 2;
+  }
+  return 0;
+}
+
+int refk_jfa_expand_labels(const unsigned char *bm, const int *cid, const float *expand,
+                           unsigned *labels, int w, int h, float max_expand, unsigned *seeds,
+                           unsigned *seeds_alt, void *stream) {
+  try {
+    turbo_ocr::kernels::cuda_jfa_expand_labels(bm, cid, expand, labels, w, h, max_expand, seeds,
+                                               seeds_alt, (cudaStream_t)stream);
+  } catch (const std::exception &) {
+    return 2;
+  }
+  return 0;
+}
+
+int refk_jfa_extract_bboxes(const unsigned *labels, int w, int h, void *boxes, int slots,
+                            void *stream) {
+  try {
+    turbo_ocr::kernels::cuda_jfa_extract_bboxes(
+        labels, w, h, static_cast<turbo_ocr::kernels::GpuDetBox *>(boxes), slots,
+        (cudaStream_t)stream);
+  } catch (const std::exception &) {
+    return 2;
+  }
+  return 0;
+}
+
+int refk_jfa_extract_oriented(const unsigned *labels, int w, int h, void *boxes, int slots,
+                              unsigned long long *mom, float *orient, void *stream) {
+  try {
+    turbo_ocr::kernels::cuda_jfa_extract_oriented(
+        labels, w, h, static_cast<turbo_ocr::kernels::GpuDetBox *>(boxes), slots, mom, orient,
+        (cudaStream_t)stream);
   } catch (const std::exception &) {
     return 2;
   }

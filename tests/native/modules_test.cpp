@@ -256,12 +256,63 @@ int gpu_mode(const std::string &pages_path, int n, const std::string &dict, cons
   return 0;
 }
 
+// PaddleDet with GPU_CCL=2 (set by the caller): run_batch and run on the
+// pages; the stand-in probability map of every page as PaddleDet computes it
+// (the map the mode-2 chain starts from) goes to <outdir>/prob<i>.f32.
+int det2_mode(const std::string &pages_path, int n, const std::string &out) {
+  const int H = 960, W = 960;
+  const size_t page_bytes = (size_t)H * W * 3;
+  std::vector<unsigned char> host(page_bytes * n);
+  {
+    std::ifstream f(pages_path, std::ios::binary);
+    f.read(reinterpret_cast<char *>(host.data()), (std::streamsize)host.size());
+    if (!f) { std::fprintf(stderr, "cannot read pages\n"); return 2; }
+  }
+  unsigned char *d_pages = nullptr;
+  ck(cudaMalloc(&d_pages, host.size()), "malloc");
+  ck(cudaMemcpy(d_pages, host.data(), host.size(), cudaMemcpyHostToDevice), "H2D");
+  cudaStream_t st;
+  ck(cudaStreamCreate(&st), "stream");
+  std::vector<GpuImage> imgs(n);
+  std::vector<std::pair<int, int>> dims(n, {H, W});
+  for (int i = 0; i < n; ++i) imgs[i] = GpuImage{d_pages + i * page_bytes, (size_t)W * 3, H, W};
+  detection::PaddleDet det;
+  if (!det.load_model("synthetic", {"max", 960, 960}, {0.3f, 0.6f, 1.5f})) return 3;
+  auto boxes = det.run_batch(imgs, dims, st);
+  auto scores = det.last_scores();
+  auto single = det.run(imgs[0], H, W, st);
+  float *d_chw = nullptr, *d_prob = nullptr;
+  ck(cudaMalloc(&d_chw, sizeof(float) * 3 * H * W), "malloc");
+  ck(cudaMalloc(&d_prob, sizeof(float) * H * W), "malloc");
+  for (int i = 0; i < n; ++i) {
+    throw_on_status(tocr_preprocess_one_f32(imgs[i].data, (int)imgs[i].step, H, W, d_chw, W, H,
+                                            nullptr, nullptr, st), "preprocess");
+    throw_on_status(tocr_det_standin_prob_f32(d_chw, 1, H, W, nullptr, nullptr, nullptr, 12.f,
+                                              d_prob, st), "stand-in prob");
+    ck(cudaStreamSynchronize(st), "sync");
+    dump(out + "/prob" + std::to_string(i) + ".f32", d_prob, (size_t)H * W);
+  }
+  std::printf("{\"single_same\":%d,\"pages\":[", (int)(single == boxes[0]));
+  for (int i = 0; i < n; ++i) {
+    std::printf("%s{\"boxes\":[", i ? "," : "");
+    for (size_t k = 0; k < boxes[i].size(); ++k) std::printf("%s%s", k ? "," : "", jbox(boxes[i][k]).c_str());
+    std::printf("],\"scores\":[");
+    for (size_t k = 0; k < scores[i].size(); ++k) std::printf("%s%.9g", k ? "," : "", (double)scores[i][k]);
+    std::printf("]}");
+  }
+  std::printf("]}\n");
+  return 0;
+}
+
 }  // namespace
 
 int main(int argc, char **argv) {
   if (argc >= 3 && std::string(argv[1]) == "host") return host_mode(argv[2]);
   if (argc >= 6 && std::string(argv[1]) == "gpu")
     return gpu_mode(argv[2], std::atoi(argv[3]), argv[4], argv[5]);
-  std::fprintf(stderr, "usage: modules_test host <dict> | gpu <pages> <n> <dict> <outdir>\n");
+  if (argc >= 5 && std::string(argv[1]) == "det2")
+    return det2_mode(argv[2], std::atoi(argv[3]), argv[4]);
+  std::fprintf(stderr, "usage: modules_test host <dict> | gpu <pages> <n> <dict> <outdir> | "
+                       "det2 <pages> <n> <outdir>\n");
   return 1;
 }

@@ -86,6 +86,11 @@ SIGNATURES: dict[str, tuple] = {
     "tocr_rec_standin_logits_f16": (_i, [_vp, _vp, _i, _i, _i, _u64, _vp]),
     "tocr_gpu_ccl_detect": (_i, [_vp, _vp, _i, _i, _f, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                  _vp]),
+    "tocr_jfa_crack_perimeter": (_i, [_vp, _vp, _i, _i, _i, _vp, _vp]),
+    "tocr_jfa_expand_per_comp": (_i, [_vp, _vp, _i, _f, _f, _f, _f, _vp, _vp]),
+    "tocr_jfa_expand_labels": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp, _vp, _vp]),
+    "tocr_jfa_extract_bboxes": (_i, [_vp, _i, _i, _vp, _i, _vp]),
+    "tocr_jfa_extract_oriented": (_i, [_vp, _i, _i, _vp, _i, _vp, _vp, _vp]),
     "tocr_compute_det_resize": (_i, [_i, _i, _i, _i, _i, _vp, _vp]),
     "tocr_read_det_resize": (_i, [_vp, _vp, _vp]),
     "tocr_effective_det_max_side": (_i, [_i]),

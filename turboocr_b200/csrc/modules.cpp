@@ -5,7 +5,10 @@
 // host results, as the reference modules do (paddle_det.cpp:136-311,
 // paddle_rec.cpp:215-448).
 #include <algorithm>
+#include <cmath>
 #include <cstdint>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <utility>
@@ -121,11 +124,29 @@ struct PaddleDet::Impl {
   static constexpr float kMinBoxSide = 3.0f;       // paddle_det.h:62
   static constexpr float kMinUnclippedSide = 5.0f; // paddle_det.h:63
 
+  static constexpr int kMaxComp = 3000;     // kMaxGpuComponents
+  static constexpr int kRec = 14;           // ints per GpuDetBox record (56 bytes)
+  static constexpr float kMaxExpand = 24.0f;  // paddle_det_ccl.cpp:190
+
   bool loaded = false;
   DetResizeParams resize = kDetResizeDefault;
   DbParams db = kDbDefaults;
+  // GPU_CCL mode (paddle_det.cpp:74-97): 0 contours, 1 CCL + per-ROI contours
+  // (the reference default), 2 per-component disc growth. Modes 0 and 1 both
+  // run the full-map contour path here (tocr_db_postprocess).
+  int mode = 1;
+  float box_thresh = kDbDefaults.box_thresh;
+  float unclip_scale = 1.0f;
   int max_side = 0;
   size_t ws_bytes = 0;
+
+  // mode 2 buffers (allocated by load_model when mode == 2)
+  DevBuf<uint8_t> bitmap;
+  DevBuf<int> ccl_labels, ccl_cid, ccl_counter, ccl_nbox, ccl_boxes, perim;
+  DevBuf<uint32_t> jfa_labels, jfa_keys, jfa_seeds;
+  DevBuf<float> expand, orient;
+  DevBuf<unsigned long long> moments;
+  PinBuf<int> h_ccl_boxes, h_exp_boxes;
 
   DevBuf<float> canvas, prob;
   DevBuf<char> ws;
@@ -167,6 +188,94 @@ struct PaddleDet::Impl {
     h_sw.alloc(kMaxBatch);
     h_dh.alloc(kMaxBatch);
     h_dw.alloc(kMaxBatch);
+    if (mode == 2) {
+      bitmap.alloc(px);
+      ccl_labels.alloc(px);
+      ccl_cid.alloc(px);
+      ccl_counter.alloc(1);
+      ccl_nbox.alloc(1);
+      ccl_boxes.alloc((size_t)2 * kMaxComp * kRec);
+      perim.alloc(kMaxComp);
+      jfa_labels.alloc(px);
+      jfa_keys.alloc(px);
+      jfa_seeds.alloc(px);
+      expand.alloc(kMaxComp);
+      moments.alloc((size_t)kMaxComp * 6);
+      orient.alloc((size_t)kMaxComp * 6);
+      h_ccl_boxes.alloc((size_t)kMaxComp * kRec);
+      h_exp_boxes.alloc((size_t)kMaxComp * kRec);
+    }
+  }
+
+  // run_gpu_ccl_fast (paddle_det_ccl.cpp:142-258) on map m of `prob` (h x w
+  // canvas, content ch x cw of an oh x ow image): CCL, crack perimeters,
+  // growth distances (min 2, max 24), disc growth, principal-axis rectangles,
+  // then the reference's host filter and scaling. The score kept per box is
+  // the component's mean prediction. Synchronises the stream.
+  std::vector<Box> post_mode2(int m, int h, int w, int oh, int ow, int ch, int cw,
+                              std::vector<float> &scores, cudaStream_t st) {
+    const float *pm = prob.p + (size_t)m * h * w;
+    throw_on_status(tocr_threshold_u8(pm, bitmap.p, w, h, 1, db.thresh, st), "PaddleDet threshold");
+    int h_nb = 0, h_total = 0;
+    throw_on_status(tocr_gpu_ccl_detect(bitmap.p, pm, w, h, box_thresh, ccl_labels.p, ccl_cid.p,
+                                        ccl_counter.p, ccl_boxes.p, ccl_nbox.p, h_ccl_boxes.p,
+                                        &h_nb, &h_total, st),
+                    "PaddleDet CCL");
+    std::vector<Box> out;
+    scores.clear();
+    if (h_nb == 0) return out;
+    const int slots = std::min(h_total, kMaxComp);
+    if (slots == 0) return out;
+    int *exp_boxes = ccl_boxes.p + (size_t)kMaxComp * kRec;
+    throw_on_status(tocr_jfa_crack_perimeter(ccl_cid.p, bitmap.p, w, h, slots, perim.p, st),
+                    "PaddleDet crack perimeter");
+    throw_on_status(tocr_jfa_expand_per_comp(ccl_boxes.p, perim.p, slots,
+                                             db.unclip_ratio * unclip_scale, 2.0f, kMaxExpand,
+                                             box_thresh, expand.p, st),
+                    "PaddleDet expand distances");
+    throw_on_status(tocr_jfa_expand_labels(bitmap.p, ccl_cid.p, expand.p, jfa_labels.p, w, h,
+                                           jfa_keys.p, jfa_seeds.p, st),
+                    "PaddleDet label growth");
+    // component means come from the pre-filter records, read before the
+    // oriented pass overwrites the filtered half of the box buffer
+    cuda_check(cudaMemcpyAsync(h_ccl_boxes.p, ccl_boxes.p, (size_t)slots * kRec * sizeof(int),
+                               cudaMemcpyDeviceToHost, st),
+               "PaddleDet D2H");
+    throw_on_status(tocr_jfa_extract_oriented(jfa_labels.p, w, h, exp_boxes, slots, moments.p,
+                                              orient.p, st),
+                    "PaddleDet oriented boxes");
+    cuda_check(cudaMemcpyAsync(h_exp_boxes.p, exp_boxes, (size_t)slots * kRec * sizeof(int),
+                               cudaMemcpyDeviceToHost, st),
+               "PaddleDet D2H");
+    cuda_check(cudaStreamSynchronize(st), "PaddleDet sync");
+    const float ratio_h = static_cast<float>(ch) / oh;
+    const float ratio_w = static_cast<float>(cw) / ow;
+    for (int i = 0; i < slots; ++i) {
+      const int *r = h_exp_boxes.p + (size_t)i * kRec;
+      const int xmin = r[0], ymin = r[1], xmax = r[2], ymax = r[3], pc = r[5];
+      if (pc < 9) continue;
+      const int bw = xmax - xmin + 1, bh = ymax - ymin + 1;
+      if (bw < kMinUnclippedSide || bh < kMinUnclippedSide) continue;
+      float px[4], py[4];
+      std::memcpy(px, r + 6, sizeof px);
+      std::memcpy(py, r + 10, sizeof py);
+      order_quad_tl_tr_br_bl(px, py);
+      Box box;
+      for (int k = 0; k < 4; ++k)
+        box[k] = {std::clamp(static_cast<int>(std::round(px[k] / ratio_w)), 0, ow - 1),
+                  std::clamp(static_cast<int>(std::round(py[k] / ratio_h)), 0, oh - 1)};
+      const int rw = static_cast<int>(std::sqrt(double((box[0][0] - box[1][0]) * (box[0][0] - box[1][0]) +
+                                                       (box[0][1] - box[1][1]) * (box[0][1] - box[1][1]))));
+      const int rh = static_cast<int>(std::sqrt(double((box[0][0] - box[3][0]) * (box[0][0] - box[3][0]) +
+                                                       (box[0][1] - box[3][1]) * (box[0][1] - box[3][1]))));
+      if (rw <= 3 || rh <= 3) continue;
+      out.push_back(box);
+      const int *pre = h_ccl_boxes.p + (size_t)i * kRec;
+      float sum;
+      std::memcpy(&sum, pre + 4, sizeof sum);
+      scores.push_back(pre[5] > 0 ? sum / (float)pre[5] : 0.0f);
+    }
+    return out;
   }
 
   char *ws_aligned() const {
@@ -179,10 +288,18 @@ struct PaddleDet::Impl {
     throw_on_status(tocr_det_standin_prob_f32(canvas.p, n, h, w, content.p, nullptr, nullptr,
                                               kStandinGain, prob.p, st),
                     "PaddleDet stand-in head");
+    if (mode == 2) {
+      std::vector<std::vector<Box>> out(n);
+      last_scores.assign(n, {});
+      for (int m = 0; m < n; ++m)
+        out[m] = post_mode2(m, h, w, h_geo.p[4 * m], h_geo.p[4 * m + 1], h_content.p[2 * m],
+                            h_content.p[2 * m + 1], last_scores[m], st);
+      return out;
+    }
     const size_t need = tocr_db_workspace_bytes(n, h, w, 0, 0);
     if (need > ws_bytes) throw InferenceError("PaddleDet: DB workspace too small");
-    throw_on_status(tocr_db_postprocess(prob.p, n, h, w, geo.p, db.thresh, db.box_thresh,
-                                        db.unclip_ratio, kMinBoxSide, kMinUnclippedSide, 0, 0,
+    throw_on_status(tocr_db_postprocess(prob.p, n, h, w, geo.p, db.thresh, box_thresh,
+                                        db.unclip_ratio * unclip_scale, kMinBoxSide, kMinUnclippedSide, 0, 0,
                                         ws_aligned(), need, boxes.p, scores.p, counts.p,
                                         kMaxBoxes, status.p, st),
                     "PaddleDet DB post-process");
@@ -224,6 +341,34 @@ TOCR_MOD_API bool PaddleDet::load_model(const std::string &model_path,
   Impl &I = *impl_;
   I.resize = read_det_resize(resize);
   I.db = read_db_params(db);
+  // GPU_CCL / GPU_BOX_THRESH / GPU_UNCLIP_SCALE (paddle_det.cpp:74-103):
+  // empty or malformed values keep the default, parsed values are clamped.
+  auto env_num = [](const char *name, float cur) {
+    const char *v = std::getenv(name);
+    if (!v || !*v) return cur;
+    char *end = nullptr;
+    const float x = std::strtof(v, &end);
+    if (end == v || *end != '\0' || std::isnan(x)) {
+      std::fprintf(stderr, "[PaddleDet] ignoring malformed %s=\"%s\"\n", name, v);
+      return cur;
+    }
+    return x;
+  };
+  {
+    const char *v = std::getenv("GPU_CCL");
+    int mode = 1;
+    if (v && *v) {
+      char *end = nullptr;
+      const long x = std::strtol(v, &end, 10);
+      if (end == v || *end != '\0')
+        std::fprintf(stderr, "[PaddleDet] ignoring malformed GPU_CCL=\"%s\"\n", v);
+      else
+        mode = (int)std::clamp<long>(x, 0, 2);
+    }
+    I.mode = mode;
+  }
+  I.box_thresh = std::clamp(env_num("GPU_BOX_THRESH", I.db.box_thresh), 0.001f, 1.0f);
+  I.unclip_scale = std::clamp(env_num("GPU_UNCLIP_SCALE", 1.0f), 0.1f, 10.0f);
   I.max_side = effective_det_max_side(I.resize);
   I.allocate();
   I.loaded = true;

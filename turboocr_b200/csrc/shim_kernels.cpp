@@ -85,6 +85,52 @@ TOCR_SHIM_API int cuda_gpu_ccl_detect(const uint8_t *d_bitmap, const float *d_pr
   return *h_num_boxes;
 }
 
+TOCR_SHIM_API void cuda_jfa_expand_labels(const uint8_t *d_bitmap, const int32_t *d_compact_ids,
+                                          const float *d_expand_per_comp,
+                                          uint32_t *d_expanded_labels, int w, int h,
+                                          float /*max_expand*/, uint32_t *d_seeds,
+                                          uint32_t *d_seeds_alt, cudaStream_t stream) {
+  throw_on_status(tocr_jfa_expand_labels(d_bitmap, d_compact_ids, d_expand_per_comp,
+                                         d_expanded_labels, w, h, d_seeds, d_seeds_alt, stream),
+                  "cuda_jfa_expand_labels");
+}
+
+TOCR_SHIM_API void cuda_accumulate_crack_perimeter(const int32_t *d_compact_ids,
+                                                   const uint8_t *d_bitmap, int w, int h,
+                                                   int num_slots, int *d_perim_per_comp,
+                                                   cudaStream_t stream) {
+  throw_on_status(tocr_jfa_crack_perimeter(d_compact_ids, d_bitmap, w, h, num_slots,
+                                           d_perim_per_comp, stream),
+                  "cuda_accumulate_crack_perimeter");
+}
+
+TOCR_SHIM_API void cuda_compute_expand_per_comp(const GpuDetBox *d_bboxes,
+                                                const int *d_perim_per_comp, int num_slots,
+                                                float unclip_ratio, float min_expand,
+                                                float max_expand, float box_thresh,
+                                                float *d_expand_per_comp, cudaStream_t stream) {
+  throw_on_status(tocr_jfa_expand_per_comp(d_bboxes, d_perim_per_comp, num_slots, unclip_ratio,
+                                           min_expand, max_expand, box_thresh,
+                                           d_expand_per_comp, stream),
+                  "cuda_compute_expand_per_comp");
+}
+
+TOCR_SHIM_API void cuda_jfa_extract_bboxes(const uint32_t *d_expanded_labels, int w, int h,
+                                           GpuDetBox *d_bboxes, int num_slots,
+                                           cudaStream_t stream) {
+  throw_on_status(tocr_jfa_extract_bboxes(d_expanded_labels, w, h, d_bboxes, num_slots, stream),
+                  "cuda_jfa_extract_bboxes");
+}
+
+TOCR_SHIM_API void cuda_jfa_extract_oriented(const uint32_t *d_expanded_labels, int w, int h,
+                                             GpuDetBox *d_bboxes, int num_slots,
+                                             unsigned long long *d_moments, float *d_orient,
+                                             cudaStream_t stream) {
+  throw_on_status(tocr_jfa_extract_oriented(d_expanded_labels, w, h, d_bboxes, num_slots,
+                                            d_moments, d_orient, stream),
+                  "cuda_jfa_extract_oriented");
+}
+
 TOCR_SHIM_API void cuda_batch_threshold_to_u8(const float *src, uint8_t *dst, int w, int h,
                                               int batch_size, float thresh,
                                               cudaStream_t stream) {
