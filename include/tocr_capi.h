@@ -315,6 +315,32 @@ TOCR_API int tocr_roi_warp_f32(const uint8_t *d_src, int src_h, int src_w, int s
                                int dst_h, int dst_w, const float *mean3, const float *inv_std3,
                                float inv_scale, float *d_dst, void *stream);
 
+/* ---- text-line angle classifier (PaddleCls, src/classification/paddle_cls.cpp) */
+
+/* The classifier network's stem: y = hardswish(conv3x3 stride 2 pad 1 (x) +
+ * b), x fp16 NCHW [n][3][h][w] (crops of tocr_roi_warp_f16), weights d_w
+ * fp32 [32][3][3][3], d_b [32]; y fp16 NHWC [n][(h-1)/2+1][(w-1)/2+1][32]
+ * (16-byte aligned). The module's synthetic model ("synthetic", no trained
+ * weights in this build) draws every tensor with tocr_synth_weights from
+ * seed 0x7EC0C150 + k: stem w (k=0, scale 0.53), b (k=1, 0.1); block j of
+ * (32,64,s1) (64,64,s2) (64,128,s1) (128,128,s2) (128,256,s1): wdw [C][9]
+ * (k=16+4j, 0.9), bdw (k=17+4j, 0.1), wpw [C_out][C] (k=18+4j, 0.48 / 0.34
+ * / 0.34 / 0.24 / 0.24), bpw (k=19+4j, 0.1), INT8; head w [2][256] (k=64,
+ * 1.0), b (k=65, 0.1). The scales keep the activation variance near one
+ * through the hardswish layers. */
+TOCR_API int tocr_cls_stem_f16(const void *d_x, int n, int h, int w, const float *d_w,
+                               const float *d_b, void *d_y, void *stream);
+
+/* The classifier network's head: per sample the mean of every channel over
+ * the hw pixels of x fp16 NHWC [n][hw][c], logits l_k = b_k + sum_c w[k][c]
+ * mean_c (k = 0, 1), scores fp32 [n][2] = softmax(l) = (score_0, score_180). */
+TOCR_API int tocr_cls_head_f32(const void *d_x, int n, int hw, int c, const float *d_w,
+                               const float *d_b, float *d_scores, void *stream);
+
+/* Host: n seeded weights in [-scale, scale): out[i] = scale * (2u - 1), u =
+ * (splitmix64(seed + (i + 1) * 0x9E3779B97F4A7C15) >> 40) / 2^24. */
+TOCR_API int tocr_synth_weights(uint64_t seed, float scale, float *out, long long n);
+
 /* ---- stand-in network heads (no trained weights in this build) ------------- */
 
 /* The detection module's stand-in for the trained DB network (the synthetic

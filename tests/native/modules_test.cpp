@@ -17,6 +17,7 @@
 #include <vector>
 
 #include "tocr_capi.h"
+#include "turbo_ocr/classification/paddle_cls.h"
 #include "turbo_ocr/common/errors.h"
 #include "turbo_ocr/common/geometry/box.h"
 #include "turbo_ocr/common/geometry/perspective.h"
@@ -25,6 +26,7 @@
 #include "turbo_ocr/detection/det_postprocess.h"
 #include "turbo_ocr/detection/paddle_det.h"
 #include "turbo_ocr/kernels/kernels.h"
+#include "turbo_ocr/pipeline/classify_angles.h"
 #include "turbo_ocr/pipeline/ocr_pipeline_detail.h"
 #include "turbo_ocr/recognition/ctc_decode.h"
 #include "turbo_ocr/recognition/paddle_rec.h"
@@ -304,12 +306,59 @@ int det2_mode(const std::string &pages_path, int n, const std::string &out) {
   return 0;
 }
 
+// PaddleCls on page 0: the boxes PaddleDet finds plus a few vertical ones;
+// run() on all of them and the pipeline's gated classify_angles().
+int cls_mode(const std::string &pages_path, const std::string &out) {
+  (void)out;
+  const int H = 960, W = 960;
+  std::vector<unsigned char> host((size_t)H * W * 3);
+  {
+    std::ifstream f(pages_path, std::ios::binary);
+    f.read(reinterpret_cast<char *>(host.data()), (std::streamsize)host.size());
+    if (!f) { std::fprintf(stderr, "cannot read pages\n"); return 2; }
+  }
+  unsigned char *d_page = nullptr;
+  ck(cudaMalloc(&d_page, host.size()), "malloc");
+  ck(cudaMemcpy(d_page, host.data(), host.size(), cudaMemcpyHostToDevice), "H2D");
+  cudaStream_t st;
+  ck(cudaStreamCreate(&st), "stream");
+  const GpuImage img{d_page, (size_t)W * 3, H, W};
+  detection::PaddleDet det;
+  if (!det.load_model("synthetic", {"max", 960, 960}, {0.3f, 0.6f, 1.5f})) return 3;
+  std::vector<Box> all = det.run(img, H, W, st);
+  for (int k = 0; k < 12; ++k) {  // vertical strips across the text lines
+    const int x = 40 + 70 * k, y = 60 + 23 * k, w = 18 + 3 * (k % 4), h = 90 + 17 * k;
+    all.push_back(Box{{{{x, y}, {x + w, y + 2}, {x + w - 1, y + h}, {x - 1, y + h - 2}}}});
+  }
+  classification::PaddleCls cls;
+  if (cls.load_model("/no/such/cls.trt")) return 4;
+  if (!cls.load_model("synthetic")) return 5;
+  cls.allocate_buffers();
+  std::vector<Box> ran = all;
+  cls.run(img, ran, st);
+  const auto scores = cls.last_scores();
+  std::vector<Box> gated = all;
+  pipeline::classify_angles(cls, img, gated, st);
+  auto list = [](const std::vector<Box> &bs) {
+    std::string o = "[";
+    for (size_t k = 0; k < bs.size(); ++k) o += (k ? "," : "") + jbox(bs[k]);
+    return o + "]";
+  };
+  std::printf("{\"in\":%s,\"out\":%s,\"gated\":%s,\"scores\":[", list(all).c_str(),
+              list(ran).c_str(), list(gated).c_str());
+  for (size_t k = 0; k < scores.size(); ++k)
+    std::printf("%s[%.9g,%.9g]", k ? "," : "", (double)scores[k][0], (double)scores[k][1]);
+  std::printf("]}\n");
+  return 0;
+}
+
 }  // namespace
 
 int main(int argc, char **argv) {
   if (argc >= 3 && std::string(argv[1]) == "host") return host_mode(argv[2]);
   if (argc >= 6 && std::string(argv[1]) == "gpu")
     return gpu_mode(argv[2], std::atoi(argv[3]), argv[4], argv[5]);
+  if (argc >= 4 && std::string(argv[1]) == "cls") return cls_mode(argv[2], argv[3]);
   if (argc >= 5 && std::string(argv[1]) == "det2")
     return det2_mode(argv[2], std::atoi(argv[3]), argv[4]);
   std::fprintf(stderr, "usage: modules_test host <dict> | gpu <pages> <n> <dict> <outdir> | "

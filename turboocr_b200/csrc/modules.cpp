@@ -14,10 +14,14 @@
 #include <utility>
 #include <vector>
 
+#include <climits>
+
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "crop_geom.cuh"
 #include "tocr_capi.h"
+#include "turbo_ocr/classification/paddle_cls.h"
 #include "turbo_ocr/common/errors.h"
 #include "turbo_ocr/common/geometry/perspective.h"
 #include "turbo_ocr/detection/det_postprocess.h"
@@ -468,6 +472,164 @@ TOCR_MOD_API const DetResizeParams &PaddleDet::resize_params() const { return im
 TOCR_MOD_API const DbParams &PaddleDet::db_params() const { return impl_->db; }
 
 }  // namespace detection
+
+// ----------------------------------------------------------------- PaddleCls --
+namespace classification {
+
+struct PaddleCls::Impl {
+  static constexpr int kBatch = 128;         // kClsBatchNum
+  static constexpr int kH = 80, kW = 160;    // kClsImageH / kClsImageW
+  static constexpr float kThresh = 0.9f;     // kClsThresh
+  static constexpr uint64_t kSeed = 0x7EC0C150ull;
+  struct BlockCfg {
+    int c, co, stride;
+    float pw_scale;
+  };
+  static constexpr BlockCfg kBlocks[5] = {
+      {32, 64, 1, 0.48f}, {64, 64, 2, 0.34f}, {64, 128, 1, 0.34f},
+      {128, 128, 2, 0.24f}, {128, 256, 1, 0.24f}};
+
+  bool loaded = false, allocated = false;
+  DevBuf<__half_raw> crops, act0, act1;
+  DevBuf<float> stem_w, stem_b, head_w, head_b, scores, minv;
+  DevBuf<char> blobs[5];
+  DevBuf<int> crop_w, crop_page, n_crops, err;
+  PinBuf<float> h_scores, h_minv;
+  PinBuf<int> h_crop_w, h_n;
+  std::vector<std::array<float, 2>> last;
+
+  static std::vector<float> synth(int k, float scale, size_t n) {
+    std::vector<float> v(n);
+    throw_on_status(tocr_synth_weights(kSeed + (uint64_t)k, scale, v.data(), (long long)n),
+                    "PaddleCls weights");
+    return v;
+  }
+  template <class T>
+  static void upload(DevBuf<T> &d, const std::vector<T> &h) {
+    d.alloc(h.size());
+    cuda_check(cudaMemcpy(d.p, h.data(), h.size() * sizeof(T), cudaMemcpyHostToDevice),
+               "PaddleCls weights H2D");
+  }
+
+  void load_weights() {
+    upload(stem_w, synth(0, 0.53f, 32 * 27));
+    upload(stem_b, synth(1, 0.1f, 32));
+    for (int j = 0; j < 5; ++j) {
+      const BlockCfg &b = kBlocks[j];
+      const auto wdw = synth(16 + 4 * j, 0.9f, (size_t)b.c * 9);
+      const auto bdw = synth(17 + 4 * j, 0.1f, (size_t)b.c);
+      const auto wpw = synth(18 + 4 * j, b.pw_scale, (size_t)b.co * b.c);
+      const auto bpw = synth(19 + 4 * j, 0.1f, (size_t)b.co);
+      const size_t bytes = tocr_dwpw_packed_bytes(b.c, b.co);
+      std::vector<char> blob(bytes);
+      throw_on_status(tocr_dwpw_pack(b.c, b.co, 0, wdw.data(), bdw.data(), wpw.data(),
+                                     bpw.data(), blob.data(), bytes),
+                      "PaddleCls block pack");
+      upload(blobs[j], blob);
+    }
+    upload(head_w, synth(64, 1.0f, 2 * 256));
+    upload(head_b, synth(65, 0.1f, 2));
+  }
+
+  void allocate() {
+    if (allocated) return;
+    crops.alloc((size_t)kBatch * 3 * kH * kW);
+    act0.alloc((size_t)kBatch * (kH / 2) * (kW / 2) * 64);
+    act1.alloc((size_t)kBatch * (kH / 2) * (kW / 2) * 64);
+    scores.alloc((size_t)kBatch * 2);
+    minv.alloc((size_t)kBatch * 9);
+    crop_w.alloc(kBatch);
+    n_crops.alloc(1);
+    err.alloc(1);
+    crop_page.alloc(kBatch);
+    cuda_check(cudaMemset(crop_page.p, 0, kBatch * sizeof(int)), "PaddleCls memset");
+    cuda_check(cudaMemset(err.p, 0, sizeof(int)), "PaddleCls memset");
+    h_scores.alloc((size_t)kBatch * 2);
+    h_minv.alloc((size_t)kBatch * 9);
+    h_crop_w.alloc(kBatch);
+    h_n.alloc(1);
+    allocated = true;
+  }
+};
+
+TOCR_MOD_API PaddleCls::PaddleCls() : impl_(std::make_unique<Impl>()) {}
+TOCR_MOD_API PaddleCls::~PaddleCls() noexcept = default;
+
+TOCR_MOD_API bool PaddleCls::load_model(const std::string &model_path) {
+  if (model_path != "synthetic") return false;
+  impl_->load_weights();
+  impl_->loaded = true;
+  return true;
+}
+
+TOCR_MOD_API void PaddleCls::allocate_buffers() { impl_->allocate(); }
+
+TOCR_MOD_API const std::vector<std::array<float, 2>> &PaddleCls::last_scores() const {
+  return impl_->last;
+}
+
+TOCR_MOD_API void PaddleCls::run(const GpuImage &img, std::vector<Box> &boxes,
+                                 cudaStream_t stream) {
+  Impl &I = *impl_;
+  I.last.clear();
+  if (boxes.empty()) return;
+  if (!I.loaded) throw InferenceError("PaddleCls::run: no model loaded");
+  if (img.step > (size_t)INT_MAX) throw InferenceError("PaddleCls::run: image step too large");
+  I.allocate();
+  const int total = (int)boxes.size();
+  I.last.resize(total);
+  for (int beg = 0; beg < total; beg += Impl::kBatch) {
+    const int nb = std::min(Impl::kBatch, total - beg);
+    for (int j = 0; j < nb; ++j) {
+      const CropTransform ct = compute_crop_transform(boxes[beg + j], Impl::kH, Impl::kW);
+      I.h_crop_w.p[j] = ct.crop_width;
+      std::memcpy(I.h_minv.p + 9 * j, ct.M_inv, 9 * sizeof(float));
+    }
+    I.h_n.p[0] = nb;
+    cuda_check(cudaMemcpyAsync(I.minv.p, I.h_minv.p, (size_t)nb * 9 * sizeof(float),
+                               cudaMemcpyHostToDevice, stream), "PaddleCls H2D");
+    cuda_check(cudaMemcpyAsync(I.crop_w.p, I.h_crop_w.p, (size_t)nb * sizeof(int),
+                               cudaMemcpyHostToDevice, stream), "PaddleCls H2D");
+    cuda_check(cudaMemcpyAsync(I.n_crops.p, I.h_n.p, sizeof(int), cudaMemcpyHostToDevice, stream),
+               "PaddleCls H2D");
+    throw_on_status(tocr_roi_warp_f16(static_cast<const uint8_t *>(img.data), 0, img.rows,
+                                      img.cols, (int)img.step, I.minv.p, I.crop_w.p,
+                                      I.crop_page.p, I.n_crops.p, nb, Impl::kH, Impl::kW,
+                                      nullptr, nullptr, 1.0f / 255.0f, I.crops.p, stream),
+                    "PaddleCls crops");
+    throw_on_status(tocr_cls_stem_f16(I.crops.p, nb, Impl::kH, Impl::kW, I.stem_w.p, I.stem_b.p,
+                                      I.act0.p, stream),
+                    "PaddleCls stem");
+    int h = Impl::kH / 2, w = Impl::kW / 2;
+    DevBuf<__half_raw> *src = &I.act0, *dst = &I.act1;
+    for (int j = 0; j < 5; ++j) {
+      const Impl::BlockCfg &b = Impl::kBlocks[j];
+      throw_on_status(tocr_dwpw_block(src->p, dst->p, nb, h, w, b.c, b.co, b.stride, 0,
+                                      I.blobs[j].p, I.err.p, stream),
+                      "PaddleCls block");
+      h = (h - 1) / b.stride + 1;
+      w = (w - 1) / b.stride + 1;
+      std::swap(src, dst);
+    }
+    throw_on_status(tocr_cls_head_f32(src->p, nb, h * w, 256, I.head_w.p, I.head_b.p, I.scores.p,
+                                      stream),
+                    "PaddleCls head");
+    cuda_check(cudaMemcpyAsync(I.h_scores.p, I.scores.p, (size_t)nb * 2 * sizeof(float),
+                               cudaMemcpyDeviceToHost, stream), "PaddleCls D2H");
+    cuda_check(cudaStreamSynchronize(stream), "PaddleCls sync");
+    for (int j = 0; j < nb; ++j) {
+      const float s0 = I.h_scores.p[2 * j], s180 = I.h_scores.p[2 * j + 1];
+      I.last[beg + j] = {s0, s180};
+      if (s180 > s0 && s180 > Impl::kThresh) {
+        Box &box = boxes[beg + j];
+        std::swap(box[0], box[2]);
+        std::swap(box[1], box[3]);
+      }
+    }
+  }
+}
+
+}  // namespace classification
 
 // ----------------------------------------------------------------- PaddleRec --
 namespace recognition {
