@@ -103,6 +103,25 @@ TOCR_API int tocr_ctc_greedy_f16(const void *d_logits, int batch_size,
                                  float *d_line_scores, int *d_step_idx,
                                  float *d_step_prob, void *stream);
 
+/* The recognizer's CTC head fused with the greedy decode, on the tensor
+ * cores: logits l = feat · W^T + bias are formed tile by tile in TMEM and
+ * reduced on the SM (never written), then collapsed as tocr_ctc_greedy_f16
+ * does. The reference writes the logits [N, T, V] from its TensorRT
+ * recognizer (src/recognition/paddle_rec.cpp:48-90) and decodes them with
+ * cuda_argmax + ctc_greedy_decode (reduce_kernels.cu:15-93,
+ * ctc_decode.cpp:25-88); per step the results are the same argmax (lowest
+ * index on ties) and p = 1 / sum_j exp(l_j - l_max).
+ * d_feat fp16 [batch_size * seq_len][K], d_w fp16 [num_classes][K] (both
+ * row-major, 16-byte aligned), d_bias fp32 [num_classes]; K = 64 or 128.
+ * Outputs and step buffers as tocr_ctc_greedy_f16. d_err (device int,
+ * caller-zeroed) receives a non-zero code if a bounded device-side wait gave
+ * up (the call itself still returns TOCR_OK). */
+TOCR_API int tocr_rec_head_ctc_f16(const void *d_feat, int batch_size, int seq_len, int K,
+                                   const void *d_w, const float *d_bias, int num_classes,
+                                   int num_labels, int *d_tokens, int *d_lengths,
+                                   float *d_line_scores, int *d_step_idx, float *d_step_prob,
+                                   int *d_err, void *stream);
+
 /* Allocation-free variant of tocr_ctc_greedy_f16 (no counterpart in the
  * reference). It is for callers that may not call cudaMalloc at all: plugins
  * hosted by an engine that owns every device allocation, or serving

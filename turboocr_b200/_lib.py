@@ -91,6 +91,8 @@ SIGNATURES: dict[str, tuple] = {
     "tocr_jfa_expand_labels": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp, _vp, _vp]),
     "tocr_jfa_extract_bboxes": (_i, [_vp, _i, _i, _vp, _i, _vp]),
     "tocr_jfa_extract_oriented": (_i, [_vp, _i, _i, _vp, _i, _vp, _vp, _vp]),
+    "tocr_rec_head_ctc_f16": (_i, [_vp, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp,
+                                   _vp, _vp]),
     "tocr_cls_stem_f16": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "tocr_cls_head_f32": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "tocr_synth_weights": (_i, [_u64, _f, _vp, _ll]),

@@ -13,6 +13,7 @@
 // only (num_classes is odd for the PP-OCR dictionaries), so each row is split
 // into a scalar head up to the first 16-byte boundary, an aligned body and a
 // scalar tail. A second, tiny launch collapses each line with one warp.
+#include "ctc_internal.h"
 #include "tocr_common.cuh"
 
 #include <cmath>
@@ -273,6 +274,17 @@ int rows_grid(K kernel, long long rows) {
 }
 
 }  // namespace
+
+int launch_ctc_collapse(const int *step_idx, const float *step_prob, int batch, int T,
+                        int num_labels, int *tokens, int *lengths, float *scores,
+                        const int *d_batch, cudaStream_t stream) {
+  if (batch <= 0) return TOCR_OK;
+  const int blocks = (batch + kCollapseWarps - 1) / kCollapseWarps;
+  ctc_collapse_kernel<<<blocks, kCollapseWarps * 32, 0, stream>>>(
+      step_idx, step_prob, batch, T, num_labels, tokens, lengths, scores, d_batch);
+  return check_launch("ctc_collapse_kernel");
+}
+
 }  // namespace tocr
 
 using namespace tocr;
