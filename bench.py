@@ -14,6 +14,8 @@ Workloads:
   preprocess  config 3: 256 u8 HWC images (sides 600..2000) -> fp16 960x960 NCHW
   dwpw        config 4: fused DW3x3+PW1x1 block, 32 x 240 x 240 x 128 -> 256, INT8
   db          config 1: DB post-process of 8 fp32 960x960 probability maps
+  rec_head    the recognizer's CTC head (K=128 -> 18385 classes) fused with the
+              greedy decode on tcgen05, 8192 lines x 80 steps per GPU
 """
 from __future__ import annotations
 
@@ -36,6 +38,17 @@ sys.path.insert(0, str(ROOT))
 
 MEASURED = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_TFLOPS = 1590.0
+
+
+def tensor_peak():
+    """Dense fp16/bf16 tensor peak: the measured cuBLAS burst figure."""
+    if MEASURED.exists():
+        try:
+            return float(json.loads(MEASURED.read_text())["bf16_tflops"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_TFLOPS, "fallback"
 
 
 def hbm_peak():
@@ -295,6 +308,79 @@ class DwPwWorkload:
         self.x.copy_(self.h_x, non_blocking=True)
         self.blk(self.x, self.y)
         self.h_y.copy_(self.y, non_blocking=True)
+
+class RecHeadWorkload:
+    """The recognizer's CTC head (fp16 features [lines*80][128] x weights
+    [18385][128] + bias) fused with the greedy decode on tcgen05
+    (tocr_rec_head_ctc_f16): the logits are formed and reduced on the SM."""
+    name = "rec_head_ctc_8192x80_k128_v18385"
+    metric = "lines/sec recognizer CTC head + greedy decode (80 steps, K=128, V=18385)"
+    unit = "lines/s"
+    dtype = "f16 operands, f32 accumulate (tcgen05 kind::f16)"
+    bound = "tensor"
+    B, T, K, V = 8192, 80, 128, 18385
+    default_units = B
+    launches_per_step = 2
+    l2_note = "features 168 MB per step > 126 MB L2 (no flush needed); weights 4.7 MB stay in L2"
+    dominant = "rec_head_kernel + ctc_collapse_kernel per launch"
+
+    def __init__(self, dev, seed, units=None):
+        L = __import__("turboocr_b200").lib()
+        self.L = L
+        if units:
+            self.B = units
+        rows = self.B * self.T
+        g = torch.Generator(device=dev).manual_seed(seed)
+        self.feat = torch.randn(rows, self.K, generator=g, device=dev).to(torch.float16)
+        self.w = (torch.randn(self.V, self.K, generator=g, device=dev) *
+                  (3.0 / self.K ** 0.5)).to(torch.float16)
+        self.bias = torch.randn(self.V, generator=g, device=dev) * 0.5
+        self.toks = torch.empty(rows, dtype=torch.int32, device=dev)
+        self.lens = torch.empty(self.B, dtype=torch.int32, device=dev)
+        self.sc = torch.empty(self.B, dtype=torch.float32, device=dev)
+        self.sidx = torch.empty(rows, dtype=torch.int32, device=dev)
+        self.sprob = torch.empty(rows, dtype=torch.float32, device=dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.units_per_step = self.B
+        self.algo_bytes = rows * self.K * 2 + self.V * self.K * 2 + self.V * 4 + rows * 4 + self.B * 8
+        self.algo_flops = 2 * rows * self.K * self.V
+        torch.cuda.synchronize()
+
+    def step(self):
+        st = self.L.tocr_rec_head_ctc_f16(
+            self.feat.data_ptr(), self.B, self.T, self.K, self.w.data_ptr(), self.bias.data_ptr(),
+            self.V, self.V - 2, self.toks.data_ptr(), self.lens.data_ptr(), self.sc.data_ptr(),
+            self.sidx.data_ptr(), self.sprob.data_ptr(), self.err.data_ptr(),
+            torch.cuda.current_stream().cuda_stream)
+        assert st == 0, self.L.tocr_last_error_string()
+
+    def dominant_kernel_ms(self, iters=10):
+        s = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(iters):
+            self.step()
+        e1.record(s)
+        torch.cuda.synchronize()
+        assert int(self.err.item()) == 0
+        return e0.elapsed_time(e1) / iters
+
+    def setup_e2e(self):
+        self.h_feat = torch.empty(self.feat.shape, dtype=torch.float16, pin_memory=True)
+        self.h_feat.copy_(self.feat)
+        self.h_tok = torch.empty(self.toks.shape, dtype=torch.int32, pin_memory=True)
+        self.h_len = torch.empty(self.B, dtype=torch.int32, pin_memory=True)
+        self.h_sc = torch.empty(self.B, dtype=torch.float32, pin_memory=True)
+        self.h2d = self.h_feat.numel() * 2
+        self.d2h = self.h_tok.numel() * 4 + self.B * 8
+
+    def e2e_step(self):
+        self.feat.copy_(self.h_feat, non_blocking=True)
+        self.step()
+        self.h_tok.copy_(self.toks, non_blocking=True)
+        self.h_len.copy_(self.lens, non_blocking=True)
+        self.h_sc.copy_(self.sc, non_blocking=True)
+
 
 def det_resize_max960(h, w):
     """compute_det_resize with {"max", 960, 960} (det_config.h:58-81), as the
@@ -556,9 +642,9 @@ E2E_SCHEDULE = [(32, 64, 1), (64, 64, 2), (64, 128, 1), (128, 128, 2),
                 (128, 128, 1), (128, 128, 2), (128, 128, 1), (128, 256, 1)]
 
 WORKLOADS = {"db": DbWorkload, "ctc": CtcWorkload, "preprocess": PreprocessWorkload,
-             "dwpw": DwPwWorkload,
+             "dwpw": DwPwWorkload, "rec_head": RecHeadWorkload,
              "e2e": E2eWorkload}
-SEEDS = {"db": 0, "ctc": 1, "preprocess": 2, "dwpw": 3, "e2e": 5}
+SEEDS = {"db": 0, "ctc": 1, "preprocess": 2, "dwpw": 3, "e2e": 5, "rec_head": 6}
 
 
 # ------------------------------------------------------------------ main ----
@@ -662,6 +748,10 @@ def main():
         value = wl.units_per_step * world / (ms_step / 1e3)
         peak, peak_kind = hbm_peak()
         achieved = wl.algo_bytes / (kernel_ms / 1e3) / 1e9
+        tensor_bound = getattr(Wl, "bound", "hbm") == "tensor"
+        if tensor_bound:
+            peak, peak_kind = tensor_peak()
+            achieved = wl.algo_flops / (kernel_ms / 1e3) / 1e12
         line = {
             "metric": Wl.metric, "value": value, "unit": Wl.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
@@ -672,12 +762,14 @@ def main():
             "gpu_launches": wl.launches_per_step * args.steps,
             "e2e": {"value": wl.units_per_step * world / (ms_e2e / 1e3), "unit": Wl.unit,
                     "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+            "roofline": {"bound": "tensor" if tensor_bound else "hbm", "achieved": achieved,
+                         "peak": peak, "unit": "TFLOP/s" if tensor_bound else "GB/s",
                          "frac": achieved / peak,
                          "traffic": getattr(Wl, "traffic_per_launch", None) or
                                     (getattr(Wl, "traffic_per_unit", 0) * wl.units_per_step or None),
                          "traffic_source": getattr(Wl, "traffic_source", None),
-                         "peak_source": f"{peak_kind} hbm_gbs",
+                         "peak_source": f"{peak_kind} " + ("bf16_tflops" if tensor_bound
+                                                            else "hbm_gbs"),
                          "algorithmic_bytes_per_launch": wl.algo_bytes},
             "clocks": clk,
         }

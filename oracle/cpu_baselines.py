@@ -176,4 +176,39 @@ def db(cores: int, n_steps: int, maps: int = 8):
                   "sample": f"{maps} maps per step, one process per map (cv2 + reference Clipper)"}
 
 
-BASELINES = {"e2e": e2e, "ctc": ctc, "preprocess": preprocess, "dwpw": dwpw, "db": db}
+def rec_head(cores: int, n_steps: int, lines: int = 0):
+    """The recognizer head + decode on the host: torch fp32 (all threads) for
+    logits = features @ W^T + bias, argmax and max softmax probability per
+    step, then the reference collapse (oracle/ctc_oracle.py). The reference
+    runs this layer inside TensorRT, so the baseline is this restatement."""
+    import torch
+    from . import ctc_oracle as co
+    T, K, V = 80, 128, 18385
+    n = lines or max(4 * cores, 32)
+    torch.set_num_threads(cores)
+    g = torch.Generator().manual_seed(SEED + 6)
+    feat = torch.randn(n * T, K, generator=g).to(torch.float16).float()
+    w = (torch.randn(V, K, generator=g) * (3.0 / K ** 0.5)).to(torch.float16).float()
+    b = torch.randn(V, generator=g) * 0.5
+
+    def once():
+        logits = feat @ w.T + b
+        m, idx = logits.max(dim=1)
+        p = 1.0 / torch.exp(logits - m[:, None]).sum(dim=1)
+        idx, p = idx.numpy(), p.numpy().astype(np.float32)
+        for line in range(n):
+            co.collapse(idx[line * T:(line + 1) * T].tolist(), p[line * T:(line + 1) * T], V - 2)
+
+    once()
+    vals = []
+    for _ in range(n_steps):
+        t0 = time.perf_counter()
+        once()
+        vals.append(n / (time.perf_counter() - t0))
+    return vals, {"kind": "port", "cores": cores, "units_per_step": n,
+                  "sample": f"{n} lines x 80 steps per step, K=128, V=18385: torch fp32 GEMM "
+                            "+ argmax + softmax max on all threads, then the reference collapse"}
+
+
+BASELINES = {"e2e": e2e, "ctc": ctc, "preprocess": preprocess, "dwpw": dwpw, "db": db,
+             "rec_head": rec_head}

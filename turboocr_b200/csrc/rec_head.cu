@@ -15,12 +15,20 @@
 // exp(l_j - l_max), the same definitions as tocr_ctc_greedy_f16 on stored
 // logits; then the same collapse kernel makes tokens and line scores.
 //
-// Roles (10 warps): warp 0 issues the TMA loads (the A tile once, then the
+// Roles (18 warps): warp 0 issues the TMA loads (the A tile once, then the
 // weight chunks into a 2-stage ring), warp 1 owns TMEM and one lane issues
-// the MMAs, warps 2..9 are the epilogue: two warps per TMEM lane quadrant,
-// each on one half (128 columns) of every chunk; the halves are combined at
-// the end. Every wait is bounded (about a second); a wait that gives up sets
-// the error word, every role unwinds and TMEM is released.
+// the MMAs, warps 2..17 are the epilogue: four warps per TMEM lane quadrant,
+// each on one quarter (64 columns) of every chunk; the quarters are combined
+// at the end. The epilogue works in the log2 domain, y = l * log2(e): the
+// four warps of a part stage bias * log2(e) of their 64 columns in shared
+// memory once per chunk (-inf past the vocabulary, so no column test is
+// left in the loop); per logit one multiply-add makes y, a max tree gives
+// the group maximum (its first index is only looked for when it beats the
+// running maximum), and exp2(y - base) goes into four partial sums, where
+// base is 0 while the row's maximum stays within 2^64 of it (no subtraction
+// then) and follows the maximum otherwise. Every
+// wait is bounded (about a second); a wait that gives up sets the error
+// word, every role unwinds and TMEM is released.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -41,9 +49,12 @@ using namespace ptx;
 
 constexpr int kRows = 128;         // timestep rows per CTA (MMA M, TMEM lanes)
 constexpr int kChunk = 256;        // vocabulary rows per chunk (MMA N)
-constexpr int kThreads = 320;      // 10 warps
 constexpr int kEpiWarp0 = 2;
-constexpr int kEpiThreads = 256;   // 8 epilogue warps
+constexpr int kEpiWarps = 16;      // four per TMEM lane quadrant
+constexpr int kParts = kEpiWarps / 4;            // column parts of a chunk
+constexpr int kPartCols = kChunk / kParts;       // 64
+constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps);
+constexpr int kEpiThreads = 32 * kEpiWarps;
 constexpr int kTmemCols = 2 * kChunk;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -58,7 +69,8 @@ struct Cfg {
   static constexpr int OFF_BAR = OFF_B + STAGES * B_BYTES;
   static constexpr int OFF_MISC = OFF_BAR + 16 * 8;
   static constexpr int OFF_COMB = OFF_MISC + 16;
-  static constexpr int SMEM = OFF_COMB + kRows * 12 + 1024;  // + alignment slack
+  static constexpr int OFF_BIAS = OFF_COMB + (kParts - 1) * 3 * kRows * 4;
+  static constexpr int SMEM = OFF_BIAS + 2 * kChunk * 4 + 1024;  // + alignment slack
 };
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -102,7 +114,8 @@ rec_head_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant_
   uint64_t *acc_empty = bars + 3 + 2 * C::STAGES;  // [2]
   uint32_t *s_tmem = reinterpret_cast<uint32_t *>(smem + C::OFF_MISC);
   volatile int *s_abort = reinterpret_cast<volatile int *>(smem + C::OFF_MISC + 4);
-  float *comb = reinterpret_cast<float *>(smem + C::OFF_COMB);  // [3][kRows]
+  float *comb = reinterpret_cast<float *>(smem + C::OFF_COMB);  // [kParts-1][3][kRows]
+  float *sbias = reinterpret_cast<float *>(smem + C::OFF_BIAS);  // [2][kChunk], bias*log2(e)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = blockIdx.x * kRows;
@@ -162,7 +175,7 @@ rec_head_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant_
         const uint32_t d = tmem + (uint32_t)(b * kChunk);
 #pragma unroll
         for (int k = 0; k < 4 * KA; ++k) {
-          const uint32_t off = (uint32_t)((k >> 2) * 0) + 32u * (k & 3);
+          const uint32_t off = 32u * (k & 3);  // K = 16 step within the 128-byte row
           const uint64_t ad = sw128_kmajor_desc(a_addr + (k >> 2) * (kRows * 128) + off);
           const uint64_t bd = sw128_kmajor_desc(b_addr + (k >> 2) * (kChunk * 128) + off);
           mma_f16(d, ad, bd, idesc, k > 0 ? 1u : 0u);
@@ -173,91 +186,119 @@ rec_head_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant_
     }
   } else {
     // ---------------------------------------------------------- epilogue --
-    const int ew = warp - kEpiWarp0;     // 0..7
-    const int half = ew >> 2;            // column half of every chunk
+    const int ew = warp - kEpiWarp0;     // 0..15
+    const int part = ew >> 2;            // column part of every chunk
     const int quad = warp & 3;           // TMEM lane quadrant this warp may read
     const int r = quad * 32 + lane;      // row within the tile
-    float m = -INFINITY, sum = 0.0f;
+    // running max of y = l*log2(e), its first column, and sum of exp2(y - base)
+    float my = -INFINITY, sum = 0.0f, base = 0.0f;
     int idx = 0;
     bool ok = true;
+    const int pt = (ew & 3) * 32 + lane;  // thread index within the part's 4 warps
     for (int c = 0; c < NC; ++c) {
       const int b = c & 1, u2 = c >> 1;
+      const int col0 = c * kChunk + part * kPartCols;
+      float *b2 = sbias + b * kChunk + part * kPartCols;
+      if (pt < kPartCols) {
+        const int col = col0 + pt;
+        b2[pt] = col < prm.V ? __ldg(prm.bias + col) * kLog2e : -INFINITY;
+      }
+      // every warp of the part meets here each chunk, so a wait that gave up
+      // in one of them ends the loop of all four together
+      if (!named_bar_and(2 + part, 128, ok)) break;
       ok = mbar_wait_bounded(&acc_full[b], u2 & 1, s_abort, prm.err, 55);
-      if (!ok) break;
+      if (!ok) continue;
       tc_fence_after();
-      const int col0 = c * kChunk + half * 128;
-      const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * kChunk + half * 128);
-#pragma unroll 1
-      for (int g = 0; g < 4; ++g) {
-        uint32_t v[32];
-        tmem_ld32(taddr + 32 * g, v);
+      const uint32_t taddr =
+          tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * kChunk + part * kPartCols);
+      uint32_t va[32], vb[32];
+      tmem_ld32(taddr, va);
+#pragma unroll
+      for (int g = 0; g < kPartCols / 32; ++g) {
+        uint32_t(&v)[32] = (g & 1) ? vb : va;
         tmem_ld_wait(v);
+        if (g + 1 < kPartCols / 32) tmem_ld32(taddr + 32 * (g + 1), (g & 1) ? va : vb);
         const int cb = col0 + 32 * g;
-        const int nvalid = min(32, prm.V - cb);  // columns past V are zero rows of the map
-        if (nvalid <= 0) continue;
-        float l[32];
-        const float4 *bp = reinterpret_cast<const float4 *>(prm.bias + cb);
+        if (cb >= prm.V) continue;
+        float y[32];
+        const float4 *bq = reinterpret_cast<const float4 *>(b2 + 32 * g);
 #pragma unroll
         for (int j4 = 0; j4 < 8; ++j4) {
-          float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (4 * j4 + 3 < nvalid) {
-            bb = __ldg(bp + j4);
-          } else {
-            float t[4] = {0.f, 0.f, 0.f, 0.f};
-            for (int q = 0; q < 4; ++q)
-              if (4 * j4 + q < nvalid) t[q] = __ldg(prm.bias + cb + 4 * j4 + q);
-            bb = make_float4(t[0], t[1], t[2], t[3]);
-          }
-          l[4 * j4 + 0] = __uint_as_float(v[4 * j4 + 0]) + bb.x;
-          l[4 * j4 + 1] = __uint_as_float(v[4 * j4 + 1]) + bb.y;
-          l[4 * j4 + 2] = __uint_as_float(v[4 * j4 + 2]) + bb.z;
-          l[4 * j4 + 3] = __uint_as_float(v[4 * j4 + 3]) + bb.w;
+          const float4 bb = bq[j4];
+          y[4 * j4 + 0] = fmaf(__uint_as_float(v[4 * j4 + 0]), kLog2e, bb.x);
+          y[4 * j4 + 1] = fmaf(__uint_as_float(v[4 * j4 + 1]), kLog2e, bb.y);
+          y[4 * j4 + 2] = fmaf(__uint_as_float(v[4 * j4 + 2]), kLog2e, bb.z);
+          y[4 * j4 + 3] = fmaf(__uint_as_float(v[4 * j4 + 3]), kLog2e, bb.w);
         }
-        // group max and its first index (strictly greater keeps the earlier)
-        float gm = -INFINITY;
-        int gi = 0;
+        // group maximum by a tree (depth 5)
+        float t16[16];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const bool in = j < nvalid;
-          if (in && l[j] > gm) {
-            gm = l[j];
-            gi = j;
+        for (int j = 0; j < 16; ++j) t16[j] = fmaxf(y[j], y[j + 16]);
+#pragma unroll
+        for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+          for (int j = 0; j < w; ++j) t16[j] = fmaxf(t16[j], t16[j + w]);
+        const float gm = t16[0];
+        if (gm > my) {  // a new running maximum: its first column
+          uint32_t eq = 0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) eq |= (y[j] == gm ? 1u : 0u) << j;
+          my = gm;
+          idx = cb + __ffs(eq) - 1;
+          if (my > base + 64.0f || my < base - 64.0f) {  // keep exp2(y - base) in range
+            sum *= ex2_approx(base - my);
+            base = my;
           }
         }
-        if (gm > m) {
-          sum = sum * ex2_approx((m - gm) * kLog2e);
-          m = gm;
-          idx = cb + gi;
-        }
-        const float mb = m * kLog2e;
-        float acc = 0.0f;
+        float s4[4] = {0.f, 0.f, 0.f, 0.f};
+        if (__any_sync(0xffffffffu, base != 0.0f)) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (j < nvalid) acc += ex2_approx(fmaf(l[j], kLog2e, -mb));
-        sum += acc;
+          for (int j = 0; j < 32; ++j) s4[j & 3] += ex2_approx(y[j] - base);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) s4[j & 3] += ex2_approx(y[j]);
+        }
+        sum += (s4[0] + s4[1]) + (s4[2] + s4[3]);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
     }
-    // combine the two halves of every row (the lower index wins a tie)
-    if (half == 1) {
-      comb[r] = m;
-      comb[kRows + r] = sum;
-      reinterpret_cast<int *>(comb)[2 * kRows + r] = idx;
+    // the row's sum relative to its maximum: sum_j exp2(y_j - my)
+    sum = my == -INFINITY ? 0.0f : sum * ex2_approx(base - my);
+    // combine the column parts of every row (the lower index wins a tie)
+    if (part > 0) {
+      float *cp = comb + (size_t)(part - 1) * 3 * kRows;
+      cp[r] = my;
+      cp[kRows + r] = sum;
+      reinterpret_cast<int *>(cp)[2 * kRows + r] = idx;
     }
     const bool all_ok = named_bar_and(1, kEpiThreads, ok);
-    if (half == 0 && all_ok) {
-      const float m1 = comb[r], s1 = comb[kRows + r];
-      const int i1 = reinterpret_cast<int *>(comb)[2 * kRows + r];
-      float M = m, S;
-      int I = idx;
-      if (m1 > m || (m1 == m && i1 < idx)) {
-        M = m1;
-        I = i1;
+    if (part == 0 && all_ok) {
+      float pm[kParts], ps[kParts];
+      int pi[kParts];
+      pm[0] = my;
+      ps[0] = sum;
+      pi[0] = idx;
+#pragma unroll
+      for (int q = 1; q < kParts; ++q) {
+        const float *cp = comb + (size_t)(q - 1) * 3 * kRows;
+        pm[q] = cp[r];
+        ps[q] = cp[kRows + r];
+        pi[q] = reinterpret_cast<const int *>(cp)[2 * kRows + r];
       }
-      S = (m == -INFINITY ? 0.f : sum * ex2_approx((m - M) * kLog2e)) +
-          (m1 == -INFINITY ? 0.f : s1 * ex2_approx((m1 - M) * kLog2e));
+      float M = pm[0];
+      int I = pi[0];
+#pragma unroll
+      for (int q = 1; q < kParts; ++q)
+        if (pm[q] > M || (pm[q] == M && pi[q] < I)) {
+          M = pm[q];
+          I = pi[q];
+        }
+      float S = 0.f;
+#pragma unroll
+      for (int q = 0; q < kParts; ++q)
+        if (pm[q] != -INFINITY) S += ps[q] * ex2_approx(pm[q] - M);
       const int row = row0 + r;
       if (row < prm.rows) {
         prm.step_idx[row] = M == -INFINITY ? 0 : I;
