@@ -19,10 +19,10 @@
 // weight chunks into a 2-stage ring), warp 1 owns TMEM and one lane issues
 // the MMAs, warps 2..17 are the epilogue: four warps per TMEM lane quadrant,
 // each on one quarter (64 columns) of every chunk; the quarters are combined
-// at the end. The epilogue works in the log2 domain, y = l * log2(e): the
-// four warps of a part stage bias * log2(e) of their 64 columns in shared
-// memory once per chunk (-inf past the vocabulary, so no column test is
-// left in the loop); per logit one multiply-add makes y, a max tree gives
+// at the end. The epilogue works in the log2 domain, y = l * log2(e): each
+// warp stages bias * log2(e) of its next 32 columns in its own slice of
+// shared memory (one coalesced load, -inf past the vocabulary, so no column
+// test is left in the loop); per logit one multiply-add makes y, a max tree gives
 // the group maximum (its first index is only looked for when it beats the
 // running maximum), and exp2(y - base) goes into four partial sums, where
 // base is 0 while the row's maximum stays within 2^64 of it (no subtraction
@@ -70,7 +70,7 @@ struct Cfg {
   static constexpr int OFF_MISC = OFF_BAR + 16 * 8;
   static constexpr int OFF_COMB = OFF_MISC + 16;
   static constexpr int OFF_BIAS = OFF_COMB + (kParts - 1) * 3 * kRows * 4;
-  static constexpr int SMEM = OFF_BIAS + 2 * kChunk * 4 + 1024;  // + alignment slack
+  static constexpr int SMEM = OFF_BIAS + kEpiWarps * 32 * 4 + 1024;  // + alignment slack
 };
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -115,7 +115,7 @@ rec_head_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant_
   uint32_t *s_tmem = reinterpret_cast<uint32_t *>(smem + C::OFF_MISC);
   volatile int *s_abort = reinterpret_cast<volatile int *>(smem + C::OFF_MISC + 4);
   float *comb = reinterpret_cast<float *>(smem + C::OFF_COMB);  // [kParts-1][3][kRows]
-  float *sbias = reinterpret_cast<float *>(smem + C::OFF_BIAS);  // [2][kChunk], bias*log2(e)
+  float *sbias = reinterpret_cast<float *>(smem + C::OFF_BIAS);  // [kEpiWarps][32], bias*log2(e)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = blockIdx.x * kRows;
@@ -194,20 +194,18 @@ rec_head_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant_
     float my = -INFINITY, sum = 0.0f, base = 0.0f;
     int idx = 0;
     bool ok = true;
-    const int pt = (ew & 3) * 32 + lane;  // thread index within the part's 4 warps
+    float *b2 = sbias + ew * 32;          // this warp's staged bias * log2(e)
     for (int c = 0; c < NC; ++c) {
       const int b = c & 1, u2 = c >> 1;
       const int col0 = c * kChunk + part * kPartCols;
-      float *b2 = sbias + b * kChunk + part * kPartCols;
-      if (pt < kPartCols) {
-        const int col = col0 + pt;
-        b2[pt] = col < prm.V ? __ldg(prm.bias + col) * kLog2e : -INFINITY;
+      float bl[kPartCols / 32];  // this lane's bias of each group, loaded before the wait
+#pragma unroll
+      for (int g = 0; g < kPartCols / 32; ++g) {
+        const int col = col0 + 32 * g + lane;
+        bl[g] = col < prm.V ? __ldg(prm.bias + col) : 0.0f;
       }
-      // every warp of the part meets here each chunk, so a wait that gave up
-      // in one of them ends the loop of all four together
-      if (!named_bar_and(2 + part, 128, ok)) break;
       ok = mbar_wait_bounded(&acc_full[b], u2 & 1, s_abort, prm.err, 55);
-      if (!ok) continue;
+      if (!ok) break;
       tc_fence_after();
       const uint32_t taddr =
           tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * kChunk + part * kPartCols);
@@ -216,12 +214,15 @@ rec_head_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant_
 #pragma unroll
       for (int g = 0; g < kPartCols / 32; ++g) {
         uint32_t(&v)[32] = (g & 1) ? vb : va;
+        const int cb = col0 + 32 * g;
+        __syncwarp();  // the previous group's reads of b2 are done
+        b2[lane] = cb + lane < prm.V ? bl[g] * kLog2e : -INFINITY;
+        __syncwarp();
         tmem_ld_wait(v);
         if (g + 1 < kPartCols / 32) tmem_ld32(taddr + 32 * (g + 1), (g & 1) ? va : vb);
-        const int cb = col0 + 32 * g;
         if (cb >= prm.V) continue;
         float y[32];
-        const float4 *bq = reinterpret_cast<const float4 *>(b2 + 32 * g);
+        const float4 *bq = reinterpret_cast<const float4 *>(b2);
 #pragma unroll
         for (int j4 = 0; j4 < 8; ++j4) {
           const float4 bb = bq[j4];
@@ -250,15 +251,15 @@ rec_head_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant_
             base = my;
           }
         }
-        float s4[4] = {0.f, 0.f, 0.f, 0.f};
+        float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         if (__any_sync(0xffffffffu, base != 0.0f)) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) s4[j & 3] += ex2_approx(y[j] - base);
+          for (int j = 0; j < 32; ++j) s8[j & 7] += ex2_approx(y[j] - base);
         } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) s4[j & 3] += ex2_approx(y[j]);
+          for (int j = 0; j < 32; ++j) s8[j & 7] += ex2_approx(y[j]);
         }
-        sum += (s4[0] + s4[1]) + (s4[2] + s4[3]);
+        sum += ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
       }
       tc_fence_before();
       __syncwarp();
