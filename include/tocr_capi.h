@@ -334,6 +334,35 @@ TOCR_API int tocr_roi_warp_f32(const uint8_t *d_src, int src_h, int src_w, int s
                                int dst_h, int dst_w, const float *mean3, const float *inv_std3,
                                float inv_scale, float *d_dst, void *stream);
 
+/* ---- DB head of the detection network (FPN neck + binarisation head) ----- */
+/* The reference runs PP-OCR's DBFPN + DBHead inside TensorRT
+ * (include/turbo_ocr/engine/trt/trt_engine.h:37). The pieces:
+ *
+ * Convolution on the tensor cores (implicit GEMM, tcgen05): y fp16 NHWC
+ * [n][h][w][cout] = conv_k(x)(+ d_bias)(+ up2(d_up))(ReLU if relu), stride
+ * 1, pad k/2, x fp16 NHWC [n][h][w][cin]; d_up (optional) is the coarser
+ * level [n][h/2][w/2][cout] added after nearest upsampling. Shapes built:
+ * k=1 cin 256 or 128 -> cout 96 (with or without d_up), k=3 cin 96 -> 24,
+ * k=3 cin 72 -> 24 with ReLU. d_packed from tocr_conv_tc_pack (weights
+ * [cout][cin][k][k] fp32). Buffers 16-byte aligned. d_err (device int,
+ * caller-zeroed) receives a code if a bounded device-side wait gave up. */
+TOCR_API size_t tocr_conv_tc_packed_bytes(int cin, int cout, int ksize);
+TOCR_API int tocr_conv_tc_pack(int cin, int cout, int ksize, const float *w, void *out,
+                               size_t out_bytes);
+TOCR_API int tocr_conv_tc_f16(const void *d_x, int n, int h, int w, int cin, int cout, int ksize,
+                              const void *d_packed, const float *d_bias, int relu,
+                              const void *d_up, void *d_y, int *d_err, void *stream);
+/* fuse fp16 NHWC [n][h][w][72] = (p4 [n][h/4][w/4][24] up 4, p3 [n][h/2][w/2][24]
+ * up 2, p2 [n][h][w][24]) along channels (nearest upsampling). */
+TOCR_API int tocr_fpn_concat_f16(const void *d_p4, const void *d_p3, const void *d_p2, int n,
+                                 int h, int w, void *d_fuse, void *stream);
+/* The head's two stride-2 2x2 transposed convolutions and the sigmoid:
+ * h1 fp16 NHWC [n][h][w][24] -> h2 = ReLU(convT(h1; w2 [24][24][2][2], b2))
+ * -> prob fp32 [n][4h][4w] = sigmoid(convT(h2; w3 [24][1][2][2], b3)). */
+TOCR_API int tocr_db_head_up_f32(const void *d_h1, int n, int h, int w, const float *d_w2,
+                                 const float *d_b2, const float *d_w3, float b3, float *d_prob,
+                                 void *stream);
+
 /* ---- text-line angle classifier (PaddleCls, src/classification/paddle_cls.cpp) */
 
 /* The classifier network's stem: y = hardswish(conv3x3 stride 2 pad 1 (x) +

@@ -93,6 +93,11 @@ SIGNATURES: dict[str, tuple] = {
     "tocr_jfa_extract_oriented": (_i, [_vp, _i, _i, _vp, _i, _vp, _vp, _vp]),
     "tocr_rec_head_ctc_f16": (_i, [_vp, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp,
                                    _vp, _vp]),
+    "tocr_conv_tc_packed_bytes": (C.c_size_t, [_i, _i, _i]),
+    "tocr_conv_tc_pack": (_i, [_i, _i, _i, _vp, _vp, C.c_size_t]),
+    "tocr_conv_tc_f16": (_i, [_vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _i, _vp, _vp, _vp, _vp]),
+    "tocr_fpn_concat_f16": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
+    "tocr_db_head_up_f32": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp, _f, _vp, _vp]),
     "tocr_cls_stem_f16": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "tocr_cls_head_f32": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "tocr_synth_weights": (_i, [_u64, _f, _vp, _ll]),
