@@ -16,6 +16,8 @@ Workloads:
   db          config 1: DB post-process of 8 fp32 960x960 probability maps
   rec_head    the recognizer's CTC head (K=128 -> 18385 classes) fused with the
               greedy decode on tcgen05, 8192 lines x 80 steps per GPU
+  db_head     the det network's DB head (FPN neck + binarisation head) on the
+              /4, /8, /16 features of 32 pages of 960x960
 """
 from __future__ import annotations
 
@@ -382,6 +384,72 @@ class RecHeadWorkload:
         self.h_sc.copy_(self.sc, non_blocking=True)
 
 
+class DbHeadWorkload:
+    """The det network's DB head (FPN neck over the /4, /8, /16 backbone
+    levels + binarisation head, turboocr_b200/dbhead.py) on 32 pages of
+    960x960: features c2 [32][240][240][128], c3 [32][120][120][128],
+    c4 [32][60][60][256] fp16 -> probability maps [32][960][960] fp32."""
+    name = "db_head_32x960x960"
+    metric = "pages/sec DB head (FPN + binarisation head, 960x960 pages)"
+    unit = "pages/s"
+    dtype = "f16 operands, f32 accumulate (tcgen05 kind::f16); fp32 probability map"
+    N = 32
+    default_units = N
+    launches_per_step = 9
+    bound = "tensor"
+    l2_note = "features 648 MB + maps 118 MB per step > 126 MB L2 (no flush needed)"
+    dominant = ("the 9 launches of one DB head pass (achieved = useful flops of its 7 "
+                "tensor-core convolutions / the pass time)")
+
+    def __init__(self, dev, seed, units=None):
+        from turboocr_b200 import dbhead
+        if units:
+            self.N = units
+        n = self.N
+        g = torch.Generator(device=dev).manual_seed(seed)
+        mk = lambda *s: torch.randn(*s, generator=g, device=dev).to(torch.float16)
+        self.c2, self.c3, self.c4 = mk(n, 240, 240, 128), mk(n, 120, 120, 128), mk(n, 60, 60, 256)
+        self.head = dbhead.DbHead(dev)
+        self.units_per_step = n
+        feat = sum(t.numel() * 2 for t in (self.c2, self.c3, self.c4))
+        self.algo_bytes = feat + n * 960 * 960 * 4  # features read once, map written once
+        # useful multiply-adds of the tensor-core convolutions (unpadded K, N)
+        px4, px8, px16 = 240 * 240, 120 * 120, 60 * 60
+        self.algo_flops = 2 * n * (px16 * 256 * 96 + px8 * 128 * 96 + px4 * 128 * 96 +
+                                   (px16 + px8 + px4) * 864 * 24 + px4 * 648 * 24)
+        self.head(self.c2, self.c3, self.c4)
+        torch.cuda.synchronize()
+
+    def step(self):
+        self.head(self.c2, self.c3, self.c4)
+
+    def dominant_kernel_ms(self, iters=10):
+        s = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(iters):
+            self.step()
+        e1.record(s)
+        torch.cuda.synchronize()
+        assert int(self.head.err.item()) == 0
+        return e0.elapsed_time(e1) / iters
+
+    def setup_e2e(self):
+        self.h_in = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in
+                     (self.c2, self.c3, self.c4)]
+        for h, d in zip(self.h_in, (self.c2, self.c3, self.c4)):
+            h.copy_(d)
+        self.h_prob = torch.empty((self.N, 960, 960), dtype=torch.float32, pin_memory=True)
+        self.h2d = sum(t.numel() * 2 for t in self.h_in)
+        self.d2h = self.h_prob.numel() * 4
+
+    def e2e_step(self):
+        for h, d in zip(self.h_in, (self.c2, self.c3, self.c4)):
+            d.copy_(h, non_blocking=True)
+        prob = self.head(self.c2, self.c3, self.c4)
+        self.h_prob.copy_(prob, non_blocking=True)
+
+
 def det_resize_max960(h, w):
     """compute_det_resize with {"max", 960, 960} (det_config.h:58-81), as the
     library computes it (config 3's DET_LIMIT_TYPE=max, 960, 960)."""
@@ -642,9 +710,9 @@ E2E_SCHEDULE = [(32, 64, 1), (64, 64, 2), (64, 128, 1), (128, 128, 2),
                 (128, 128, 1), (128, 128, 2), (128, 128, 1), (128, 256, 1)]
 
 WORKLOADS = {"db": DbWorkload, "ctc": CtcWorkload, "preprocess": PreprocessWorkload,
-             "dwpw": DwPwWorkload, "rec_head": RecHeadWorkload,
+             "dwpw": DwPwWorkload, "rec_head": RecHeadWorkload, "db_head": DbHeadWorkload,
              "e2e": E2eWorkload}
-SEEDS = {"db": 0, "ctc": 1, "preprocess": 2, "dwpw": 3, "e2e": 5, "rec_head": 6}
+SEEDS = {"db": 0, "ctc": 1, "preprocess": 2, "dwpw": 3, "e2e": 5, "rec_head": 6, "db_head": 7}
 
 
 # ------------------------------------------------------------------ main ----
@@ -775,6 +843,19 @@ def main():
         }
         if hasattr(wl, "dominant"):
             line["roofline"]["kernel"] = wl.dominant
+        if args.workload == "db" and not args.units and world == 1:
+            # the survey's batch sweep: one call over 64 and 512 maps (the
+            # call's latency is the longest union sweep, more maps run beside it)
+            sweep = {"8": value}
+            for n in (64, 512):
+                big = Wl(dev, seed + n, n)
+                big.step()
+                torch.cuda.synchronize()
+                sweep[str(n)] = n / (big.dominant_kernel_ms(iters=2) / 1e3)
+                del big
+                torch.cuda.empty_cache()
+            line["batch_sweep_maps_per_s"] = sweep
+            line["latency_ms_batch8"] = kernel_ms
         if args.workload == "e2e":
             line["crops_per_page"] = round(wl.crops_per_page, 2)
             bpp = wl.path_bytes_per_page()

@@ -210,5 +210,63 @@ def rec_head(cores: int, n_steps: int, lines: int = 0):
                             "+ argmax + softmax max on all threads, then the reference collapse"}
 
 
+def db_head(cores: int, n_steps: int, pages: int = 1):
+    """The DB head on the host: the fp32 torch restatement of the network
+    (turboocr_b200/dbhead.py reference), all threads; weights drawn by the
+    same formula as tocr_synth_weights (restated in numpy here, so no product
+    library is loaded)."""
+    import torch
+    torch.set_num_threads(cores)
+    M64 = (1 << 64) - 1
+
+    def synth(seed, scale, n):
+        i = np.arange(1, n + 1, dtype=np.uint64)
+        with np.errstate(over="ignore"):
+            z = np.uint64(seed) + i * np.uint64(0x9E3779B97F4A7C15)
+            z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+            z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+            z ^= z >> np.uint64(31)
+        u = (z >> np.uint64(40)).astype(np.float32) * np.float32(1.0 / 16777216.0)
+        return np.float32(scale) * (np.float32(2.0) * u - np.float32(1.0))
+
+    shapes = {"lat4": (0, (96, 256, 1, 1), 0.108), "lat3": (1, (96, 128, 1, 1), 0.153),
+              "lat2": (2, (96, 128, 1, 1), 0.153), "p4": (3, (24, 96, 3, 3), 0.059),
+              "p3": (4, (24, 96, 3, 3), 0.059), "p2": (5, (24, 96, 3, 3), 0.059),
+              "head": (6, (24, 72, 3, 3), 0.068), "b1": (7, (24,), 0.1),
+              "up1": (8, (24, 24, 2, 2), 0.354), "b2": (9, (24,), 0.1),
+              "up2": (10, (24, 1, 2, 2), 0.354), "b3": (11, (1,), 0.1)}
+    w = {k: synth(0x7EC0DB00 + s, sc, int(np.prod(sh))).reshape(sh)
+         for k, (s, sh, sc) in shapes.items()}
+    g = torch.Generator().manual_seed(SEED + 7)
+    c2 = torch.randn(pages, 240, 240, 128, generator=g).to(torch.float16)
+    c3 = torch.randn(pages, 120, 120, 128, generator=g).to(torch.float16)
+    c4 = torch.randn(pages, 60, 60, 256, generator=g).to(torch.float16)
+    F = torch.nn.functional
+
+    def once():  # the same network as turboocr_b200.dbhead.reference
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a))
+        x2, x3, x4 = (c.permute(0, 3, 1, 2).float() for c in (c2, c3, c4))
+        up = lambda x, s: F.interpolate(x, scale_factor=s, mode="nearest")
+        in4 = F.conv2d(x4, t(w["lat4"]))
+        out3 = F.conv2d(x3, t(w["lat3"])) + up(in4, 2)
+        out2 = F.conv2d(x2, t(w["lat2"])) + up(out3, 2)
+        fuse = torch.cat([up(F.conv2d(in4, t(w["p4"]), padding=1), 4),
+                          up(F.conv2d(out3, t(w["p3"]), padding=1), 2),
+                          F.conv2d(out2, t(w["p2"]), padding=1)], dim=1)
+        h1 = F.relu(F.conv2d(fuse, t(w["head"]), t(w["b1"]), padding=1))
+        h2 = F.relu(F.conv_transpose2d(h1, t(w["up1"]), t(w["b2"]), stride=2))
+        return torch.sigmoid(F.conv_transpose2d(h2, t(w["up2"]), t(w["b3"]), stride=2))
+
+    once()
+    vals = []
+    for _ in range(n_steps):
+        t0 = time.perf_counter()
+        once()
+        vals.append(pages / (time.perf_counter() - t0))
+    return vals, {"kind": "port", "cores": cores, "units_per_step": pages,
+                  "sample": f"{pages} page(s) per step: the fp32 torch restatement of the DB head "
+                            "on all threads (the reference runs it in TensorRT/ORT)"}
+
+
 BASELINES = {"e2e": e2e, "ctc": ctc, "preprocess": preprocess, "dwpw": dwpw, "db": db,
-             "rec_head": rec_head}
+             "rec_head": rec_head, "db_head": db_head}

@@ -256,9 +256,11 @@ concat_kernel(const __half *__restrict__ p4, const __half *__restrict__ p3,
   }
 }
 
-// The two transposed convolutions and the sigmoid: one thread per /4 pixel
-// of h1 (24 channels) writes its 4 x 4 block of the /1 probability map.
+// The two transposed convolutions and the sigmoid: one thread per two /4
+// pixels of h1 (24 channels each; every weight read from shared memory feeds
+// both) writes their 4 x 4 blocks of the /1 probability map.
 // w2 [24 in][24 out][2][2], w3 [24 in][2][2] (PyTorch ConvTranspose2d order).
+constexpr int kUpPix = 2;
 __global__ void __launch_bounds__(256)
 head_up_kernel(const __half *__restrict__ h1, int N, int H, int W, const float *__restrict__ w2,
                const float *__restrict__ b2, const float *__restrict__ w3, float b3,
@@ -270,47 +272,75 @@ head_up_kernel(const __half *__restrict__ h1, int N, int H, int W, const float *
   if (threadIdx.x < 24) s_b2[threadIdx.x] = b2[threadIdx.x];
   if (threadIdx.x < 96) s_w3[threadIdx.x] = w3[threadIdx.x];
   __syncthreads();
-  const long long total = (long long)N * H * W;
+  const int Wg = (W + kUpPix - 1) / kUpPix;
+  const long long total = (long long)N * H * Wg;
   const int Wo = 4 * W;
-  for (long long pix = (long long)blockIdx.x * blockDim.x + threadIdx.x; pix < total;
-       pix += (long long)gridDim.x * blockDim.x) {
-    const int x = (int)(pix % W), y = (int)((pix / W) % H), n = (int)(pix / ((long long)W * H));
-    float in[24];
-    const uint4 *src = reinterpret_cast<const uint4 *>(h1 + pix * 24);
+  for (long long gi = (long long)blockIdx.x * blockDim.x + threadIdx.x; gi < total;
+       gi += (long long)gridDim.x * blockDim.x) {
+    const int xg = (int)(gi % Wg), y = (int)((gi / Wg) % H), n = (int)(gi / ((long long)Wg * H));
+    const int x0 = xg * kUpPix;
+    const int np = min(kUpPix, W - x0);
+    float in[kUpPix][24];
 #pragma unroll
-    for (int v = 0; v < 3; ++v) {
-      const uint4 u = src[v];
-      const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+    for (int q = 0; q < kUpPix; ++q) {
+      const long long pix = ((long long)n * H + y) * W + min(x0 + q, W - 1);
+      const uint4 *src = reinterpret_cast<const uint4 *>(h1 + pix * 24);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float2 g = __half22float2(h[q]);
-        in[8 * v + 2 * q] = g.x;
-        in[8 * v + 2 * q + 1] = g.y;
+      for (int v = 0; v < 3; ++v) {
+        const uint4 u = src[v];
+        const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 g = __half22float2(h[e]);
+          in[q][8 * v + 2 * e] = g.x;
+          in[q][8 * v + 2 * e + 1] = g.y;
+        }
       }
     }
-    float out[4][4];
+    float out[kUpPix][4][4];
 #pragma unroll
     for (int i = 0; i < 2; ++i)
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-        float acc[4] = {b3, b3, b3, b3};  // the 2 x 2 outputs of this /2 pixel
+        float acc[kUpPix][4];
+#pragma unroll
+        for (int q = 0; q < kUpPix; ++q)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) acc[q][k] = b3;
         for (int c = 0; c < 24; ++c) {
-          float h = s_b2[c];
+          float hq[kUpPix];
 #pragma unroll
-          for (int ci = 0; ci < 24; ++ci) h = fmaf(in[ci], s_w2[((ci * 24 + c) * 2 + i) * 2 + j], h);
-          h = fmaxf(h, 0.f);
+          for (int q = 0; q < kUpPix; ++q) hq[q] = s_b2[c];
 #pragma unroll
-          for (int k = 0; k < 4; ++k) acc[k] = fmaf(h, s_w3[c * 4 + k], acc[k]);
+          for (int ci = 0; ci < 24; ++ci) {
+            const float wv = s_w2[((ci * 24 + c) * 2 + i) * 2 + j];
+#pragma unroll
+            for (int q = 0; q < kUpPix; ++q) hq[q] = fmaf(in[q][ci], wv, hq[q]);
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float w3v = s_w3[c * 4 + k];
+#pragma unroll
+            for (int q = 0; q < kUpPix; ++q) acc[q][k] = fmaf(fmaxf(hq[q], 0.f), w3v, acc[q][k]);
+          }
         }
 #pragma unroll
-        for (int k = 0; k < 2; ++k)
+        for (int q = 0; q < kUpPix; ++q)
 #pragma unroll
-          for (int l = 0; l < 2; ++l) out[2 * i + k][2 * j + l] = 1.f / (1.f + expf(-acc[2 * k + l]));
+          for (int k = 0; k < 2; ++k)
+#pragma unroll
+            for (int l = 0; l < 2; ++l)
+              out[q][2 * i + k][2 * j + l] = 1.f / (1.f + expf(-acc[q][2 * k + l]));
       }
-    float *o = prob + ((long long)n * 4 * H + 4 * y) * Wo + 4 * x;
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
-      *reinterpret_cast<float4 *>(o + (long long)r * Wo) = make_float4(out[r][0], out[r][1], out[r][2], out[r][3]);
+    for (int q = 0; q < kUpPix; ++q) {
+      if (q >= np) break;
+      float *o = prob + ((long long)n * 4 * H + 4 * y) * Wo + 4 * (x0 + q);
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+        *reinterpret_cast<float4 *>(o + (long long)r * Wo) =
+            make_float4(out[q][r][0], out[q][r][1], out[q][r][2], out[q][r][3]);
+    }
   }
 }
 
@@ -479,7 +509,7 @@ TOCR_API int tocr_db_head_up_f32(const void *d_h1, int n, int h, int w, const fl
   if (n == 0) return TOCR_OK;
   TOCR_REQUIRE(d_h1 && d_w2 && d_b2 && d_w3 && d_prob, "tocr_db_head_up_f32: null pointer");
   TOCR_REQUIRE(aligned(d_h1, 16) && aligned(d_prob, 16), "tocr_db_head_up_f32: alignment");
-  const long long total = (long long)n * h * w;
+  const long long total = (long long)n * h * ((w + dbh::kUpPix - 1) / dbh::kUpPix);
   const unsigned grid = (unsigned)std::min<long long>((total + 255) / 256, (long long)sm_count() * 16);
   dbh::head_up_kernel<<<grid, 256, 0, as_stream(stream)>>>(static_cast<const __half *>(d_h1), n, h,
                                                            w, d_w2, d_b2, d_w3, b3, d_prob);
