@@ -111,3 +111,26 @@ def test_bit_exact_vs_reference_kernel(tocr, cuda):
                   for k, (buf, h, w, step) in enumerate(imgs)])
     mism = int((c.view(np.uint32) != r.view(np.uint32)).sum())
     assert mism == 0, f"C restatement differs from the reference kernel at {mism} values"
+
+
+def test_config3_full_batch_vs_reference_kernel(tocr, cuda):
+    """Config 3 at its full size: 256 images with sides U{600..2000}, the
+    det resize policy, one launch; the fp16 canvas must be the
+    round-to-nearest of the reference kernel's fp32 canvas everywhere
+    (compared on the device)."""
+    from oracle import ref_kernels as rk
+    from turboocr_b200 import kernels as K
+    rng = np.random.default_rng(3)
+    dims = [(int(rng.integers(600, 2001)), int(rng.integers(600, 2001))) for _ in range(256)]
+    g = torch.Generator(device=cuda).manual_seed(3)
+    bufs = [torch.randint(0, 256, (h, w * 3), dtype=torch.uint8, device=cuda, generator=g)
+            for (h, w) in dims]
+    content = [po.det_resize(h, w, "max", 960, 960) for (h, w) in dims]
+    meta = K.PreprocessMeta([b.data_ptr() for b in bufs], [w * 3 for (_, w) in dims], dims,
+                            content, cuda)
+    ref = torch.empty(256, 3, 960, 960, dtype=torch.float32, device=cuda)
+    rk.batch_preprocess(meta, ref)
+    o16 = torch.empty(ref.shape, dtype=torch.float16, device=cuda)
+    K.preprocess_batch(meta, o16)
+    torch.cuda.synchronize()
+    assert torch.equal(o16.view(torch.int16), ref.half().view(torch.int16))
