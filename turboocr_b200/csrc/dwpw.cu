@@ -70,7 +70,10 @@ struct Cfg {
   static constexpr int A_SUB = TP * 128;               // one K atom of A
   static constexpr int A_TILE = A_SUB * KATOMS * (FP8 ? 2 : 1);
   static constexpr int B_BYTES = CO * 128 * KATOMS;
-  static constexpr int STG = TP * C * 2;
+  // fp16 staging of the depthwise output, needed only when a pixel's
+  // channels arrive in several chunks (its quantisation scale needs all of
+  // them); with one chunk the DW threads quantise from registers
+  static constexpr int STG = NCH == 1 ? 0 : TP * C * 2;
   static constexpr int OUT = TP * CO * 2;
   static constexpr int NBOX = CO / 64;
   static constexpr int TMEM_COLS = 2 * CO < 32 ? 32 : 2 * CO;
@@ -91,7 +94,8 @@ struct Cfg {
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;        // tmem base, abort flag
   static constexpr int SMEM = OFF_MISC + 16;
   static constexpr int SMEM_ALLOC = SMEM + 1024;             // runtime 1024 alignment slack
-  static_assert(C % 32 == 0 && C % CCH == 0 && (CCH == 32 || CCH == 64), "channels");
+  static_assert(C % 32 == 0 && C % CCH == 0 && (CCH == 32 || CCH == 64 || CCH == 128),
+                "channels");
   static_assert(CO % 64 == 0 && CO <= 256, "C_out");
   static_assert(TW % SEG == 0 && (TP / SEG) * PARTS == kDwThreads, "thread mapping");
   static constexpr int NGRP = CO >= 128 ? 2 : 1;        // epilogue column groups
@@ -295,6 +299,7 @@ dwpw_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
       float amax[K::SEG];
 #pragma unroll
       for (int j = 0; j < K::SEG; ++j) amax[j] = 0.f;
+      __half2 keep[K::SEG][4];  // one-chunk configurations: the tile's DW output
       bool ok = true;
       for (int ch = 0; ch < K::NCH; ++ch, ++g) {
         const int st = g % K::XST;
@@ -351,10 +356,15 @@ dwpw_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
             m = __hmax2(m, __habs2(h));
           }
           amax[j] = fmaxf(amax[j], fmaxf(__low2float(m), __high2float(m)));
-          const int p = seg_row * TW + seg_col + j;
-          const int vs = (c0 / 8) ^ (p & (K::C / 8 - 1) & 7);
-          *reinterpret_cast<uint4 *>(sstg + (p * K::C + vs * 8) * 2) =
-              make_uint4(h2u(acc[j][0]), h2u(acc[j][1]), h2u(acc[j][2]), h2u(acc[j][3]));
+          if constexpr (K::NCH == 1) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) keep[j][q] = acc[j][q];
+          } else {
+            const int p = seg_row * TW + seg_col + j;
+            const int vs = (c0 / 8) ^ (p & (K::C / 8 - 1) & 7);
+            *reinterpret_cast<uint4 *>(sstg + (p * K::C + vs * 8) * 2) =
+                make_uint4(h2u(acc[j][0]), h2u(acc[j][1]), h2u(acc[j][2]), h2u(acc[j][3]));
+          }
         }
       }
       // per-pixel amax across the PARTS lanes of a segment
@@ -363,6 +373,74 @@ dwpw_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
 #pragma unroll
         for (int off = 1; off < K::PARTS; off <<= 1)
           amax[j] = fmaxf(amax[j], __shfl_xor_sync(0xffffffffu, amax[j], off));
+      }
+      if constexpr (K::NCH == 1) {
+        // quantise straight from registers: same scale and rounding as the
+        // staged pass below (fp16 values, the pixel's |max| over its channels)
+        const int ast = i % K::AST;
+        const int ss = i & 3;
+        if (ok) ok = mbar_wait_bounded(&a_empty[ast], ((i / K::AST) & 1) ^ 1, s_abort, prm.err, 32);
+        if (ok) ok = mbar_wait_bounded(&scl_empty[ss], ((i >> 2) & 1) ^ 1, s_abort, prm.err, 33);
+        if (!named_bar_and(1, kDwThreads, ok)) break;
+        const float qmax = K::FP8 ? 448.f : 127.f;
+        const int c0 = part * 8;
+        const int j16 = c0 / 16, atom = j16 / 8, chunk = j16 % 8, hb = (c0 % 16) / 8;
+#pragma unroll
+        for (int j = 0; j < K::SEG; ++j) {
+          const int p = seg_row * TW + seg_col + j;
+          const float am = amax[j];
+          const float inv = am > 0.f ? qmax / am : 0.f;
+          if (part == 0) sscale[ss * TP + p] = am / qmax;
+          float f[8];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 ff = __half22float2(keep[j][q]);
+            f[2 * q] = ff.x;
+            f[2 * q + 1] = ff.y;
+          }
+          uint8_t *dst = sa + ast * K::A_TILE + p * 128 + atom * K::A_SUB +
+                         ((chunk ^ (p & 7)) * 16) + hb * 8;
+          if (!K::FP8) {
+            uint32_t wd[2];
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              const uint32_t b0 = __float_as_uint(fmaf(f[4 * q + 0], inv, 12582912.f));
+              const uint32_t b1 = __float_as_uint(fmaf(f[4 * q + 1], inv, 12582912.f));
+              const uint32_t b2 = __float_as_uint(fmaf(f[4 * q + 2], inv, 12582912.f));
+              const uint32_t b3 = __float_as_uint(fmaf(f[4 * q + 3], inv, 12582912.f));
+              wd[q] = __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+            }
+            *reinterpret_cast<uint2 *>(dst) = make_uint2(wd[0], wd[1]);
+          } else {
+            uint32_t hi[2], lo[2];
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              float s4[4], r[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) s4[e] = f[4 * q + e] * inv;
+              const __nv_fp8x2_storage_t h01 = __nv_cvt_float2_to_fp8x2(make_float2(s4[0], s4[1]), __NV_SATFINITE, __NV_E4M3);
+              const __nv_fp8x2_storage_t h23 = __nv_cvt_float2_to_fp8x2(make_float2(s4[2], s4[3]), __NV_SATFINITE, __NV_E4M3);
+              const __half2_raw b01 = __nv_cvt_fp8x2_to_halfraw2(h01, __NV_E4M3);
+              const __half2_raw b23 = __nv_cvt_fp8x2_to_halfraw2(h23, __NV_E4M3);
+              const float2 g01 = __half22float2(*reinterpret_cast<const __half2 *>(&b01));
+              const float2 g23 = __half22float2(*reinterpret_cast<const __half2 *>(&b23));
+              r[0] = s4[0] - g01.x; r[1] = s4[1] - g01.y; r[2] = s4[2] - g23.x; r[3] = s4[3] - g23.y;
+              const __nv_fp8x2_storage_t l01 = __nv_cvt_float2_to_fp8x2(make_float2(r[0], r[1]), __NV_SATFINITE, __NV_E4M3);
+              const __nv_fp8x2_storage_t l23 = __nv_cvt_float2_to_fp8x2(make_float2(r[2], r[3]), __NV_SATFINITE, __NV_E4M3);
+              hi[q] = (uint32_t)h01 | ((uint32_t)h23 << 16);
+              lo[q] = (uint32_t)l01 | ((uint32_t)l23 << 16);
+            }
+            *reinterpret_cast<uint2 *>(dst) = make_uint2(hi[0], hi[1]);
+            *reinterpret_cast<uint2 *>(dst + K::A_SUB * K::KATOMS) = make_uint2(lo[0], lo[1]);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&a_full[ast]);
+          mbar_arrive(&scl_full[ss]);
+        }
+        continue;
       }
       if (part == 0) {
 #pragma unroll
