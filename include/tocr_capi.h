@@ -480,6 +480,70 @@ TOCR_API int tocr_dwpw_pack(int C, int C_out, int kind, const float *wdw,
 TOCR_API int tocr_dwpw_dequant_pw(const void *blob, int C, int C_out, int kind,
                                   float *w_out);
 
+
+/* ---- PNG decode to device BGR ---------------------------------------- */
+/* Replaces the reference's CPU decode + upload of one page image:
+ * turbo_ocr::decode::FastPngDecoder::decode (src/decode/fast_png_decoder.cpp:48-128,
+ * include/turbo_ocr/decode/fast_png_decoder.h:12-15; Wuffs v0.4 to a BGR
+ * cv::Mat, 16-bit files through cv::imdecode) followed by
+ * OcrPipeline::upload_image (src/pipeline/ocr/ocr_pipeline_runtime.cpp:120-147),
+ * whose result is a GpuImage (include/turbo_ocr/decode/gpu_image.h:9-16):
+ * here the files go to HBM compressed and the pixels are made there.
+ * Output pixels match the reference decode byte for byte: Wuffs' BGR for
+ * 1-8 bit files (grey scaled up, alpha premultiplied, tRNS keys and palette
+ * alphas applied, palette indices past the PLTE black), OpenCV's for
+ * 16-bit files (high byte, alpha dropped). */
+typedef struct tocr_png_info {
+  int32_t width, height;
+  int32_t bit_depth, color_type, interlace;
+  int32_t reserved;
+  uint64_t raw_bytes;     /* inflated scanline bytes (all passes, filter bytes included) */
+  uint64_t scratch_bytes; /* device scratch this file needs (tocr_png_job.scratch_off) */
+} tocr_png_info;
+
+typedef struct tocr_png_job {
+  uint64_t src_off, src_len; /* the file at d_src + src_off */
+  uint64_t dst_off;          /* BGR u8 rows at d_dst + dst_off, dst_pitch bytes apart */
+  uint64_t dst_pitch;        /* >= 3 * width */
+  uint64_t scratch_off;      /* 16-byte aligned; scratch_bytes from tocr_png_peek */
+  int32_t width, height;     /* from tocr_png_peek; the device re-reads the IHDR */
+} tocr_png_job;
+
+/* Per-image status written by tocr_png_decode_batch. */
+enum {
+  TOCR_PNG_OK = 0,
+  TOCR_PNG_BAD_HEADER = 1,      /* signature or IHDR                                */
+  TOCR_PNG_BAD_CHUNK = 2,       /* chunk layout, truncation, PLTE / tRNS rules       */
+  TOCR_PNG_BAD_CHECKSUM = 3,    /* CRC-32 of a critical chunk, or the zlib Adler-32  */
+  TOCR_PNG_MISSING_PALETTE = 4, /* colour type 3 without PLTE                        */
+  TOCR_PNG_BAD_ZLIB = 5,        /* zlib header                                       */
+  TOCR_PNG_BAD_DEFLATE = 6,     /* DEFLATE block, Huffman code or distance           */
+  TOCR_PNG_TOO_MUCH_DATA = 7,   /* more scanline bytes than the IHDR implies         */
+  TOCR_PNG_NOT_ENOUGH_DATA = 8, /* fewer scanline bytes than the IHDR implies        */
+  TOCR_PNG_BAD_FILTER = 9,      /* a scanline filter type above 4                    */
+  TOCR_PNG_SIZE_MISMATCH = 10,  /* IHDR differs from the job's width / height        */
+  TOCR_PNG_UNSUPPORTED = 11     /* a side above 16777215                             */
+};
+
+/* Host only, no GPU: the signature and IHDR of one file (the first 33 bytes),
+ * as image_dims.h:31-48 peeks them, then the reference's caps
+ * (fast_png_decoder.cpp:84-93): TOCR_ERR_INVALID when the bytes are not a
+ * PNG, the IHDR is malformed, a side is 0 or above max_dim, or
+ * width * height > max_pixels (info->width / height are filled whenever the
+ * IHDR could be read). On TOCR_OK, info->scratch_bytes is the device scratch
+ * the file needs for a file of src_len bytes. */
+TOCR_API int tocr_png_peek(const uint8_t *data, size_t len, int max_dim, long long max_pixels,
+                           tocr_png_info *info);
+
+/* Decodes n files: d_src holds the files, d_jobs (device, n entries) says
+ * where each one is, where its pixels go and which scratch it uses; d_status
+ * (device, n int32) receives TOCR_PNG_* per file. The pixels of a file whose
+ * status is not TOCR_PNG_OK are unspecified. Three kernels, no allocation,
+ * no synchronisation. */
+TOCR_API int tocr_png_decode_batch(const uint8_t *d_src, const tocr_png_job *d_jobs, int n,
+                                   uint8_t *d_dst, uint8_t *d_scratch, int32_t *d_status,
+                                   void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -101,6 +101,8 @@ SIGNATURES: dict[str, tuple] = {
     "tocr_cls_stem_f16": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "tocr_cls_head_f32": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "tocr_synth_weights": (_i, [_u64, _f, _vp, _ll]),
+    "tocr_png_peek": (_i, [_vp, C.c_size_t, _i, _ll, _vp]),
+    "tocr_png_decode_batch": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _vp]),
     "tocr_compute_det_resize": (_i, [_i, _i, _i, _i, _i, _vp, _vp]),
     "tocr_read_det_resize": (_i, [_vp, _vp, _vp]),
     "tocr_effective_det_max_side": (_i, [_i]),

@@ -31,7 +31,8 @@ COMMON = ["-O3", "-lineinfo", "-std=c++20", "-Xcompiler", "-fPIC", "-Xcompiler",
 
 LIBS = {
     "libtocr_b200.so": ["capi_common.cu", "ctc.cu", "preprocess.cu", "threshold.cu", "dwpw.cu",
-                        "db.cu", "pagekernels.cu", "crop.cu", "jfa.cu", "cls.cu", "rec_head.cu", "dbhead.cu"],
+                        "db.cu", "pagekernels.cu", "crop.cu", "jfa.cu", "cls.cu", "rec_head.cu", "dbhead.cu",
+                        "png.cu"],
     "libtocr_synth.so": ["synth.cu"],
 }
 # C++ host sources (reference-signature shims), built into libtocr_b200.so.
