@@ -450,6 +450,67 @@ class DbHeadWorkload:
         self.h_prob.copy_(prob, non_blocking=True)
 
 
+class PngWorkload:
+    """PNG decode to device BGR (turboocr_b200/decode.py, csrc/png.cu): 64
+    document pages of 1240x1754 (A4 at 150 dpi) as OpenCV's PNG writer
+    encodes them (turboocr_b200/pagegen.py). Device arm: the compressed
+    files resident in HBM -> BGR u8 pages; e2e: host bytes -> pinned
+    staging -> H2D -> decode -> per-page status back."""
+    name = "png_decode_64xA4"
+    metric = "pages/sec PNG decode to device BGR (1240x1754 document pages)"
+    unit = "pages/s"
+    dtype = "u8 (DEFLATE + PNG filters, integer)"
+    N = 64
+    default_units = N
+    launches_per_step = 3
+    bound = "hbm"
+    l2_note = ("per step: 24 MB of files, 420 MB of scanlines and 418 MB of pixels "
+               "written and read once > 126 MB L2 (no flush needed)")
+    dominant = ("the 3 launches of one decode (parse, inflate, unfilter); achieved = files "
+                "read + pixels written per decode / its time")
+
+    def __init__(self, dev, seed, units=None):
+        from turboocr_b200 import decode as D, pagegen
+        if units:
+            self.N = units
+        self.files = pagegen.png_pages(self.N, seed)
+        self.dec = D.PngBatchDecoder(dev)
+        out = self.dec.decode(self.files)  # sizes the buffers, checks the statuses
+        assert all(s == D.PNG_OK for s in out.status), out.status
+        jobs, ok, self.nsrc, self.nscr, self.ndst = self.dec.plan(self.files)
+        self.d_in = self.dec._bufs["d_src"]
+        self.jo = (self.nsrc + 15) & ~15
+        self.units_per_step = self.N
+        self.algo_bytes = self.nsrc + sum(int(j["height"]) * 3 * int(j["width"]) for j in jobs)
+        self.status = torch.zeros(self.N, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize()
+
+    def step(self):
+        from turboocr_b200._lib import call
+        s = torch.cuda.current_stream()
+        call("tocr_png_decode_batch", self.d_in.data_ptr(), self.d_in.data_ptr() + self.jo,
+             self.N, self.dec._bufs["dst"].data_ptr(), self.dec._bufs["scratch"].data_ptr(),
+             self.status.data_ptr(), s.cuda_stream)
+
+    def dominant_kernel_ms(self, iters=5):
+        s = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(iters):
+            self.step()
+        e1.record(s)
+        torch.cuda.synchronize()
+        assert int((self.status != 0).sum()) == 0
+        return e0.elapsed_time(e1) / iters
+
+    def setup_e2e(self):
+        self.h2d = self.nsrc + self.N * 48
+        self.d2h = self.N * 4
+
+    def e2e_step(self):
+        self.dec.decode(self.files)
+
+
 def det_resize_max960(h, w):
     """compute_det_resize with {"max", 960, 960} (det_config.h:58-81), as the
     library computes it (config 3's DET_LIMIT_TYPE=max, 960, 960)."""
@@ -711,8 +772,9 @@ E2E_SCHEDULE = [(32, 64, 1), (64, 64, 2), (64, 128, 1), (128, 128, 2),
 
 WORKLOADS = {"db": DbWorkload, "ctc": CtcWorkload, "preprocess": PreprocessWorkload,
              "dwpw": DwPwWorkload, "rec_head": RecHeadWorkload, "db_head": DbHeadWorkload,
-             "e2e": E2eWorkload}
-SEEDS = {"db": 0, "ctc": 1, "preprocess": 2, "dwpw": 3, "e2e": 5, "rec_head": 6, "db_head": 7}
+             "png": PngWorkload, "e2e": E2eWorkload}
+SEEDS = {"db": 0, "ctc": 1, "preprocess": 2, "dwpw": 3, "e2e": 5, "rec_head": 6, "db_head": 7,
+         "png": 8}
 
 
 # ------------------------------------------------------------------ main ----

@@ -522,7 +522,8 @@ enum {
   TOCR_PNG_NOT_ENOUGH_DATA = 8, /* fewer scanline bytes than the IHDR implies        */
   TOCR_PNG_BAD_FILTER = 9,      /* a scanline filter type above 4                    */
   TOCR_PNG_SIZE_MISMATCH = 10,  /* IHDR differs from the job's width / height        */
-  TOCR_PNG_UNSUPPORTED = 11     /* a side above 16777215                             */
+  TOCR_PNG_UNSUPPORTED = 11,    /* a side above 16777215                             */
+  TOCR_PNG_TIMEOUT = 12         /* a bounded wait between row groups gave up         */
 };
 
 /* Host only, no GPU: the signature and IHDR of one file (the first 33 bytes),

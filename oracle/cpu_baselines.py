@@ -268,5 +268,37 @@ def db_head(cores: int, n_steps: int, pages: int = 1):
                             "on all threads (the reference runs it in TensorRT/ORT)"}
 
 
+def _pagegen():
+    """turboocr_b200/pagegen.py loaded by path (numpy + cv2 only), so that the
+    package and its native library stay unloaded."""
+    import importlib.util
+    from pathlib import Path
+    path = Path(__file__).resolve().parents[1] / "turboocr_b200" / "pagegen.py"
+    spec = importlib.util.spec_from_file_location("_tocr_pagegen", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def png(cores: int, n_steps: int, pages: int = 64):
+    """PNG decode as the reference does it (FastPngDecoder::decode: its
+    vendored Wuffs, compiled in place, to BGR), the bench's 64 A4 pages
+    spread over `cores` threads (the C decode releases the GIL)."""
+    from concurrent.futures import ThreadPoolExecutor
+    from . import png_oracle as po
+    files = _pagegen().png_pages(pages, SEED + 8)
+    vals = []
+    with ThreadPoolExecutor(max_workers=cores) as ex:
+        list(ex.map(po.wuffs_decode, files[:cores]))
+        for _ in range(n_steps):
+            t0 = time.perf_counter()
+            outs = list(ex.map(po.wuffs_decode, files))
+            vals.append(pages / (time.perf_counter() - t0))
+            assert all(o[0] is not None for o in outs)
+    return vals, {"kind": "reference", "cores": cores, "units_per_step": pages,
+                  "sample": f"{pages} A4 pages of 1240x1754 (OpenCV-encoded PNG) per step, the "
+                            "reference's Wuffs decode to BGR, one page per thread task"}
+
+
 BASELINES = {"e2e": e2e, "ctc": ctc, "preprocess": preprocess, "dwpw": dwpw, "db": db,
-             "rec_head": rec_head, "db_head": db_head}
+             "rec_head": rec_head, "db_head": db_head, "png": png}

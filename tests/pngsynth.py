@@ -11,6 +11,8 @@ import zlib
 
 import numpy as np
 
+from turboocr_b200.pagegen import page_like  # noqa: F401  (re-exported for the tests)
+
 SIG = b"\x89PNG\r\n\x1a\n"
 CHANNELS = {0: 1, 2: 3, 3: 1, 4: 2, 6: 4}
 ADAM7 = [(0, 0, 8, 8), (4, 0, 8, 8), (0, 4, 4, 8), (2, 0, 4, 4), (0, 2, 2, 4), (1, 0, 2, 2),
@@ -133,28 +135,6 @@ def encode(img: np.ndarray, color_type: int, depth: int = 8, *, filters="random"
     for i in range(0, max(len(z), 1), idat_size):
         body += chunk(b"IDAT", z[i:i + idat_size])
     return SIG + body + chunk(b"IEND", b"")
-
-
-def page_like(h: int, w: int, seed: int, channels: int = 3) -> np.ndarray:
-    """A document-like page: white background, dark text-like strokes, a few
-    coloured blocks and mild noise in one band (so both long LZ77 matches and
-    literal runs occur)."""
-    rng = np.random.default_rng(seed)
-    img = np.full((h, w, channels), 250, np.uint8)
-    for _ in range(max(1, h // 24)):
-        y = int(rng.integers(0, max(1, h - 12)))
-        x = int(rng.integers(0, max(1, w - 40)))
-        L = int(rng.integers(10, max(11, w // 2)))
-        img[y:y + 8, x:x + L] = rng.integers(0, 60, (1, 1, channels))
-        for k in range(0, L, 7):
-            img[y:y + 8, x + k:x + k + 2] = 245
-    for _ in range(3):
-        y, x = int(rng.integers(0, h)), int(rng.integers(0, w))
-        img[y:y + h // 10, x:x + w // 10] = rng.integers(0, 256, (1, 1, channels))
-    band = slice(h // 3, h // 3 + max(1, h // 20))
-    img[band] = np.clip(img[band].astype(np.int32) + rng.integers(-20, 21, img[band].shape), 0,
-                        255).astype(np.uint8)
-    return img
 
 
 def premul(c, a):

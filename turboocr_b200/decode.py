@@ -22,7 +22,7 @@ PNG_OK = 0
 STATUS_NAMES = {
     0: "ok", 1: "bad header", 2: "bad chunk", 3: "bad checksum", 4: "missing palette",
     5: "bad zlib header", 6: "bad deflate data", 7: "too much data", 8: "not enough data",
-    9: "bad filter", 10: "size mismatch", 11: "unsupported dimension",
+    9: "bad filter", 10: "size mismatch", 11: "unsupported dimension", 12: "timeout",
     -1: "rejected on the host (not a PNG, malformed IHDR or over the size caps)",
 }
 
