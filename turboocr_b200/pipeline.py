@@ -95,8 +95,10 @@ class PagePipeline:
         # + stand-in rec logits (2) + CTC (2)
         self.launches_per_run = 1 + len(SCHEDULE) + 1 + 1 + 16 + 2 + 1 + 2 + 2
 
-    def run(self, pages: torch.Tensor, stream=None) -> None:
-        """Enqueue the whole path for pages u8 [B, H, W, 3] (device)."""
+    def run(self, pages: torch.Tensor, stream=None, rec: bool = True) -> None:
+        """Enqueue the whole path for pages u8 [B, H, W, 3] (device). rec=False
+        stops after the crops (the detection half: no stand-in rec logits and
+        no CTC decode)."""
         B, H, W = self.B, self.H, self.W
         assert pages.shape == (B, H, W, 3) and pages.dtype == torch.uint8
         st = _stream(stream)
@@ -120,6 +122,8 @@ class PagePipeline:
         call("tocr_roi_warp_f16", _ptr(pages), page_stride, H, W, W * 3, _ptr(self.minv),
              _ptr(self.crop_w), _ptr(self.crop_page), _ptr(n_crops), self.max_crops, REC_H, REC_W,
              None, None, 1.0 / 255.0, _ptr(self.crops), st)
+        if not rec:
+            return
         synth().tocr_synth_rec_logits(_ptr(self.logits), _ptr(n_crops), self.max_crops, REC_T,
                                       REC_V, self.seed, st)
         call("tocr_ctc_greedy_f16_dev", _ptr(self.logits), _ptr(n_crops), self.max_crops, REC_T,
