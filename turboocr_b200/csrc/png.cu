@@ -350,8 +350,8 @@ __constant__ uint8_t kClOrder[19] = {16, 17, 18, 0, 8, 7, 9, 6, 10, 5, 11, 4, 12
 constexpr int kInfImgs = 1;                 // images per CTA: small batches spread over the SMs
 constexpr uint32_t kWin = 32768, kWinMask = kWin - 1;
 constexpr int kFastBits = 10;
-constexpr int kMaxTok = 64;
-constexpr int kMaxLit = 512;
+constexpr int kMaxTok = 256;
+constexpr int kMaxLit = 2048;
 constexpr uint32_t kFlush = 4096;
 constexpr uint32_t kAdlerMod = 65521;
 constexpr uint16_t kStoredTok = 0xFFFF;     // token dist of a stored-block copy from the stream
