@@ -350,8 +350,9 @@ __constant__ uint8_t kClOrder[19] = {16, 17, 18, 0, 8, 7, 9, 6, 10, 5, 11, 4, 12
 constexpr int kInfImgs = 1;                 // images per CTA: small batches spread over the SMs
 constexpr uint32_t kWin = 32768, kWinMask = kWin - 1;
 constexpr int kFastBits = 10;
-constexpr int kMaxTok = 256;
-constexpr int kMaxLit = 2048;
+constexpr int kPairBits = 11;               // two-literal table: both codes within 11 bits
+constexpr int kMaxTok = 128;
+constexpr int kMaxLit = 1024;
 constexpr uint32_t kFlush = 4096;
 constexpr uint32_t kAdlerMod = 65521;
 constexpr uint16_t kStoredTok = 0xFFFF;     // token dist of a stored-block copy from the stream
@@ -384,6 +385,7 @@ struct Batch {
 struct alignas(16) InflateImg {  // 16-byte aligned: the window is read as uint4
   uint8_t win[kWin];
   Huff lit, dist;                 // `dist` also holds the code-length code
+  uint32_t pair[1 << kPairBits];  // literal pairs of the current literal/length code
   Batch batch[2];
   uint16_t run[16];
   uint8_t lens[320];
@@ -706,12 +708,36 @@ __device__ void run_batch(InflateImg &S, const Batch &B, const uint8_t *z, uint8
   }
 }
 
+// The two-literal table of the current literal/length code: entry i holds
+// the first code of the bits i (least significant first) and the code after
+// it when both are literals whose lengths add up to at most kPairBits, as
+// sym1 | sym2 << 8 | (len1 + len2) << 16 | 2 << 24; 0 otherwise. A literal
+// run (5 bits per literal on document pages) then takes one lookup per two
+// literals on the decoder's dependent chain.
+__device__ void build_pairs(InflateImg &S, int lane) {
+  __syncwarp();
+  for (int i = lane; i < (1 << kPairBits); i += 32) {
+    uint32_t v = 0;
+    const uint32_t e1 = S.lit.fast[i & ((1 << kFastBits) - 1)];
+    const uint32_t l1 = e1 >> 9, s1 = e1 & 511u;
+    if (l1 != 0 && s1 < 256 && l1 < (uint32_t)kPairBits) {
+      const uint32_t e2 = S.lit.fast[((uint32_t)i >> l1) & ((1u << kFastBits) - 1)];
+      const uint32_t l2 = e2 >> 9, s2 = e2 & 511u;
+      if (l2 != 0 && s2 < 256 && l1 + l2 <= (uint32_t)kPairBits)
+        v = s1 | s2 << 8 | (l1 + l2) << 16 | 2u << 24;
+    }
+    S.pair[i] = v;
+  }
+  __syncwarp();
+}
+
 __device__ void build_fixed(InflateImg &S, int lane) {
   for (int i = lane; i < 320; i += 32)
     S.lens[i] = i < 144 ? 8 : i < 256 ? 9 : i < 280 ? 7 : i < 288 ? 8 : 5;
   __syncwarp();
   build_huff(S.lit, S.lens, 288, false, S.run, lane);
   build_huff(S.dist, S.lens + 288, 32, true, S.run, lane);
+  build_pairs(S, lane);
 }
 
 // The dynamic block header (RFC 1951 3.2.7) with Wuffs' checks: at most 286
@@ -769,6 +795,7 @@ __device__ int read_dynamic(InflateImg &S, BitReader &br, int lane) {
   if (st != kOk) return st;
   st = build_huff(S.lit, S.lens, hlit, false, S.run, lane);
   if (st != kOk) return st;
+  build_pairs(S, lane);
   return build_huff(S.dist, S.lens + hlit, hdist, true, S.run, lane);
 }
 
@@ -897,6 +924,7 @@ __device__ void fill_batch(InflateImg &S, Batch &B, DecState &ds, const Meta &m,
       uint32_t nextw = ds.br.nextw;
       const uint64_t base = ds.produced;
       const uint16_t *lfast = S.lit.fast, *dfast = S.dist.fast;
+      const uint32_t *pairs = S.pair;
       uint8_t *lit = B.lit;
       for (;;) {
         if (cnt < 32) {
@@ -907,9 +935,20 @@ __device__ void fill_batch(InflateImg &S, Batch &B, DecState &ds, const Meta &m,
           nextw = zw[wi];
           if ((wi + 64) * 4 < zlen) prefetch_l1(zw + wi + 64);
         }
+        const uint32_t pe = pairs[buf & ((1u << kPairBits) - 1)];
+        if (pe != 0 && nlit + 2 <= kMaxLit) {  // two literals with short codes
+          const int l2 = (int)((pe >> 16) & 255u);
+          buf >>= l2;
+          cnt -= l2;
+          lit[nlit] = (uint8_t)pe;
+          lit[nlit + 1] = (uint8_t)(pe >> 8);
+          nlit += 2;
+          if (nlit == kMaxLit) break;
+          continue;
+        }
         const uint32_t e = lfast[buf & ((1u << kFastBits) - 1)];
         int l = (int)(e >> 9), sym = (int)(e & 511u);
-        if (l != 0 && sym < 256) {  // the common case: a literal with a short code
+        if (l != 0 && sym < 256) {  // a literal with a short code
           buf >>= l;
           cnt -= l;
           lit[nlit++] = (uint8_t)sym;
