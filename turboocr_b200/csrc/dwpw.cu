@@ -295,6 +295,19 @@ dwpw_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
     const int seg_row = K::ROWMAP ? seg % TH : seg / (TW / K::SEG);
     const int seg_col = (K::ROWMAP ? seg / TH : seg % (TW / K::SEG)) * K::SEG;
     uint32_t g = 0, i = 0;
+    // one-chunk configurations: a thread's channels are the same in every
+    // tile, so its depthwise weights and bias stay in registers
+    __half2 w[9][4], wb[4];
+    auto load_w = [&](int c0) {
+#pragma unroll
+      for (int tp = 0; tp < 9; ++tp) {
+        const uint4 v = *reinterpret_cast<const uint4 *>(swdw + tp * K::C + c0);
+        w[tp][0] = u2h(v.x); w[tp][1] = u2h(v.y); w[tp][2] = u2h(v.z); w[tp][3] = u2h(v.w);
+      }
+      const uint4 bv = *reinterpret_cast<const uint4 *>(swdw + 9 * K::C + c0);
+      wb[0] = u2h(bv.x); wb[1] = u2h(bv.y); wb[2] = u2h(bv.z); wb[3] = u2h(bv.w);
+    };
+    if constexpr (K::NCH == 1) load_w(part * 8);
     for (int t = blockIdx.x; t < prm.ntiles; t += gridDim.x, ++i) {
       float amax[K::SEG];
 #pragma unroll
@@ -307,19 +320,11 @@ dwpw_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
         if (!ok) continue;
         const uint8_t *xs = sx + st * K::HALO_ST;
         const int c0 = ch * K::CCH + part * 8;     // first channel of this thread
-        __half2 w[9][4];
-#pragma unroll
-        for (int tp = 0; tp < 9; ++tp) {
-          const uint4 v = *reinterpret_cast<const uint4 *>(swdw + tp * K::C + c0);
-          w[tp][0] = u2h(v.x); w[tp][1] = u2h(v.y); w[tp][2] = u2h(v.z); w[tp][3] = u2h(v.w);
-        }
+        if constexpr (K::NCH != 1) load_w(c0);
         __half2 acc[K::SEG][4];
-        {
-          const uint4 bv = *reinterpret_cast<const uint4 *>(swdw + 9 * K::C + c0);
 #pragma unroll
-          for (int j = 0; j < K::SEG; ++j) {
-            acc[j][0] = u2h(bv.x); acc[j][1] = u2h(bv.y); acc[j][2] = u2h(bv.z); acc[j][3] = u2h(bv.w);
-          }
+        for (int j = 0; j < K::SEG; ++j) {
+          acc[j][0] = wb[0]; acc[j][1] = wb[1]; acc[j][2] = wb[2]; acc[j][3] = wb[3];
         }
         // every input column that the SEG outputs touch: (SEG-1)*S + 3
 #pragma unroll
