@@ -166,12 +166,24 @@ ccl_local_kernel(const float *__restrict__ pred, uint8_t *__restrict__ bitmap, i
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int x = tx0 + lane;
   const unsigned in_row = (W - tx0 >= 32) ? 0xffffffffu : ((1u << (W - tx0)) - 1u);
-  for (int ly = warp; ly < kTileH; ly += 8) {
+  // the warp's four rows of the map are loaded before any is used, so four
+  // loads per thread are in flight (one at a time left the kernel far below
+  // the memory bandwidth)
+  constexpr int kRowsPerWarp = kTileH / 8;
+  float pv[kRowsPerWarp];
+#pragma unroll
+  for (int k = 0; k < kRowsPerWarp; ++k) {
+    const int y = ty0 + warp + 8 * k;
+    pv[k] = (pred && x < W && y < H) ? pred[base + (size_t)y * W + x] : 0.f;
+  }
+#pragma unroll
+  for (int k = 0; k < kRowsPerWarp; ++k) {
+    const int ly = warp + 8 * k;
     const int y = ty0 + ly;
     bool f = false;
     if (x < W && y < H) {
       if (pred) {  // threshold the map; else label the given bitmap
-        f = pred[base + (size_t)y * W + x] > thresh;
+        f = pv[k] > thresh;
         bitmap[base + (size_t)y * W + x] = f ? 255 : 0;
       } else {
         f = bitmap[base + (size_t)y * W + x] != 0;
