@@ -185,22 +185,22 @@ stem_tc_kernel(const uint8_t *__restrict__ pages, int H, int W, long long page_s
     if (crow < stc::WR) *reinterpret_cast<uint4 *>(win + crow * stc::WB + 16 * ck) = chunk;
     __syncthreads();
     chunk = load_chunk(t + gridDim.x);  // next tile's window, in flight meanwhile
-    {  // A row of this pixel: tap bytes in (ky, kx, ci) order, twice
+    {  // A row of this pixel: tap bytes in (ky, kx, ci) order, twice. A tap
+       // outside the image reads a zero: load_chunk leaves the window's rows
+       // above / below the image and its 16-byte chunks left / right of a row
+       // at zero, so no per-tap bounds test is needed.
       uint32_t pk[16];
       __half prev = __ushort2half_rn(0);
+      const int off0 = (int)(3ll * (ix0 + 2 * px) - a0);
 #pragma unroll
       for (int ky = 0; ky < 3; ++ky) {
-        const int y = iy0 + 2 * py + ky;
-        const uint8_t *wr = win + (2 * py + ky) * stc::WB;
+        const uint8_t *wr = win + (2 * py + ky) * stc::WB + off0;
 #pragma unroll
         for (int kx = 0; kx < 3; ++kx) {
-          const int x = ix0 + 2 * px + kx;
-          const bool in = y >= 0 && y < H && x >= 0 && x < W;
-          const int off = (int)(3ll * x - a0);
 #pragma unroll
           for (int ci = 0; ci < 3; ++ci) {
             const int k = (ky * 3 + kx) * 3 + ci;
-            const __half v = __ushort2half_rn(in ? wr[off + ci] : 0);
+            const __half v = __ushort2half_rn(wr[3 * kx + ci]);
             if (k & 1) pk[k >> 1] = pack_h2(prev, v);
             else prev = v;
           }
