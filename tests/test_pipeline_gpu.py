@@ -199,3 +199,26 @@ def test_pipeline_small_batch(cuda):
         ref_toks, ref_score = co.decode_logits(logits[c], REC_V)
         assert res[m][k][2] == ref_toks
         assert abs(res[m][k][3] - ref_score) <= 1e-3
+
+
+def test_detection_half_matches_the_full_run(cuda):
+    """run(rec=False) (the bench's det_only figure) enqueues the same
+    detection stages: boxes, scores, crop transforms and crops identical to
+    a full run's, and no recognition output written."""
+    from turboocr_b200.pipeline import PagePipeline
+    B = 2
+    p = pages(cuda, B, first=7)
+    full = PagePipeline(cuda, B)
+    full.run(p)
+    det = PagePipeline(cuda, B)
+    det.lengths.fill_(-7)
+    det.run(p, rec=False)
+    torch.cuda.synchronize()
+    assert full.errors() == 0 and det.errors() == 0
+    n = int(full.crop_off[B].item())
+    assert n > 0 and int(det.crop_off[B].item()) == n
+    for a, b in ((full.db.boxes, det.db.boxes), (full.db.scores, det.db.scores),
+                 (full.db.counts, det.db.counts), (full.minv[:n], det.minv[:n]),
+                 (full.crops[:n], det.crops[:n])):
+        assert torch.equal(a, b)
+    assert bool((det.lengths == -7).all())
