@@ -390,16 +390,34 @@ dwpw_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
         const float qmax = K::FP8 ? 448.f : 127.f;
         const int c0 = part * 8;
         const int j16 = c0 / 16, atom = j16 / 8, chunk = j16 % 8, hb = (c0 % 16) / 8;
+        // With the row-major lane map a warp's eight lane groups hold pixels
+        // 16 rows apart, which share one 128-byte swizzle pattern; odd rows
+        // take their pixels in the other order, so that one store of the warp
+        // covers two patterns (4-way instead of 8-way bank conflicts).
+        const bool flip = K::ROWMAP && (seg_row & 1);
+        if constexpr (K::ROWMAP) {  // SEG == 2: swap the two pixels in place
+          static_assert(!K::ROWMAP || K::SEG == 2, "row map pairs");
 #pragma unroll
-        for (int j = 0; j < K::SEG; ++j) {
+          for (int q = 0; q < 4; ++q) {
+            const __half2 a0 = keep[0][q], a1 = keep[1][q];
+            keep[0][q] = flip ? a1 : a0;
+            keep[1][q] = flip ? a0 : a1;
+          }
+          const float m0 = amax[0], m1 = amax[1];
+          amax[0] = flip ? m1 : m0;
+          amax[1] = flip ? m0 : m1;
+        }
+#pragma unroll
+        for (int jj = 0; jj < K::SEG; ++jj) {
+          const int j = flip ? K::SEG - 1 - jj : jj;
           const int p = seg_row * TW + seg_col + j;
-          const float am = amax[j];
+          const float am = amax[jj];
           const float inv = am > 0.f ? qmax / am : 0.f;
           if (part == 0) sscale[ss * TP + p] = am / qmax;
           float f[8];
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            const float2 ff = __half22float2(keep[j][q]);
+            const float2 ff = __half22float2(keep[jj][q]);
             f[2 * q] = ff.x;
             f[2 * q + 1] = ff.y;
           }
