@@ -91,6 +91,24 @@ def test_batch_of_64_pages_checksums(cuda):
     _check_batch(cuda, files, exp)
 
 
+def test_batch_with_several_files_per_sm(cuda):
+    """448 files in one call: three or more inflate CTAs resident per SM
+    (the bench's batch shape), every image byte-exact with the reference."""
+    rng = np.random.default_rng(8)
+    files, exp = [], []
+    for k in range(448):
+        h, w = int(rng.integers(40, 160)), int(rng.integers(40, 200))
+        ct = int(rng.choice([0, 2, 6]))
+        page = ps.page_like(h, w, 5000 + k, channels=ps.CHANNELS[ct])
+        if ct == 0:
+            page = page[..., 0]
+        b = ps.encode(page, ct, 8, filters="random", seed=k,
+                      strategy=int(rng.choice([zlib.Z_DEFAULT_STRATEGY, zlib.Z_RLE, zlib.Z_FIXED])))
+        files.append(b)
+        exp.append((f"s{k}", po.reference_decode(b)))
+    _check_batch(cuda, files, exp)
+
+
 def test_size_caps_reject_on_the_host(cuda, monkeypatch):
     big = ps.encode(np.zeros((70, 90, 3), np.uint8), 2, 8)
     monkeypatch.setenv("MAX_IMAGE_DIM", "80")
